@@ -1,0 +1,389 @@
+#!/usr/bin/env python3
+"""Benchmark of the vx27 attention hot path on B200: BASELINE.json's metric
+"DeltaNet+GQA decode tokens/s at 1/2/4/8 B200; % of HBM roofline" on its config 2
+(batched hybrid decode step: 48 Gated DeltaNet + 16 gated GQA layers, 256 sequences per
+GPU, BF16 KV cache of 4096 tokens per layer, 64 decode steps, seed 2).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One process per GPU (torchrun for N > 1). Every rank holds its own 256 sequences (weak
+scaling, no collective on the data path). Timing: W untimed steps, then K steps between a
+barrier + cuda synchronize, CUDA events on the launching stream, max over ranks. The
+resident working set (~84 GB per GPU) is far larger than L2, so no flush is needed.
+Rank 0 prints one JSON line.
+
+--impl reference times the reference's own CPU implementation of the same step
+(oracle/_ref, compiled from the reference's sources; the oracle port if absent) on the
+host cores, on a bounded sample of sequences per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "DeltaNet+GQA decode tokens/s at 1/2/4/8 B200; % of HBM roofline"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples every 200 ms while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
+    import torch
+    import torch.distributed as dist
+    from vx27_b200.hybrid import HybridConfig, HybridDecoder, N_FULL, N_LIN
+
+    torch.cuda.set_device(local_rank)
+    cfg = HybridConfig(batch=args.batch, ctx=args.ctx, steps=args.warmup + args.steps + 2,
+                       seed=2 + rank * 1000)
+    dec = HybridDecoder(cfg)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up, then the device-resident timed region
+    for _ in range(args.warmup):
+        dec.step()
+    barrier()
+    ev = {"dn": [], "gqa": []}
+
+    def on_layer(kind, i, phase):
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        ev[kind].append(e)
+
+    ctx0 = int(dec.pos[0].item())
+    with ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ
+                      else int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank])) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        launches = 0
+        for _ in range(args.steps):
+            launches += dec.step(on_layer=on_layer)
+        t1.record(stream)
+        barrier()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ms_step = ms / args.steps
+
+    def avg_ms(kind):
+        e = ev[kind]
+        return sum(e[2 * j].elapsed_time(e[2 * j + 1]) for j in range(len(e) // 2)) / (len(e) // 2)
+
+    # attended positions per step average (positions 0..pos inclusive)
+    ctx_avg = ctx0 + 1 + (args.steps - 1) / 2.0
+    by = dec.bytes_per_step(ctx_avg)
+    c = cfg
+    gqa_bytes = by["kv"] / N_FULL + (c.batch * c.nq * c.hd * 2 * 2) + c.batch * c.nq * c.hd * 4
+    dn_bytes = (by["dn_state"] + by["dn_conv"] + by["dn_act"]) / N_LIN
+    peak, peak_src = peaks()
+    gqa_ms, dn_ms = avg_ms("gqa"), avg_ms("dn")
+    gqa_gbs = gqa_bytes / (gqa_ms * 1e-3) / 1e9
+    dn_gbs = dn_bytes / (dn_ms * 1e-3) / 1e9
+    step_gbs = by["total"] / (ms_step * 1e-3) / 1e9
+
+    # end-to-end through the public API with host buffers: H2D of the step's
+    # activations from pinned memory, the step, D2H of the step's attention outputs
+    hin = [t.cpu().pin_memory() for t in dec.step_inputs()]
+    hout = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in dec.step_outputs()]
+    h2d = sum(t.numel() * t.element_size() for t in hin)
+    d2h = sum(t.numel() * t.element_size() for t in hout)
+
+    def e2e_step():
+        for d, h in zip(dec.step_inputs(), hin):
+            d.copy_(h, non_blocking=True)
+        dec.step()
+        for h, d in zip(hout, dec.step_outputs()):
+            h.copy_(d, non_blocking=True)
+
+    dec.reset_positions()
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+
+    from vx27_b200 import ops
+    status = ops.device_status()
+    if rank != 0:
+        return None
+    tokens = c.batch * world * args.steps
+    return {
+        "metric": METRIC,
+        "value": round(tokens / (ms * 1e-3), 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded splitmix64 + Box-Muller, config 2 distributions)",
+        "config": {
+            "workload": "config 2: batched hybrid decode step, 48 Gated DeltaNet + 16 gated GQA "
+                        "layers (3:1 order), hd 128 / 24Q-4KV hd 256, BF16 KV cache",
+            "batch_per_gpu": c.batch, "global_batch": c.batch * world,
+            "ctx_at_first_step": ctx0 + 1, "decode_steps": args.steps,
+            "state": "fp32 S ~N(0,0.05); KV bf16 ~N(0,1); activations bf16 ~N(0,1)",
+            "l2": "inputs larger than L2 (resident working set %.1f GB/GPU)" %
+                  (sum(t.numel() * t.element_size() for t in (dec.S, dec.ring, dec.kc, dec.vc))
+                   / 1e9),
+            "parallelism": f"dp{world} (sequences sharded, no collective)",
+        },
+        "roofline": {
+            "bound": "hbm", "kernel": "gqa split-KV decode (per layer, + combine)",
+            "achieved": round(gqa_gbs, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(gqa_gbs / peak, 4), "traffic": None, "peak_source": peak_src,
+            "algorithmic_bytes_per_launch": int(gqa_bytes), "avg_launch_ms": round(gqa_ms, 4),
+        },
+        "roofline_other": {
+            "deltanet_decode": {"achieved": round(dn_gbs, 1), "frac": round(dn_gbs / peak, 4),
+                                "algorithmic_bytes_per_launch": int(dn_bytes),
+                                "avg_launch_ms": round(dn_ms, 4)},
+            "whole_step": {"achieved": round(step_gbs, 1), "frac": round(step_gbs / peak, 4),
+                           "algorithmic_bytes_per_step": int(by["total"]),
+                           "frac_of_nominal_8TBps": round(step_gbs / 8000.0, 4)},
+        },
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms / args.steps, 4)},
+        "gpu_launches": launches,
+        "device_status": status,
+        "clocks": clk.summary(),
+    }
+
+
+# ------------------------------------------------------------ CPU reference
+def cpu_reference_step_sampler(n_seq: int, ctx: int, threads: int):
+    """Builds host buffers for n_seq sequences of config 2 and returns (run_step, kind).
+    run_step() runs one decode step of those sequences through all 64 layers with the
+    reference's step_exact/conv1d_step/gate_params/rmsnorm/rope (oracle/_ref) when built,
+    else the oracle port; the attention loop is the restatement of src/vx27_qfwd.c:347-371
+    over a BF16 cache (the reference has no callable long-context attention)."""
+    from oracle import oracle as orc
+    kind = "reference" if orc.use_reference(True) else "port"
+    L = orc.lib()
+    P = orc.P
+    nqk = nv = 16
+    hd, nq, nkv, HD = 128, 24, 4, 256
+    C = (2 * nqk + nv) * hd
+    cap = ctx + 1
+    rng = np.random.default_rng(2)
+    block = rng.standard_normal(1 << 20).astype(np.float32)
+
+    def tiled(n, scale=1.0, dtype=np.float32):
+        reps = -(-n // block.size)
+        a = np.tile(block * scale, reps)[:n]
+        return np.ascontiguousarray(a if dtype == np.float32 else orc.to_bf16(a))
+
+    S = [tiled(n_seq * nv * hd * hd, 0.05) for _ in range(48)]
+    ring = [tiled(n_seq * 4 * C) for _ in range(48)]
+    qkv = tiled(n_seq * C, dtype=np.uint16)
+    ab = tiled(n_seq * nv, dtype=np.uint16)
+    conv_w = tiled(C * 4, 0.5)
+    A_log = np.log(np.linspace(1, 16, nv)).astype(np.float32)
+    dt_bias = tiled(nv, 0.1)
+    kc = [tiled(n_seq * nkv * cap * HD, dtype=np.uint16) for _ in range(16)]
+    vc = [tiled(n_seq * nkv * cap * HD, dtype=np.uint16) for _ in range(16)]
+    qi = tiled(n_seq * nq * HD, dtype=np.uint16)
+    ki = tiled(n_seq * nkv * HD, dtype=np.uint16)
+    gate = tiled(n_seq * nq * HD, dtype=np.uint16)
+    wn = np.ones(HD, np.float32)
+    o = np.zeros(n_seq * nv * hd, np.float32)
+    qo = np.zeros(n_seq * nq * HD, np.float32)
+    att = np.zeros(n_seq * nq * HD, np.float32)
+    pos = np.full(n_seq, ctx, np.int32)
+
+    def run_step():
+        for layer in range(64):
+            if (layer + 1) % 4:
+                i = layer - (layer + 1) // 4
+                L.orc_deltanet_decode_batch_mt(P(S[i]), P(ring[i]), P(qkv), P(ab), P(ab),
+                                               P(A_log), P(dt_bias), P(conv_w), P(pos), P(o),
+                                               n_seq, nqk, nv, hd, orc.F_ACT_BF16, threads)
+            else:
+                i = layer // 4
+                L.orc_gqa_append(P(qi), P(ki), P(ki), P(wn), P(wn), P(pos), P(kc[i]), P(vc[i]),
+                                 cap, P(qo), n_seq, nq, nkv, HD, 64, 1e7, 1e-6, orc.F_ACT_BF16)
+                L.orc_gqa_attend_mt(P(qo), P(gate), P(kc[i]), P(vc[i]), cap, P(pos), P(att),
+                                    n_seq, nq, nkv, HD, orc.F_ACT_BF16, threads)
+    return run_step, kind
+
+
+def cpu_baseline(n_seq: int, ctx: int, min_s: float = 3.0, max_reps: int = 10) -> dict:
+    threads = os.cpu_count() or 1
+    run, kind = cpu_reference_step_sampler(n_seq, ctx, threads)
+    run()  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_s or reps >= max_reps:
+            break
+    return {"value": round(n_seq * reps / el, 3), "unit": "tokens/s", "cores": threads,
+            "kind": kind,
+            "sample": f"{n_seq} sequences x {reps} decode steps x 64 layers at ctx {ctx} "
+                      f"({el:.1f} s wall, all host threads)"}
+
+
+def run_reference(args, rank: int) -> dict | None:
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    n_seq = args.ref_seqs
+    run, kind = cpu_reference_step_sampler(n_seq, args.ctx, threads)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    el = time.perf_counter() - t0
+    v = round(n_seq * args.steps / el, 3)
+    return {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate/f32",
+        "data": "synthetic",
+        "config": {"workload": "config 2 (bounded CPU sample of sequences per step)",
+                   "sequences_per_step": n_seq, "ctx": args.ctx},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": f"{n_seq} sequences per step x 64 layers, {args.steps} "
+                                   f"steps"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=256, help="sequences per GPU")
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--ref-seqs", type=int, default=4)
+    ap.add_argument("--cpu-seqs", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line:
+            print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+        if line is not None:
+            if world == 1 and not args.no_cpu_baseline:
+                line["cpu_baseline"] = cpu_baseline(args.cpu_seqs, args.ctx)
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

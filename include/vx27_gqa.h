@@ -1,0 +1,84 @@
+/*
+ * Gated GQA attention on B200 (libvx27cuda). Drop-in for src/vx27_gqa.h of
+ * DavidPandleton/vx27 (first block, same signatures, host pointers), plus the batched
+ * device-resident decode over a BF16 KV cache (second block).
+ */
+#ifndef VX27_GQA_H
+#define VX27_GQA_H
+#include <stddef.h>
+#include "vx27cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------- reference entry points (src/vx27_gqa.h) ----------------------- */
+/* q_head * 4 / 24. Host integer arithmetic. Replaces src/vx27_gqa.h:8. */
+int vx27_gqa_kv_for_q(int q_head);
+/* y = x / sqrt(mean(x^2) + eps) * w, sum in double; on the GPU.
+ * Replaces src/vx27_gqa.h:9. */
+void vx27_rmsnorm(const float *x, const float *w, float *y, int n, float eps);
+/* Single-query attention, 24 Q / 4 KV heads of 256, fp32 caches [pos][4][256], on the
+ * GPU. Same arithmetic as the reference; the reference's 1024-position limit (a static
+ * score buffer) does not apply, and the function is reentrant.
+ * Replaces src/vx27_gqa.h:12-13. */
+void vx27_attn_1q(const float *q, const float *kcache, const float *vcache, int n_pos,
+                  float *out);
+
+/* ---------------- batched device-resident tier (no reference counterpart) ------- */
+/*
+ * Per-token prologue of a full-attention layer, for B sequences (src/vx27_qfwd.c:
+ * 339-346): RMSNorm of q and k per head (eps, weights q_norm_w/k_norm_w [hd]; standard
+ * x*s*w, or x*s*(1+w) with VX27_F_NORM_1P), partial NeoX RoPE of the first rope_dim
+ * dims at position pos[b] (row pos[b] of a table from vx27_rope_table_build), then a
+ * bf16 store of the rotated k and of v into slot pos[b] - slot_base of the caches.
+ *   q_in [B][nq][hd], k_in/v_in [B][nkv][hd]   activations (act dtype)
+ *   k_cache/v_cache bf16 [B][nkv][cap][hd]; NULL skips the store, as does a slot
+ *                   outside [0, cap) (context-parallel shards that do not own pos)
+ *   q_out [B][nq][hd] fp32: normalised, rotated q for vx27_gqa_decode_batch
+ */
+int vx27_gqa_append(const void *q_in, const void *k_in, const void *v_in,
+                    const float *q_norm_w, const float *k_norm_w, const float *rope_table,
+                    int rope_table_len, const int *pos, int slot_base, void *k_cache,
+                    void *v_cache, int cap, float *q_out, int B, int nq, int nkv, int hd,
+                    int rope_dim, float eps, int flags, void *stream, char *err,
+                    size_t errlen);
+
+/*
+ * Decode attention of q (from vx27_gqa_append) over slots [0, pos[b]] of the caches,
+ * softmax(q k^T / sqrt(hd)) v per Q head (Q head h reads KV head h*nkv/nq), then
+ * out = att * sigmoid(gate) (src/vx27_qfwd.c:347-371). Split-KV flash decoding: each
+ * (sequence, KV head, split) block serves the nq/nkv Q heads of its group; splits are
+ * merged with a log-sum-exp combine. n_splits = 0 picks a split count for the device.
+ *   gate [B][nq][hd] (act dtype); out [B][nq][hd] (fp32 or bf16 per VX27_F_OUT_BF16)
+ *   workspace: vx27_gqa_decode_workspace_size(B, nq, nkv, hd, cap, n_splits) bytes of
+ *   device memory; a smaller workspace lowers the automatic split count to what fits.
+ *   hd must be 256.
+ */
+size_t vx27_gqa_decode_workspace_size(int B, int nq, int nkv, int hd, int max_ctx,
+                                      int n_splits);
+int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
+                          const void *v_cache, int cap, const int *pos, void *out,
+                          void *workspace, size_t workspace_bytes, int B, int nq, int nkv,
+                          int hd, int n_splits, int flags, void *stream, char *err,
+                          size_t errlen);
+
+/*
+ * Context-parallel pieces. A partial record covers cache slots [p_begin, p_end) (the
+ * same range for all B sequences): for each (b, Q head) m = max scaled score,
+ * l = sum exp(s - m), o = sum exp(s - m) v / l. Record layout (fp32):
+ *   o [B][nq][hd] followed by ml [B][nq][2]; record size B*nq*(hd+2) floats.
+ * An empty range yields m = -inf, l = 0, o = 0. vx27_gqa_combine merges n_parts
+ * consecutive records (m* = max m_i, l* = sum l_i e^{m_i-m*}, o = sum o_i l_i
+ * e^{m_i-m*} / l*) and applies the sigmoid gate.
+ */
+int vx27_gqa_partial(const float *q, const void *k_cache, const void *v_cache, int cap,
+                     int p_begin, int p_end, float *part, int B, int nq, int nkv, int hd,
+                     void *stream, char *err, size_t errlen);
+int vx27_gqa_combine(const float *parts, int n_parts, const void *gate, void *out, int B,
+                     int nq, int hd, int flags, void *stream, char *err, size_t errlen);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,127 @@
+"""K1 (vx27_deltanet_decode_batch) against the CPU oracle on the same seeded inputs.
+
+Tolerance: DeltaNet output and state within 1e-4 max-abs of the reference path
+(conv1d_step -> gate_params -> step_exact per head, src/vx27_qfwd.c:276-297)."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import dev, host
+from vx27_b200 import ops
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+def make_layer(orc, seed, B, nqk, nv, hd=128, s_std=0.0):
+    Cch = (2 * nqk + nv) * hd
+    S = (orc.normal(B * nv * hd * hd, seed, 10, 0.0, s_std) if s_std > 0
+         else np.zeros(B * nv * hd * hd, np.float32))
+    return dict(S=S, ring=np.zeros(B * 4 * Cch, np.float32),
+                conv_w=orc.normal(Cch * 4, seed, 4, 0.0, 0.5),
+                A_log=np.log(orc.uniform(nv, seed, 5, 1.0, 16.0)).astype(np.float32),
+                dt_bias=orc.normal(nv, seed, 6, 0.0, 0.1), C=Cch)
+
+
+def run_both(orc, lay, T, B, nqk, nv, seed, bf16, pos0=None, gates_f64=False, out_bf16=False):
+    hd = 128
+    Cch = lay["C"]
+    qkv_all = orc.normal(T * B * Cch, seed, 1, bf16=bf16).reshape(T, B * Cch)
+    a_all = orc.normal(T * B * nv, seed, 2, bf16=bf16).reshape(T, B * nv)
+    b_all = orc.normal(T * B * nv, seed, 3, bf16=bf16).reshape(T, B * nv)
+    pos0 = np.zeros(B, np.int32) if pos0 is None else pos0.astype(np.int32)
+    # oracle
+    S, ring = lay["S"].copy(), lay["ring"].copy()
+    o_ref = np.zeros((T, B * nv * hd), np.float32)
+    L = orc.lib()
+    flags = orc.F_ACT_BF16 if bf16 else 0
+    for t in range(T):
+        posv = pos0 + t
+        q, a, b = (np.ascontiguousarray(x[t]) for x in (qkv_all, a_all, b_all))
+        o = np.zeros(B * nv * hd, np.float32)
+        L.orc_deltanet_decode_batch_mt(orc.P(S), orc.P(ring), orc.P(q), orc.P(a), orc.P(b),
+                                       orc.P(lay["A_log"]), orc.P(lay["dt_bias"]),
+                                       orc.P(lay["conv_w"]), orc.P(posv), orc.P(o), B, nqk, nv,
+                                       hd, flags, 8)
+        o_ref[t] = o
+    # GPU
+    dS = dev(lay["S"]).view(B, nv, hd, hd)
+    dring = dev(lay["ring"])
+    dq = dev(qkv_all, bf16)
+    if gates_f64:
+        # host-computed gates through the reference-identical C-ABI gate function
+        from oracle.oracle import from_bf16
+        af = from_bf16(a_all) if bf16 else a_all
+        bf = from_bf16(b_all) if bf16 else b_all
+        gb = np.zeros((T, B * nv)), np.zeros((T, B * nv))
+        for t in range(T):
+            for i in range(B * nv):
+                gb[0][t, i], gb[1][t, i] = ops.vx27_deltanet_gate_params(
+                    float(af[t, i]), float(lay["A_log"][i % nv]), float(bf[t, i]),
+                    float(lay["dt_bias"][i % nv]))
+        da, db = dev(gb[0]), dev(gb[1])
+    else:
+        da, db = dev(a_all, bf16), dev(b_all, bf16)
+    dA, dd, dw = dev(lay["A_log"]), dev(lay["dt_bias"]), dev(lay["conv_w"])
+    dpos = dev(pos0)
+    do = torch.empty((T, B * nv * hd), dtype=torch.bfloat16 if out_bf16 else torch.float32,
+                     device="cuda")
+    for t in range(T):
+        ops.deltanet_decode_batch(dS, dring, dq[t], da[t], db[t], dA, dd, dw, dpos, do[t], nqk, nv,
+                                  gates_f64=gates_f64)
+        ops.add_int(dpos, 1)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    o_gpu = host(do)
+    if out_bf16:
+        o_gpu = (o_gpu.astype(np.uint32) << 16).view(np.float32)
+    return o_ref, S, ring, o_gpu, host(dS).reshape(-1), host(dring)
+
+
+def test_config0_full_2000_tokens(cuda, orc):
+    """Config 0: 16 heads, batch 1, zero state, 2000 tokens, fp32 activations, seed 0."""
+    B, nqk, nv, T = 1, 16, 16, 2000
+    lay = make_layer(orc, 0, B, nqk, nv)
+    o_ref, S_ref, ring_ref, o, S, ring = run_both(orc, lay, T, B, nqk, nv, 0, bf16=False)
+    err_o, err_s = np.abs(o - o_ref).max(), np.abs(S - S_ref).max()
+    print(f"config0: max|o-ref|={err_o:.3e} max|S-ref|={err_s:.3e}")
+    assert err_o < TOL and err_s < TOL
+    assert np.array_equal(ring, ring_ref)  # the conv history is copied bits
+
+
+def test_bf16_grouped_heads_ragged_positions(cuda, orc):
+    """Real-model head grouping (48 V heads over 16 QK heads), bf16 activations, a batch
+    whose sequences sit at different positions, non-zero initial state."""
+    B, nqk, nv, T = 3, 16, 48, 12
+    lay = make_layer(orc, 5, B, nqk, nv, s_std=0.05)
+    o_ref, S_ref, _, o, S, _ = run_both(orc, lay, T, B, nqk, nv, 5, bf16=True,
+                                        pos0=np.array([0, 2, 117]))
+    assert np.abs(o - o_ref).max() < TOL and np.abs(S - S_ref).max() < TOL
+
+
+def test_host_gates_and_bf16_output(cuda, orc):
+    B, nqk, nv, T = 2, 2, 6, 6
+    lay = make_layer(orc, 6, B, nqk, nv, s_std=0.05)
+    o_ref, S_ref, _, o, S, _ = run_both(orc, lay, T, B, nqk, nv, 6, bf16=True, gates_f64=True,
+                                        out_bf16=True)
+    assert np.abs(S - S_ref).max() < TOL
+    # bf16 output: within one bf16 rounding of the fp32 reference
+    assert np.all(np.abs(o - o_ref) <= np.abs(o_ref) * 2.0 ** -8 + TOL)
+
+
+def test_conv_ring_import_export_roundtrip(cuda, orc):
+    import ctypes as C
+    from vx27_b200._lib import errbuf, load
+    B, Cch = 3, 640
+    state = orc.normal(B * Cch * 3, 12, 1)
+    pos = np.array([0, 5, 1030], np.int32)
+    ring = torch.zeros(B * 4 * Cch, device="cuda")
+    e = errbuf()
+    lib = load()
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.vx27_deltanet_conv_import(C.c_void_p(ring.data_ptr()), state.ctypes.data_as(C.c_void_p),
+                                         pos.ctypes.data_as(C.c_void_p), B, Cch, st, e, 512) == 0
+    back = np.zeros_like(state)
+    assert lib.vx27_deltanet_conv_export(C.c_void_p(ring.data_ptr()), back.ctypes.data_as(C.c_void_p),
+                                         pos.ctypes.data_as(C.c_void_p), B, Cch, st, e, 512) == 0
+    assert np.array_equal(back, state)

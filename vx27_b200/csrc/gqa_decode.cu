@@ -1,0 +1,363 @@
+// K2: gated GQA decode over a BF16 KV cache.
+//   gqa_append_k   per-token prologue: QK RMSNorm, partial RoPE, bf16 K/V store
+//                  (src/vx27_qfwd.c:339-346)
+//   gqa_split_k    split-KV flash decoding, one CTA per (sequence, KV head, split)
+//                  serving the nq/nkv Q heads of the group, online softmax in fp32;
+//                  writes one partial record (m, l, o) per split
+//   gqa_combine_k  log-sum-exp merge of the partial records + sigmoid output gate
+//                  (src/vx27_qfwd.c:347-371)
+#include <math.h>
+#include "common.cuh"
+#include "../../include/vx27_gqa.h"
+
+namespace vx27 {
+namespace {
+
+constexpr int HD = 256;
+constexpr int TILE = 128;  // split boundaries fall on multiples of TILE positions
+
+// ---- append -------------------------------------------------------------------
+template <bool ACT_BF16, bool ONE_P>
+__global__ void __launch_bounds__(HD)
+gqa_append_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
+             const void *__restrict__ v_in, const float *__restrict__ qw,
+             const float *__restrict__ kw, const float *__restrict__ rope, int rope_len,
+             const int *__restrict__ pos, int slot_base, uint16_t *__restrict__ kc,
+             uint16_t *__restrict__ vc, int cap, float *__restrict__ q_out, int nq, int nkv,
+             int rope_dim, float eps, uint32_t *status) {
+    const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const bool is_q = head < nq;
+    const int h = is_q ? head : head - nq;
+    const size_t row = is_q ? ((size_t)b * nq + h) * HD : ((size_t)b * nkv + h) * HD;
+    const float x = act_ld<ACT_BF16>(is_q ? q_in : k_in, row + d);
+    __shared__ double red[HD / 32];
+    __shared__ float r_s;
+    __shared__ float y_s[HD];
+    double ss = warp_sum_d((double)x * (double)x);
+    if ((d & 31) == 0) red[d >> 5] = ss;
+    __syncthreads();
+    if (d == 0) {
+        double t = 0.0;
+        for (int w = 0; w < HD / 32; w++) t += red[w];
+        r_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(t / HD), eps)));
+    }
+    __syncthreads();
+    float w = is_q ? qw[d] : kw[d];
+    if (ONE_P) w = __fadd_rn(w, 1.0f);
+    const float y = __fmul_rn(__fmul_rn(x, r_s), w);
+    y_s[d] = y;
+    __syncthreads();
+    const int p = pos[b];
+    const int half = rope_dim / 2;
+    float out = y;
+    if (d < rope_dim) {
+        if (p < 0 || p >= rope_len) {
+            if (d == 0) dev_flag(status, VX_DEV_BAD_ARG);
+        } else {
+            const float *rr = rope + (size_t)p * rope_dim;
+            const int i = d < half ? d : d - half;
+            const float c = rr[i], s = rr[half + i];
+            const float x0 = y_s[i], x1 = y_s[i + half];
+            out = d < half ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s))
+                           : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        }
+    }
+    if (is_q) {
+        q_out[row + d] = out;
+    } else if (kc) {
+        const int slot = p - slot_base;
+        if (slot >= 0 && slot < cap) {
+            const size_t o = (((size_t)b * nkv + h) * cap + slot) * HD + d;
+            kc[o] = f32_to_bf16(out);
+            vc[o] = f32_to_bf16(act_ld<ACT_BF16>(v_in, row + d));
+        }
+    }
+}
+
+// ---- split-KV attention (CUDA cores) ----------------------------------------------
+__device__ __forceinline__ void bf16x8_to_f32(uint4 u, float *f) {
+    f[0] = u32_as_f32(u.x << 16); f[1] = u32_as_f32(u.x & 0xffff0000u);
+    f[2] = u32_as_f32(u.y << 16); f[3] = u32_as_f32(u.y & 0xffff0000u);
+    f[4] = u32_as_f32(u.z << 16); f[5] = u32_as_f32(u.z & 0xffff0000u);
+    f[6] = u32_as_f32(u.w << 16); f[7] = u32_as_f32(u.w & 0xffff0000u);
+}
+
+// Range of cache slots for (sequence b, split s): a fixed range when p_end >= 0,
+// else slots [0, pos[b]] cut into n_splits pieces on TILE boundaries.
+__device__ __forceinline__ void split_range(const int *pos, int b, int s, int n_splits,
+                                            int p_begin, int p_end, int *p0, int *p1) {
+    if (p_end >= 0) { *p0 = p_begin; *p1 = p_end; return; }
+    const int n = pos[b] + 1;
+    const int tiles = (n + TILE - 1) / TILE;
+    const int per = (tiles + n_splits - 1) / n_splits;
+    const int a = s * per * TILE;
+    const int e = min(n, (s + 1) * per * TILE);
+    *p0 = a;
+    *p1 = e > a ? e : a;
+}
+
+template <int G>
+__global__ void __launch_bounds__(256)
+gqa_split_k(const float *__restrict__ q, const uint16_t *__restrict__ kc,
+            const uint16_t *__restrict__ vc, int cap, const int *__restrict__ pos,
+            float *__restrict__ parts, int B, int nq, int nkv, int n_splits, int p_begin,
+            int p_end) {
+    const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int p0, p1;
+    split_range(pos, b, s, n_splits, p_begin, p_end, &p0, &p1);
+    if (p0 < 0) p0 = 0;
+    if (p1 > cap) p1 = cap;
+    const int h0 = kvh * G;  // Q heads h with h*nkv/nq == kvh
+    float qr[G][8];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const float4 *qp = reinterpret_cast<const float4 *>(q + ((size_t)b * nq + h0 + g) * HD + lane * 8);
+        const float4 a = qp[0], c = qp[1];
+        qr[g][0] = a.x; qr[g][1] = a.y; qr[g][2] = a.z; qr[g][3] = a.w;
+        qr[g][4] = c.x; qr[g][5] = c.y; qr[g][6] = c.z; qr[g][7] = c.w;
+    }
+    float m[G], l[G], acc[G][8];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) acc[g][i] = 0.0f;
+    }
+    const size_t base = ((size_t)b * nkv + kvh) * cap;
+    const uint4 *K = reinterpret_cast<const uint4 *>(kc + base * HD);
+    const uint4 *V = reinterpret_cast<const uint4 *>(vc + base * HD);
+    for (int p = p0 + warp; p < p1; p += 8) {
+        float kf[8], vf[8];
+        bf16x8_to_f32(__ldcs(K + (size_t)p * (HD / 8) + lane), kf);
+        bf16x8_to_f32(__ldcs(V + (size_t)p * (HD / 8) + lane), vf);
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float dot = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) dot = fmaf(qr[g][i], kf[i], dot);
+            const float sc = warp_sum(dot) * 0.0625f;  // 1/sqrt(256), exact
+            const float mn = fmaxf(m[g], sc);
+            const float corr = expf(m[g] - mn);
+            const float pe = expf(sc - mn);
+            l[g] = l[g] * corr + pe;
+#pragma unroll
+            for (int i = 0; i < 8; i++) acc[g][i] = fmaf(pe, vf[i], acc[g][i] * corr);
+            m[g] = mn;
+        }
+    }
+    // merge the 8 warps
+    extern __shared__ float sm[];  // [8][G][HD] acc, then [8][G][2] (m, l)
+    float *sacc = sm, *sml = sm + 8 * G * HD;
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) sacc[(warp * G + g) * HD + lane * 8 + i] = acc[g][i];
+        if (lane == 0) { sml[(warp * G + g) * 2] = m[g]; sml[(warp * G + g) * 2 + 1] = l[g]; }
+    }
+    __syncthreads();
+    const size_t rec = (size_t)B * nq * (HD + 2);
+    float *po = parts + (size_t)s * rec;
+    float *pml = po + (size_t)B * nq * HD;
+    for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
+        const int g = e / HD, dd = e % HD;
+        float M = -INFINITY;
+        for (int w = 0; w < 8; w++) M = fmaxf(M, sml[(w * G + g) * 2]);
+        float L = 0.0f, O = 0.0f;
+        if (M != -INFINITY) {
+            for (int w = 0; w < 8; w++) {
+                const float mw = sml[(w * G + g) * 2];
+                if (mw == -INFINITY) continue;
+                const float f = expf(mw - M);
+                L += sml[(w * G + g) * 2 + 1] * f;
+                O += sacc[(w * G + g) * HD + dd] * f;
+            }
+        }
+        const size_t hq = (size_t)b * nq + h0 + g;
+        po[hq * HD + dd] = L > 0.0f ? O / L : 0.0f;
+        if (dd == 0) { pml[hq * 2] = L > 0.0f ? M : -INFINITY; pml[hq * 2 + 1] = L; }
+    }
+}
+
+// ---- combine ------------------------------------------------------------------------
+template <bool ACT_BF16, bool OUT_BF16>
+__global__ void __launch_bounds__(HD)
+gqa_combine_k(const float *__restrict__ parts, int n_parts, const void *__restrict__ gate,
+              void *__restrict__ out, int B, int nq) {
+    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const size_t rec = (size_t)B * nq * (HD + 2);
+    const size_t hq = (size_t)b * nq + h;
+    float M = -INFINITY;
+    for (int r = 0; r < n_parts; r++) {
+        const float *ml = parts + (size_t)r * rec + (size_t)B * nq * HD + hq * 2;
+        if (ml[1] > 0.0f) M = fmaxf(M, ml[0]);
+    }
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+        for (int r = 0; r < n_parts; r++) {
+            const float *pr = parts + (size_t)r * rec;
+            const float *ml = pr + (size_t)B * nq * HD + hq * 2;
+            if (!(ml[1] > 0.0f)) continue;
+            const float w = ml[1] * expf(ml[0] - M);
+            L += w;
+            O = fmaf(w, pr[hq * HD + d], O);
+        }
+    }
+    const float att = L > 0.0f ? O / L : 0.0f;
+    const float g = act_ld<ACT_BF16>(gate, hq * HD + d);
+    act_st<OUT_BF16>(out, hq * HD + d, att * (1.0f / (1.0f + expf(-g))));
+}
+
+int auto_splits(int B, int nkv, int max_ctx) {
+    const int blocks = B * nkv;
+    int n = (2 * num_sms() + blocks - 1) / blocks;
+    const int max_by_ctx = (max_ctx + TILE - 1) / TILE;
+    if (n > max_by_ctx) n = max_by_ctx;
+    if (n > 128) n = 128;
+    return n < 1 ? 1 : n;
+}
+
+int launch_split(const float *q, const void *kc, const void *vc, int cap, const int *pos,
+                 float *parts, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
+                 cudaStream_t st, char *err, size_t errlen) {
+    const int G = nq / nkv;
+    const dim3 grid(n_splits, nkv, B);
+    const size_t smem = (size_t)8 * G * (HD + 2) * sizeof(float);
+#define VX_G(GG)                                                                        \
+    case GG: {                                                                          \
+        static bool attr = false;                                                       \
+        if (!attr) {                                                                    \
+            VX_CK(cudaFuncSetAttribute(gqa_split_k<GG>,                                 \
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,     \
+                                       (int)smem));                                     \
+            attr = true;                                                                \
+        }                                                                               \
+        gqa_split_k<GG><<<grid, 256, smem, st>>>(q, (const uint16_t *)kc,               \
+                                                 (const uint16_t *)vc, cap, pos, parts, B, \
+                                                 nq, nkv, n_splits, p_begin, p_end);    \
+        break;                                                                          \
+    }
+    switch (G) {
+        VX_G(1) VX_G(2) VX_G(4) VX_G(6) VX_G(8)
+        default:
+            return fail(err, errlen, "vx27_gqa: group size %d (nq/nkv) unsupported", G);
+    }
+#undef VX_G
+    VX_CK(cudaGetLastError());
+    return 0;
+}
+
+int launch_combine(const float *parts, int n_parts, const void *gate, void *out, int B, int nq,
+                   int flags, cudaStream_t st, char *err, size_t errlen) {
+    const dim3 grid(nq, B);
+    const bool a = flags & VX27_F_ACT_BF16, o = flags & VX27_F_OUT_BF16;
+    if (a && o) gqa_combine_k<true, true><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq);
+    else if (a) gqa_combine_k<true, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq);
+    else if (o) gqa_combine_k<false, true><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq);
+    else gqa_combine_k<false, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq);
+    VX_CK(cudaGetLastError());
+    return 0;
+}
+
+int check_shape(const char *fn, int B, int nq, int nkv, int hd, char *err, size_t errlen) {
+    if (hd != HD) return fail(err, errlen, "%s: hd=%d unsupported (256 only)", fn, hd);
+    if (B <= 0 || B > 65535 || nq <= 0 || nkv <= 0 || nkv > 65535 || nq % nkv)
+        return fail(err, errlen, "%s: bad shape B=%d nq=%d nkv=%d", fn, B, nq, nkv);
+    return 0;
+}
+
+}  // namespace
+}  // namespace vx27
+
+using namespace vx27;
+
+extern "C" {
+
+int vx27_gqa_append(const void *q_in, const void *k_in, const void *v_in,
+                    const float *q_norm_w, const float *k_norm_w, const float *rope_table,
+                    int rope_table_len, const int *pos, int slot_base, void *k_cache,
+                    void *v_cache, int cap, float *q_out, int B, int nq, int nkv, int hd,
+                    int rope_dim, float eps, int flags, void *stream, char *err,
+                    size_t errlen) {
+    if (check_shape("vx27_gqa_append", B, nq, nkv, hd, err, errlen)) return -1;
+    if (rope_dim < 0 || rope_dim > hd || (rope_dim & 1))
+        return fail(err, errlen, "vx27_gqa_append: rope_dim=%d", rope_dim);
+    if (!q_in || !k_in || !v_in || !q_norm_w || !k_norm_w || !pos || !q_out ||
+        (rope_dim && !rope_table))
+        return fail(err, errlen, "vx27_gqa_append: null pointer argument");
+    if ((k_cache == nullptr) != (v_cache == nullptr))
+        return fail(err, errlen, "vx27_gqa_append: k_cache and v_cache must both be set or both NULL");
+    const dim3 grid(nq + nkv, B);
+    cudaStream_t st = (cudaStream_t)stream;
+    const bool a = flags & VX27_F_ACT_BF16, one = flags & VX27_F_NORM_1P;
+#define VX_A(A_, O_)                                                                    \
+    gqa_append_k<A_, O_><<<grid, HD, 0, st>>>(q_in, k_in, v_in, q_norm_w, k_norm_w,     \
+                                              rope_table, rope_table_len, pos, slot_base, \
+                                              (uint16_t *)k_cache, (uint16_t *)v_cache, cap, \
+                                              q_out, nq, nkv, rope_dim, eps, dev_status())
+    if (a && one) VX_A(true, true);
+    else if (a) VX_A(true, false);
+    else if (one) VX_A(false, true);
+    else VX_A(false, false);
+#undef VX_A
+    VX_CK(cudaGetLastError());
+    return 0;
+}
+
+size_t vx27_gqa_decode_workspace_size(int B, int nq, int nkv, int hd, int max_ctx,
+                                      int n_splits) {
+    if (B <= 0 || nq <= 0 || nkv <= 0 || hd <= 0) return 0;
+    if (n_splits <= 0) n_splits = auto_splits(B, nkv, max_ctx);
+    return (size_t)n_splits * B * nq * (hd + 2) * sizeof(float);
+}
+
+int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
+                          const void *v_cache, int cap, const int *pos, void *out,
+                          void *workspace, size_t workspace_bytes, int B, int nq, int nkv,
+                          int hd, int n_splits, int flags, void *stream, char *err,
+                          size_t errlen) {
+    if (check_shape("vx27_gqa_decode_batch", B, nq, nkv, hd, err, errlen)) return -1;
+    if (!q || !gate || !k_cache || !v_cache || !pos || !out || !workspace || cap <= 0)
+        return fail(err, errlen, "vx27_gqa_decode_batch: null pointer argument");
+    const size_t rec = (size_t)B * nq * (hd + 2) * sizeof(float);
+    const int fit = (int)(workspace_bytes / rec);
+    if (n_splits <= 0) {
+        n_splits = auto_splits(B, nkv, cap);
+        if (n_splits > fit) n_splits = fit;
+    }
+    if (n_splits < 1 || n_splits > fit || n_splits > 65535)
+        return fail(err, errlen,
+                    "vx27_gqa_decode_batch: workspace of %zu bytes holds %d splits, need %d",
+                    workspace_bytes, fit, n_splits < 1 ? 1 : n_splits);
+    cudaStream_t st = (cudaStream_t)stream;
+    float *parts = (float *)workspace;
+    if (launch_split(q, k_cache, v_cache, cap, pos, parts, B, nq, nkv, n_splits, 0, -1, st, err,
+                     errlen))
+        return -1;
+    return launch_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen);
+}
+
+int vx27_gqa_partial(const float *q, const void *k_cache, const void *v_cache, int cap,
+                     int p_begin, int p_end, float *part, int B, int nq, int nkv, int hd,
+                     void *stream, char *err, size_t errlen) {
+    if (check_shape("vx27_gqa_partial", B, nq, nkv, hd, err, errlen)) return -1;
+    if (!q || !k_cache || !v_cache || !part)
+        return fail(err, errlen, "vx27_gqa_partial: null pointer argument");
+    if (p_begin < 0 || p_end < p_begin || p_end > cap)
+        return fail(err, errlen, "vx27_gqa_partial: range [%d, %d) outside cache of %d", p_begin,
+                    p_end, cap);
+    return launch_split(q, k_cache, v_cache, cap, nullptr, part, B, nq, nkv, 1, p_begin, p_end,
+                        (cudaStream_t)stream, err, errlen);
+}
+
+int vx27_gqa_combine(const float *parts, int n_parts, const void *gate, void *out, int B,
+                     int nq, int hd, int flags, void *stream, char *err, size_t errlen) {
+    if (hd != HD) return fail(err, errlen, "vx27_gqa_combine: hd=%d unsupported (256 only)", hd);
+    if (!parts || !gate || !out || n_parts < 1 || B <= 0 || nq <= 0)
+        return fail(err, errlen, "vx27_gqa_combine: bad arguments");
+    return launch_combine(parts, n_parts, gate, out, B, nq, flags, (cudaStream_t)stream, err,
+                          errlen);
+}
+
+}  // extern "C"

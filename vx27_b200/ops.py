@@ -1,0 +1,244 @@
+"""Python mirror of the vx27 hot-path interface over libvx27cuda.
+
+Two groups, matching the two tiers of the C ABI:
+
+* reference mirror -- the functions of src/vx27_deltanet.h, src/vx27_gqa.h,
+  src/vx27_rope.h and src/vx27_kv.h of DavidPandleton/vx27 under the same names,
+  taking numpy float32 arrays (host memory) and computing on the GPU;
+* batched tier -- device-resident entry points taking torch CUDA tensors.
+
+Errors of the batched tier raise Vx27Error with the library's message. Nothing here
+computes on the CPU: every tensor operation goes through libvx27cuda.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from ._lib import Vx27Error, check, errbuf, load
+
+F_ACT_BF16 = 0x1
+F_OUT_BF16 = 0x2
+F_NORM_1P = 0x4
+F_GATES_F64 = 0x8
+
+
+def _np(a: np.ndarray, dtype=np.float32) -> C.c_void_p:
+    if a.dtype != dtype or not a.flags["C_CONTIGUOUS"]:
+        raise Vx27Error(f"expected a C-contiguous {np.dtype(dtype).name} array")
+    return a.ctypes.data_as(C.c_void_p)  # keeps the array alive with the pointer
+
+
+# ----------------------------------------------------------- reference mirror
+def vx27_deltanet_state_per_layer() -> int:
+    return load().vx27_deltanet_state_per_layer()
+
+
+def vx27_deltanet_state_total() -> int:
+    return load().vx27_deltanet_state_total()
+
+
+def vx27_deltanet_state_mb(bytes_per_elem: int) -> float:
+    return load().vx27_deltanet_state_mb(bytes_per_elem)
+
+
+def vx27_deltanet_update_ref(S, k, v, decay: float, hd: int) -> None:
+    load().vx27_deltanet_update_ref(_np(S), _np(k), _np(v), decay, hd)
+
+
+def vx27_deltanet_update_tiled(S, k, v, decay: float, hd: int) -> None:
+    load().vx27_deltanet_update_tiled(_np(S), _np(k), _np(v), decay, hd)
+
+
+def vx27_deltanet_update_avx2(S, k, v, decay: float, hd: int) -> None:
+    load().vx27_deltanet_update_avx2(_np(S), _np(k), _np(v), decay, hd)
+
+
+def vx27_deltanet_retrieve_ref(S, q, o, hd: int) -> None:
+    load().vx27_deltanet_retrieve_ref(_np(S), _np(q), _np(o), hd)
+
+
+def vx27_deltanet_retrieve_tiled(S, q, o, hd: int) -> None:
+    load().vx27_deltanet_retrieve_tiled(_np(S), _np(q), _np(o), hd)
+
+
+def vx27_deltanet_retrieve_avx2(S, q, o, hd: int) -> None:
+    load().vx27_deltanet_retrieve_avx2(_np(S), _np(q), _np(o), hd)
+
+
+def vx27_deltanet_l2norm(x, y, n: int) -> None:
+    load().vx27_deltanet_l2norm(_np(x), _np(y), n)
+
+
+def vx27_deltanet_step_exact(S, q, k, v, beta: float, g_log: float, o, hd: int) -> None:
+    load().vx27_deltanet_step_exact(_np(S), _np(q), _np(k), _np(v), beta, g_log, _np(o), hd)
+
+
+def vx27_deltanet_gate_params(a: float, A_log: float, b: float, dt_bias: float):
+    beta, g = C.c_double(), C.c_double()
+    load().vx27_deltanet_gate_params(a, A_log, b, dt_bias, C.byref(beta), C.byref(g))
+    return beta.value, g.value
+
+
+def vx27_conv1d_step(state, x, w, y, C_: int, apply_silu: int) -> None:
+    load().vx27_conv1d_step(_np(state), _np(x), _np(w), _np(y), C_, apply_silu)
+
+
+def vx27_gqa_kv_for_q(q_head: int) -> int:
+    return load().vx27_gqa_kv_for_q(q_head)
+
+
+def vx27_rmsnorm(x, w, y, n: int, eps: float) -> None:
+    load().vx27_rmsnorm(_np(x), _np(w), _np(y), n, eps)
+
+
+def vx27_attn_1q(q, kcache, vcache, n_pos: int, out) -> None:
+    load().vx27_attn_1q(_np(q), _np(kcache), _np(vcache), n_pos, _np(out))
+
+
+def vx27_rope_cos_sin(pos: int, cosv, sinv, rope_dim: int, theta: float, yarn: float) -> None:
+    load().vx27_rope_cos_sin(pos, _np(cosv), _np(sinv), rope_dim, theta, yarn)
+
+
+def vx27_rope_apply(v, n_heads: int, head_dim: int, rope_dim: int, cosv, sinv) -> None:
+    load().vx27_rope_apply(_np(v), n_heads, head_dim, rope_dim, _np(cosv), _np(sinv))
+
+
+def vx27_mrope_cos_sin_text(pos: int, cosv, sinv) -> None:
+    load().vx27_mrope_cos_sin_text(pos, _np(cosv), _np(sinv))
+
+
+def vx27_kv_elems(ctx: int) -> int:
+    return load().vx27_kv_elems(ctx)
+
+
+def vx27_kv_gb(ctx: int, bytes_per_elem: float) -> float:
+    return load().vx27_kv_gb(ctx, bytes_per_elem)
+
+
+def vx27_kv_fits(ctx: int, bytes_per_elem: float, budget_gb: float) -> int:
+    return load().vx27_kv_fits(ctx, bytes_per_elem, budget_gb)
+
+
+# ------------------------------------------------------------- batched tier
+def _t(t) -> C.c_void_p:
+    import torch
+    if t is None:
+        return C.c_void_p(0)
+    if not t.is_cuda or not t.is_contiguous():
+        raise Vx27Error("expected a contiguous CUDA tensor")
+    return C.c_void_p(t.data_ptr())
+
+
+def _stream(stream) -> C.c_void_p:
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
+
+
+def _is_bf16(t) -> bool:
+    import torch
+    return t.dtype == torch.bfloat16
+
+
+def deltanet_decode_batch(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, nqk: int,
+                          nv: int, gates_f64: bool = False, stream=None) -> None:
+    """One DeltaNet decode step for a batch (vx27_deltanet_decode_batch)."""
+    B = S.shape[0]
+    hd = S.shape[-1]
+    flags = (F_ACT_BF16 if _is_bf16(qkv) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0) | \
+        (F_GATES_F64 if gates_f64 else 0)
+    e = errbuf()
+    rc = load().vx27_deltanet_decode_batch(_t(S), _t(conv_ring), _t(qkv), _t(a), _t(b),
+                                           _t(A_log), _t(dt_bias), _t(conv_w), _t(pos), _t(o),
+                                           B, nqk, nv, hd, flags, _stream(stream), e, 512)
+    check(rc, e)
+
+
+def rope_table(n_pos: int, rope_dim: int = 64, theta: float = 1e7, yarn: float = 1.0,
+               device=None):
+    """Device RoPE table [n_pos][rope_dim] (cos | sin), values from vx27_rope_cos_sin."""
+    import torch
+    t = torch.empty((n_pos, rope_dim), dtype=torch.float32, device=device or "cuda")
+    e = errbuf()
+    check(load().vx27_rope_table_build(_t(t), n_pos, rope_dim, theta, yarn, e, 512), e)
+    return t
+
+
+def gqa_append(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, pos, k_cache, v_cache, q_out,
+               eps: float = 1e-6, slot_base: int = 0, norm_one_plus: bool = False,
+               stream=None) -> None:
+    B, nq, hd = q_in.shape
+    nkv = k_in.shape[1]
+    cap = k_cache.shape[2] if k_cache is not None else 0
+    flags = (F_ACT_BF16 if _is_bf16(q_in) else 0) | (F_NORM_1P if norm_one_plus else 0)
+    e = errbuf()
+    rc = load().vx27_gqa_append(_t(q_in), _t(k_in), _t(v_in), _t(q_norm_w), _t(k_norm_w),
+                                _t(rope), rope.shape[0], _t(pos), slot_base, _t(k_cache),
+                                _t(v_cache), cap, _t(q_out), B, nq, nkv, hd, rope.shape[1], eps,
+                                flags, _stream(stream), e, 512)
+    check(rc, e)
+
+
+def gqa_workspace_bytes(B: int, nq: int, nkv: int, hd: int, max_ctx: int,
+                        n_splits: int = 0) -> int:
+    return load().vx27_gqa_decode_workspace_size(B, nq, nkv, hd, max_ctx, n_splits)
+
+
+def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: int = 0,
+                     stream=None) -> None:
+    B, nq, hd = q.shape
+    nkv, cap = k_cache.shape[1], k_cache.shape[2]
+    flags = (F_ACT_BF16 if _is_bf16(gate) else 0) | (F_OUT_BF16 if _is_bf16(out) else 0)
+    e = errbuf()
+    rc = load().vx27_gqa_decode_batch(_t(q), _t(gate), _t(k_cache), _t(v_cache), cap, _t(pos),
+                                      _t(out), _t(workspace),
+                                      workspace.numel() * workspace.element_size(), B, nq, nkv,
+                                      hd, n_splits, flags, _stream(stream), e, 512)
+    check(rc, e)
+
+
+def gqa_partial(q, k_cache, v_cache, p_begin: int, p_end: int, part, stream=None) -> None:
+    B, nq, hd = q.shape
+    nkv, cap = k_cache.shape[1], k_cache.shape[2]
+    e = errbuf()
+    rc = load().vx27_gqa_partial(_t(q), _t(k_cache), _t(v_cache), cap, p_begin, p_end, _t(part),
+                                 B, nq, nkv, hd, _stream(stream), e, 512)
+    check(rc, e)
+
+
+def gqa_combine(parts, n_parts: int, gate, out, stream=None) -> None:
+    B, nq, hd = gate.shape
+    flags = (F_ACT_BF16 if _is_bf16(gate) else 0) | (F_OUT_BF16 if _is_bf16(out) else 0)
+    e = errbuf()
+    rc = load().vx27_gqa_combine(_t(parts), n_parts, _t(gate), _t(out), B, nq, hd, flags,
+                                 _stream(stream), e, 512)
+    check(rc, e)
+
+
+def fill_normal(t, seed: int, stream_id: int, mean: float = 0.0, std: float = 1.0,
+                stream=None) -> None:
+    e = errbuf()
+    rc = load().vx27cuda_fill_normal(_t(t), t.numel(), 1 if _is_bf16(t) else 0, seed, stream_id,
+                                     mean, std, _stream(stream), e, 512)
+    check(rc, e)
+
+
+def fill_uniform(t, seed: int, stream_id: int, lo: float, hi: float, stream=None) -> None:
+    e = errbuf()
+    check(load().vx27cuda_fill_uniform(_t(t), t.numel(), seed, stream_id, lo, hi,
+                                       _stream(stream), e, 512), e)
+
+
+def add_int(t, delta: int, stream=None) -> None:
+    e = errbuf()
+    check(load().vx27cuda_add_int(_t(t), t.numel(), delta, _stream(stream), e, 512), e)
+
+
+def device_status(clear: bool = True, stream=None) -> int:
+    st = C.c_uint32()
+    e = errbuf()
+    check(load().vx27cuda_device_status(_stream(stream), C.byref(st), 1 if clear else 0, e, 512), e)
+    return st.value
