@@ -7,14 +7,13 @@
 //      flight; a warp reads whole 512-byte rows, so every load is coalesced);
 //   2. while they are in flight it runs the width-4 causal conv + SiLU on its 384
 //      channels (q and k of its QK head, v of its V head), the l2 norms (double sums
-//      as the reference), q/sqrt(128), and the gates (correctly rounded exp/log);
+//      as the reference), q/sqrt(128), and the gates (double precision);
 //   3. S' = S*decay and the column sums kv = S'^T k (per-thread partials over 16 rows,
 //      then an 8-way reduction through shared memory);
 //   4. d = (v - kv)*beta, S'' = S' + k d^T, o = S''^T q, and the state store.
 // The state never leaves registers between the two reductions. The kernel is bound by
 // HBM: 2 x 64 KB of state per (sequence, head) per step.
 #include "common.cuh"
-#include "ddmath.h"
 #include "../../include/vx27_deltanet.h"
 
 namespace vx27 {
@@ -22,6 +21,18 @@ namespace {
 
 constexpr int HD = 128;
 constexpr int NT = 256;  // 8 warps; warp w owns rows [16w, 16w+16), lane l columns [4l, 4l+4)
+
+// The gate mapping of src/vx27_deltanet.c:58-69 in double with the device exp/log (a few
+// hundred cycles; the correctly rounded ddmath.h versions would put microseconds of
+// serial fp64 work on every CTA's critical path). Callers that need the C library's
+// exact bits pass host-computed gates (VX27_F_GATES_F64).
+__device__ __forceinline__ void gates_device(double a, double A_log, double b, double dt,
+                                             double *beta, double *g_log) {
+    *beta = 1.0 / (1.0 + exp(-b));
+    const double x = a + dt;
+    const double sp = x > 20.0 ? x : (x < -20.0 ? exp(x) : log(1.0 + exp(x)));
+    *g_log = -exp(A_log) * sp;
+}
 
 template <bool ACT_BF16, bool OUT_BF16, bool GATES_F64>
 __global__ void __launch_bounds__(NT, 2)
@@ -86,11 +97,11 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             beta = ((const double *)ga)[gi];
             g = ((const double *)gb)[gi];
         } else {
-            vx_gate_params((double)act_ld<ACT_BF16>(ga, gi), (double)A_log[vh],
-                           (double)act_ld<ACT_BF16>(gb, gi), (double)dt_bias[vh], &beta, &g);
+            gates_device((double)act_ld<ACT_BF16>(ga, gi), (double)A_log[vh],
+                         (double)act_ld<ACT_BF16>(gb, gi), (double)dt_bias[vh], &beta, &g);
         }
         par_s[2] = (float)beta;
-        par_s[3] = (float)vx_exp(g);
+        par_s[3] = (float)exp(g);
     }
     __syncthreads();
     if (tid < HD) {

@@ -1,8 +1,8 @@
 // K2: gated GQA decode over a BF16 KV cache.
 //   gqa_append_k   per-token prologue: QK RMSNorm, partial RoPE, bf16 K/V store
 //                  (src/vx27_qfwd.c:339-346)
-//   gqa_split_k    split-KV flash decoding, one CTA per (sequence, KV head, split)
-//                  serving the nq/nkv Q heads of the group, online softmax in fp32;
+//   split kernel   tensor-core split-KV flash decoding (gqa_tc.cu), one CTA per
+//                  (sequence, KV head, split) serving the nq/nkv Q heads of the group;
 //                  writes one partial record (m, l, o) per split
 //   gqa_combine_k  log-sum-exp merge of the partial records + sigmoid output gate
 //                  (src/vx27_qfwd.c:347-371)
@@ -11,6 +11,12 @@
 #include "../../include/vx27_gqa.h"
 
 namespace vx27 {
+
+// gqa_tc.cu: the tensor-core split-KV kernel (one CTA per sequence, KV head and split)
+int launch_split_tc(const void *kc, const void *vc, const float *q, const int *pos, float *parts,
+                    int cap, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
+                    cudaStream_t st, char *err, size_t errlen);
+
 namespace {
 
 constexpr int HD = 256;
@@ -74,112 +80,6 @@ gqa_append_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
     }
 }
 
-// ---- split-KV attention (CUDA cores) ----------------------------------------------
-__device__ __forceinline__ void bf16x8_to_f32(uint4 u, float *f) {
-    f[0] = u32_as_f32(u.x << 16); f[1] = u32_as_f32(u.x & 0xffff0000u);
-    f[2] = u32_as_f32(u.y << 16); f[3] = u32_as_f32(u.y & 0xffff0000u);
-    f[4] = u32_as_f32(u.z << 16); f[5] = u32_as_f32(u.z & 0xffff0000u);
-    f[6] = u32_as_f32(u.w << 16); f[7] = u32_as_f32(u.w & 0xffff0000u);
-}
-
-// Range of cache slots for (sequence b, split s): a fixed range when p_end >= 0,
-// else slots [0, pos[b]] cut into n_splits pieces on TILE boundaries.
-__device__ __forceinline__ void split_range(const int *pos, int b, int s, int n_splits,
-                                            int p_begin, int p_end, int *p0, int *p1) {
-    if (p_end >= 0) { *p0 = p_begin; *p1 = p_end; return; }
-    const int n = pos[b] + 1;
-    const int tiles = (n + TILE - 1) / TILE;
-    const int per = (tiles + n_splits - 1) / n_splits;
-    const int a = s * per * TILE;
-    const int e = min(n, (s + 1) * per * TILE);
-    *p0 = a;
-    *p1 = e > a ? e : a;
-}
-
-template <int G>
-__global__ void __launch_bounds__(256)
-gqa_split_k(const float *__restrict__ q, const uint16_t *__restrict__ kc,
-            const uint16_t *__restrict__ vc, int cap, const int *__restrict__ pos,
-            float *__restrict__ parts, int B, int nq, int nkv, int n_splits, int p_begin,
-            int p_end) {
-    const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int p0, p1;
-    split_range(pos, b, s, n_splits, p_begin, p_end, &p0, &p1);
-    if (p0 < 0) p0 = 0;
-    if (p1 > cap) p1 = cap;
-    const int h0 = kvh * G;  // Q heads h with h*nkv/nq == kvh
-    float qr[G][8];
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-        const float4 *qp = reinterpret_cast<const float4 *>(q + ((size_t)b * nq + h0 + g) * HD + lane * 8);
-        const float4 a = qp[0], c = qp[1];
-        qr[g][0] = a.x; qr[g][1] = a.y; qr[g][2] = a.z; qr[g][3] = a.w;
-        qr[g][4] = c.x; qr[g][5] = c.y; qr[g][6] = c.z; qr[g][7] = c.w;
-    }
-    float m[G], l[G], acc[G][8];
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-        m[g] = -INFINITY;
-        l[g] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; i++) acc[g][i] = 0.0f;
-    }
-    const size_t base = ((size_t)b * nkv + kvh) * cap;
-    const uint4 *K = reinterpret_cast<const uint4 *>(kc + base * HD);
-    const uint4 *V = reinterpret_cast<const uint4 *>(vc + base * HD);
-    for (int p = p0 + warp; p < p1; p += 8) {
-        float kf[8], vf[8];
-        bf16x8_to_f32(__ldcs(K + (size_t)p * (HD / 8) + lane), kf);
-        bf16x8_to_f32(__ldcs(V + (size_t)p * (HD / 8) + lane), vf);
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            float dot = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 8; i++) dot = fmaf(qr[g][i], kf[i], dot);
-            const float sc = warp_sum(dot) * 0.0625f;  // 1/sqrt(256), exact
-            const float mn = fmaxf(m[g], sc);
-            const float corr = expf(m[g] - mn);
-            const float pe = expf(sc - mn);
-            l[g] = l[g] * corr + pe;
-#pragma unroll
-            for (int i = 0; i < 8; i++) acc[g][i] = fmaf(pe, vf[i], acc[g][i] * corr);
-            m[g] = mn;
-        }
-    }
-    // merge the 8 warps
-    extern __shared__ float sm[];  // [8][G][HD] acc, then [8][G][2] (m, l)
-    float *sacc = sm, *sml = sm + 8 * G * HD;
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-#pragma unroll
-        for (int i = 0; i < 8; i++) sacc[(warp * G + g) * HD + lane * 8 + i] = acc[g][i];
-        if (lane == 0) { sml[(warp * G + g) * 2] = m[g]; sml[(warp * G + g) * 2 + 1] = l[g]; }
-    }
-    __syncthreads();
-    const size_t rec = (size_t)B * nq * (HD + 2);
-    float *po = parts + (size_t)s * rec;
-    float *pml = po + (size_t)B * nq * HD;
-    for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
-        const int g = e / HD, dd = e % HD;
-        float M = -INFINITY;
-        for (int w = 0; w < 8; w++) M = fmaxf(M, sml[(w * G + g) * 2]);
-        float L = 0.0f, O = 0.0f;
-        if (M != -INFINITY) {
-            for (int w = 0; w < 8; w++) {
-                const float mw = sml[(w * G + g) * 2];
-                if (mw == -INFINITY) continue;
-                const float f = expf(mw - M);
-                L += sml[(w * G + g) * 2 + 1] * f;
-                O += sacc[(w * G + g) * HD + dd] * f;
-            }
-        }
-        const size_t hq = (size_t)b * nq + h0 + g;
-        po[hq * HD + dd] = L > 0.0f ? O / L : 0.0f;
-        if (dd == 0) { pml[hq * 2] = L > 0.0f ? M : -INFINITY; pml[hq * 2 + 1] = L; }
-    }
-}
-
 // ---- combine ------------------------------------------------------------------------
 template <bool ACT_BF16, bool OUT_BF16>
 __global__ void __launch_bounds__(HD)
@@ -221,31 +121,8 @@ int auto_splits(int B, int nkv, int max_ctx) {
 int launch_split(const float *q, const void *kc, const void *vc, int cap, const int *pos,
                  float *parts, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
                  cudaStream_t st, char *err, size_t errlen) {
-    const int G = nq / nkv;
-    const dim3 grid(n_splits, nkv, B);
-    const size_t smem = (size_t)8 * G * (HD + 2) * sizeof(float);
-#define VX_G(GG)                                                                        \
-    case GG: {                                                                          \
-        static bool attr = false;                                                       \
-        if (!attr) {                                                                    \
-            VX_CK(cudaFuncSetAttribute(gqa_split_k<GG>,                                 \
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,     \
-                                       (int)smem));                                     \
-            attr = true;                                                                \
-        }                                                                               \
-        gqa_split_k<GG><<<grid, 256, smem, st>>>(q, (const uint16_t *)kc,               \
-                                                 (const uint16_t *)vc, cap, pos, parts, B, \
-                                                 nq, nkv, n_splits, p_begin, p_end);    \
-        break;                                                                          \
-    }
-    switch (G) {
-        VX_G(1) VX_G(2) VX_G(4) VX_G(6) VX_G(8)
-        default:
-            return fail(err, errlen, "vx27_gqa: group size %d (nq/nkv) unsupported", G);
-    }
-#undef VX_G
-    VX_CK(cudaGetLastError());
-    return 0;
+    return launch_split_tc(kc, vc, q, pos, parts, cap, B, nq, nkv, n_splits, p_begin, p_end, st,
+                           err, errlen);
 }
 
 int launch_combine(const float *parts, int n_parts, const void *gate, void *out, int B, int nq,
