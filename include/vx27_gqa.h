@@ -64,6 +64,33 @@ int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
                           size_t errlen);
 
 /*
+ * No counterpart in the reference. vx27_gqa_decode_batch without the workspace: same
+ * arguments, same kernels and results, but the split partial records go to a fixed
+ * array of VX27_GQA_NOALLOC_SCRATCH_BYTES in the library's own device memory, and the
+ * call itself allocates nothing (no cudaMalloc, no cudaFree, no allocating library call).
+ * It is for callers that cannot provide device scratch: an engine that has already
+ * handed all free device memory to its KV cache and weights, or a host that reaches this
+ * library through a fixed C interface (such as the reference's) that has no workspace
+ * argument and no way to own a device buffer.
+ * Limits and rules:
+ *  - the array is 8 MiB and is reserved on every GPU that loads the library, until the
+ *    process exits; one split's records take B*nq*(hd+2)*4 bytes, so a call needs
+ *    n_splits*B*nq*(hd+2)*4 <= 8 MiB (n_splits = 0 picks the largest automatic count
+ *    that fits; a batch whose single record does not fit is rejected with an error);
+ *  - the first call on a device, made with that device current, looks up the array's
+ *    device address (cudaGetSymbolAddress); make that first call before any stream
+ *    capture;
+ *  - all calls on a device share the array and it keeps the last call's contents: two
+ *    calls whose kernels overlap on the GPU (different streams, no ordering) race and
+ *    both results are undefined; calls ordered on one stream are safe.
+ */
+#define VX27_GQA_NOALLOC_SCRATCH_BYTES (8u << 20)
+int vx27_gqa_decode_batch_noalloc(const float *q, const void *gate, const void *k_cache,
+                                  const void *v_cache, int cap, const int *pos, void *out,
+                                  int B, int nq, int nkv, int hd, int n_splits, int flags,
+                                  void *stream, char *err, size_t errlen);
+
+/*
  * Context-parallel pieces. A partial record covers cache slots [p_begin, p_end) (the
  * same range for all B sequences): for each (b, Q head) m = max scaled score,
  * l = sum exp(s - m), o = sum exp(s - m) v / l. Record layout (fp32):

@@ -54,6 +54,8 @@ PROTOTYPES: dict[str, tuple] = {
     "vx27_gqa_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),
     "vx27_gqa_decode_batch": (_i, [_p, _p, _p, _p, _i, _p, _p, _p, _sz, _i, _i, _i, _i, _i, _i,
                                    _p, _cp, _sz]),
+    "vx27_gqa_decode_batch_noalloc": (_i, [_p, _p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _i,
+                                           _p, _cp, _sz]),
     "vx27_gqa_partial": (_i, [_p, _p, _p, _i, _i, _i, _p, _i, _i, _i, _i, _p, _cp, _sz]),
     "vx27_gqa_combine": (_i, [_p, _i, _p, _p, _i, _i, _i, _i, _p, _cp, _sz]),
     # vx27_kv.h

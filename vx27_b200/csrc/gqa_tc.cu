@@ -403,6 +403,41 @@ int launch_split_tc(const void *kc, const void *vc, const float *q, const int *p
     return 0;
 }
 
+// Same launch with an explicit device status word (null: timeouts end the waits without
+// being recorded). Touches no allocator, for the entry point that allocates nothing.
+int launch_split_tc_status(const void *kc, const void *vc, const float *q, const int *pos,
+                           float *parts, int cap, int B, int nq, int nkv, int n_splits,
+                           uint32_t *status, cudaStream_t st, char *err, size_t errlen) {
+    CUtensorMap mk, mv;
+    const uint64_t rows = (uint64_t)B * nkv * cap;
+    if (make_tmap_bf16_2d(&mk, kc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
+        make_tmap_bf16_2d(&mv, vc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen))
+        return -1;
+    const size_t smem = tc_smem_bytes();
+    const dim3 grid(n_splits, nkv, B);
+#define VX_TCS(GG)                                                                        \
+    case GG: {                                                                            \
+        static bool attr = false;                                                         \
+        if (!attr) {                                                                      \
+            VX_CK(cudaFuncSetAttribute(gqa_split_tc<GG>,                                  \
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,       \
+                                       (int)smem));                                       \
+            attr = true;                                                                  \
+        }                                                                                 \
+        gqa_split_tc<GG><<<grid, TC_THREADS, smem, st>>>(mk, mv, q, pos, parts, cap, B, nq, \
+                                                         nkv, n_splits, 0, -1, status);   \
+        break;                                                                            \
+    }
+    switch (nq / nkv) {
+        VX_TCS(1) VX_TCS(2) VX_TCS(4) VX_TCS(6) VX_TCS(8)
+        default:
+            return fail(err, errlen, "vx27_gqa: group size %d (nq/nkv) unsupported", nq / nkv);
+    }
+#undef VX_TCS
+    VX_CK(cudaGetLastError());
+    return 0;
+}
+
 // ---- host: tensor maps ---------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
