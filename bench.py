@@ -157,19 +157,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     dn_gbs = dn_bytes / (dn_ms * 1e-3) / 1e9
     step_gbs = by["total"] / (ms_step * 1e-3) / 1e9
 
-    # end-to-end through the public API with host buffers: H2D of the step's
-    # activations from pinned memory, the step, D2H of the step's attention outputs
+    # end-to-end through the public API with host buffers: every step copies its
+    # activations in from pinned host memory and its attention outputs back (per layer,
+    # overlapped with the other layers' kernels), all inside the timed region
     hin = [t.cpu().pin_memory() for t in dec.step_inputs()]
     hout = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in dec.step_outputs()]
     h2d = sum(t.numel() * t.element_size() for t in hin)
     d2h = sum(t.numel() * t.element_size() for t in hout)
 
     def e2e_step():
-        for d, h in zip(dec.step_inputs(), hin):
-            d.copy_(h, non_blocking=True)
-        dec.step()
-        for h, d in zip(hout, dec.step_outputs()):
-            h.copy_(d, non_blocking=True)
+        return dec.step_host(hin, hout)
 
     dec.reset_positions()
     for _ in range(args.warmup):
@@ -238,6 +235,67 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "device_status": status,
         "clocks": clk.summary(),
     }
+
+
+# ------------------------------------------------- single-layer workloads
+def run_layer(args) -> dict:
+    """One attention layer launched repeatedly (kernel rooflines in isolation and ncu
+    captures at a chosen size): --workload dn_layer | gqa_layer."""
+    import torch
+    from vx27_b200 import ops
+    torch.cuda.set_device(0)
+    B = args.batch
+    peak, peak_src = peaks()
+    bf = torch.bfloat16
+    if args.workload == "dn_layer":
+        nqk = nv = 16
+        C = (2 * nqk + nv) * 128
+        S = torch.empty(B, nv, 128, 128, device="cuda")
+        ring = torch.empty(B, 4, C, device="cuda")
+        qkv = torch.empty(B, C, dtype=bf, device="cuda")
+        a = torch.empty(B, nv, dtype=bf, device="cuda")
+        b = torch.empty(B, nv, dtype=bf, device="cuda")
+        w = torch.empty(C, 4, device="cuda")
+        A = torch.empty(nv, device="cuda")
+        dt = torch.empty(nv, device="cuda")
+        o = torch.empty(B, nv, 128, dtype=bf, device="cuda")
+        for n, t in enumerate((S, ring, qkv, a, b, w, dt)):
+            ops.fill_normal(t, 2, n, 0.0, 0.05 if n == 0 else 1.0)
+        ops.fill_uniform(A, 2, 9, 1.0, 16.0)
+        A.log_()
+        pos = torch.full((B,), args.ctx, dtype=torch.int32, device="cuda")
+        run = lambda: ops.deltanet_decode_batch(S, ring, qkv, a, b, A, dt, w, pos, o, nqk, nv)
+        nbytes = B * nv * 128 * 128 * 4 * 2 + B * C * (16 + 2) + B * nv * 128 * 2
+        name = "dn_decode_k (fused DeltaNet decode), one layer"
+    else:
+        nq, nkv, hd, cap = 24, 4, 256, args.ctx + 1
+        kc = torch.empty(B, nkv, cap, hd, dtype=bf, device="cuda")
+        vc = torch.empty(B, nkv, cap, hd, dtype=bf, device="cuda")
+        q = torch.empty(B, nq, hd, device="cuda")
+        gate = torch.empty(B, nq, hd, dtype=bf, device="cuda")
+        out = torch.empty(B, nq, hd, dtype=bf, device="cuda")
+        for n, t in enumerate((kc, vc, q, gate)):
+            ops.fill_normal(t, 3, n)
+        ws = torch.empty(ops.gqa_workspace_bytes(B, nq, nkv, hd, cap) // 4 + 1, device="cuda")
+        pos = torch.full((B,), args.ctx, dtype=torch.int32, device="cuda")
+        run = lambda: ops.gqa_decode_batch(q, gate, kc, vc, pos, out, ws)
+        nbytes = B * nkv * cap * hd * 2 * 2 + B * nq * hd * (4 + 2 + 2)
+        name = "gqa_split_tc + combine (split-KV decode), one layer"
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": args.workload, "kernel": name, "batch": B, "ctx": args.ctx,
+            "ms_per_launch": round(ms, 4), "algorithmic_bytes_per_launch": nbytes,
+            "achieved_GBps": round(gbs, 1), "peak": peak, "frac": round(gbs / peak, 4),
+            "peak_source": peak_src}
 
 
 # ------------------------------------------------------------ CPU reference
@@ -354,11 +412,19 @@ def main() -> None:
     ap.add_argument("--ref-seqs", type=int, default=4)
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["config2", "dn_layer", "gqa_layer"],
+                    default="config2",
+                    help="config2 (the metric); single-layer workloads are for kernel "
+                         "rooflines and profiling")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.workload != "config2":
+        print(json.dumps(run_layer(args)), flush=True)
+        return
 
     if args.impl == "reference":
         line = run_reference(args, rank)

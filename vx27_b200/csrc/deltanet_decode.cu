@@ -1,18 +1,23 @@
-// K1: fused Gated DeltaNet decode step for B sequences, one CTA per (sequence, V head).
+// K1: fused Gated DeltaNet decode step for B sequences.
 //
 // Per token the reference runs, per V head, conv1d_step -> gate_params -> step_exact
-// (src/vx27_qfwd.c:276-297, src/vx27_deltanet.c:51-122). Here one kernel does all of
-// it with the 128x128 fp32 state read once and written once:
-//   1. the CTA issues its 16 x 16-byte state loads per thread first (64 KB per CTA in
-//      flight; a warp reads whole 512-byte rows, so every load is coalesced);
-//   2. while they are in flight it runs the width-4 causal conv + SiLU on its 384
-//      channels (q and k of its QK head, v of its V head), the l2 norms (double sums
-//      as the reference), q/sqrt(128), and the gates (double precision);
-//   3. S' = S*decay and the column sums kv = S'^T k (per-thread partials over 16 rows,
-//      then an 8-way reduction through shared memory);
-//   4. d = (v - kv)*beta, S'' = S' + k d^T, o = S''^T q, and the state store.
-// The state never leaves registers between the two reductions. The kernel is bound by
-// HBM: 2 x 64 KB of state per (sequence, head) per step.
+// (src/vx27_qfwd.c:276-297, src/vx27_deltanet.c:51-122). Here one persistent kernel
+// does it for all (sequence, V head) items, each 128x128 fp32 state read once and
+// written once. One CTA per SM, three warp roles:
+//   TMA warp      streams each item's 64 KB state into a 3-slot shared-memory ring
+//                 (one 1-D bulk copy per item), two items ahead of the compute warps;
+//   prep warps    (4) each prepares whole items on its own, up to 8 items ahead:
+//                 width-4 causal conv + SiLU on the item's 384 channels (q, k of its QK
+//                 head, v of its V head) with the conv-history update, the l2 norms
+//                 (double sums as src/vx27_deltanet.c:51), q/sqrt(128), and the gates
+//                 (double precision) -> a parameter slot in shared memory;
+//   compute warps (8) state from shared memory into registers (thread = 16 rows x 4
+//                 columns), S' = S*decay, column sums kv = S'^T k, d = (v - kv)*beta,
+//                 S'' = S' + k d^T, o = S''^T q, state stored straight from registers.
+// Waits on the mbarriers are bounded (2 s, %globaltimer); in the compute group a single
+// thread waits and publishes the outcome before the group's bar.sync, and a prep warp
+// broadcasts its lane 0's outcome, so a timeout makes a whole group leave together and no
+// barrier is left half-arrived.
 #include "common.cuh"
 #include "../../include/vx27_deltanet.h"
 
@@ -20,12 +25,61 @@ namespace vx27 {
 namespace {
 
 constexpr int HD = 128;
-constexpr int NT = 256;  // 8 warps; warp w owns rows [16w, 16w+16), lane l columns [4l, 4l+4)
+constexpr int NCOMP = 256;                 // compute threads (warps 0-7)
+constexpr int NPREP = 128;                 // prep threads (warps 8-11)
+constexpr int NTHREADS = NCOMP + NPREP + 32;  // + TMA warp (warp 12)
+constexpr int NSTATE = 3;                  // state ring slots
+constexpr int NPARAM = 8;                  // parameter ring slots
+constexpr int STATE_BYTES = HD * HD * 4;   // 64 KB
+constexpr int BAR_COMP = 1;                // named barrier id of the compute warps
 
-// The gate mapping of src/vx27_deltanet.c:58-69 in double with the device exp/log (a few
-// hundred cycles; the correctly rounded ddmath.h versions would put microseconds of
-// serial fp64 work on every CTA's critical path). Callers that need the C library's
-// exact bits pass host-computed gates (VX27_F_GATES_F64).
+struct Params {        // one item's prepared inputs
+    float qn[HD], kn[HD], v[HD];
+    float beta, decay;
+};
+
+struct DnSmem {
+    float state[NSTATE][HD * HD];
+    Params prm[NPARAM];
+    float red[8][HD];
+    float d[HD];
+    uint64_t sfull[NSTATE], sempty[NSTATE], pfull[NPARAM], pempty[NPARAM];
+    int flag_comp, abort;
+};
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait; false when the CTA aborted or ~2 s passed (then it aborts).
+__device__ bool dn_wait(uint64_t *bar, uint32_t parity, DnSmem &sm, uint32_t *status,
+                        uint32_t code) {
+    const uint32_t addr = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
+            "selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+        if (ok) return true;
+        if ((it & 255) == 0) {
+            if (*(volatile int *)&sm.abort) return false;
+            const uint64_t now = gtimer();
+            if (it == 0) t0 = now;
+            else if (now - t0 > 2000000000ull) {
+                *(volatile int *)&sm.abort = 1;
+                dev_flag(status, code);
+                return false;
+            }
+        }
+    }
+}
+
+// The gate mapping of src/vx27_deltanet.c:58-69 in double with the device exp/log.
+// Callers that need the C library's exact bits pass host-computed gates
+// (VX27_F_GATES_F64).
 __device__ __forceinline__ void gates_device(double a, double A_log, double b, double dt,
                                              double *beta, double *g_log) {
     *beta = 1.0 / (1.0 + exp(-b));
@@ -35,139 +89,227 @@ __device__ __forceinline__ void gates_device(double a, double A_log, double b, d
 }
 
 template <bool ACT_BF16, bool OUT_BF16, bool GATES_F64>
-__global__ void __launch_bounds__(NT, 2)
+__global__ void __launch_bounds__(NTHREADS, 1)
 dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restrict__ qkv,
             const void *__restrict__ ga, const void *__restrict__ gb,
             const float *__restrict__ A_log, const float *__restrict__ dt_bias,
             const float *__restrict__ conv_w, const int *__restrict__ pos, void *__restrict__ o,
-            int nqk, int nv) {
-    const int vh = blockIdx.x, bi = blockIdx.y;
+            int B, int nqk, int nv, uint32_t *status) {
+    extern __shared__ uint8_t dn_smem_raw[];
+    DnSmem &sm = *reinterpret_cast<DnSmem *>(((uintptr_t)dn_smem_raw + 127) & ~(uintptr_t)127);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int qk = vh * nqk / nv;
-    // the first V head of a QK group writes that group's q/k conv history
-    const bool qk_owner = (vh == 0) || ((vh - 1) * nqk / nv != qk);
+    const int n_items_total = B * nv;
+    // items of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...
+    const int n_items = blockIdx.x < n_items_total
+                            ? (n_items_total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const int C = (2 * nqk + nv) * HD;
 
-    __shared__ float y_s[3 * HD];  // conv+SiLU output: q | k | v of this head
-    __shared__ float qn_s[HD], kn_s[HD], d_s[HD];
-    __shared__ __align__(16) float red[8][HD];
-    __shared__ float par_s[4];  // 1/|q|, 1/|k|, beta, decay
-
-    // 1. state loads, issued before anything else
-    float4 *S4 = reinterpret_cast<float4 *>(S + ((size_t)bi * nv + vh) * HD * HD);
-    float4 s[16];
-#pragma unroll
-    for (int r = 0; r < 16; r++) s[r] = __ldcs(S4 + (warp * 16 + r) * (HD / 4) + lane);
-
-    // 2a. causal conv (tap 0 = oldest) + SiLU; ring slot t&3 receives this token's input
-    const int t = pos[bi];
-    const int sl0 = (t - 3) & 3, sl1 = (t - 2) & 3, sl2 = (t - 1) & 3, slw = t & 3;
-    float *rb = ring + (size_t)bi * 4 * C;
-    for (int e = tid; e < 3 * HD; e += NT) {
-        const int part = e / HD, d = e % HD;
-        const int c = part == 0 ? qk * HD + d
-                    : part == 1 ? (nqk + qk) * HD + d
-                                : 2 * nqk * HD + vh * HD + d;
-        const float x = act_ld<ACT_BF16>(qkv, (size_t)bi * C + c);
-        const float4 w = *reinterpret_cast<const float4 *>(conv_w + (size_t)c * 4);
-        float acc = __fmul_rn(w.x, rb[(size_t)sl0 * C + c]);
-        acc = __fadd_rn(acc, __fmul_rn(w.y, rb[(size_t)sl1 * C + c]));
-        acc = __fadd_rn(acc, __fmul_rn(w.z, rb[(size_t)sl2 * C + c]));
-        acc = __fadd_rn(acc, __fmul_rn(w.w, x));
-        y_s[e] = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
-        if (part == 2 || qk_owner) rb[(size_t)slw * C + c] = x;
+    if (tid == 0) {
+        for (int i = 0; i < NSTATE; i++) { mbar_init(&sm.sfull[i], 1); mbar_init(&sm.sempty[i], 1); }
+        for (int i = 0; i < NPARAM; i++) { mbar_init(&sm.pfull[i], 1); mbar_init(&sm.pempty[i], 1); }
+        sm.abort = 0;
+        fence_barrier_init();
     }
     __syncthreads();
 
-    // 2b. l2 norms (warps 0, 1) and gates (warp 2)
-    if (warp < 2) {
-        const float *src = y_s + warp * HD;
-        double ss = 0.0;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const double x = (double)src[lane * 4 + j];
-            ss += x * x;
+    if (warp == 12) {
+        // ---- TMA: state of item i -> ring slot i % NSTATE --------------------------
+        if (lane == 0) {
+            int i = 0;
+            for (; i < n_items; i++) {
+                const int slot = i % NSTATE;
+                if (i >= NSTATE &&
+                    !dn_wait(&sm.sempty[slot], ((i / NSTATE) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
+                    break;
+                const int item = blockIdx.x + i * gridDim.x;
+                mbar_arrive_expect_tx(&sm.sfull[slot], STATE_BYTES);
+                bulk_g2s(sm.state[slot], S + (size_t)item * HD * HD, STATE_BYTES, &sm.sfull[slot]);
+            }
+            if (sm.abort) {  // let issued copies land before the CTA exits
+                for (int k = max(0, i - NSTATE); k < i; k++) {
+                    const uint32_t addr = smem_u32(&sm.sfull[k % NSTATE]);
+                    for (int it = 0; it < (1 << 20); it++) {
+                        uint32_t ok;
+                        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                                     : "=r"(ok) : "r"(addr), "r"((uint32_t)((k / NSTATE) & 1)) : "memory");
+                        if (ok) break;
+                    }
+                }
+            }
         }
-        ss = warp_sum_d(ss);
-        if (lane == 0) par_s[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, 1e-6f)));
-    } else if (warp == 2 && lane == 0) {
-        double beta, g;
-        const size_t gi = (size_t)bi * nv + vh;
-        if constexpr (GATES_F64) {
-            beta = ((const double *)ga)[gi];
-            g = ((const double *)gb)[gi];
-        } else {
-            gates_device((double)act_ld<ACT_BF16>(ga, gi), (double)A_log[vh],
-                         (double)act_ld<ACT_BF16>(gb, gi), (double)dt_bias[vh], &beta, &g);
+    } else if (warp >= 8) {
+        // ---- prep: warp pw prepares items pw, pw+4, ... into parameter slot i % NPARAM.
+        // One warp per item (lane = 4 channels of each of q, k, v), warp-level reductions
+        // only, so four items are prepared concurrently.
+        const int pw = warp - 8;
+        for (int i = pw; i < n_items; i += NPREP / 32) {
+            const int slot = i % NPARAM;
+            const int item = blockIdx.x + i * gridDim.x;
+            const int bi = item / nv, vh = item % nv;
+            const int tp = pos[bi];
+            // issue the gate inputs early (lane 0)
+            double ga_v = 0.0, gb_v = 0.0;
+            float al = 0.f, dtb = 0.f;
+            const size_t gi = (size_t)bi * nv + vh;
+            if (lane == 0) {
+                if constexpr (GATES_F64) {
+                    ga_v = ((const double *)ga)[gi];
+                    gb_v = ((const double *)gb)[gi];
+                } else {
+                    ga_v = (double)act_ld<ACT_BF16>(ga, gi);
+                    gb_v = (double)act_ld<ACT_BF16>(gb, gi);
+                    al = A_log[vh];
+                    dtb = dt_bias[vh];
+                }
+            }
+            int ok = 1;
+            if (lane == 0 && i >= NPARAM)
+                ok = dn_wait(&sm.pempty[slot], ((i / NPARAM) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            const int qk = vh * nqk / nv;
+            const bool qk_owner = (vh == 0) || ((vh - 1) * nqk / nv != qk);
+            const int sl0 = (tp - 3) & 3, sl1 = (tp - 2) & 3, sl2 = (tp - 1) & 3, slw = tp & 3;
+            float *rb = ring + (size_t)bi * 4 * C;
+            float y[3][4];
+#pragma unroll
+            for (int part = 0; part < 3; part++) {
+                const int c0 = part == 0 ? qk * HD : part == 1 ? (nqk + qk) * HD
+                                                               : 2 * nqk * HD + vh * HD;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int c = c0 + lane + 32 * j;
+                    const float x = act_ld<ACT_BF16>(qkv, (size_t)bi * C + c);
+                    const float4 w = *reinterpret_cast<const float4 *>(conv_w + (size_t)c * 4);
+                    float acc = __fmul_rn(w.x, rb[(size_t)sl0 * C + c]);
+                    acc = __fadd_rn(acc, __fmul_rn(w.y, rb[(size_t)sl1 * C + c]));
+                    acc = __fadd_rn(acc, __fmul_rn(w.z, rb[(size_t)sl2 * C + c]));
+                    acc = __fadd_rn(acc, __fmul_rn(w.w, x));
+                    y[part][j] = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
+                    if (part == 2 || qk_owner) rb[(size_t)slw * C + c] = x;
+                }
+            }
+            double sq = 0.0, sk = 0.0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                sq += (double)y[0][j] * (double)y[0][j];
+                sk += (double)y[1][j] * (double)y[1][j];
+            }
+            sq = warp_sum_d(sq);
+            sk = warp_sum_d(sk);
+            const float rq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)sq, 1e-6f)));
+            const float rk = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)sk, 1e-6f)));
+            const float qs = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+            Params &P = sm.prm[slot];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int d = lane + 32 * j;
+                P.qn[d] = __fmul_rn(__fmul_rn(y[0][j], rq), qs);
+                P.kn[d] = __fmul_rn(y[1][j], rk);
+                P.v[d] = y[2][j];
+            }
+            if (lane == 0) {
+                double beta, g;
+                if constexpr (GATES_F64) {
+                    beta = ga_v;
+                    g = gb_v;
+                } else {
+                    gates_device(ga_v, (double)al, gb_v, (double)dtb, &beta, &g);
+                }
+                P.beta = (float)beta;
+                P.decay = (float)exp(g);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.pfull[slot]);
         }
-        par_s[2] = (float)beta;
-        par_s[3] = (float)exp(g);
-    }
-    __syncthreads();
-    if (tid < HD) {
-        const float qs = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-        qn_s[tid] = __fmul_rn(__fmul_rn(y_s[tid], par_s[0]), qs);
-        kn_s[tid] = __fmul_rn(y_s[HD + tid], par_s[1]);
-    }
-    __syncthreads();
-
-    // 3. decay and column partial sums of S'^T k
-    const float decay = par_s[3];
-    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+        // ---- compute: delta rule on item i ------------------------------------------
+        for (int i = 0; i < n_items; i++) {
+            const int sslot = i % NSTATE, pslot = i % NPARAM;
+            if (tid == 0) {
+                const bool ok =
+                    dn_wait(&sm.sfull[sslot], (i / NSTATE) & 1, sm, status, VX_DEV_TIMEOUT_TMA) &&
+                    dn_wait(&sm.pfull[pslot], (i / NPARAM) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+                sm.flag_comp = ok ? 0 : 1;
+            }
+            named_bar_sync(BAR_COMP, NCOMP);
+            if (sm.flag_comp) break;
+            const int item = blockIdx.x + i * gridDim.x;
+            const Params &P = sm.prm[pslot];
+            const float4 *st = reinterpret_cast<const float4 *>(sm.state[sslot]);
+            float4 s[16];
 #pragma unroll
-    for (int r = 0; r < 16; r++) {
-        const float k = kn_s[warp * 16 + r];
-        s[r].x = __fmul_rn(s[r].x, decay);
-        s[r].y = __fmul_rn(s[r].y, decay);
-        s[r].z = __fmul_rn(s[r].z, decay);
-        s[r].w = __fmul_rn(s[r].w, decay);
-        kv.x = fmaf(s[r].x, k, kv.x);
-        kv.y = fmaf(s[r].y, k, kv.y);
-        kv.z = fmaf(s[r].z, k, kv.z);
-        kv.w = fmaf(s[r].w, k, kv.w);
-    }
-    *reinterpret_cast<float4 *>(&red[warp][lane * 4]) = kv;
-    __syncthreads();
-    if (tid < HD) {
-        float acc = 0.0f;
+            for (int r = 0; r < 16; r++) s[r] = st[(warp * 16 + r) * (HD / 4) + lane];
+            const float decay = P.decay;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int w = 0; w < 8; w++) acc += red[w][tid];
-        d_s[tid] = (y_s[2 * HD + tid] - acc) * par_s[2];
+            for (int r = 0; r < 16; r++) {
+                const float k = P.kn[warp * 16 + r];
+                s[r].x = __fmul_rn(s[r].x, decay);
+                s[r].y = __fmul_rn(s[r].y, decay);
+                s[r].z = __fmul_rn(s[r].z, decay);
+                s[r].w = __fmul_rn(s[r].w, decay);
+                kv.x = fmaf(s[r].x, k, kv.x);
+                kv.y = fmaf(s[r].y, k, kv.y);
+                kv.z = fmaf(s[r].z, k, kv.z);
+                kv.w = fmaf(s[r].w, k, kv.w);
+            }
+            *reinterpret_cast<float4 *>(&sm.red[warp][lane * 4]) = kv;
+            named_bar_sync(BAR_COMP, NCOMP);  // partials ready; state slot fully read
+            if (tid == 0) mbar_arrive(&sm.sempty[sslot]);
+            if (tid < HD) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int w = 0; w < 8; w++) acc += sm.red[w][tid];
+                sm.d[tid] = (P.v[tid] - acc) * P.beta;
+            }
+            named_bar_sync(BAR_COMP, NCOMP);
+            const float4 dj = *reinterpret_cast<const float4 *>(&sm.d[lane * 4]);
+            float4 op = make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 *Sg = reinterpret_cast<float4 *>(S + (size_t)item * HD * HD);
+#pragma unroll
+            for (int r = 0; r < 16; r++) {
+                const float k = P.kn[warp * 16 + r], q = P.qn[warp * 16 + r];
+                s[r].x = fmaf(k, dj.x, s[r].x);
+                s[r].y = fmaf(k, dj.y, s[r].y);
+                s[r].z = fmaf(k, dj.z, s[r].z);
+                s[r].w = fmaf(k, dj.w, s[r].w);
+                op.x = fmaf(s[r].x, q, op.x);
+                op.y = fmaf(s[r].y, q, op.y);
+                op.z = fmaf(s[r].z, q, op.z);
+                op.w = fmaf(s[r].w, q, op.w);
+                __stcs(Sg + (warp * 16 + r) * (HD / 4) + lane, s[r]);
+            }
+            *reinterpret_cast<float4 *>(&sm.red[warp][lane * 4]) = op;
+            named_bar_sync(BAR_COMP, NCOMP);
+            if (tid < HD) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int w = 0; w < 8; w++) acc += sm.red[w][tid];
+                act_st<OUT_BF16>(o, (size_t)item * HD + tid, acc);
+            }
+            named_bar_sync(BAR_COMP, NCOMP);  // parameter slot and red[] free again
+            if (tid == 0) mbar_arrive(&sm.pempty[pslot]);
+        }
     }
     __syncthreads();
-
-    // 4. rank-1 update, retrieve partials, state store
-    const float4 dj = *reinterpret_cast<const float4 *>(&d_s[lane * 4]);
-    float4 op = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int r = 0; r < 16; r++) {
-        const float k = kn_s[warp * 16 + r], q = qn_s[warp * 16 + r];
-        s[r].x = fmaf(k, dj.x, s[r].x);
-        s[r].y = fmaf(k, dj.y, s[r].y);
-        s[r].z = fmaf(k, dj.z, s[r].z);
-        s[r].w = fmaf(k, dj.w, s[r].w);
-        op.x = fmaf(s[r].x, q, op.x);
-        op.y = fmaf(s[r].y, q, op.y);
-        op.z = fmaf(s[r].z, q, op.z);
-        op.w = fmaf(s[r].w, q, op.w);
-        __stcs(S4 + (warp * 16 + r) * (HD / 4) + lane, s[r]);
-    }
-    *reinterpret_cast<float4 *>(&red[warp][lane * 4]) = op;
-    __syncthreads();
-    if (tid < HD) {
-        float acc = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 8; w++) acc += red[w][tid];
-        act_st<OUT_BF16>(o, ((size_t)bi * nv + vh) * HD + tid, acc);
-    }
 }
 
 template <bool A, bool O, bool G>
-void launch(dim3 grid, cudaStream_t st, float *S, float *ring, const void *qkv, const void *a,
-            const void *b, const float *A_log, const float *dt_bias, const float *conv_w,
-            const int *pos, void *o, int nqk, int nv) {
-    dn_decode_k<A, O, G><<<grid, NT, 0, st>>>(S, ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o,
-                                              nqk, nv);
+int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, const void *a,
+           const void *b, const float *A_log, const float *dt_bias, const float *conv_w,
+           const int *pos, void *o, int B, int nqk, int nv, char *err, size_t errlen) {
+    static bool attr = false;
+    const size_t smem = sizeof(DnSmem) + 128;
+    if (!attr) {
+        VX_CK(cudaFuncSetAttribute(dn_decode_k<A, O, G>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr = true;
+    }
+    dn_decode_k<A, O, G><<<grid, NTHREADS, smem, st>>>(S, ring, qkv, a, b, A_log, dt_bias,
+                                                        conv_w, pos, o, B, nqk, nv, dev_status());
+    VX_CK(cudaGetLastError());
+    return 0;
 }
 
 }  // namespace
@@ -183,7 +325,7 @@ extern "C" int vx27_deltanet_decode_batch(float *S, float *conv_ring, const void
                                           size_t errlen) {
     if (hd != HD)
         return fail(err, errlen, "vx27_deltanet_decode_batch: hd=%d unsupported (128 only)", hd);
-    if (B <= 0 || B > 65535 || nqk <= 0 || nv <= 0 || nv < nqk || nv > 65535)
+    if (B <= 0 || nqk <= 0 || nv <= 0 || nv < nqk || (long long)B * nv > (1ll << 30))
         return fail(err, errlen, "vx27_deltanet_decode_batch: bad shape B=%d nqk=%d nv=%d", B,
                     nqk, nv);
     if (!S || !conv_ring || !qkv || !a || !b || !conv_w || !pos || !o)
@@ -193,12 +335,13 @@ extern "C" int vx27_deltanet_decode_batch(float *S, float *conv_ring, const void
         return fail(err, errlen, "vx27_deltanet_decode_batch: A_log/dt_bias required");
     if (((uintptr_t)S & 15) || ((uintptr_t)conv_w & 15))
         return fail(err, errlen, "vx27_deltanet_decode_batch: S and conv_w must be 16-byte aligned");
-    const dim3 grid(nv, B);
+    const int items = B * nv;
+    const int grid = items < num_sms() ? items : num_sms();
     cudaStream_t st = (cudaStream_t)stream;
     const int key = (flags & VX27_F_ACT_BF16 ? 1 : 0) | (flags & VX27_F_OUT_BF16 ? 2 : 0) |
                     (g64 ? 4 : 0);
 #define VX_L(K, A_, O_, G_) \
-    case K: launch<A_, O_, G_>(grid, st, S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, nqk, nv); break;
+    case K: return launch<A_, O_, G_>(grid, st, S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, B, nqk, nv, err, errlen);
     switch (key) {
         VX_L(0, false, false, false)
         VX_L(1, true, false, false)
@@ -210,6 +353,5 @@ extern "C" int vx27_deltanet_decode_batch(float *S, float *conv_ring, const void
         VX_L(7, true, true, true)
     }
 #undef VX_L
-    VX_CK(cudaGetLastError());
-    return 0;
+    return fail(err, errlen, "vx27_deltanet_decode_batch: bad flags");
 }

@@ -153,6 +153,75 @@ class HybridDecoder:
     def reset_positions(self) -> None:
         self.pos.fill_(self.cfg.ctx)
 
+    # ------------------------------------------------------ host-buffer step
+    def layer_inputs(self, L: int) -> list[torch.Tensor]:
+        full, i = layer_kind(L)
+        if full:
+            return [self.q_in[i], self.k_in[i], self.v_in[i], self.gate[i]]
+        return [self.qkv[i], self.a[i], self.b[i]]
+
+    def layer_output(self, L: int) -> torch.Tensor:
+        full, i = layer_kind(L)
+        return self.att_out[i] if full else self.dn_out[i]
+
+    def step_host(self, host_in: list[torch.Tensor], host_out: list[torch.Tensor]) -> int:
+        """One decode step with the activations in pinned host memory (host_in matches
+        step_inputs(), host_out matches step_outputs()). Layer L's inputs are copied in on a
+        copy stream while earlier layers compute, and its output is copied back on a second
+        stream as soon as its kernel is done; per-layer events keep the next step's copies
+        from overwriting buffers a pending kernel or copy still uses. Returns kernels
+        launched."""
+        if not hasattr(self, "_h2d"):
+            self._h2d = torch.cuda.Stream(self.dev)
+            self._d2h = torch.cuda.Stream(self.dev)
+            self._done = [None] * N_LAYERS   # kernel of layer L finished (previous step)
+            self._out_read = [None] * N_LAYERS  # output of layer L copied out (previous step)
+        comp = torch.cuda.current_stream(self.dev)
+        names = ["qkv", "a", "b", "q_in", "k_in", "v_in", "gate"]
+        hmap = dict(zip(names, host_in))
+        n = 0
+        c = self.cfg
+        for L in range(N_LAYERS):
+            full, i = layer_kind(L)
+            srcs = ([hmap["q_in"][i], hmap["k_in"][i], hmap["v_in"][i], hmap["gate"][i]] if full
+                    else [hmap["qkv"][i], hmap["a"][i], hmap["b"][i]])
+            with torch.cuda.stream(self._h2d):
+                if self._done[L] is not None:
+                    self._h2d.wait_event(self._done[L])
+                for d, h in zip(self.layer_inputs(L), srcs):
+                    d.copy_(h, non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(self._h2d)
+            comp.wait_event(ready)
+            if self._out_read[L] is not None:
+                comp.wait_event(self._out_read[L])
+            if not full:
+                ops.deltanet_decode_batch(self.S[i], self.ring[i], self.qkv[i], self.a[i],
+                                          self.b[i], self.A_log[i], self.dt_bias[i],
+                                          self.conv_w[i], self.pos, self.dn_out[i], c.nqk, c.nv,
+                                          stream=comp)
+                n += 1
+            else:
+                ops.gqa_append(self.q_in[i], self.k_in[i], self.v_in[i], self.q_norm_w[i],
+                               self.k_norm_w[i], self.rope, self.pos, self.kc[i], self.vc[i],
+                               self.qn, eps=c.eps, stream=comp)
+                ops.gqa_decode_batch(self.qn, self.gate[i], self.kc[i], self.vc[i], self.pos,
+                                     self.att_out[i], self.ws, stream=comp)
+                n += 3
+            done = torch.cuda.Event()
+            done.record(comp)
+            self._done[L] = done
+            with torch.cuda.stream(self._d2h):
+                self._d2h.wait_event(done)
+                dst = host_out[1][i] if full else host_out[0][i]
+                dst.copy_(self.layer_output(L), non_blocking=True)
+                rd = torch.cuda.Event()
+                rd.record(self._d2h)
+                self._out_read[L] = rd
+        ops.add_int(self.pos, 1, stream=comp)
+        comp.wait_stream(self._d2h)  # the step ends when its outputs are on the host
+        return n + 1
+
     # -------------------------------------------------------------- accounting
     def bytes_per_step(self, ctx_attended: float) -> dict[str, float]:
         """Algorithmic HBM bytes of one step when each sequence attends ctx_attended
