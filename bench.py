@@ -298,6 +298,88 @@ def run_layer(args) -> dict:
             "peak_source": peak_src}
 
 
+# ------------------------------------------------- config 3 (long context)
+def run_longctx(args, rank: int, world: int, local: int) -> dict | None:
+    """Config 3: 16 gated GQA layers at context 262144, query at 262143.
+    config3a: 16 sequences sharded across ranks (no collective); a rank whose share does
+    not fit in HBM runs it in waves (the cache of the next wave is regenerated between
+    waves, outside the timed region). config3b: one sequence, KV range sharded across
+    ranks, one all-gather of the partial records per step."""
+    import torch
+    import torch.distributed as dist
+    from vx27_b200.dist import shard_range
+    from vx27_b200.longctx import LongContextGQA
+    torch.cuda.set_device(local)
+    ctx, layers = args.ctx3, 16
+    seq_bytes = layers * 4 * ctx * 256 * 2 * 2
+    split = args.workload == "config3b"
+    if split:
+        waves, total_seq = [(1, 0)], 1
+    else:
+        total_seq = args.seqs3
+        b0, b1 = shard_range(total_seq, world, rank)
+        w = max(1, min(b1 - b0, int(args.hbm_budget_gb * 1e9 // seq_bytes)))
+        waves = [(min(w, b1 - s), s) for s in range(b0, b1, w)]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    step_ms, kv_bytes, launches = 0.0, 0, 0
+    for bsz, off in waves:
+        dec = LongContextGQA(bsz, ctx, layers, rank=rank, world=world, split_kv=split,
+                             seq_offset=off)
+        for _ in range(args.warmup):
+            per_step = dec.step()
+        graph = None
+        if args.graph:  # one CUDA graph per step: no host launch overhead between kernels
+            barrier()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                dec.step()
+            graph.replay()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            if graph is not None:
+                graph.replay()
+                launches += per_step
+            else:
+                launches += dec.step()
+        e1.record()
+        barrier()
+        del graph
+        step_ms += e0.elapsed_time(e1) / args.steps
+        kv_bytes += dec.kv_bytes()
+        del dec
+        torch.cuda.empty_cache()
+    mx = step_ms
+    if world > 1:
+        t = torch.tensor([step_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        mx = float(t.item())
+    peak, peak_src = peaks()
+    gbs = kv_bytes / (step_ms * 1e-3) / 1e9
+    if rank != 0:
+        return None
+    return {"metric": "long-context gated GQA decode tokens/s (config 3); % of HBM roofline",
+            "workload": args.workload, "value": round(total_seq / (mx * 1e-3), 3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(mx, 4), "higher_is_better": True,
+            "scaling": "strong" if split else "weak",
+            "config": {"ctx": ctx, "layers": layers, "sequences": total_seq,
+                       "waves_rank0": [w[0] for w in waves],
+                       "wave_note": "caches regenerated between waves, outside timing",
+                       "parallelism": (f"kv-split{world} (NCCL all-gather of partial records)"
+                                       if split else f"dp{world} (sequences sharded)")},
+            "roofline_rank0": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak,
+                               "unit": "GB/s", "frac": round(gbs / peak, 4),
+                               "kv_bytes_per_step": kv_bytes, "peak_source": peak_src},
+            "gpu_launches": launches, "cuda_graph": bool(args.graph)}
+
+
 # ------------------------------------------------------------ CPU reference
 def cpu_reference_step_sampler(n_seq: int, ctx: int, threads: int):
     """Builds host buffers for n_seq sequences of config 2 and returns (run_step, kind).
@@ -412,17 +494,22 @@ def main() -> None:
     ap.add_argument("--ref-seqs", type=int, default=4)
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config2", "dn_layer", "gqa_layer"],
-                    default="config2",
-                    help="config2 (the metric); single-layer workloads are for kernel "
-                         "rooflines and profiling")
+    ap.add_argument("--workload", choices=["config2", "config3a", "config3b", "dn_layer",
+                                           "gqa_layer"], default="config2",
+                    help="config2 (the metric); config3a/3b long context; single-layer "
+                         "workloads are for kernel rooflines and profiling")
+    ap.add_argument("--ctx3", type=int, default=262144)
+    ap.add_argument("--seqs3", type=int, default=16)
+    ap.add_argument("--hbm-budget-gb", type=float, default=150.0)
+    ap.add_argument("--graph", action="store_true",
+                    help="config3: replay each step as one CUDA graph")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
-    if args.workload != "config2":
+    if args.workload in ("dn_layer", "gqa_layer"):
         print(json.dumps(run_layer(args)), flush=True)
         return
 
@@ -440,6 +527,11 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.workload in ("config3a", "config3b"):
+            line = run_longctx(args, rank, world, local_rank)
+            if line is not None:
+                print(json.dumps(line), flush=True)
+            return
         line = run_ours(args, rank, world, local_rank)
         if line is not None:
             if world == 1 and not args.no_cpu_baseline:

@@ -95,15 +95,21 @@ int vx27_gqa_decode_batch_noalloc(const float *q, const void *gate, const void *
  * same range for all B sequences): for each (b, Q head) m = max scaled score,
  * l = sum exp(s - m), o = sum exp(s - m) v / l. Record layout (fp32):
  *   o [B][nq][hd] followed by ml [B][nq][2]; record size B*nq*(hd+2) floats.
- * An empty range yields m = -inf, l = 0, o = 0. vx27_gqa_combine merges n_parts
- * consecutive records (m* = max m_i, l* = sum l_i e^{m_i-m*}, o = sum o_i l_i
- * e^{m_i-m*} / l*) and applies the sigmoid gate.
+ * An empty range yields m = -inf, l = 0, o = 0. vx27_gqa_combine merges n_parts records
+ * placed part_stride floats apart (0: back to back) -- m* = max m_i, l* = sum l_i
+ * e^{m_i-m*}, o = sum o_i l_i e^{m_i-m*} / l* -- and applies the sigmoid gate.
+ * A long range is split across CTAs and merged into the one record; the sub-records need
+ * vx27_gqa_partial_workspace_size(B, nq, nkv, hd, p_end - p_begin) bytes of workspace (a
+ * smaller or NULL workspace lowers the split count, down to one CTA per KV head).
  */
+size_t vx27_gqa_partial_workspace_size(int B, int nq, int nkv, int hd, int max_range);
 int vx27_gqa_partial(const float *q, const void *k_cache, const void *v_cache, int cap,
                      int p_begin, int p_end, float *part, int B, int nq, int nkv, int hd,
-                     void *stream, char *err, size_t errlen);
-int vx27_gqa_combine(const float *parts, int n_parts, const void *gate, void *out, int B,
-                     int nq, int hd, int flags, void *stream, char *err, size_t errlen);
+                     void *workspace, size_t workspace_bytes, void *stream, char *err,
+                     size_t errlen);
+int vx27_gqa_combine(const float *parts, int n_parts, size_t part_stride, const void *gate,
+                     void *out, int B, int nq, int hd, int flags, void *stream, char *err,
+                     size_t errlen);
 
 #ifdef __cplusplus
 }

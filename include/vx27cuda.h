@@ -43,10 +43,11 @@ int vx27cuda_device_status(void *stream, uint32_t *status, int clear, char *err,
 int vx27cuda_num_sms(void);
 
 /* Seeded synthetic inputs on the device: element i of (seed, stream_id) is the same
- * splitmix64 + Box-Muller value on every device and every call; bf16 != 0 writes
- * bf16 (round to nearest even), else fp32. */
+ * splitmix64 + Box-Muller value on every device and every call; dst[e] receives element
+ * offset + e; bf16 != 0 writes bf16 (round to nearest even), else fp32. */
 int vx27cuda_fill_normal(void *dst, size_t n, int bf16, uint64_t seed, uint64_t stream_id,
-                         float mean, float stddev, void *stream, char *err, size_t errlen);
+                         uint64_t offset, float mean, float stddev, void *stream, char *err,
+                         size_t errlen);
 int vx27cuda_fill_uniform(float *dst, size_t n, uint64_t seed, uint64_t stream_id, float lo,
                           float hi, void *stream, char *err, size_t errlen);
 /* Sets n ints to value (positions arrays); adds delta to n ints. */

@@ -129,13 +129,16 @@ def test_partial_combine_context_parallel(cuda, orc, rope):
                    dev(x["pos"]), kc, vc, q)
     n = 4
     rec = B * NQ * (HD + 2)
-    parts = torch.empty(n * rec, device="cuda")
-    for r in range(n):
-        ops.gqa_partial(q, kc, vc, r * cap // n, (r + 1) * cap // n, parts[r * rec:(r + 1) * rec])
-    out = torch.empty(B, NQ, HD, device="cuda")
-    ops.gqa_combine(parts, n, dev(x["gate"], True).view(B, NQ, HD), out)
-    torch.cuda.synchronize()
-    assert rel_err(host(out).reshape(-1), full) < 1e-5
+    ws = torch.empty(ops.gqa_partial_workspace_bytes(B, NQ, NKV, HD, cap) // 4 + 1, device="cuda")
+    for workspace in (None, ws):  # one CTA per KV head, or split across CTAs and merged
+        parts = torch.empty(n * rec, device="cuda")
+        for r in range(n):
+            ops.gqa_partial(q, kc, vc, r * cap // n, (r + 1) * cap // n,
+                            parts[r * rec:(r + 1) * rec], workspace)
+        out = torch.empty(B, NQ, HD, device="cuda")
+        ops.gqa_combine(parts, n, dev(x["gate"], True).view(B, NQ, HD), out)
+        torch.cuda.synchronize()
+        assert rel_err(host(out).reshape(-1), full) < 1e-5
 
 
 def test_append_q_only_and_foreign_slot(cuda, orc, rope):

@@ -22,7 +22,7 @@ PROTOTYPES: dict[str, tuple] = {
     "vx27cuda_last_error": (_cp, []),
     "vx27cuda_device_status": (_i, [_p, C.POINTER(C.c_uint32), _i, _cp, _sz]),
     "vx27cuda_num_sms": (_i, []),
-    "vx27cuda_fill_normal": (_i, [_p, _sz, _i, _u64, _u64, _f, _f, _p, _cp, _sz]),
+    "vx27cuda_fill_normal": (_i, [_p, _sz, _i, _u64, _u64, _u64, _f, _f, _p, _cp, _sz]),
     "vx27cuda_fill_uniform": (_i, [_p, _sz, _u64, _u64, _f, _f, _p, _cp, _sz]),
     "vx27cuda_fill_int": (_i, [_p, _sz, _i, _p, _cp, _sz]),
     "vx27cuda_add_int": (_i, [_p, _sz, _i, _p, _cp, _sz]),
@@ -56,8 +56,10 @@ PROTOTYPES: dict[str, tuple] = {
                                    _p, _cp, _sz]),
     "vx27_gqa_decode_batch_noalloc": (_i, [_p, _p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _i,
                                            _p, _cp, _sz]),
-    "vx27_gqa_partial": (_i, [_p, _p, _p, _i, _i, _i, _p, _i, _i, _i, _i, _p, _cp, _sz]),
-    "vx27_gqa_combine": (_i, [_p, _i, _p, _p, _i, _i, _i, _i, _p, _cp, _sz]),
+    "vx27_gqa_partial_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "vx27_gqa_partial": (_i, [_p, _p, _p, _i, _i, _i, _p, _i, _i, _i, _i, _p, _sz, _p, _cp,
+                              _sz]),
+    "vx27_gqa_combine": (_i, [_p, _i, _sz, _p, _p, _i, _i, _i, _i, _p, _cp, _sz]),
     # vx27_kv.h
     "vx27_kv_elems": (_u64, [_i]),
     "vx27_kv_gb": (_d, [_i, _d]),

@@ -84,9 +84,8 @@ gqa_append_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
 template <bool ACT_BF16, bool OUT_BF16>
 __global__ void __launch_bounds__(HD)
 gqa_combine_k(const float *__restrict__ parts, int n_parts, const void *__restrict__ gate,
-              void *__restrict__ out, int B, int nq) {
+              void *__restrict__ out, int B, int nq, size_t rec) {
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-    const size_t rec = (size_t)B * nq * (HD + 2);
     const size_t hq = (size_t)b * nq + h;
     float M = -INFINITY;
     for (int r = 0; r < n_parts; r++) {
@@ -109,13 +108,60 @@ gqa_combine_k(const float *__restrict__ parts, int n_parts, const void *__restri
     act_st<OUT_BF16>(out, hq * HD + d, att * (1.0f / (1.0f + expf(-g))));
 }
 
+// Merges n_parts partial records into one partial record (same layout), for a range
+// that was split across CTAs: m = max m_i, l = sum l_i e^{m_i - m}, o = sum o_i l_i
+// e^{m_i - m} / l.
+__global__ void __launch_bounds__(HD)
+gqa_merge_k(const float *__restrict__ parts, int n_parts, float *__restrict__ rec_out, int B,
+            int nq) {
+    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const size_t rec = (size_t)B * nq * (HD + 2);
+    const size_t hq = (size_t)b * nq + h;
+    float M = -INFINITY;
+    for (int r = 0; r < n_parts; r++) {
+        const float *ml = parts + (size_t)r * rec + (size_t)B * nq * HD + hq * 2;
+        if (ml[1] > 0.0f) M = fmaxf(M, ml[0]);
+    }
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+        for (int r = 0; r < n_parts; r++) {
+            const float *pr = parts + (size_t)r * rec;
+            const float *ml = pr + (size_t)B * nq * HD + hq * 2;
+            if (!(ml[1] > 0.0f)) continue;
+            const float w = ml[1] * expf(ml[0] - M);
+            L += w;
+            O = fmaf(w, pr[hq * HD + d], O);
+        }
+    }
+    rec_out[hq * HD + d] = L > 0.0f ? O / L : 0.0f;
+    if (d == 0) {
+        float *ml = rec_out + (size_t)B * nq * HD + hq * 2;
+        ml[0] = L > 0.0f ? M : -INFINITY;
+        ml[1] = L;
+    }
+}
+
+// Split count for B*nkv (sequence, KV head) blocks over max_ctx positions. The split
+// kernel runs one CTA per SM, so a launch takes ceil(CTAs / SMs) waves of
+// (tiles per split + ~2 tiles of pipeline fill and drain); pick the count that minimises
+// that estimate (ties: fewer splits, i.e. fewer partial records to merge).
 int auto_splits(int B, int nkv, int max_ctx) {
-    const int blocks = B * nkv;
-    int n = (2 * num_sms() + blocks - 1) / blocks;
-    const int max_by_ctx = (max_ctx + TILE - 1) / TILE;
-    if (n > max_by_ctx) n = max_by_ctx;
-    if (n > 128) n = 128;
-    return n < 1 ? 1 : n;
+    const long long blocks = (long long)B * nkv;
+    const long long sms = num_sms();
+    const int tiles = (max_ctx + TILE - 1) / TILE;
+    if (tiles <= 1 || blocks >= 8 * sms) return 1;
+    int best = 1;
+    long long best_t = -1;
+    const int n_max = tiles < 512 ? tiles : 512;
+    for (int n = 1; n <= n_max; n++) {
+        const int per = (tiles + n - 1) / n;          // tiles per split
+        const int active = (tiles + per - 1) / per;   // splits that get work
+        if (active < n) continue;                     // same as a smaller n
+        const long long waves = (blocks * n + sms - 1) / sms;
+        const long long t = waves * (per + 2);
+        if (best_t < 0 || t < best_t) { best_t = t; best = n; }
+    }
+    return best;
 }
 
 int launch_split(const float *q, const void *kc, const void *vc, int cap, const int *pos,
@@ -126,13 +172,14 @@ int launch_split(const float *q, const void *kc, const void *vc, int cap, const 
 }
 
 int launch_combine(const float *parts, int n_parts, const void *gate, void *out, int B, int nq,
-                   int flags, cudaStream_t st, char *err, size_t errlen) {
+                   int flags, cudaStream_t st, char *err, size_t errlen, size_t stride = 0) {
     const dim3 grid(nq, B);
     const bool a = flags & VX27_F_ACT_BF16, o = flags & VX27_F_OUT_BF16;
-    if (a && o) gqa_combine_k<true, true><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq);
-    else if (a) gqa_combine_k<true, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq);
-    else if (o) gqa_combine_k<false, true><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq);
-    else gqa_combine_k<false, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq);
+    const size_t rec = stride ? stride : (size_t)B * nq * (HD + 2);
+    if (a && o) gqa_combine_k<true, true><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
+    else if (a) gqa_combine_k<true, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
+    else if (o) gqa_combine_k<false, true><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
+    else gqa_combine_k<false, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
     VX_CK(cudaGetLastError());
     return 0;
 }
@@ -222,26 +269,51 @@ int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
     return launch_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen);
 }
 
+size_t vx27_gqa_partial_workspace_size(int B, int nq, int nkv, int hd, int max_range) {
+    if (B <= 0 || nq <= 0 || nkv <= 0 || hd <= 0) return 0;
+    const int n = auto_splits(B, nkv, max_range);
+    return n > 1 ? (size_t)n * B * nq * (hd + 2) * sizeof(float) : 0;
+}
+
 int vx27_gqa_partial(const float *q, const void *k_cache, const void *v_cache, int cap,
                      int p_begin, int p_end, float *part, int B, int nq, int nkv, int hd,
-                     void *stream, char *err, size_t errlen) {
+                     void *workspace, size_t workspace_bytes, void *stream, char *err,
+                     size_t errlen) {
     if (check_shape("vx27_gqa_partial", B, nq, nkv, hd, err, errlen)) return -1;
     if (!q || !k_cache || !v_cache || !part)
         return fail(err, errlen, "vx27_gqa_partial: null pointer argument");
     if (p_begin < 0 || p_end < p_begin || p_end > cap)
         return fail(err, errlen, "vx27_gqa_partial: range [%d, %d) outside cache of %d", p_begin,
                     p_end, cap);
-    return launch_split(q, k_cache, v_cache, cap, nullptr, part, B, nq, nkv, 1, p_begin, p_end,
-                        (cudaStream_t)stream, err, errlen);
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t rec = (size_t)B * nq * (hd + 2) * sizeof(float);
+    int n = auto_splits(B, nkv, p_end - p_begin);
+    const int fit = workspace ? (int)(workspace_bytes / rec) : 0;
+    if (n > fit) n = fit;
+    if (n <= 1)  // one CTA per (sequence, KV head) writes the record directly
+        return launch_split(q, k_cache, v_cache, cap, nullptr, part, B, nq, nkv, 1, p_begin,
+                            p_end, st, err, errlen);
+    float *sub = (float *)workspace;
+    if (launch_split(q, k_cache, v_cache, cap, nullptr, sub, B, nq, nkv, n, p_begin, p_end, st,
+                     err, errlen))
+        return -1;
+    gqa_merge_k<<<dim3(nq, B), HD, 0, st>>>(sub, n, part, B, nq);
+    VX_CK(cudaGetLastError());
+    return 0;
 }
 
-int vx27_gqa_combine(const float *parts, int n_parts, const void *gate, void *out, int B,
-                     int nq, int hd, int flags, void *stream, char *err, size_t errlen) {
+int vx27_gqa_combine(const float *parts, int n_parts, size_t part_stride, const void *gate,
+                     void *out, int B, int nq, int hd, int flags, void *stream, char *err,
+                     size_t errlen) {
     if (hd != HD) return fail(err, errlen, "vx27_gqa_combine: hd=%d unsupported (256 only)", hd);
     if (!parts || !gate || !out || n_parts < 1 || B <= 0 || nq <= 0)
         return fail(err, errlen, "vx27_gqa_combine: bad arguments");
+    const size_t rec = (size_t)B * nq * (hd + 2);
+    if (part_stride && part_stride < rec)
+        return fail(err, errlen, "vx27_gqa_combine: part_stride %zu < record size %zu",
+                    part_stride, rec);
     return launch_combine(parts, n_parts, gate, out, B, nq, flags, (cudaStream_t)stream, err,
-                          errlen);
+                          errlen, part_stride);
 }
 
 }  // extern "C"

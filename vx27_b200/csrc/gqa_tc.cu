@@ -92,15 +92,17 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h0 = kvh * G;  // the G query heads of this KV head (G = nq / nkv)
 
+    // range of this split: [p_begin, p_end) (decode: [0, pos[b]]) cut into n_splits
+    // pieces on 128-position boundaries
     int p0, p1;
-    if (p_end >= 0) {
-        p0 = p_begin; p1 = p_end;
-    } else {
-        const int n = pos[b] + 1;
-        const int tiles = (n + TC_TILE - 1) / TC_TILE;
+    {
+        const int rb = p_end >= 0 ? p_begin : 0;
+        const int re = p_end >= 0 ? p_end : pos[b] + 1;
+        const int tiles = (re - rb + TC_TILE - 1) / TC_TILE;
         const int per = (tiles + n_splits - 1) / n_splits;
-        p0 = s * per * TC_TILE;
-        p1 = min(n, (s + 1) * per * TC_TILE);
+        p0 = rb + s * per * TC_TILE;
+        p1 = min(re, rb + (s + 1) * per * TC_TILE);
+        if (p1 < p0) p1 = p0;
     }
     p0 = max(p0, 0);
     p1 = min(p1, cap);

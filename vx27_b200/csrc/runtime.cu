@@ -71,9 +71,10 @@ static uint64_t stream_key(uint64_t seed, uint64_t stream) {
     return splitmix64(splitmix64(seed) ^ (stream * 0xD1B54A32D192ED03ull));
 }
 __global__ void fill_normal_k(void *dst, size_t n, int bf16, uint64_t key, float mean,
-                              float stddev) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-         i += (size_t)gridDim.x * blockDim.x) {
+                              float stddev, uint64_t offset) {
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n;
+         e += (size_t)gridDim.x * blockDim.x) {
+        const uint64_t i = e + offset;  // element index within the stream
         const uint64_t j = i >> 1;
         const uint64_t r1 = splitmix64(key + 2 * j), r2 = splitmix64(key + 2 * j + 1);
         const double u1 = (double)((r1 >> 11) + 1) * 0x1.0p-53;
@@ -82,8 +83,8 @@ __global__ void fill_normal_k(void *dst, size_t n, int bf16, uint64_t key, float
         const double th = 6.283185307179586 * u2;
         const double z = (i & 1) ? rad * sin(th) : rad * cos(th);
         const float x = (float)((double)mean + (double)stddev * z);
-        if (bf16) ((uint16_t *)dst)[i] = f32_to_bf16(x);
-        else ((float *)dst)[i] = x;
+        if (bf16) ((uint16_t *)dst)[e] = f32_to_bf16(x);
+        else ((float *)dst)[e] = x;
     }
 }
 __global__ void fill_uniform_k(float *dst, size_t n, uint64_t key, float lo, float hi) {
@@ -190,11 +191,12 @@ int vx27cuda_device_status(void *stream, uint32_t *status, int clear, char *err,
 }
 
 int vx27cuda_fill_normal(void *dst, size_t n, int bf16, uint64_t seed, uint64_t stream_id,
-                         float mean, float stddev, void *stream, char *err, size_t errlen) {
+                         uint64_t offset, float mean, float stddev, void *stream, char *err,
+                         size_t errlen) {
     if (n == 0) return 0;
     if (!dst) return fail(err, errlen, "vx27cuda_fill_normal: null destination");
     fill_normal_k<<<grid_for(n), 256, 0, (cudaStream_t)stream>>>(
-        dst, n, bf16, stream_key(seed, stream_id), mean, stddev);
+        dst, n, bf16, stream_key(seed, stream_id), mean, stddev, offset);
     VX_CK(cudaGetLastError());
     return 0;
 }

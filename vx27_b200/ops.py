@@ -200,29 +200,41 @@ def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: i
     check(rc, e)
 
 
-def gqa_partial(q, k_cache, v_cache, p_begin: int, p_end: int, part, stream=None) -> None:
+def gqa_partial_workspace_bytes(B: int, nq: int, nkv: int, hd: int, max_range: int) -> int:
+    return load().vx27_gqa_partial_workspace_size(B, nq, nkv, hd, max_range)
+
+
+def gqa_partial(q, k_cache, v_cache, p_begin: int, p_end: int, part, workspace=None,
+                stream=None) -> None:
+    """Partial record over cache slots [p_begin, p_end) (split across CTAs when a
+    workspace is given)."""
     B, nq, hd = q.shape
     nkv, cap = k_cache.shape[1], k_cache.shape[2]
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     e = errbuf()
     rc = load().vx27_gqa_partial(_t(q), _t(k_cache), _t(v_cache), cap, p_begin, p_end, _t(part),
-                                 B, nq, nkv, hd, _stream(stream), e, 512)
+                                 B, nq, nkv, hd, _t(workspace), ws_bytes, _stream(stream), e, 512)
     check(rc, e)
 
 
-def gqa_combine(parts, n_parts: int, gate, out, stream=None) -> None:
+def gqa_combine(parts, n_parts: int, gate, out, part_stride: int = 0, stream=None) -> None:
+    """Merges n_parts partial records placed part_stride floats apart (0: contiguous)."""
     B, nq, hd = gate.shape
     flags = (F_ACT_BF16 if _is_bf16(gate) else 0) | (F_OUT_BF16 if _is_bf16(out) else 0)
     e = errbuf()
-    rc = load().vx27_gqa_combine(_t(parts), n_parts, _t(gate), _t(out), B, nq, hd, flags,
-                                 _stream(stream), e, 512)
+    if parts.is_cuda and not parts.is_contiguous():
+        raise Vx27Error("parts must be contiguous")
+    rc = load().vx27_gqa_combine(C.c_void_p(parts.data_ptr()), n_parts, part_stride, _t(gate),
+                                 _t(out), B, nq, hd, flags, _stream(stream), e, 512)
     check(rc, e)
 
 
 def fill_normal(t, seed: int, stream_id: int, mean: float = 0.0, std: float = 1.0,
-                stream=None) -> None:
+                offset: int = 0, stream=None) -> None:
+    """t[e] = element offset+e of the seeded normal stream (seed, stream_id)."""
     e = errbuf()
     rc = load().vx27cuda_fill_normal(_t(t), t.numel(), 1 if _is_bf16(t) else 0, seed, stream_id,
-                                     mean, std, _stream(stream), e, 512)
+                                     offset, mean, std, _stream(stream), e, 512)
     check(rc, e)
 
 
