@@ -91,6 +91,26 @@ int vx27_gqa_decode_batch_noalloc(const float *q, const void *gate, const void *
                                   void *stream, char *err, size_t errlen);
 
 /*
+ * Causal gated GQA prefill of T prompt tokens at positions p0 .. p0+T-1 of one sequence
+ * (config 4), on the tensor cores. Per token: QK RMSNorm and partial RoPE as
+ * vx27_gqa_append (the rotated k and v are written into the bf16 cache slots p0 + t,
+ * ready for decode; slots up to the next multiple of 64 past p0 + T are zeroed); then
+ * out[t] = softmax over cache positions [0, p0 + t] of (q_t k^T / sqrt(hd)) v, times
+ * sigmoid(gate[t]).
+ *   q_in, gate [T][nq][hd], k_in, v_in [T][nkv][hd] (act dtype); out [T][nq][hd]
+ *   k_cache, v_cache bf16 [nkv][cap][hd] (batch 1 layout of vx27_kv), p0 + T <= cap
+ *   workspace: vx27_gqa_prefill_workspace_size(T, nq, hd) bytes (normalised q, bf16)
+ * q and p enter the tensor cores as bf16 (accumulation fp32). hd must be 256.
+ */
+size_t vx27_gqa_prefill_workspace_size(int T, int nq, int hd);
+int vx27_gqa_prefill(const void *q_in, const void *k_in, const void *v_in, const void *gate,
+                     const float *q_norm_w, const float *k_norm_w, const float *rope_table,
+                     int rope_table_len, int p0, void *k_cache, void *v_cache, int cap,
+                     void *out, void *workspace, size_t workspace_bytes, int T, int nq, int nkv,
+                     int hd, int rope_dim, float eps, int flags, void *stream, char *err,
+                     size_t errlen);
+
+/*
  * Context-parallel pieces. A partial record covers cache slots [p_begin, p_end) (the
  * same range for all B sequences): for each (b, Q head) m = max scaled score,
  * l = sum exp(s - m), o = sum exp(s - m) v / l. Record layout (fp32):

@@ -56,6 +56,9 @@ PROTOTYPES: dict[str, tuple] = {
                                    _p, _cp, _sz]),
     "vx27_gqa_decode_batch_noalloc": (_i, [_p, _p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _i,
                                            _p, _cp, _sz]),
+    "vx27_gqa_prefill_workspace_size": (_sz, [_i, _i, _i]),
+    "vx27_gqa_prefill": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i, _p, _p, _i, _p, _p, _sz, _i, _i,
+                              _i, _i, _i, _f, _i, _p, _cp, _sz]),
     "vx27_gqa_partial_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "vx27_gqa_partial": (_i, [_p, _p, _p, _i, _i, _i, _p, _i, _i, _i, _i, _p, _sz, _p, _cp,
                               _sz]),

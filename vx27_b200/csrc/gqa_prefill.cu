@@ -1,0 +1,432 @@
+// K4: causal gated GQA prefill of T prompt tokens on the tensor cores (config 4).
+//
+//   prep kernel   per token and head: QK RMSNorm, partial RoPE at position p0 + t (host
+//                 table), q -> bf16 Qn[nq][T][256], k/v -> the bf16 KV cache slots p0 + t
+//                 (the cache the decode continues from); src/vx27_qfwd.c:339-346 per token
+//   main kernel   one CTA per (128-query tile, query head), flash-attention forward:
+//     warp 0      TMA: the Q tile (128 x 256, resident) and 64-key K / V tiles, two stages
+//     warp 1      tcgen05.mma: S = Q K^T (128 x 64, TMEM, double buffered) and
+//                 O += P V (128 x 256 in TMEM, V read as an MN-major operand)
+//     warps 2-5   one thread per query row (its TMEM lane): causal mask, running max in
+//                 log2 units, p = 2^(x - m) as bf16 rows of P in shared memory; O is
+//                 rescaled in TMEM only when a row's max grows by more than 2^8 (lazy
+//                 rescale); epilogue O / l * sigmoid(gate).
+// Query tiles are issued longest first; the six query heads of a KV head run on
+// neighbouring CTAs so their K/V tiles are served from L2.
+#include <math.h>
+#include "common.cuh"
+#include "tc.cuh"
+#include "../../include/vx27_gqa.h"
+
+namespace vx27 {
+namespace {
+
+constexpr int HDP = 256;
+constexpr int QT = 128;          // queries per CTA
+constexpr int KT = 64;           // keys per tile
+constexpr int PF_THREADS = 192;
+constexpr float RESCALE_LOG2 = 8.0f;
+
+struct PfSmem {
+    uint8_t q[4][QT * 128];      // Q tile, 4 chunks of [128 rows x 64 dims], 128B swizzle
+    uint8_t k[2][4][KT * 128];   // K stages
+    uint8_t v[2][4][KT * 128];   // V stages
+    uint8_t p[2][QT * 128];      // P rows (64 keys, bf16), two buffers
+    uint64_t qfull, kfull[2], kempty[2], vfull[2], vempty[2];
+    uint64_t s_full[2], s_empty[2], p_full[2], pv_done[2], o_final, mma_done;
+    uint32_t tmem_base;
+    int abort;
+};
+
+__device__ __forceinline__ uint64_t pf_timer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ bool pf_wait(uint64_t *bar, uint32_t parity, PfSmem &sm, uint32_t *status,
+                        uint32_t code) {
+    const uint32_t addr = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
+            "selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+        if (ok) return true;
+        if ((it & 255) == 0) {
+            if (*(volatile int *)&sm.abort) return false;
+            const uint64_t now = pf_timer();
+            if (it == 0) t0 = now;
+            else if (now - t0 > 2000000000ull) {
+                *(volatile int *)&sm.abort = 1;
+                dev_flag(status, code);
+                return false;
+            }
+        }
+    }
+}
+
+// ---- prep ----------------------------------------------------------------------------
+template <bool ACT_BF16, bool ONE_P>
+__global__ void __launch_bounds__(HDP)
+prefill_prep_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
+               const void *__restrict__ v_in, const float *__restrict__ qw,
+               const float *__restrict__ kw, const float *__restrict__ rope, int rope_len,
+               int p0, uint16_t *__restrict__ qn, uint16_t *__restrict__ kc,
+               uint16_t *__restrict__ vc, int cap, int T, int nq, int nkv, int rope_dim,
+               float eps, uint32_t *status) {
+    const int head = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
+    const bool is_q = head < nq;
+    const int h = is_q ? head : head - nq;
+    const size_t row = is_q ? ((size_t)t * nq + h) * HDP : ((size_t)t * nkv + h) * HDP;
+    const float x = act_ld<ACT_BF16>(is_q ? q_in : k_in, row + d);
+    __shared__ double red[HDP / 32];
+    __shared__ float r_s;
+    __shared__ float y_s[HDP];
+    double ss = warp_sum_d((double)x * (double)x);
+    if ((d & 31) == 0) red[d >> 5] = ss;
+    __syncthreads();
+    if (d == 0) {
+        double tt = 0.0;
+        for (int w = 0; w < HDP / 32; w++) tt += red[w];
+        r_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(tt / HDP), eps)));
+    }
+    __syncthreads();
+    float w = is_q ? qw[d] : kw[d];
+    if (ONE_P) w = __fadd_rn(w, 1.0f);
+    const float y = __fmul_rn(__fmul_rn(x, r_s), w);
+    y_s[d] = y;
+    __syncthreads();
+    const int p = p0 + t;
+    const int half = rope_dim / 2;
+    float out = y;
+    if (d < rope_dim) {
+        if (p < 0 || p >= rope_len) {
+            if (d == 0) dev_flag(status, VX_DEV_BAD_ARG);
+        } else {
+            const float *rr = rope + (size_t)p * rope_dim;
+            const int i = d < half ? d : d - half;
+            const float c = rr[i], s = rr[half + i];
+            const float x0 = y_s[i], x1 = y_s[i + half];
+            out = d < half ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s))
+                           : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        }
+    }
+    if (is_q) {
+        qn[((size_t)h * T + t) * HDP + d] = f32_to_bf16(out);
+    } else if (p < cap) {
+        const size_t o = ((size_t)h * cap + p) * HDP + d;
+        kc[o] = f32_to_bf16(out);
+        vc[o] = f32_to_bf16(act_ld<ACT_BF16>(v_in, row + d));
+    }
+}
+
+// Zero cache slots [from, to) of every KV head so the last key tile reads finite values.
+__global__ void zero_slots_k(uint16_t *kc, uint16_t *vc, int cap, int nkv, int from, int to) {
+    const int h = blockIdx.y;
+    const size_t n = (size_t)(to - from) * HDP;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n;
+         e += (size_t)gridDim.x * blockDim.x) {
+        const size_t o = ((size_t)h * cap + from) * HDP + e;
+        kc[o] = 0;
+        vc[o] = 0;
+    }
+}
+
+// ---- main kernel ------------------------------------------------------------------------
+template <bool ACT_BF16, bool OUT_BF16>
+__global__ void __launch_bounds__(PF_THREADS, 1)
+prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                const __grid_constant__ CUtensorMap tmv, const void *__restrict__ gate,
+                void *__restrict__ out, int T, int p0, int nq, int nkv, int cap,
+                uint32_t *status) {
+    extern __shared__ uint8_t pf_smem_raw[];
+    PfSmem &sm = *reinterpret_cast<PfSmem *>(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n_qt = (T + QT - 1) / QT;
+    const int qt = n_qt - 1 - (int)(blockIdx.x / nq);  // longest tiles first
+    const int h = blockIdx.x % nq;
+    const int kvh = h * nkv / nq;
+    const int t0 = qt * QT;
+    const int t_end = min(T, t0 + QT);
+    const int n_kt = (p0 + t_end + KT - 1) / KT;  // key tiles up to the last query's position
+
+    if (tid == 0) {
+        mbar_init(&sm.qfull, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&sm.kfull[i], 1); mbar_init(&sm.kempty[i], 1);
+            mbar_init(&sm.vfull[i], 1); mbar_init(&sm.vempty[i], 1);
+            mbar_init(&sm.s_full[i], 1); mbar_init(&sm.s_empty[i], 128);
+            mbar_init(&sm.p_full[i], 128); mbar_init(&sm.pv_done[i], 1);
+        }
+        mbar_init(&sm.o_final, 1);
+        mbar_init(&sm.mma_done, 1);
+        sm.abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&sm.tmem_base, 512);
+        tmem_relinquish();
+        if (lane == 0) { tma_prefetch_desc(&tmq); tma_prefetch_desc(&tmk); tma_prefetch_desc(&tmv); }
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+    const uint32_t tS = tmem, tO = tmem + 128;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer
+            mbar_arrive_expect_tx(&sm.qfull, 4 * QT * 128);
+            for (int c = 0; c < 4; c++) tma_load_2d(sm.q[c], &tmq, c * 64, h * T + t0, &sm.qfull);
+            const int krow0 = kvh * cap;  // rows of this KV head in the [nkv*cap][256] maps
+            for (int j = 0; j < n_kt; j++) {
+                const int st = j & 1;
+                if (j >= 2 && !pf_wait(&sm.kempty[st], ((j >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
+                    break;
+                mbar_arrive_expect_tx(&sm.kfull[st], 4 * KT * 128);
+                for (int c = 0; c < 4; c++)
+                    tma_load_2d(sm.k[st][c], &tmk, c * 64, krow0 + j * KT, &sm.kfull[st]);
+                if (j >= 2 && !pf_wait(&sm.vempty[st], ((j >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
+                    break;
+                mbar_arrive_expect_tx(&sm.vfull[st], 4 * KT * 128);
+                for (int c = 0; c < 4; c++)
+                    tma_load_2d(sm.v[st][c], &tmv, c * 64, krow0 + j * KT, &sm.vfull[st]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---- MMA issuer
+            const uint32_t id1 = idesc_bf16(128, KT, false, false);
+            const uint32_t id2 = idesc_bf16(128, HDP, false, true);
+            bool ok = pf_wait(&sm.qfull, 0, sm, status, VX_DEV_TIMEOUT_TMA);
+            const uint32_t q0 = smem_u32(sm.q[0]);
+            for (int j = 0; j <= n_kt && ok; j++) {
+                if (j < n_kt) {
+                    const int b = j & 1;
+                    if (j >= 2) ok = pf_wait(&sm.s_empty[b], ((j >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                    ok = ok && pf_wait(&sm.kfull[b], (j >> 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t kb = smem_u32(sm.k[b][0]);
+#pragma unroll
+                    for (int c = 0; c < 4; c++)
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++)
+                            mma_bf16(tS + b * KT,
+                                     sdesc_sw128(q0 + c * QT * 128 + kk * 32, 16, 1024),
+                                     sdesc_sw128(kb + c * KT * 128 + kk * 32, 16, 1024), id1,
+                                     (c | kk) != 0);
+                    mma_commit(&sm.kempty[b]);
+                    mma_commit(&sm.s_full[b]);
+                }
+                if (j >= 1) {
+                    const int t = j - 1, b = t & 1;
+                    ok = pf_wait(&sm.p_full[b], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA) &&
+                         pf_wait(&sm.vfull[b], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t pb = smem_u32(sm.p[b]), vb = smem_u32(sm.v[b][0]);
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_bf16(tO, sdesc_sw128(pb + kk * 32, 16, 1024),
+                                 sdesc_sw128(vb + kk * 2048, KT * 128, 1024), id2,
+                                 (t > 0 || kk > 0) ? 1u : 0u);
+                    mma_commit(&sm.vempty[b]);
+                    mma_commit(&sm.pv_done[b]);
+                    if (t == n_kt - 1) mma_commit(&sm.o_final);
+                }
+            }
+            mma_commit(&sm.mma_done);
+            pf_wait(&sm.mma_done, 0, sm, status, VX_DEV_TIMEOUT_MMA);
+        }
+    } else {
+        // ---- softmax / rescale / epilogue: thread = query row r of the tile
+        const int q4 = warp & 3;
+        const int r = q4 * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+        const int qpos = p0 + t0 + r;
+        const float sc2 = 1.4426950408889634f * 0.0625f;  // log2(e) / sqrt(256)
+        float m_run = -INFINITY, l_run = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < n_kt && ok; j++) {
+            const int b = j & 1;
+            ok = pf_wait(&sm.s_full[b], (j >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+            ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld/st are warp-wide
+            if (!ok) break;
+            tc_fence_after();
+            float s[KT];
+#pragma unroll
+            for (int i = 0; i < KT / 16; i++) tmem_ld16(tS + lane_off + b * KT + 16 * i, s + 16 * i);
+            tc_fence_before();
+            mbar_arrive(&sm.s_empty[b]);
+            const int kbase = j * KT;
+            float mt = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < KT; c++) {
+                s[c] = (kbase + c <= qpos) ? s[c] * sc2 : -INFINITY;
+                mt = fmaxf(mt, s[c]);
+            }
+            float alpha = 1.0f;
+            const bool grow = mt > m_run + RESCALE_LOG2;
+            if (grow) {
+                alpha = (m_run == -INFINITY) ? 0.0f : exp2f(m_run - mt);
+                m_run = mt;
+            }
+            // rescale this warp's O rows when one of its rows raised its max (not on the
+            // first tile of a row, where O holds nothing yet)
+            const bool need = grow && alpha > 0.0f;
+            if (__any_sync(0xffffffffu, need)) {
+                ok = pf_wait(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, sm, status,
+                             VX_DEV_TIMEOUT_MMA);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int i = 0; i < HDP / 16; i++) {
+                    float o[16];
+                    tmem_ld16(tO + lane_off + 16 * i, o);
+#pragma unroll
+                    for (int e = 0; e < 16; e++) o[e] *= alpha;
+                    tmem_st16(tO + lane_off + 16 * i, o);
+                }
+                tmem_st_wait();
+                tc_fence_before();
+            }
+            if (j >= 2) {  // P buffer b is free once P V of tile j-2 is done
+                ok = pf_wait(&sm.pv_done[b], ((j >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+            }
+            float lsum = 0.0f;
+            uint8_t *prow = sm.p[b] + r * 128;
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                uint32_t w4[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float pa = exp2f(s[u * 8 + 2 * e] - m_run);
+                    const float pb = exp2f(s[u * 8 + 2 * e + 1] - m_run);
+                    lsum += pa + pb;
+                    w4[e] = (uint32_t)f32_to_bf16(pa) | ((uint32_t)f32_to_bf16(pb) << 16);
+                }
+                *reinterpret_cast<uint4 *>(prow + (((u ^ (r & 7)) & 7) << 4)) =
+                    make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+            l_run = fmaf(l_run, alpha, lsum);
+            fence_proxy_async();
+            mbar_arrive(&sm.p_full[b]);
+        }
+        if (ok) ok = pf_wait(&sm.o_final, 0, sm, status, VX_DEV_TIMEOUT_MMA);
+        ok = __all_sync(0xffffffffu, ok);
+        if (ok) {
+            tc_fence_after();
+            const int t = t0 + r;
+            const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+            const size_t base = ((size_t)t * nq + h) * HDP;
+#pragma unroll 1
+            for (int i = 0; i < HDP / 16; i++) {
+                float o[16];
+                tmem_ld16(tO + lane_off + 16 * i, o);
+                if (t < T) {
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        const float g = act_ld<ACT_BF16>(gate, base + 16 * i + e);
+                        act_st<OUT_BF16>(out, base + 16 * i + e,
+                                         o[e] * inv * (1.0f / (1.0f + expf(-g))));
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+template <bool A, bool O>
+int launch_attn(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
+                const void *gate, void *out, int T, int p0, int nq, int nkv, int cap,
+                cudaStream_t st, char *err, size_t errlen) {
+    static bool attr = false;
+    const size_t smem = sizeof(PfSmem) + 1024;
+    if (!attr) {
+        VX_CK(cudaFuncSetAttribute(prefill_attn_tc<A, O>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr = true;
+    }
+    const int n_qt = (T + QT - 1) / QT;
+    prefill_attn_tc<A, O><<<n_qt * nq, PF_THREADS, smem, st>>>(mq, mk, mv, gate, out, T, p0, nq,
+                                                                 nkv, cap, dev_status());
+    VX_CK(cudaGetLastError());
+    return 0;
+}
+
+}  // namespace
+}  // namespace vx27
+
+using namespace vx27;
+
+extern "C" size_t vx27_gqa_prefill_workspace_size(int T, int nq, int hd) {
+    if (T <= 0 || nq <= 0 || hd <= 0) return 0;
+    // normalised, rotated bf16 q [nq][T][hd] plus the TMA boxes' overhang of one tile
+    return ((size_t)nq * T + QT) * hd * sizeof(uint16_t);
+}
+
+extern "C" int vx27_gqa_prefill(const void *q_in, const void *k_in, const void *v_in,
+                                const void *gate, const float *q_norm_w, const float *k_norm_w,
+                                const float *rope_table, int rope_table_len, int p0,
+                                void *k_cache, void *v_cache, int cap, void *out,
+                                void *workspace, size_t workspace_bytes, int T, int nq, int nkv,
+                                int hd, int rope_dim, float eps, int flags, void *stream,
+                                char *err, size_t errlen) {
+    const char *fn = "vx27_gqa_prefill";
+    if (hd != HDP) return fail(err, errlen, "%s: hd=%d unsupported (256 only)", fn, hd);
+    if (T <= 0 || nq <= 0 || nkv <= 0 || nq % nkv || nq * ((T + QT - 1) / QT) > (1 << 30))
+        return fail(err, errlen, "%s: bad shape T=%d nq=%d nkv=%d", fn, T, nq, nkv);
+    if (p0 < 0 || p0 + T > cap)
+        return fail(err, errlen, "%s: positions [%d, %d) exceed the cache capacity %d", fn, p0,
+                    p0 + T, cap);
+    if (rope_dim < 0 || rope_dim > hd || (rope_dim & 1) || p0 + T > rope_table_len)
+        return fail(err, errlen, "%s: rope_dim=%d / table of %d positions", fn, rope_dim,
+                    rope_table_len);
+    if (!q_in || !k_in || !v_in || !gate || !q_norm_w || !k_norm_w || !k_cache || !v_cache ||
+        !out || !workspace || (rope_dim && !rope_table))
+        return fail(err, errlen, "%s: null pointer argument", fn);
+    if (workspace_bytes < vx27_gqa_prefill_workspace_size(T, nq, hd))
+        return fail(err, errlen, "%s: workspace of %zu bytes, need %zu", fn, workspace_bytes,
+                    vx27_gqa_prefill_workspace_size(T, nq, hd));
+    cudaStream_t st = (cudaStream_t)stream;
+    uint16_t *qn = (uint16_t *)workspace;
+    const bool a = flags & VX27_F_ACT_BF16, one = flags & VX27_F_NORM_1P;
+    const dim3 pg(nq + nkv, T);
+#define VX_P(A_, O_)                                                                         \
+    prefill_prep_k<A_, O_><<<pg, HDP, 0, st>>>(q_in, k_in, v_in, q_norm_w, k_norm_w,          \
+                                               rope_table, rope_table_len, p0, qn,            \
+                                               (uint16_t *)k_cache, (uint16_t *)v_cache, cap, \
+                                               T, nq, nkv, rope_dim, eps, dev_status())
+    if (a && one) VX_P(true, true);
+    else if (a) VX_P(true, false);
+    else if (one) VX_P(false, true);
+    else VX_P(false, false);
+#undef VX_P
+    VX_CK(cudaGetLastError());
+    // the last key tile may reach past p0 + T: give those slots finite values
+    const int tail_end = min(cap, ((p0 + T + KT - 1) / KT) * KT);
+    if (tail_end > p0 + T) {
+        zero_slots_k<<<dim3(4, nkv), 256, 0, st>>>((uint16_t *)k_cache, (uint16_t *)v_cache,
+                                                    cap, nkv, p0 + T, tail_end);
+        VX_CK(cudaGetLastError());
+    }
+    CUtensorMap mq, mk, mv;
+    if (make_tmap_bf16_2d(&mq, qn, (uint64_t)nq * T, HDP, HDP * 2, 64, QT, err, errlen) ||
+        make_tmap_bf16_2d(&mk, k_cache, (uint64_t)nkv * cap, HDP, HDP * 2, 64, KT, err, errlen) ||
+        make_tmap_bf16_2d(&mv, v_cache, (uint64_t)nkv * cap, HDP, HDP * 2, 64, KT, err, errlen))
+        return -1;
+    const bool o = flags & VX27_F_OUT_BF16;
+    if (a && o) return launch_attn<true, true>(mq, mk, mv, gate, out, T, p0, nq, nkv, cap, st, err, errlen);
+    if (a) return launch_attn<true, false>(mq, mk, mv, gate, out, T, p0, nq, nkv, cap, st, err, errlen);
+    if (o) return launch_attn<false, true>(mq, mk, mv, gate, out, T, p0, nq, nkv, cap, st, err, errlen);
+    return launch_attn<false, false>(mq, mk, mv, gate, out, T, p0, nq, nkv, cap, st, err, errlen);
+}

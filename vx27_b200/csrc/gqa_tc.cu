@@ -260,6 +260,7 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
         auto correction = [&](int t) {  // folds O(t) in with alpha_t = al_prev
             const int bb = t & 1;
             ok = ok && tc_wait(&sm.o_full[bb], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+            ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is warp-wide
             if (!ok) return;
             tc_fence_after();
             float oa[16], ob[16];
@@ -278,6 +279,7 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
         for (int i = 0; i < n_tiles && ok; i++) {
             const int bb = i & 1;
             ok = tc_wait(&sm.s_full[bb], (i >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+            ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
             float v[16];

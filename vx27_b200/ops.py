@@ -229,6 +229,28 @@ def gqa_combine(parts, n_parts: int, gate, out, part_stride: int = 0, stream=Non
     check(rc, e)
 
 
+def gqa_prefill(q_in, k_in, v_in, gate, q_norm_w, k_norm_w, rope, k_cache, v_cache, out,
+                workspace=None, p0: int = 0, eps: float = 1e-6, norm_one_plus: bool = False,
+                stream=None):
+    """Causal gated GQA prefill of T tokens (vx27_gqa_prefill); k_cache/v_cache [nkv][cap][hd]."""
+    import torch
+    T, nq, hd = q_in.shape
+    nkv = k_in.shape[1]
+    cap = k_cache.shape[1]
+    need = load().vx27_gqa_prefill_workspace_size(T, nq, hd)
+    if workspace is None:
+        workspace = torch.empty(need // 2 + 1, dtype=torch.int16, device=q_in.device)
+    flags = (F_ACT_BF16 if _is_bf16(q_in) else 0) | (F_OUT_BF16 if _is_bf16(out) else 0) | \
+        (F_NORM_1P if norm_one_plus else 0)
+    e = errbuf()
+    rc = load().vx27_gqa_prefill(_t(q_in), _t(k_in), _t(v_in), _t(gate), _t(q_norm_w),
+                                 _t(k_norm_w), _t(rope), rope.shape[0], p0, _t(k_cache),
+                                 _t(v_cache), cap, _t(out), _t(workspace),
+                                 workspace.numel() * workspace.element_size(), T, nq, nkv, hd,
+                                 rope.shape[1], eps, flags, _stream(stream), e, 512)
+    check(rc, e)
+
+
 def fill_normal(t, seed: int, stream_id: int, mean: float = 0.0, std: float = 1.0,
                 offset: int = 0, stream=None) -> None:
     """t[e] = element offset+e of the seeded normal stream (seed, stream_id)."""
