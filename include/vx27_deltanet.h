@@ -73,6 +73,25 @@ int vx27_deltanet_decode_batch(float *S, float *conv_ring, const void *qkv, cons
                                int nv, int hd, int flags, void *stream, char *err,
                                size_t errlen);
 
+/*
+ * Chunked gated delta rule over T prompt tokens (config 4): the token-by-token recurrence
+ * of vx27_deltanet_step_exact (l2-normalised q and k, q / sqrt(hd), gates of
+ * vx27_deltanet_gate_params) evaluated 64 tokens at a time in the WY/UT form, within
+ * 1e-3 of the recurrent reference over 32768 tokens.
+ *   q, k [T][nqk][hd], v [T][nv][hd], a, b [T][nv] (act dtype; VX27_F_GATES_F64: a/b are
+ *   host-computed beta/g_log as double); A_log, dt_bias [nv] fp32
+ *   S [nv][hd][hd] fp32: initial state in, final state out
+ *   o [T][nv][hd] (fp32, or bf16 with VX27_F_OUT_BF16)
+ *   workspace: vx27_deltanet_prefill_workspace_size(T, nqk, nv, hd) bytes
+ * hd must be 128; V head vh reads QK head vh*nqk/nv.
+ */
+size_t vx27_deltanet_prefill_workspace_size(int T, int nqk, int nv, int hd);
+int vx27_deltanet_prefill_chunked(const void *q, const void *k, const void *v, const void *a,
+                                  const void *b, const float *A_log, const float *dt_bias,
+                                  float *S, void *o, void *workspace, size_t workspace_bytes,
+                                  int T, int nqk, int nv, int hd, int flags, void *stream,
+                                  char *err, size_t errlen);
+
 /* Conv history conversion between the reference layout state[B][C][3] (host, oldest
  * first) and the device ring [B][4][C] at positions pos[B] (host array). */
 int vx27_deltanet_conv_import(float *conv_ring, const float *state, const int *pos, int B,

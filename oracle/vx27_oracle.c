@@ -487,6 +487,16 @@ void orc_gqa_combine(const float *o_parts, const float *ml_parts, int n_parts,
     }
 }
 
+/* gate_params over a [T][nv] grid of logits (fp32 values); beta/g_log [T][nv] */
+void orc_gate_params_grid(const float *a, const float *b, const float *A_log,
+                          const float *dt_bias, int T, int nv, double *beta, double *g_log) {
+    for (long i = 0; i < (long)T * nv; i++) {
+        const int vh = (int)(i % nv);
+        g_gate((double)a[i], (double)A_log[vh], (double)b[i], (double)dt_bias[vh], beta + i,
+               g_log + i);
+    }
+}
+
 /* ------------------------------------------------------------- prefill refs */
 void orc_deltanet_recurrent(float *S, const void *q, const void *k, const void *v,
                             long ld, const double *beta, const double *g_log,

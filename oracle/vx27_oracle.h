@@ -111,6 +111,10 @@ void orc_deltanet_recurrent(float *S, const void *q, const void *k, const void *
                             long ld, const double *beta, const double *g_log,
                             float *o, int T, int hd, int flags);
 
+/* gate_params (the selected implementation) over a [T][nv] grid of fp32 logits. */
+void orc_gate_params_grid(const float *a, const float *b, const float *A_log,
+                          const float *dt_bias, int T, int nv, double *beta, double *g_log);
+
 /* Causal gated GQA prefill reference for selected query rows.
  * q,k,v [T][heads][hd] raw (act dtype); rows[n_rows]; out [n_rows][nq][hd] fp32. */
 void orc_gqa_prefill_rows(const void *q, const void *k, const void *v, const void *gate,

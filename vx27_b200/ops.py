@@ -157,6 +157,26 @@ def deltanet_decode_batch(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, 
     check(rc, e)
 
 
+def deltanet_prefill_chunked(q, k, v, a, b, A_log, dt_bias, S, o, workspace=None,
+                             gates_f64: bool = False, stream=None) -> None:
+    """Chunked gated delta rule over T tokens (vx27_deltanet_prefill_chunked).
+    q, k [T][nqk][128], v [T][nv][128], a, b [T][nv], S [nv][128][128] in/out."""
+    import torch
+    T, nqk, hd = q.shape
+    nv = v.shape[1]
+    need = load().vx27_deltanet_prefill_workspace_size(T, nqk, nv, hd)
+    if workspace is None:
+        workspace = torch.empty(need // 4 + 1, dtype=torch.float32, device=q.device)
+    flags = (F_ACT_BF16 if _is_bf16(q) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0) | \
+        (F_GATES_F64 if gates_f64 else 0)
+    e = errbuf()
+    rc = load().vx27_deltanet_prefill_chunked(_t(q), _t(k), _t(v), _t(a), _t(b), _t(A_log),
+                                              _t(dt_bias), _t(S), _t(o), _t(workspace),
+                                              workspace.numel() * workspace.element_size(), T,
+                                              nqk, nv, hd, flags, _stream(stream), e, 512)
+    check(rc, e)
+
+
 def rope_table(n_pos: int, rope_dim: int = 64, theta: float = 1e7, yarn: float = 1.0,
                device=None):
     """Device RoPE table [n_pos][rope_dim] (cos | sin), values from vx27_rope_cos_sin."""
