@@ -44,6 +44,16 @@ def peaks() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
 
 
+def tensor_peak() -> tuple[float, str]:
+    """Dense bf16 tensor peak for a kernel timed alone (the burst figure)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops)"
+    except Exception:
+        return 1590.0, "fallback 1.59 PFLOP/s"
+
+
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
     """nvidia-smi samples every 200 ms while the timed region runs."""
@@ -298,6 +308,118 @@ def run_layer(args) -> dict:
             "peak_source": peak_src}
 
 
+# ------------------------------------------------- config 4 (prefill)
+def prefill_flops(T: int) -> tuple[float, float]:
+    """Algorithmic FLOPs of one config-4 layer of each kind.
+    GQA: causal QK^T and PV over T(T+1)/2 (query, key) pairs, 24 heads, hd 256.
+    DeltaNet (chunk 64, 16 heads, 128x128 state), per chunk and head: K K^T and Q K^T
+    (2*64*64*128 each), T V and T K (2*64*64*128 each), U = W_v - W_k S and the state
+    update (2*64*128*128 each), Q S (2*64*128*128) and the intra-chunk P U (2*64*64*128)."""
+    pairs = T * (T + 1) / 2
+    gqa = 2 * 2 * pairs * 24 * 256
+    per_chunk = 5 * (2 * 64 * 64 * 128) + 3 * (2 * 64 * 128 * 128)
+    dn = per_chunk * 16 * ((T + 63) // 64)
+    return gqa, dn
+
+
+def run_prefill(args) -> dict:
+    """Config 4: a 32768-token prompt, batch 1, through one DeltaNet layer (chunked gated
+    delta rule, 16 heads) and one gated GQA layer (causal 24Q/4KV hd256 on the tensor
+    cores). value = prompt tokens/s through one layer of each kind."""
+    import torch
+    from vx27_b200 import ops
+    torch.cuda.set_device(0)
+    T = args.prefill_T
+    bf = torch.bfloat16
+    hbm, hbm_src = peaks()
+    tc_peak, tc_src = tensor_peak()
+    # DeltaNet layer inputs (gates as in config 0), seed 4
+    nqk = nv = 16
+    q = torch.empty(T, nqk, 128, dtype=bf, device="cuda")
+    k = torch.empty_like(q)
+    v = torch.empty(T, nv, 128, dtype=bf, device="cuda")
+    a = torch.empty(T, nv, dtype=bf, device="cuda")
+    b = torch.empty_like(a)
+    A = torch.empty(nv, device="cuda")
+    dt = torch.empty(nv, device="cuda")
+    S = torch.zeros(nv, 128, 128, device="cuda")
+    o = torch.empty(T, nv, 128, dtype=bf, device="cuda")
+    for n, t in enumerate((q, k, v, a, b)):
+        ops.fill_normal(t, 4, n + 1)
+    ops.fill_normal(dt, 4, 7, 0.0, 0.1)
+    ops.fill_uniform(A, 4, 6, 1.0, 16.0)
+    A.log_()
+    ws_dn = torch.empty(ops.load().vx27_deltanet_prefill_workspace_size(T, nqk, nv, 128) // 4 + 1,
+                        device="cuda")
+    run_dn = lambda: ops.deltanet_prefill_chunked(q, k, v, a, b, A, dt, S, o, ws_dn)
+    # GQA layer inputs
+    nq, nkv, hd = 24, 4, 256
+    gq = torch.empty(T, nq, hd, dtype=bf, device="cuda")
+    gk = torch.empty(T, nkv, hd, dtype=bf, device="cuda")
+    gv = torch.empty_like(gk)
+    gate = torch.empty_like(gq)
+    qw = torch.empty(hd, device="cuda")
+    kw = torch.empty(hd, device="cuda")
+    for n, t in enumerate((gq, gk, gv, gate)):
+        ops.fill_normal(t, 4, 10 + n)
+    ops.fill_normal(qw, 4, 14, 1.0, 0.02)
+    ops.fill_normal(kw, 4, 15, 1.0, 0.02)
+    kc = torch.empty(nkv, T, hd, dtype=bf, device="cuda")
+    vc = torch.empty_like(kc)
+    out = torch.empty(T, nq, hd, dtype=bf, device="cuda")
+    rope = ops.rope_table(T)
+    ws_g = torch.empty(ops.load().vx27_gqa_prefill_workspace_size(T, nq, hd) // 2 + 1,
+                       dtype=torch.int16, device="cuda")
+    run_gqa = lambda: ops.gqa_prefill(gq, gk, gv, gate, qw, kw, rope, kc, vc, out, ws_g)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for e0, e1 in evs:
+            e0.record()
+            fn()
+            e1.record()
+        torch.cuda.synchronize()
+        return [e0.elapsed_time(e1) for e0, e1 in evs]
+
+    with ClockSampler(0) as clk:
+        t_dn = timed(run_dn)
+        t_gqa = timed(run_gqa)
+    if ops.device_status() != 0:
+        raise RuntimeError("device status flag set during the prefill run")
+    ms_dn, ms_gqa = statistics.mean(t_dn), statistics.mean(t_gqa)
+    f_gqa, f_dn = prefill_flops(T)
+    # HBM bytes the DeltaNet layer must move: q,k,v,a,b in (bf16), o out (bf16), S in/out
+    dn_bytes = T * (2 * nqk + nv) * 128 * 2 + T * nv * 2 * 2 + T * nv * 128 * 2 + \
+        2 * nv * 128 * 128 * 4
+    tflops = f_gqa / (ms_gqa * 1e-3) / 1e12
+    return {
+        "metric": "prompt tokens/s through one DeltaNet + one gated GQA layer (config 4)",
+        "value": round(T / ((ms_dn + ms_gqa) * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_dn + ms_gqa, 4), "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic (seed 4)",
+        "config": {"workload": f"config 4: prefill of a {T}-token prompt, batch 1",
+                   "l2": "inputs and workspaces larger than L2"},
+        "gqa_prefill": {"ms": round(ms_gqa, 4), "tflops": round(tflops, 1),
+                        "algorithmic_flops": f_gqa,
+                        "roofline": {"bound": "tensor", "achieved": round(tflops, 1),
+                                     "peak": tc_peak, "unit": "TFLOP/s",
+                                     "frac": round(tflops / tc_peak, 4),
+                                     "peak_source": tc_src}},
+        "deltanet_prefill": {"ms": round(ms_dn, 4), "algorithmic_flops": f_dn,
+                             "tflops": round(f_dn / (ms_dn * 1e-3) / 1e12, 2),
+                             "algorithmic_bytes": dn_bytes,
+                             "hbm_GBps": round(dn_bytes / (ms_dn * 1e-3) / 1e9, 1),
+                             "hbm_frac": round(dn_bytes / (ms_dn * 1e-3) / 1e9 / hbm, 4),
+                             "hbm_peak_source": hbm_src},
+        "clocks": clk.summary(),
+    }
+
+
 # ------------------------------------------------- config 3 (long context)
 def run_longctx(args, rank: int, world: int, local: int) -> dict | None:
     """Config 3: 16 gated GQA layers at context 262144, query at 262143.
@@ -494,13 +616,14 @@ def main() -> None:
     ap.add_argument("--ref-seqs", type=int, default=4)
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config2", "config3a", "config3b", "dn_layer",
-                                           "gqa_layer"], default="config2",
+    ap.add_argument("--workload", choices=["config2", "config3a", "config3b", "config4",
+                                           "dn_layer", "gqa_layer"], default="config2",
                     help="config2 (the metric); config3a/3b long context; single-layer "
                          "workloads are for kernel rooflines and profiling")
     ap.add_argument("--ctx3", type=int, default=262144)
     ap.add_argument("--seqs3", type=int, default=16)
     ap.add_argument("--hbm-budget-gb", type=float, default=150.0)
+    ap.add_argument("--prefill-T", type=int, default=32768, help="config4 prompt length")
     ap.add_argument("--graph", action="store_true",
                     help="config3: replay each step as one CUDA graph")
     args = ap.parse_args()
@@ -511,6 +634,9 @@ def main() -> None:
 
     if args.workload in ("dn_layer", "gqa_layer"):
         print(json.dumps(run_layer(args)), flush=True)
+        return
+    if args.workload == "config4":
+        print(json.dumps(run_prefill(args)), flush=True)
         return
 
     if args.impl == "reference":

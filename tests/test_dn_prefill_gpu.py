@@ -16,13 +16,14 @@ HD = 128
 TOL = 1e-3
 
 
-def make(orc, seed, T, nqk, nv, s_std=0.0):
+def make(orc, seed, T, nqk, nv, s_std=0.0, a_range=(1.0, 16.0)):
+    """Config-0 gates by default: A_log = log U[1,16]; a smaller range gives slow decay."""
     g = lambda n, s, m=0.0, sd=1.0, b=True: orc.normal(n, seed, s, m, sd, bf16=b)
     S0 = (orc.normal(nv * HD * HD, seed, 9, 0.0, s_std) if s_std else
           np.zeros(nv * HD * HD, np.float32))
     return dict(q=g(T * nqk * HD, 1), k=g(T * nqk * HD, 2), v=g(T * nv * HD, 3),
                 a=g(T * nv, 4), b=g(T * nv, 5),
-                A_log=np.log(orc.uniform(nv, seed, 6, 1.0, 16.0)).astype(np.float32),
+                A_log=np.log(orc.uniform(nv, seed, 6, *a_range)).astype(np.float32),
                 dt=g(nv, 7, 0.0, 0.1, False), S0=S0)
 
 
@@ -85,6 +86,33 @@ def test_grouped_heads(cuda, orc):
     o_ref, S_ref = recurrent(orc, x, T, nqk, nv)
     o, S = gpu(x, T, nqk, nv)
     assert np.abs(o - o_ref).max() < TOL and np.abs(S - S_ref).max() < TOL
+
+
+def test_slow_decay_long_memory(cuda, orc):
+    """Decay rates 1e-3..5e-2 of config 0's: the state carries information across hundreds
+    of chunks, so errors in the chunk transfer would accumulate."""
+    T, nqk, nv = 4000, 2, 4
+    x = make(orc, 55, T, nqk, nv, s_std=0.05, a_range=(0.001, 0.05))
+    o_ref, S_ref = recurrent(orc, x, T, nqk, nv)
+    o, S = gpu(x, T, nqk, nv)
+    eo, es = np.abs(o - o_ref).max(), np.abs(S - S_ref).max()
+    print(f"slow decay: max|o-ref| {eo:.3e}, max|S-ref| {es:.3e}, max|S| {np.abs(S_ref).max():.3f}")
+    assert eo < TOL and es < TOL
+
+
+def test_bf16_output_and_f32_rejected(cuda, orc):
+    T, nqk, nv = 130, 2, 2
+    x = make(orc, 8, T, nqk, nv, s_std=0.05)
+    o_ref, S_ref = recurrent(orc, x, T, nqk, nv)
+    o, S = gpu(x, T, nqk, nv, out_bf16=True)
+    assert np.abs(o - o_ref).max() < 1e-2 and np.abs(S - S_ref).max() < TOL
+    q = dev(x["q"], True).view(T, nqk, HD).float()
+    with pytest.raises(ops.Vx27Error, match="bf16"):
+        ops.deltanet_prefill_chunked(q, q, dev(x["v"], True).view(T, nv, HD).float(),
+                                     dev(x["a"], True).view(T, nv), dev(x["b"], True).view(T, nv),
+                                     dev(x["A_log"]), dev(x["dt"]),
+                                     dev(x["S0"]).view(nv, HD, HD),
+                                     torch.empty(T, nv, HD, device="cuda"))
 
 
 def test_config4_deltanet_32768(cuda, orc):

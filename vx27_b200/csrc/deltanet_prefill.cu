@@ -1,54 +1,104 @@
-// K3: chunked gated delta rule for prefill (config 4), chunks of 64 tokens.
+// K3: chunked gated delta rule prefill on the tensor cores (config 4, DeltaNet path).
 //
-// Token-by-token, per V head (src/vx27_deltanet.c:71-102):
-//   S <- g_t S;  u_t = beta_t (v_t - S^T k_t);  S <- S + k_t u_t^T;  o_t = S^T q_t
-// with q, k l2-normalised and q scaled by 1/sqrt(128). Within a chunk starting from S0,
-// with gamma_t the product of the chunk's decays up to t (G_t = log gamma_t, summed in
-// double):
-//   (I + L) U = diag(beta) (V - diag(gamma) K S0),  L_ts = beta_t (gamma_t/gamma_s) k_t.k_s, s < t
-//   so U = Wv - Wk S0 with T = (I + L)^-1 diag(beta), Wv = T V, Wk = T diag(gamma) K;
-//   O   = diag(gamma) Q S0 + Pm U,   Pm_ts = (gamma_t/gamma_s) q_t.k_s for s <= t
-//   S_C = gamma_C S0 + K^T diag(gamma_C/gamma) U
+// Per V head, tokens are taken 64 at a time (chunk C = 64). With k^ = l2norm(k), q^ =
+// l2norm(q)/sqrt(128), per-token gates beta_t, g_t and G_t = sum_{s<=t} g_s inside the chunk,
+// the token-by-token recurrence of src/vx27_deltanet.c:71-102 over one chunk is exactly
+//   X   = (I + L)^-1 diag(beta),   L_ts = beta_t e^{G_t-G_s} k^_t.k^_s  (s < t)
+//   U   = X V - X diag(e^G) K^ S0                       (= Wv - Wk S0)
+//   O   = diag(e^G) Q^ S0 + Pm U,  Pm_ts = e^{G_t-G_s} q^_t.k^_s  (s <= t)
+//   S_C = e^{G_C} S0 + Kr^T U,     Kr_t = e^{G_C-G_t} k^_t
+// with S0 the state at the chunk start. Every product runs on tcgen05 (kind::f16, bf16
+// operands, fp32 accumulation in TMEM). Raw q/k/v are bf16 already, so the l2 norms, gates
+// and decays are folded into per-row / per-column scales and those operands enter exactly;
+// fp32 intermediates (X, Wk, Kr, Pm, U, S) enter as hi + lo bf16 pairs, either as two
+// passes or as stacked rows / columns of one MMA whose parts are summed in the epilogue.
+//
 // Three kernels:
-//   dn_chunk_prep   one CTA per (V head, chunk), all chunks in parallel: norms, gates,
-//                   K K^T and Q K^T, the unit lower-triangular solve for T, Wv, Wk
-//   dn_chunk_scan   one CTA per (V head, 16 state columns): the only sequential part,
-//                   U_c = Wv - Wk S_c and S_{c+1} = gamma_C S_c + Kr^T U_c over the chunks
-//                   (state columns are independent, so a head's state is split over 8 CTAs)
-//   dn_chunk_out    one CTA per (V head, chunk): O = Qg S_c + Pm U
-// All arithmetic fp32 (fp64 for the decay sums), so the result stays within 1e-3 of the
-// token-by-token reference over 32768 tokens.
+//   dn_prep_tc   one CTA per (chunk, V head), all chunks in parallel: gates, norms, the
+//                Gram products [K;Q] K^T, the 64x64 triangular solve for X (one column
+//                per thread), Wv^T = V^T X^T and Wk^T = K^T (X diag(e^G rk))^T
+//   dn_scan_tc   one CTA per (CB state columns, V head): the sequential part,
+//                U = Wv - Wk S and dS = Kr^T U per chunk, the state in fp32 registers
+//   dn_out_tc    one CTA per (chunk, V head): O^T = diag-scaled S0^T Q^T + U^T Pm^T
+// Intermediate tiles travel through the workspace as byte images of their swizzled
+// shared-memory layout, moved by 1-D bulk copies (cp.async.bulk) in both directions.
 #include <math.h>
 #include "common.cuh"
+#include "tc.cuh"
 #include "../../include/vx27_deltanet.h"
 
 namespace vx27 {
 namespace {
 
-constexpr int CK = 64;    // chunk
-constexpr int D = 128;    // head dim
-constexpr int CB = 16;    // state columns per scan CTA
-constexpr int LDS = D + 1;
+constexpr int CK = 64;   // chunk
+constexpr int D = 128;   // head dim
 
-struct Ws {  // workspace views; blk = vh * n_chunks + chunk
-    float *Wk, *Wv, *Qg, *Kr, *Pm, *U, *Sc, *g63;
-};
-__host__ __device__ inline size_t ws_floats_per_blk() {
-    return 4 * (size_t)CK * D + (size_t)CK * CK + (size_t)CK * D + (size_t)D * D + 4;
+// Byte offset of element (r, c) in a 128-byte-swizzled tile whose 64-element column
+// blocks hold R rows each (K-major operand: r = M/N index, c = K index; MN-major operand:
+// r = K index, c = M/N index).
+__device__ __forceinline__ uint32_t swz(int r, int c, int R) {
+    return (uint32_t)((c >> 6) * (R * 128) + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) +
+                      ((c & 7) << 1));
 }
-__host__ __device__ inline Ws ws_views(float *base, size_t nblk) {
-    Ws w;
-    w.Wk = base;
-    w.Wv = w.Wk + nblk * CK * D;
-    w.Qg = w.Wv + nblk * CK * D;
-    w.Kr = w.Qg + nblk * CK * D;
-    w.Pm = w.Kr + nblk * CK * D;
-    w.U = w.Pm + nblk * CK * CK;
-    w.Sc = w.U + nblk * CK * D;
-    w.g63 = w.Sc + nblk * D * D;
+__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
+    return (uint8_t *)(((uintptr_t)p + 1023) & ~(uintptr_t)1023);
+}
+__device__ __forceinline__ void split_bf16(float x, uint16_t &h, uint16_t &l) {
+    h = f32_to_bf16(x);
+    l = f32_to_bf16(x - bf16_to_f32(h));
+}
+__device__ __forceinline__ void st16(uint8_t *base, uint32_t off, uint16_t v) {
+    *reinterpret_cast<uint16_t *>(base + off) = v;
+}
+
+// ---- 1-D bulk copies shared -> global ------------------------------------------------------
+__device__ __forceinline__ void bulk_s2g(void *gdst, const void *ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 ::"l"(gdst), "r"(smem_u32(ssrc)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait0() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// ---- workspace: per (V head, chunk) block, blk = vh * n_chunks + chunk --------------------
+constexpr size_t SZ_WKA = 32768;  // [Wk_hi; Wk_lo] rows t, K-major over d (scan MMA1 A)
+constexpr size_t SZ_KR = 16384;   // Kr^T hi or lo: MN-major image rows t, cols d (scan MMA2 A)
+constexpr size_t SZ_QB = 16384;   // raw Q rows t, K-major over d (out MMA1 B)
+constexpr size_t SZ_PM = 16384;   // [Pm_hi; Pm_lo] rows t, K-major over s (out MMA2 B)
+constexpr size_t SZ_SC = 32768;   // S0^T hi or lo: rows v, K-major over d (out MMA1 A)
+constexpr size_t SZ_U = 16384;    // U^T hi or lo: rows v, K-major over t (out MMA2 A)
+constexpr size_t SZ_WV = 32768;   // Wv [t][d] fp32
+constexpr size_t SZ_SCAL = 512;   // [0] = e^{G_C}; [64 + t] = e^{G_t} rq_t / sqrt(128)
+constexpr size_t BLK_BYTES =
+    SZ_WKA + 2 * SZ_KR + SZ_QB + SZ_PM + 2 * SZ_SC + 2 * SZ_U + SZ_WV + SZ_SCAL;
+
+struct Wsp {
+    uint8_t *WkA, *KrH, *KrL, *QB, *PmB, *ScH, *ScL, *UH, *UL;
+    float *Wv, *scal;
+};
+inline Wsp wsp_views(uint8_t *p, size_t nblk) {
+    Wsp w;
+    w.WkA = p; p += nblk * SZ_WKA;
+    w.KrH = p; p += nblk * SZ_KR;
+    w.KrL = p; p += nblk * SZ_KR;
+    w.QB = p; p += nblk * SZ_QB;
+    w.PmB = p; p += nblk * SZ_PM;
+    w.ScH = p; p += nblk * SZ_SC;
+    w.ScL = p; p += nblk * SZ_SC;
+    w.UH = p; p += nblk * SZ_U;
+    w.UL = p; p += nblk * SZ_U;
+    w.Wv = reinterpret_cast<float *>(p); p += nblk * SZ_WV;
+    w.scal = reinterpret_cast<float *>(p);
     return w;
 }
 
+// src/vx27_deltanet.c:65-69 in double, with the three-regime softplus of :58-63
 __device__ __forceinline__ void gates_dev(double a, double A_log, double b, double dt,
                                           double *beta, double *g_log) {
     *beta = 1.0 / (1.0 + exp(-b));
@@ -57,241 +107,576 @@ __device__ __forceinline__ void gates_dev(double a, double A_log, double b, doub
     *g_log = -exp(A_log) * sp;
 }
 
-// ---- phase 1: per-chunk preparation ----------------------------------------------------
-template <bool ACT_BF16, bool GATES_F64>
-__global__ void __launch_bounds__(256)
-dn_chunk_prep(const void *__restrict__ q, const void *__restrict__ k, const void *__restrict__ v,
-              const void *__restrict__ ga, const void *__restrict__ gb,
-              const float *__restrict__ A_log, const float *__restrict__ dt_bias, Ws ws, int T,
-              int nqk, int nv, int n_chunks) {
-    extern __shared__ float psm[];
-    float *Kh = psm;                 // [CK][LDS] normalised k
-    float *Qh = Kh + CK * LDS;       // [CK][LDS] normalised, scaled q
-    float *Vs = Qh + CK * LDS;       // [CK][LDS] v
-    float *Lm = Vs + CK * LDS;       // [CK][CK+1] L, then T
-    float *Xs = Lm + CK * (CK + 1);  // [CK][CK+1] T
-    double *G = reinterpret_cast<double *>(Xs + CK * (CK + 1));  // [CK]
-    float *beta = reinterpret_cast<float *>(G + CK);             // [CK]
-    float *gam = beta + CK;                                      // [CK] exp(G)
-    const int vh = blockIdx.x, c = blockIdx.y, tid = threadIdx.x, warp = tid >> 5,
+// ---- phase 1: per-chunk preparation ------------------------------------------------------
+// shared memory (after 1024-byte alignment)
+constexpr uint32_t P_AKQ = 0;        // [K;Q] raw, K-major 128 rows x 128; later [Wk_hi;Wk_lo]
+constexpr uint32_t P_VT = 32768;     // V raw, rows s x cols d (MN-major A of Wv^T)
+constexpr uint32_t P_XV = 49152;     // [X_hi; X_lo] rows t, K-major over s (B of Wv^T)
+constexpr uint32_t P_XK = 65536;     // [(X diag(e^G rk))_hi; _lo]
+constexpr uint32_t P_L = 81920;      // L fp32 [64][68]
+constexpr int LST = 68;
+constexpr uint32_t P_G = P_L + CK * LST * 4;  // double G[64]
+constexpr uint32_t P_F = P_G + CK * 8;        // float beta, rk, rq, xs, er [64] each
+constexpr uint32_t P_BAR = P_F + 5 * CK * 4;
+constexpr uint32_t PREP_SMEM = P_BAR + 16 + 1024;
+
+template <bool GATES_F64>
+__global__ void __launch_bounds__(128, 2)
+dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
+           const uint16_t *__restrict__ v, const void *__restrict__ ga,
+           const void *__restrict__ gb, const float *__restrict__ A_log,
+           const float *__restrict__ dt_bias, Wsp ws, int T, int nqk, int nv, int n_chunks,
+           uint32_t *status) {
+    extern __shared__ uint8_t smraw[];
+    uint8_t *sm = align1024(smraw);
+    uint8_t *AKQ = sm + P_AKQ, *VT = sm + P_VT, *XV = sm + P_XV, *XK = sm + P_XK;
+    float *Lf = reinterpret_cast<float *>(sm + P_L);
+    double *G = reinterpret_cast<double *>(sm + P_G);
+    float *beta = reinterpret_cast<float *>(sm + P_F), *rk = beta + CK, *rq = rk + CK,
+          *xs = rq + CK, *er = xs + CK;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + P_BAR);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 1);
+    const int c = blockIdx.x, vh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5,
               lane = tid & 31;
-    const int qk = vh * nqk / nv;
-    const int t0 = c * CK;
+    const int qk = vh * nqk / nv, t0 = c * CK;
     const size_t blk = (size_t)vh * n_chunks + c;
-    // 1. load (tokens past T are identity steps: zero q/k/v, beta = 0, g = 0)
-    for (int e = tid; e < CK * D; e += 256) {
-        const int t = e / D, d = e % D, tt = t0 + t;
-        float qv = 0.f, kv = 0.f, vv = 0.f;
-        if (tt < T) {
-            qv = act_ld<ACT_BF16>(q, ((size_t)tt * nqk + qk) * D + d);
-            kv = act_ld<ACT_BF16>(k, ((size_t)tt * nqk + qk) * D + d);
-            vv = act_ld<ACT_BF16>(v, ((size_t)tt * nv + vh) * D + d);
-        }
-        Qh[t * LDS + d] = qv;
-        Kh[t * LDS + d] = kv;
-        Vs[t * LDS + d] = vv;
+
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_barrier_init();
     }
+    if (warp == 0) {
+        tmem_alloc(tslot, 256);
+        tmem_relinquish();
+    }
+    // 1. raw rows into the swizzled tiles; l2 norms from double sums (src/vx27_deltanet.c:51)
+    for (int i = warp; i < CK; i += 4) {
+        const int tt = t0 + i;
+        uint2 qv = make_uint2(0u, 0u), kv = qv, vv = qv;
+        if (tt < T) {
+            qv = *reinterpret_cast<const uint2 *>(q + ((size_t)tt * nqk + qk) * D + 4 * lane);
+            kv = *reinterpret_cast<const uint2 *>(k + ((size_t)tt * nqk + qk) * D + 4 * lane);
+            vv = *reinterpret_cast<const uint2 *>(v + ((size_t)tt * nv + vh) * D + 4 * lane);
+        }
+        const float k0 = bf16_to_f32(kv.x & 0xffffu), k1 = bf16_to_f32(kv.x >> 16),
+                    k2 = bf16_to_f32(kv.y & 0xffffu), k3 = bf16_to_f32(kv.y >> 16);
+        const float q0 = bf16_to_f32(qv.x & 0xffffu), q1 = bf16_to_f32(qv.x >> 16),
+                    q2 = bf16_to_f32(qv.y & 0xffffu), q3 = bf16_to_f32(qv.y >> 16);
+        double sk = (double)k0 * k0 + (double)k1 * k1 + (double)k2 * k2 + (double)k3 * k3;
+        double sq = (double)q0 * q0 + (double)q1 * q1 + (double)q2 * q2 + (double)q3 * q3;
+        sk = warp_sum_d(sk);
+        sq = warp_sum_d(sq);
+        *reinterpret_cast<uint2 *>(AKQ + swz(i, 4 * lane, 128)) = kv;
+        *reinterpret_cast<uint2 *>(AKQ + swz(CK + i, 4 * lane, 128)) = qv;
+        *reinterpret_cast<uint2 *>(VT + swz(i, 4 * lane, CK)) = vv;
+        if (lane == 0) {
+            rk[i] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)sk, 1e-6f)));
+            rq[i] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)sq, 1e-6f)));
+        }
+    }
+    // 2. gates (tokens past T are identity steps: beta = 0, g = 0)
     if (tid < CK) {
         const int tt = t0 + tid;
         double bt = 0.0, gl = 0.0;
         if (tt < T) {
             const size_t gi = (size_t)tt * nv + vh;
             if constexpr (GATES_F64) {
-                bt = ((const double *)ga)[gi];
-                gl = ((const double *)gb)[gi];
+                bt = static_cast<const double *>(ga)[gi];
+                gl = static_cast<const double *>(gb)[gi];
             } else {
-                gates_dev((double)act_ld<ACT_BF16>(ga, gi), (double)A_log[vh],
-                          (double)act_ld<ACT_BF16>(gb, gi), (double)dt_bias[vh], &bt, &gl);
+                gates_dev((double)act_ld<true>(ga, gi), (double)A_log[vh],
+                          (double)act_ld<true>(gb, gi), (double)dt_bias[vh], &bt, &gl);
             }
         }
         beta[tid] = (float)bt;
         G[tid] = gl;
     }
+    fence_proxy_async();
     __syncthreads();
-    // 2. l2 norms (double sums as src/vx27_deltanet.c:51) and the decay prefix sum
-    for (int row = warp; row < 2 * CK; row += 8) {
-        float *x = row < CK ? Qh + row * LDS : Kh + (row - CK) * LDS;
-        double ss = 0.0;
-        for (int d = lane; d < D; d += 32) ss += (double)x[d] * (double)x[d];
-        ss = warp_sum_d(ss);
-        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, 1e-6f)));
-        for (int d = lane; d < D; d += 32) {
-            float y = __fmul_rn(x[d], r);
-            if (row < CK) y = __fmul_rn(y, __fdiv_rn(1.0f, __fsqrt_rn((float)D)));
-            x[d] = y;
-        }
-    }
     if (tid == 0) {
         double acc = 0.0;
-        for (int t = 0; t < CK; t++) { acc += G[t]; G[t] = acc; }
+        for (int t = 0; t < CK; t++) {
+            acc += G[t];
+            G[t] = acc;
+        }
     }
     __syncthreads();
-    if (tid < CK) gam[tid] = (float)exp(G[tid]);
-    // 3. L (strictly lower, with beta and decay) and Pm (lower incl. diagonal)
-    float *Pm = ws.Pm + blk * CK * CK;
-    for (int e = tid; e < CK * CK; e += 256) {
-        const int t = e / CK, s = e % CK;
-        float kk = 0.f, qkv = 0.f;
-        if (s <= t) {
-            const float *kt = Kh + t * LDS, *ks = Kh + s * LDS, *qt = Qh + t * LDS;
-#pragma unroll 8
-            for (int d = 0; d < D; d++) {
-                kk = fmaf(kt[d], ks[d], kk);
-                qkv = fmaf(qt[d], ks[d], qkv);
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    const float qscale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
+    if (tid < CK) {
+        const float gam = (float)exp(G[tid]);
+        xs[tid] = gam * rk[tid];
+        er[tid] = (float)exp(G[CK - 1] - G[tid]) * rk[tid];
+        ws.scal[blk * 128 + 64 + tid] = gam * __fmul_rn(rq[tid], qscale);
+    }
+    if (tid == 0) {
+        ws.scal[blk * 128] = (float)exp(G[CK - 1]);
+        // raw Q (rows 64..127 of each column block) -> the out kernel's B operand image
+        bulk_s2g(ws.QB + blk * SZ_QB, AKQ + 8192, 8192);
+        bulk_s2g(ws.QB + blk * SZ_QB + 8192, AKQ + 16384 + 8192, 8192);
+        bulk_commit();
+        // Gram: D[0:128, 0:64] = [K;Q] K^T
+        const uint32_t id = idesc_bf16(128, CK, false, false);
+        const uint32_t a0 = smem_u32(AKQ);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; kk++) {
+            const uint64_t de = sdesc_sw128(a0 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+            mma_bf16(tbase, de, de, id, kk > 0);
+        }
+        mma_commit(bar);
+    }
+    __syncthreads();  // er[] visible
+    // 3. Kr^T = K^T diag(e^{G_C - G} rk) as hi/lo MN-major images (rows t, cols d)
+    for (int ch = tid; ch < 1024; ch += 128) {
+        const int b = ch >> 9, t = (ch >> 3) & 63, pc = ch & 7;
+        const int d0 = b * 64 + ((pc ^ (t & 7)) << 3);
+        const uint4 raw = *reinterpret_cast<const uint4 *>(AKQ + swz(t, d0, 128));
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+        const float s = er[t];
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            uint16_t h0, l0, h1, l1;
+            split_bf16(bf16_to_f32(w[e] & 0xffffu) * s, h0, l0);
+            split_bf16(bf16_to_f32(w[e] >> 16) * s, h1, l1);
+            hw[e] = h0 | ((uint32_t)h1 << 16);
+            lw[e] = l0 | ((uint32_t)l1 << 16);
+        }
+        *reinterpret_cast<uint4 *>(ws.KrH + blk * SZ_KR + ch * 16) =
+            make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4 *>(ws.KrL + blk * SZ_KR + ch * 16) =
+            make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    bool ok = mbar_wait(bar, 0, status, VX_DEV_TIMEOUT_MMA);
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    if (ok) {
+        // 4. Gram epilogue: rows 0..63 -> L (fp32, shared), rows 64..127 -> Pm (hi/lo image)
+        const int r = warp * 32 + lane;
+        const bool low = r < CK;
+        const int t = low ? r : r - CK;
+        const double Gt = G[t];
+        const float sc_t = low ? beta[t] * rk[t] : __fmul_rn(rq[t], qscale);
+        const uint32_t ta = tbase + ((uint32_t)(warp * 32) << 16);
+        uint8_t *pm = ws.PmB + blk * SZ_PM;
+#pragma unroll
+        for (int c16 = 0; c16 < CK; c16 += 16) {
+            float dv[16];
+            tmem_ld16(ta + c16, dv);
+            float val[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int s = c16 + j;
+                const bool keep = low ? s < t : s <= t;
+                val[j] = keep ? sc_t * rk[s] * expf((float)(Gt - G[s])) * dv[j] : 0.f;
+            }
+            if (low) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                    *reinterpret_cast<float4 *>(Lf + t * LST + c16 + j) =
+                        make_float4(val[j], val[j + 1], val[j + 2], val[j + 3]);
+            } else {
+#pragma unroll
+                for (int half = 0; half < 2; half++) {
+                    uint32_t hw[4], lw[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        uint16_t h0, l0, h1, l1;
+                        split_bf16(val[half * 8 + 2 * e], h0, l0);
+                        split_bf16(val[half * 8 + 2 * e + 1], h1, l1);
+                        hw[e] = h0 | ((uint32_t)h1 << 16);
+                        lw[e] = l0 | ((uint32_t)l1 << 16);
+                    }
+                    const int cc = c16 + half * 8;
+                    *reinterpret_cast<uint4 *>(pm + swz(t, cc, 128)) =
+                        make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    *reinterpret_cast<uint4 *>(pm + swz(CK + t, cc, 128)) =
+                        make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                }
             }
         }
-        const float dec = s <= t ? (float)exp(G[t] - G[s]) : 0.f;
-        Lm[t * (CK + 1) + s] = s < t ? beta[t] * dec * kk : 0.f;
-        Pm[e] = s <= t ? dec * qkv : 0.f;
-    }
-    __syncthreads();
-    // 4. T = (I + L)^-1 diag(beta), row by row: T_t = beta_t e_t - sum_{r<t} L_tr T_r
-    for (int t = 0; t < CK; t++) {
-        // 64 columns x 4 partial sums per column
-        const int s = tid >> 2, part = tid & 3;
-        float acc = 0.f;
-        if (s < t)
-            for (int r = s + part; r < t; r += 4) acc = fmaf(Lm[t * (CK + 1) + r], Xs[r * (CK + 1) + s], acc);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-        if (part == 0) Xs[t * (CK + 1) + s] = s < t ? -acc : (s == t ? beta[t] : 0.f);
+        tc_fence_before();
         __syncthreads();
-    }
-    // 5. Wv = T V, Wk = T diag(gamma) K; Qg = diag(gamma) Q; Kr = diag(gamma_C/gamma) K
-    float *Wv = ws.Wv + blk * CK * D, *Wk = ws.Wk + blk * CK * D;
-    float *Qg = ws.Qg + blk * CK * D, *Kr = ws.Kr + blk * CK * D;
-    for (int e = tid; e < CK * D; e += 256) {
-        const int t = e / D, d = e % D;
-        float av = 0.f, ak = 0.f;
-        for (int s = 0; s <= t; s++) {
-            const float x = Xs[t * (CK + 1) + s];
-            av = fmaf(x, Vs[s * LDS + d], av);
-            ak = fmaf(x * gam[s], Kh[s * LDS + d], ak);
+        // 5. X = (I + L)^-1 diag(beta), one column per thread (forward substitution)
+        if (tid < CK) {
+            const int j = tid;
+            float x[CK];
+#pragma unroll
+            for (int t2 = 0; t2 < CK; t2++) {
+                float a0 = (t2 == j) ? beta[t2] : 0.f, a1 = 0.f;
+                const float *Lr = Lf + t2 * LST;
+#pragma unroll
+                for (int s4 = 0; s4 < t2; s4 += 4) {
+                    const float4 l4 = *reinterpret_cast<const float4 *>(Lr + s4);
+                    a0 = fmaf(-l4.x, x[s4], a0);
+                    if (s4 + 1 < t2) a1 = fmaf(-l4.y, x[s4 + 1], a1);
+                    if (s4 + 2 < t2) a0 = fmaf(-l4.z, x[s4 + 2], a0);
+                    if (s4 + 3 < t2) a1 = fmaf(-l4.w, x[s4 + 3], a1);
+                }
+                x[t2] = a0 + a1;
+            }
+            const float xk = xs[j];
+#pragma unroll
+            for (int t2 = 0; t2 < CK; t2++) {
+                uint16_t h, l;
+                split_bf16(x[t2], h, l);
+                st16(XV, swz(t2, j, 128), h);
+                st16(XV, swz(CK + t2, j, 128), l);
+                split_bf16(x[t2] * xk, h, l);
+                st16(XK, swz(t2, j, 128), h);
+                st16(XK, swz(CK + t2, j, 128), l);
+            }
         }
-        Wv[e] = av;
-        Wk[e] = ak;
-        Qg[e] = gam[t] * Qh[t * LDS + d];
-        Kr[e] = (float)exp(G[CK - 1] - G[t]) * Kh[t * LDS + d];
+        fence_proxy_async();
+        __syncthreads();
+        // 6. Wv^T = V^T X^T (cols 0..127) and Wk^T = K^T Xk^T (cols 128..255), hi | lo columns
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t id = idesc_bf16(128, 128, true, false);
+#pragma unroll
+            for (int kk = 0; kk < CK / 16; kk++)
+                mma_bf16(tbase, sdesc_sw128(smem_u32(VT) + kk * 2048, 8192, 1024),
+                         sdesc_sw128(smem_u32(XV) + kk * 32, 16, 1024), id, kk > 0);
+#pragma unroll
+            for (int kk = 0; kk < CK / 16; kk++)
+                mma_bf16(tbase + 128, sdesc_sw128(smem_u32(AKQ) + kk * 2048, 16384, 1024),
+                         sdesc_sw128(smem_u32(XK) + kk * 32, 16, 1024), id, kk > 0);
+            mma_commit(bar);
+        }
+        ok = mbar_wait(bar, 1, status, VX_DEV_TIMEOUT_MMA);
+        if (tid == 0) bulk_wait_read0();  // the Q image copy has left AKQ
+        ok = __syncthreads_and(ok);
+        tc_fence_after();
+        if (ok) {
+            // 7. Wv -> workspace fp32 [t][d]; Wk -> [Wk_hi; Wk_lo] staged in AKQ
+            const int d = warp * 32 + lane;
+            const uint32_t ta2 = tbase + ((uint32_t)(warp * 32) << 16);
+            float *Wv = ws.Wv + blk * (CK * D);
+#pragma unroll
+            for (int c16 = 0; c16 < CK; c16 += 16) {
+                float a[16], b2[16];
+                tmem_ld16(ta2 + c16, a);
+                tmem_ld16(ta2 + 64 + c16, b2);
+#pragma unroll
+                for (int j = 0; j < 16; j++) Wv[(c16 + j) * D + d] = a[j] + b2[j];
+                tmem_ld16(ta2 + 128 + c16, a);
+                tmem_ld16(ta2 + 192 + c16, b2);
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    uint16_t h, l;
+                    split_bf16(a[j] + b2[j], h, l);
+                    st16(AKQ, swz(c16 + j, d, 128), h);
+                    st16(AKQ, swz(CK + c16 + j, d, 128), l);
+                }
+            }
+            fence_proxy_async();
+            __syncthreads();
+            if (tid == 0) {
+                bulk_s2g(ws.WkA + blk * SZ_WKA, AKQ, 32768);
+                bulk_commit();
+            }
+        }
     }
-    if (tid == 0) ws.g63[blk] = (float)exp(G[CK - 1]);
+    if (tid == 0) bulk_wait0();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tbase, 256);
 }
 
-// ---- phase 2: the sequential state scan --------------------------------------------------
-struct ScanSmem {
-    float Wk_s[CK][D + 1];
-    float Kr_s[CK][D + 1];
-    float S_s[D][CB + 1];
-    float U_s[CK][CB + 1];
+// ---- phase 2: the sequential state scan ---------------------------------------------------
+// CTA (column block cb, V head vh) owns state columns [cb*CB, cb*CB + CB). Warps 0-3 run
+// the epilogues and thread 0 issues the MMAs; warp 4 streams Wk and Kr^T tiles (two stages).
+//   MMA1: D1[128 x 2CB] = [Wk_hi; Wk_lo] [S_hi | S_lo]   (U = Wv - sum of the 4 quadrants)
+//   MMA2: D2[128 x 2CB] = Kr^T_hi [U_hi | U_lo] + Kr^T_lo [U_hi | U_lo]   (dS = both halves)
+template <int CB>
+struct ScanLayout {
+    static constexpr int NB = 2 * CB;
+    static constexpr uint32_t STAGE = 65536;  // Wk 32K | Kr^T hi 16K | Kr^T lo 16K
+    static constexpr uint32_t SB = 2 * STAGE;                 // [S_hi; S_lo] over d: 2 blocks
+    static constexpr uint32_t UB = SB + 2 * NB * 128;          // [U_hi; U_lo] over t: 1 block
+    static constexpr uint32_t XCH = UB + NB * 128;             // float [CB/2][128]
+    static constexpr uint32_t BAR = XCH + (CB / 2) * 128 * 4;  // full[2] empty[2] m1 m2
+    static constexpr uint32_t SMEM = BAR + 6 * 8 + 16 + 1024;
 };
 
-__global__ void __launch_bounds__(256)
-dn_chunk_scan(Ws ws, float *__restrict__ S, int nv, int n_chunks) {
-    extern __shared__ float ssm_raw[];
-    ScanSmem &sm = *reinterpret_cast<ScanSmem *>(ssm_raw);
-    auto &Wk_s = sm.Wk_s;
-    auto &Kr_s = sm.Kr_s;
-    auto &S_s = sm.S_s;
-    auto &U_s = sm.U_s;
-    const int vh = blockIdx.x, cb = blockIdx.y, tid = threadIdx.x;
-    float *Sh = S + (size_t)vh * D * D;
-    // thread owns state rows tid/2 and 8 of the CB columns
-    const int r = tid >> 1, j0 = (tid & 1) * 8;
-    float s[8];
+template <int CB>
+__global__ void __launch_bounds__(160, 1)
+dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
+    using Lay = ScanLayout<CB>;
+    constexpr int NB = Lay::NB;
+    constexpr int HC = CB / 2;
+    extern __shared__ uint8_t smraw[];
+    uint8_t *sm = align1024(smraw);
+    uint8_t *stg = sm, *SB = sm + Lay::SB, *UB = sm + Lay::UB;
+    float *xch = reinterpret_cast<float *>(sm + Lay::XCH);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + Lay::BAR);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 6);
+    volatile int *abort_ = reinterpret_cast<volatile int *>(tslot + 1);
+    const int cb = blockIdx.x, vh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5,
+              lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < 6; i++) mbar_init(&bars[i], 1);
+        *abort_ = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(tslot, 2 * NB);
+        tmem_relinquish();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+
+    if (warp == 4) {  // producer
+        if (lane == 0) {
+            for (int c = 0; c < n_chunks; c++) {
+                const int s = c & 1;
+                if (c >= 2 && (*abort_ || !mbar_wait(&bars[2 + s], ((c >> 1) - 1) & 1, status,
+                                                     VX_DEV_TIMEOUT_MMA))) {
+                    *abort_ = 1;
+                    break;
+                }
+                const size_t blk = (size_t)vh * n_chunks + c;
+                uint8_t *dst = stg + s * Lay::STAGE;
+                mbar_arrive_expect_tx(&bars[s], Lay::STAGE);
+                bulk_g2s(dst, ws.WkA + blk * SZ_WKA, 32768, &bars[s]);
+                bulk_g2s(dst + 32768, ws.KrH + blk * SZ_KR, 16384, &bars[s]);
+                bulk_g2s(dst + 49152, ws.KrL + blk * SZ_KR, 16384, &bars[s]);
+            }
+        }
+        return;
+    }
+
+    const int d = tid;                      // state row in the S epilogue
+    const int t = (warp & 1) * 32 + lane;   // chunk row in the U epilogue
+    const int jh = warp < 2 ? 0 : HC;       // own half of the columns in the U epilogue
+    const int jo = HC - jh;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t tD1 = tbase + lane_off, tD2 = tbase + NB + lane_off;
+    float *Sh = S + (size_t)vh * D * D + (size_t)d * D + cb * CB;
+    float s[CB];
 #pragma unroll
-    for (int j = 0; j < 8; j++) s[j] = Sh[r * D + cb * CB + j0 + j];
+    for (int j = 0; j < CB; j++) s[j] = Sh[j];
+    auto write_sb = [&]() {
+#pragma unroll
+        for (int j = 0; j < CB; j++) {
+            uint16_t h, l;
+            split_bf16(s[j], h, l);
+            st16(SB, swz(j, d, NB), h);
+            st16(SB, swz(CB + j, d, NB), l);
+        }
+        fence_proxy_async();
+    };
+    write_sb();
+
     for (int c = 0; c < n_chunks; c++) {
+        const int st = c & 1;
         const size_t blk = (size_t)vh * n_chunks + c;
-        const float *Wk = ws.Wk + blk * CK * D, *Kr = ws.Kr + blk * CK * D;
-        const float *Wv = ws.Wv + blk * CK * D;
-        float *Sc = ws.Sc + blk * D * D, *U = ws.U + blk * CK * D;
-        for (int e = tid; e < CK * D; e += 256) {
-            Wk_s[e / D][e % D] = Wk[e];
-            Kr_s[e / D][e % D] = Kr[e];
-        }
+        uint8_t *stage = stg + st * Lay::STAGE;
+        tc_fence_before();
+        named_bar_sync(1, 128);
+        if (tid == 0) {
+            if (!*abort_ && !mbar_wait(&bars[st], (c >> 1) & 1, status, VX_DEV_TIMEOUT_TMA))
+                *abort_ = 1;
+            if (!*abort_) {
+                tc_fence_after();
+                const uint32_t id = idesc_bf16(128, NB, false, false);
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            S_s[r][j0 + j] = s[j];
-            Sc[r * D + cb * CB + j0 + j] = s[j];  // state at the chunk start, for the output
-        }
-        __syncthreads();
-        // U = Wv - Wk S  (64 x CB): 4 outputs per thread
-        for (int e = tid; e < CK * CB; e += 256) {
-            const int t = e / CB, j = e % CB;
-            float acc = 0.f;
-#pragma unroll 8
-            for (int d = 0; d < D; d++) acc = fmaf(Wk_s[t][d], S_s[d][j], acc);
-            const float u = Wv[t * D + cb * CB + j] - acc;
-            U_s[t][j] = u;
-            U[t * D + cb * CB + j] = u;
-        }
-        __syncthreads();
-        // S = gamma_C S + Kr^T U
-        const float g = ws.g63[blk];
+                for (int kk = 0; kk < D / 16; kk++)
+                    mma_bf16(tbase,
+                             sdesc_sw128(smem_u32(stage) + (kk >> 2) * 16384 + (kk & 3) * 32,
+                                         16, 1024),
+                             sdesc_sw128(smem_u32(SB) + (kk >> 2) * (NB * 128) + (kk & 3) * 32,
+                                         16, 1024),
+                             id, kk > 0);
+                mma_commit(&bars[4]);
+                // the state at this chunk's start -> S0^T images for the output kernel
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            float acc = 0.f;
-#pragma unroll 8
-            for (int t = 0; t < CK; t++) acc = fmaf(Kr_s[t][r], U_s[t][j0 + j], acc);
-            s[j] = fmaf(g, s[j], acc);
+                for (int b = 0; b < 2; b++) {
+                    bulk_s2g(ws.ScH + blk * SZ_SC + b * 16384 + cb * CB * 128, SB + b * NB * 128,
+                             CB * 128);
+                    bulk_s2g(ws.ScL + blk * SZ_SC + b * 16384 + cb * CB * 128,
+                             SB + b * NB * 128 + CB * 128, CB * 128);
+                }
+                bulk_commit();
+            }
         }
-        __syncthreads();
+        // Wv (own half of the columns) and the chunk decay, ahead of the MMA
+        float wv[HC];
+        const float *wsrc = ws.Wv + blk * (CK * D) + t * D + cb * CB + jh;
+#pragma unroll
+        for (int j = 0; j < HC; j += 4) {
+            const float4 f = *reinterpret_cast<const float4 *>(wsrc + j);
+            wv[j] = f.x;
+            wv[j + 1] = f.y;
+            wv[j + 2] = f.z;
+            wv[j + 3] = f.w;
+        }
+        const float g63 = ws.scal[blk * 128];
+        if (!*abort_ && !mbar_wait(&bars[4], c & 1, status, VX_DEV_TIMEOUT_MMA)) *abort_ = 1;
+        tc_fence_after();
+        // quadrant sums: own half kept, the other half handed to the partner thread tid ^ 64
+#pragma unroll
+        for (int j0 = 0; j0 < HC; j0 += 16) {
+            float a[16], b2[16];
+            tmem_ld16(tD1 + jo + j0, a);
+            tmem_ld16(tD1 + CB + jo + j0, b2);
+#pragma unroll
+            for (int j = 0; j < 16; j++) xch[(j0 + j) * 128 + (tid ^ 64)] = a[j] + b2[j];
+            tmem_ld16(tD1 + jh + j0, a);
+            tmem_ld16(tD1 + CB + jh + j0, b2);
+#pragma unroll
+            for (int j = 0; j < 16; j++) wv[j0 + j] -= a[j] + b2[j];
+        }
+        if (tid == 0) bulk_wait_read0();  // the previous U image and this S0 image have left
+        named_bar_sync(2, 128);
+#pragma unroll
+        for (int j = 0; j < HC; j++) {
+            const float u = wv[j] - xch[j * 128 + tid];
+            uint16_t h, l;
+            split_bf16(u, h, l);
+            st16(UB, swz(jh + j, t, NB), h);
+            st16(UB, swz(CB + jh + j, t, NB), l);
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        named_bar_sync(1, 128);
+        if (tid == 0 && !*abort_) {
+            tc_fence_after();
+            const uint32_t id = idesc_bf16(128, NB, true, false);
+#pragma unroll
+            for (int kk = 0; kk < CK / 16; kk++)
+                mma_bf16(tbase + NB,
+                         sdesc_sw128(smem_u32(stage) + 32768 + kk * 2048, 8192, 1024),
+                         sdesc_sw128(smem_u32(UB) + kk * 32, 16, 1024), id, kk > 0);
+#pragma unroll
+            for (int kk = 0; kk < CK / 16; kk++)
+                mma_bf16(tbase + NB,
+                         sdesc_sw128(smem_u32(stage) + 49152 + kk * 2048, 8192, 1024),
+                         sdesc_sw128(smem_u32(UB) + kk * 32, 16, 1024), id, 1);
+            mma_commit(&bars[5]);
+            mma_commit(&bars[2 + st]);
+            bulk_s2g(ws.UH + blk * SZ_U + cb * CB * 128, UB, CB * 128);
+            bulk_s2g(ws.UL + blk * SZ_U + cb * CB * 128, UB + CB * 128, CB * 128);
+            bulk_commit();
+        }
+        if (!*abort_ && !mbar_wait(&bars[5], c & 1, status, VX_DEV_TIMEOUT_MMA)) *abort_ = 1;
+        tc_fence_after();
+#pragma unroll
+        for (int j0 = 0; j0 < CB; j0 += 16) {
+            float a[16], b2[16];
+            tmem_ld16(tD2 + j0, a);
+            tmem_ld16(tD2 + CB + j0, b2);
+#pragma unroll
+            for (int j = 0; j < 16; j++) s[j0 + j] = fmaf(g63, s[j0 + j], a[j] + b2[j]);
+        }
+        write_sb();
     }
 #pragma unroll
-    for (int j = 0; j < 8; j++) Sh[r * D + cb * CB + j0 + j] = s[j];
+    for (int j = 0; j < CB; j++) Sh[j] = s[j];
+    if (tid == 0) bulk_wait0();
+    tc_fence_before();
+    named_bar_sync(1, 128);
+    if (warp == 0) tmem_dealloc(tbase, 2 * NB);
 }
 
 // ---- phase 3: outputs ---------------------------------------------------------------------
+constexpr uint32_t O_QB = 0, O_SCH = 16384, O_SCL = 49152, O_UH = 81920, O_UL = 98304,
+                   O_PM = 114688, O_CT = 131072, O_BAR = O_CT + CK * 4;
+constexpr uint32_t OUT_SMEM = O_BAR + 16 + 1024;
+
 template <bool OUT_BF16>
-__global__ void __launch_bounds__(256)
-dn_chunk_out(Ws ws, void *__restrict__ o, int T, int nv, int n_chunks) {
-    extern __shared__ float osm[];
-    float *Qg = osm;                 // [CK][D+1]
-    float *Pm = Qg + CK * (D + 1);   // [CK][CK+1]
-    float *Sc = Pm + CK * (CK + 1);  // [D][64+1]  (one half of the columns)
-    float *Us = Sc + D * 65;         // [CK][64+1]
-    const int vh = blockIdx.x, c = blockIdx.y, tid = threadIdx.x;
+__global__ void __launch_bounds__(128)
+dn_out_tc(Wsp ws, void *__restrict__ o, int T, int nv, int n_chunks, uint32_t *status) {
+    extern __shared__ uint8_t smraw[];
+    uint8_t *sm = align1024(smraw);
+    float *ct = reinterpret_cast<float *>(sm + O_CT);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + O_BAR);
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 1);
+    volatile int *okf = reinterpret_cast<volatile int *>(tslot + 1);
+    const int c = blockIdx.x, vh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5,
+              lane = tid & 31;
     const size_t blk = (size_t)vh * n_chunks + c;
-    const float *gQg = ws.Qg + blk * CK * D, *gPm = ws.Pm + blk * CK * CK;
-    const float *gSc = ws.Sc + blk * D * D, *gU = ws.U + blk * CK * D;
-    for (int e = tid; e < CK * D; e += 256) Qg[(e / D) * (D + 1) + e % D] = gQg[e];
-    for (int e = tid; e < CK * CK; e += 256) Pm[(e / CK) * (CK + 1) + e % CK] = gPm[e];
-    for (int half = 0; half < 2; half++) {
-        for (int e = tid; e < D * 64; e += 256)
-            Sc[(e / 64) * 65 + e % 64] = gSc[(e / 64) * D + half * 64 + e % 64];
-        for (int e = tid; e < CK * 64; e += 256)
-            Us[(e / 64) * 65 + e % 64] = gU[(e / 64) * D + half * 64 + e % 64];
-        __syncthreads();
-        // 64 x 64 outputs: thread -> 4 rows x 4 columns
-        const int tr = (tid >> 4) * 4, tc = (tid & 15) * 4;
-        float acc[4][4] = {};
-        for (int d = 0; d < D; d++) {
-            float a[4], b[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) { a[i] = Qg[(tr + i) * (D + 1) + d]; b[i] = Sc[d * 65 + tc + i]; }
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int jj = 0; jj < 4; jj++) acc[i][jj] = fmaf(a[i], b[jj], acc[i][jj]);
-        }
-        for (int s = 0; s < CK; s++) {
-            float a[4], b[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) { a[i] = Pm[(tr + i) * (CK + 1) + s]; b[i] = Us[s * 65 + tc + i]; }
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int jj = 0; jj < 4; jj++) acc[i][jj] = fmaf(a[i], b[jj], acc[i][jj]);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int tt = c * CK + tr + i;
-            if (tt >= T) continue;
-#pragma unroll
-            for (int jj = 0; jj < 4; jj++)
-                act_st<OUT_BF16>(o, ((size_t)tt * nv + vh) * D + half * 64 + tc + jj, acc[i][jj]);
-        }
-        __syncthreads();
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(bar, 131072);
+        bulk_g2s(sm + O_QB, ws.QB + blk * SZ_QB, 16384, bar);
+        bulk_g2s(sm + O_SCH, ws.ScH + blk * SZ_SC, 32768, bar);
+        bulk_g2s(sm + O_SCL, ws.ScL + blk * SZ_SC, 32768, bar);
+        bulk_g2s(sm + O_UH, ws.UH + blk * SZ_U, 16384, bar);
+        bulk_g2s(sm + O_UL, ws.UL + blk * SZ_U, 16384, bar);
+        bulk_g2s(sm + O_PM, ws.PmB + blk * SZ_PM, 16384, bar);
     }
+    if (warp == 0) {
+        tmem_alloc(tslot, 256);
+        tmem_relinquish();
+    }
+    if (tid < CK) ct[tid] = ws.scal[blk * 128 + 64 + tid];
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    if (tid == 0) {
+        const bool ok = mbar_wait(bar, 0, status, VX_DEV_TIMEOUT_TMA);
+        *okf = ok ? 1 : 0;
+        if (ok) {
+            tc_fence_after();
+            const uint32_t b0 = smem_u32(sm);
+            // D[v][t] cols 0..63: S0^T Q^T (hi and lo passes)
+            const uint32_t id1 = idesc_bf16(128, CK, false, false);
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+#pragma unroll
+                for (int kk = 0; kk < D / 16; kk++)
+                    mma_bf16(tbase,
+                             sdesc_sw128(b0 + (h ? O_SCL : O_SCH) + (kk >> 2) * 16384 +
+                                             (kk & 3) * 32, 16, 1024),
+                             sdesc_sw128(b0 + O_QB + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
+                             id1, (h | kk) > 0);
+            // D[v][t'] cols 64..191: U^T [Pm_hi | Pm_lo]^T (hi and lo passes)
+            const uint32_t id2 = idesc_bf16(128, 128, false, false);
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+#pragma unroll
+                for (int kk = 0; kk < CK / 16; kk++)
+                    mma_bf16(tbase + 64, sdesc_sw128(b0 + (h ? O_UL : O_UH) + kk * 32, 16, 1024),
+                             sdesc_sw128(b0 + O_PM + kk * 32, 16, 1024), id2, (h | kk) > 0);
+            mma_commit(bar);
+        }
+    }
+    __syncthreads();
+    bool ok = *okf != 0;
+    if (ok) ok = mbar_wait(bar, 1, status, VX_DEV_TIMEOUT_MMA);
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    if (ok) {
+        const int vcol = warp * 32 + lane;
+        const uint32_t ta = tbase + ((uint32_t)(warp * 32) << 16);
+#pragma unroll
+        for (int c16 = 0; c16 < CK; c16 += 16) {
+            float a[16], b2[16], e[16];
+            tmem_ld16(ta + c16, a);
+            tmem_ld16(ta + 64 + c16, b2);
+            tmem_ld16(ta + 128 + c16, e);
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int tt = c * CK + c16 + j;
+                if (tt < T)
+                    act_st<OUT_BF16>(o, ((size_t)tt * nv + vh) * D + vcol,
+                                     fmaf(ct[c16 + j], a[j], b2[j] + e[j]));
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tbase, 256);
+}
+
+template <typename K>
+int set_smem(K kernel, uint32_t bytes, char *err, size_t errlen) {
+    VX_CK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    return 0;
 }
 
 }  // namespace
@@ -303,7 +688,7 @@ extern "C" size_t vx27_deltanet_prefill_workspace_size(int T, int nqk, int nv, i
     (void)nqk;
     if (T <= 0 || nv <= 0 || hd != D) return 0;
     const size_t n_chunks = ((size_t)T + CK - 1) / CK;
-    return n_chunks * nv * ws_floats_per_blk() * sizeof(float);
+    return n_chunks * nv * BLK_BYTES;
 }
 
 extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const void *v,
@@ -316,64 +701,77 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
     if (hd != D) return fail(err, errlen, "%s: hd=%d unsupported (128 only)", fn, hd);
     if (T <= 0 || nqk <= 0 || nv < nqk || nv > 65535)
         return fail(err, errlen, "%s: bad shape T=%d nqk=%d nv=%d", fn, T, nqk, nv);
+    if (!(flags & VX27_F_ACT_BF16))
+        return fail(err, errlen, "%s: q/k/v/a/b must be bf16 (VX27_F_ACT_BF16)", fn);
     const bool g64 = flags & VX27_F_GATES_F64;
     if (!q || !k || !v || !a || !b || !S || !o || !workspace || (!g64 && (!A_log || !dt_bias)))
         return fail(err, errlen, "%s: null pointer argument", fn);
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 7)
+        return fail(err, errlen, "%s: q, k and v must be 8-byte aligned", fn);
+    if ((uintptr_t)workspace & 15)
+        return fail(err, errlen, "%s: workspace must be 16-byte aligned", fn);
     const size_t need = vx27_deltanet_prefill_workspace_size(T, nqk, nv, hd);
     if (workspace_bytes < need)
         return fail(err, errlen, "%s: workspace of %zu bytes, need %zu", fn, workspace_bytes, need);
     const int n_chunks = (T + CK - 1) / CK;
-    if (n_chunks > 65535) return fail(err, errlen, "%s: T=%d too long", fn, T);
     cudaStream_t st = (cudaStream_t)stream;
-    Ws ws = ws_views((float *)workspace, (size_t)n_chunks * nv);
-    const size_t prep_smem = (3 * CK * LDS + 2 * CK * (CK + 1)) * sizeof(float) +
-                             CK * sizeof(double) + 2 * CK * sizeof(float);
-    const bool bf = flags & VX27_F_ACT_BF16;
-#define VX_PREP(A_, G_)                                                                     \
-    {                                                                                       \
-        static bool attr = false;                                                           \
-        if (!attr) {                                                                        \
-            VX_CK(cudaFuncSetAttribute(dn_chunk_prep<A_, G_>,                               \
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,         \
-                                       (int)prep_smem));                                    \
-            attr = true;                                                                    \
-        }                                                                                   \
-        dn_chunk_prep<A_, G_><<<dim3(nv, n_chunks), 256, prep_smem, st>>>(                  \
-            q, k, v, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks);                       \
-    }
-    if (bf && g64) VX_PREP(true, true)
-    else if (bf) VX_PREP(true, false)
-    else if (g64) VX_PREP(false, true)
-    else VX_PREP(false, false)
-#undef VX_PREP
-    VX_CK(cudaGetLastError());
-    {
+    uint32_t *status = dev_status();
+    if (!status) return fail(err, errlen, "%s: device status word unavailable", fn);
+    Wsp ws = wsp_views((uint8_t *)workspace, (size_t)n_chunks * nv);
+    const auto *q16 = (const uint16_t *)q, *k16 = (const uint16_t *)k, *v16 = (const uint16_t *)v;
+
+    if (g64) {
         static bool attr = false;
         if (!attr) {
-            VX_CK(cudaFuncSetAttribute(dn_chunk_scan, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sizeof(ScanSmem)));
+            if (set_smem(dn_prep_tc<true>, PREP_SMEM, err, errlen)) return -1;
             attr = true;
         }
-        dn_chunk_scan<<<dim3(nv, D / CB), 256, sizeof(ScanSmem), st>>>(ws, S, nv, n_chunks);
-    }
-    VX_CK(cudaGetLastError());
-    const size_t out_smem = (CK * (D + 1) + CK * (CK + 1) + D * 65 + CK * 65) * sizeof(float);
-    if (flags & VX27_F_OUT_BF16) {
-        static bool attr = false;
-        if (!attr) {
-            VX_CK(cudaFuncSetAttribute(dn_chunk_out<true>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)out_smem));
-            attr = true;
-        }
-        dn_chunk_out<true><<<dim3(nv, n_chunks), 256, out_smem, st>>>(ws, o, T, nv, n_chunks);
+        dn_prep_tc<true><<<dim3(n_chunks, nv), 128, PREP_SMEM, st>>>(
+            q16, k16, v16, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
     } else {
         static bool attr = false;
         if (!attr) {
-            VX_CK(cudaFuncSetAttribute(dn_chunk_out<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)out_smem));
+            if (set_smem(dn_prep_tc<false>, PREP_SMEM, err, errlen)) return -1;
             attr = true;
         }
-        dn_chunk_out<false><<<dim3(nv, n_chunks), 256, out_smem, st>>>(ws, o, T, nv, n_chunks);
+        dn_prep_tc<false><<<dim3(n_chunks, nv), 128, PREP_SMEM, st>>>(
+            q16, k16, v16, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
+    }
+    VX_CK(cudaGetLastError());
+    // scan: 32 state columns per CTA while that grid fits in one wave, else 64
+    if (nv * (D / 32) <= num_sms()) {
+        static bool attr = false;
+        if (!attr) {
+            if (set_smem(dn_scan_tc<32>, ScanLayout<32>::SMEM, err, errlen)) return -1;
+            attr = true;
+        }
+        dn_scan_tc<32><<<dim3(D / 32, nv), 160, ScanLayout<32>::SMEM, st>>>(ws, S, n_chunks,
+                                                                             status);
+    } else {
+        static bool attr = false;
+        if (!attr) {
+            if (set_smem(dn_scan_tc<64>, ScanLayout<64>::SMEM, err, errlen)) return -1;
+            attr = true;
+        }
+        dn_scan_tc<64><<<dim3(D / 64, nv), 160, ScanLayout<64>::SMEM, st>>>(ws, S, n_chunks,
+                                                                             status);
+    }
+    VX_CK(cudaGetLastError());
+    if (flags & VX27_F_OUT_BF16) {
+        static bool attr = false;
+        if (!attr) {
+            if (set_smem(dn_out_tc<true>, OUT_SMEM, err, errlen)) return -1;
+            attr = true;
+        }
+        dn_out_tc<true><<<dim3(n_chunks, nv), 128, OUT_SMEM, st>>>(ws, o, T, nv, n_chunks, status);
+    } else {
+        static bool attr = false;
+        if (!attr) {
+            if (set_smem(dn_out_tc<false>, OUT_SMEM, err, errlen)) return -1;
+            attr = true;
+        }
+        dn_out_tc<false><<<dim3(n_chunks, nv), 128, OUT_SMEM, st>>>(ws, o, T, nv, n_chunks,
+                                                                    status);
     }
     VX_CK(cudaGetLastError());
     return 0;
