@@ -40,6 +40,8 @@ __device__ __forceinline__ uint32_t swz(int r, int c, int R) {
     return (uint32_t)((c >> 6) * (R * 128) + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) +
                       ((c & 7) << 1));
 }
+// fp32 64x64 tile in shared memory, rows of 64 with float4 groups XOR-swizzled by row
+__device__ __forceinline__ int fsw(int r, int c) { return r * 64 + (c ^ ((r & 7) << 2)); }
 __device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
     return (uint8_t *)(((uintptr_t)p + 1023) & ~(uintptr_t)1023);
 }
@@ -73,7 +75,7 @@ constexpr size_t SZ_QB = 16384;   // raw Q rows t, K-major over d (out MMA1 B)
 constexpr size_t SZ_PM = 16384;   // [Pm_hi; Pm_lo] rows t, K-major over s (out MMA2 B)
 constexpr size_t SZ_SC = 32768;   // S0^T hi or lo: rows v, K-major over d (out MMA1 A)
 constexpr size_t SZ_U = 16384;    // U^T hi or lo: rows v, K-major over t (out MMA2 A)
-constexpr size_t SZ_WV = 32768;   // Wv [t][d] fp32
+constexpr size_t SZ_WV = 32768;   // Wv fp32 in 16-column groups: [d/16][t][16]
 constexpr size_t SZ_SCAL = 512;   // [0] = e^{G_C}; [64 + t] = e^{G_t} rq_t / sqrt(128)
 constexpr size_t BLK_BYTES =
     SZ_WKA + 2 * SZ_KR + SZ_QB + SZ_PM + 2 * SZ_SC + 2 * SZ_U + SZ_WV + SZ_SCAL;
@@ -111,26 +113,28 @@ __device__ __forceinline__ void gates_dev(double a, double A_log, double b, doub
 // shared memory (after 1024-byte alignment)
 constexpr uint32_t P_AKQ = 0;        // [K;Q] raw, K-major 128 rows x 128; later [Wk_hi;Wk_lo]
 constexpr uint32_t P_VT = 32768;     // V raw, rows s x cols d (MN-major A of Wv^T)
-constexpr uint32_t P_XV = 49152;     // [X_hi; X_lo] rows t, K-major over s (B of Wv^T)
+constexpr uint32_t P_XV = 49152;     // L fp32 (swizzled [64][64]); then [X_hi; X_lo] rows t,
+                                     // K-major over s (B of Wv^T)
 constexpr uint32_t P_XK = 65536;     // [(X diag(e^G rk))_hi; _lo]
-constexpr uint32_t P_L = 81920;      // L fp32 [64][68]
-constexpr int LST = 68;
-constexpr uint32_t P_G = P_L + CK * LST * 4;  // double G[64]
+constexpr uint32_t P_LI = 81920;     // (I + L)^-1 fp32 (swizzled [64][64])
+constexpr uint32_t P_MS = 98304;     // 16x16 block products of the blocked inversion, [3][256]
+constexpr uint32_t P_G = P_MS + 3 * 256 * 4;  // double G[64]
 constexpr uint32_t P_F = P_G + CK * 8;        // float beta, rk, rq, xs, er [64] each
 constexpr uint32_t P_BAR = P_F + 5 * CK * 4;
 constexpr uint32_t PREP_SMEM = P_BAR + 16 + 1024;
 
 template <bool GATES_F64>
 __global__ void __launch_bounds__(128, 2)
-dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
-           const uint16_t *__restrict__ v, const void *__restrict__ ga,
+dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+           const __grid_constant__ CUtensorMap tv, const void *__restrict__ ga,
            const void *__restrict__ gb, const float *__restrict__ A_log,
            const float *__restrict__ dt_bias, Wsp ws, int T, int nqk, int nv, int n_chunks,
            uint32_t *status) {
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = align1024(smraw);
     uint8_t *AKQ = sm + P_AKQ, *VT = sm + P_VT, *XV = sm + P_XV, *XK = sm + P_XK;
-    float *Lf = reinterpret_cast<float *>(sm + P_L);
+    float *Lf = reinterpret_cast<float *>(sm + P_XV), *Li = reinterpret_cast<float *>(sm + P_LI);
+    float *Ms = reinterpret_cast<float *>(sm + P_MS);
     double *G = reinterpret_cast<double *>(sm + P_G);
     float *beta = reinterpret_cast<float *>(sm + P_F), *rk = beta + CK, *rq = rk + CK,
           *xs = rq + CK, *er = xs + CK;
@@ -141,38 +145,21 @@ dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
     const int qk = vh * nqk / nv, t0 = c * CK;
     const size_t blk = (size_t)vh * n_chunks + c;
 
+    // 1. raw q, k, v rows of the chunk into the swizzled tiles (TMA; rows past T read zero)
     if (tid == 0) {
         mbar_init(bar, 1);
         fence_barrier_init();
+        mbar_arrive_expect_tx(bar, 6 * 8192);
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+            tma_load_3d(AKQ + b * 16384, &tk, b * 64, qk, t0, bar);
+            tma_load_3d(AKQ + b * 16384 + 8192, &tq, b * 64, qk, t0, bar);
+            tma_load_3d(VT + b * 8192, &tv, b * 64, vh, t0, bar);
+        }
     }
     if (warp == 0) {
         tmem_alloc(tslot, 256);
         tmem_relinquish();
-    }
-    // 1. raw rows into the swizzled tiles; l2 norms from double sums (src/vx27_deltanet.c:51)
-    for (int i = warp; i < CK; i += 4) {
-        const int tt = t0 + i;
-        uint2 qv = make_uint2(0u, 0u), kv = qv, vv = qv;
-        if (tt < T) {
-            qv = *reinterpret_cast<const uint2 *>(q + ((size_t)tt * nqk + qk) * D + 4 * lane);
-            kv = *reinterpret_cast<const uint2 *>(k + ((size_t)tt * nqk + qk) * D + 4 * lane);
-            vv = *reinterpret_cast<const uint2 *>(v + ((size_t)tt * nv + vh) * D + 4 * lane);
-        }
-        const float k0 = bf16_to_f32(kv.x & 0xffffu), k1 = bf16_to_f32(kv.x >> 16),
-                    k2 = bf16_to_f32(kv.y & 0xffffu), k3 = bf16_to_f32(kv.y >> 16);
-        const float q0 = bf16_to_f32(qv.x & 0xffffu), q1 = bf16_to_f32(qv.x >> 16),
-                    q2 = bf16_to_f32(qv.y & 0xffffu), q3 = bf16_to_f32(qv.y >> 16);
-        double sk = (double)k0 * k0 + (double)k1 * k1 + (double)k2 * k2 + (double)k3 * k3;
-        double sq = (double)q0 * q0 + (double)q1 * q1 + (double)q2 * q2 + (double)q3 * q3;
-        sk = warp_sum_d(sk);
-        sq = warp_sum_d(sq);
-        *reinterpret_cast<uint2 *>(AKQ + swz(i, 4 * lane, 128)) = kv;
-        *reinterpret_cast<uint2 *>(AKQ + swz(CK + i, 4 * lane, 128)) = qv;
-        *reinterpret_cast<uint2 *>(VT + swz(i, 4 * lane, CK)) = vv;
-        if (lane == 0) {
-            rk[i] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)sk, 1e-6f)));
-            rq[i] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)sq, 1e-6f)));
-        }
     }
     // 2. gates (tokens past T are identity steps: beta = 0, g = 0)
     if (tid < CK) {
@@ -191,16 +178,42 @@ dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
         beta[tid] = (float)bt;
         G[tid] = gl;
     }
-    fence_proxy_async();
-    __syncthreads();
-    if (tid == 0) {
-        double acc = 0.0;
-        for (int t = 0; t < CK; t++) {
-            acc += G[t];
-            G[t] = acc;
-        }
+    __syncthreads();  // barrier initialised, gates written
+    bool ok = mbar_wait(bar, 0, status, VX_DEV_TIMEOUT_TMA);
+    // l2 norms from double sums of squares (src/vx27_deltanet.c:51-56), one row per thread:
+    // rows 0..63 of AKQ are k, rows 64..127 are q
+    {
+        double ss = 0.0;
+#pragma unroll
+        for (int b = 0; b < 2; b++)
+#pragma unroll
+            for (int pc = 0; pc < 8; pc++) {
+                const uint4 w4 = *reinterpret_cast<const uint4 *>(AKQ + b * 16384 + tid * 128 + pc * 16);
+                const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const double x0 = bf16_to_f32(w[e] & 0xffffu), x1 = bf16_to_f32(w[e] >> 16);
+                    ss += x0 * x0;
+                    ss += x1 * x1;
+                }
+            }
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, 1e-6f)));
+        if (tid < CK) rk[tid] = r;
+        else rq[tid - CK] = r;
     }
-    __syncthreads();
+    if (warp == 0) {  // G_t = sum_{s<=t} g_s: pairs per lane, then a warp scan of pair sums
+        const double g0 = G[2 * lane], g1 = G[2 * lane + 1];
+        double incl = g0 + g1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const double y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const double excl = incl - (g0 + g1);
+        G[2 * lane] = excl + g0;
+        G[2 * lane + 1] = incl;
+    }
+    ok = __syncthreads_and(ok);
     tc_fence_after();
     const uint32_t tbase = *tslot;
     const float qscale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
@@ -210,7 +223,7 @@ dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
         er[tid] = (float)exp(G[CK - 1] - G[tid]) * rk[tid];
         ws.scal[blk * 128 + 64 + tid] = gam * __fmul_rn(rq[tid], qscale);
     }
-    if (tid == 0) {
+    if (tid == 0 && ok) {
         ws.scal[blk * 128] = (float)exp(G[CK - 1]);
         // raw Q (rows 64..127 of each column block) -> the out kernel's B operand image
         bulk_s2g(ws.QB + blk * SZ_QB, AKQ + 8192, 8192);
@@ -228,6 +241,7 @@ dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
     }
     __syncthreads();  // er[] visible
     // 3. Kr^T = K^T diag(e^{G_C - G} rk) as hi/lo MN-major images (rows t, cols d)
+#pragma unroll 1
     for (int ch = tid; ch < 1024; ch += 128) {
         const int b = ch >> 9, t = (ch >> 3) & 63, pc = ch & 7;
         const int d0 = b * 64 + ((pc ^ (t & 7)) << 3);
@@ -248,7 +262,7 @@ dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
         *reinterpret_cast<uint4 *>(ws.KrL + blk * SZ_KR + ch * 16) =
             make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
-    bool ok = mbar_wait(bar, 0, status, VX_DEV_TIMEOUT_MMA);
+    if (ok) ok = mbar_wait(bar, 1, status, VX_DEV_TIMEOUT_MMA);
     ok = __syncthreads_and(ok);
     tc_fence_after();
     if (ok) {
@@ -260,7 +274,7 @@ dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
         const float sc_t = low ? beta[t] * rk[t] : __fmul_rn(rq[t], qscale);
         const uint32_t ta = tbase + ((uint32_t)(warp * 32) << 16);
         uint8_t *pm = ws.PmB + blk * SZ_PM;
-#pragma unroll
+#pragma unroll 1
         for (int c16 = 0; c16 < CK; c16 += 16) {
             float dv[16];
             tmem_ld16(ta + c16, dv);
@@ -274,7 +288,7 @@ dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
             if (low) {
 #pragma unroll
                 for (int j = 0; j < 16; j += 4)
-                    *reinterpret_cast<float4 *>(Lf + t * LST + c16 + j) =
+                    *reinterpret_cast<float4 *>(Lf + fsw(t, c16 + j)) =
                         make_float4(val[j], val[j + 1], val[j + 2], val[j + 3]);
             } else {
 #pragma unroll
@@ -298,35 +312,59 @@ dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
         }
         tc_fence_before();
         __syncthreads();
-        // 5. X = (I + L)^-1 diag(beta), one column per thread (forward substitution)
-        if (tid < CK) {
-            const int j = tid;
-            float x[CK];
+        // 5. Li = (I + L)^-1 by 16x16 blocks: the diagonal blocks by forward substitution
+        //    (warp w, one column per lane), then the off-diagonal blocks one block diagonal
+        //    at a time, Li_ij = -Li_ii sum_{k=j}^{i-1} L_ik Li_kj
+        if (lane < 16) {
+            const int o = warp * 16;
+            float x[16];
 #pragma unroll
-            for (int t2 = 0; t2 < CK; t2++) {
-                float a0 = (t2 == j) ? beta[t2] : 0.f, a1 = 0.f;
-                const float *Lr = Lf + t2 * LST;
+            for (int t2 = 0; t2 < 16; t2++) {
+                float acc = (t2 == lane) ? 1.f : 0.f;
 #pragma unroll
-                for (int s4 = 0; s4 < t2; s4 += 4) {
-                    const float4 l4 = *reinterpret_cast<const float4 *>(Lr + s4);
-                    a0 = fmaf(-l4.x, x[s4], a0);
-                    if (s4 + 1 < t2) a1 = fmaf(-l4.y, x[s4 + 1], a1);
-                    if (s4 + 2 < t2) a0 = fmaf(-l4.z, x[s4 + 2], a0);
-                    if (s4 + 3 < t2) a1 = fmaf(-l4.w, x[s4 + 3], a1);
-                }
-                x[t2] = a0 + a1;
+                for (int s2 = 0; s2 < t2; s2++) acc = fmaf(-Lf[fsw(o + t2, o + s2)], x[s2], acc);
+                x[t2] = acc;
+                Li[fsw(o + t2, o + lane)] = acc;
             }
-            const float xk = xs[j];
+        }
+        __syncthreads();
+#pragma unroll 1
+        for (int dg = 1; dg < 4; dg++) {
+            const int nb = 4 - dg;
+            for (int e = tid; e < nb * 256; e += 128) {
+                const int j = e >> 8, i = j + dg, r = (e >> 4) & 15, cc = e & 15;
+                float acc = 0.f;
+                for (int kb = j; kb < i; kb++)
 #pragma unroll
-            for (int t2 = 0; t2 < CK; t2++) {
-                uint16_t h, l;
-                split_bf16(x[t2], h, l);
-                st16(XV, swz(t2, j, 128), h);
-                st16(XV, swz(CK + t2, j, 128), l);
-                split_bf16(x[t2] * xk, h, l);
-                st16(XK, swz(t2, j, 128), h);
-                st16(XK, swz(CK + t2, j, 128), l);
+                    for (int kk = 0; kk < 16; kk++)
+                        acc = fmaf(Lf[fsw(16 * i + r, 16 * kb + kk)],
+                                   Li[fsw(16 * kb + kk, 16 * j + cc)], acc);
+                Ms[e] = acc;
             }
+            __syncthreads();
+            for (int e = tid; e < nb * 256; e += 128) {
+                const int j = e >> 8, i = j + dg, r = (e >> 4) & 15, cc = e & 15;
+                float acc = 0.f;
+#pragma unroll
+                for (int kk = 0; kk < 16; kk++)
+                    acc = fmaf(Li[fsw(16 * i + r, 16 * i + kk)], Ms[(j << 8) + kk * 16 + cc], acc);
+                Li[fsw(16 * i + r, 16 * j + cc)] = -acc;
+            }
+            __syncthreads();
+        }
+        // X = Li diag(beta) (lower triangle) -> [X_hi; X_lo] over L's space, and
+        // X diag(e^G rk) -> its hi/lo pair; a warp covers 32 columns s of one row t
+#pragma unroll 2
+        for (int e = tid; e < CK * CK; e += 128) {
+            const int t2 = e >> 6, sc = e & 63;
+            const float xv = sc <= t2 ? Li[fsw(t2, sc)] * beta[sc] : 0.f;
+            uint16_t h, l;
+            split_bf16(xv, h, l);
+            st16(XV, swz(t2, sc, 128), h);
+            st16(XV, swz(CK + t2, sc, 128), l);
+            split_bf16(xv * xs[sc], h, l);
+            st16(XK, swz(t2, sc, 128), h);
+            st16(XK, swz(CK + t2, sc, 128), l);
         }
         fence_proxy_async();
         __syncthreads();
@@ -344,22 +382,23 @@ dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
                          sdesc_sw128(smem_u32(XK) + kk * 32, 16, 1024), id, kk > 0);
             mma_commit(bar);
         }
-        ok = mbar_wait(bar, 1, status, VX_DEV_TIMEOUT_MMA);
+        ok = mbar_wait(bar, 0, status, VX_DEV_TIMEOUT_MMA);  // third phase
         if (tid == 0) bulk_wait_read0();  // the Q image copy has left AKQ
         ok = __syncthreads_and(ok);
         tc_fence_after();
         if (ok) {
-            // 7. Wv -> workspace fp32 [t][d]; Wk -> [Wk_hi; Wk_lo] staged in AKQ
+            // 7. Wv -> workspace fp32 [d/16][t][16]; Wk -> [Wk_hi; Wk_lo] staged in AKQ
             const int d = warp * 32 + lane;
             const uint32_t ta2 = tbase + ((uint32_t)(warp * 32) << 16);
             float *Wv = ws.Wv + blk * (CK * D);
-#pragma unroll
+#pragma unroll 1
             for (int c16 = 0; c16 < CK; c16 += 16) {
                 float a[16], b2[16];
                 tmem_ld16(ta2 + c16, a);
                 tmem_ld16(ta2 + 64 + c16, b2);
 #pragma unroll
-                for (int j = 0; j < 16; j++) Wv[(c16 + j) * D + d] = a[j] + b2[j];
+                for (int j = 0; j < 16; j++)
+                    Wv[(d >> 4) * (CK * 16) + (c16 + j) * 16 + (d & 15)] = a[j] + b2[j];
                 tmem_ld16(ta2 + 128 + c16, a);
                 tmem_ld16(ta2 + 192 + c16, b2);
 #pragma unroll
@@ -386,14 +425,19 @@ dn_prep_tc(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
 
 // ---- phase 2: the sequential state scan ---------------------------------------------------
 // CTA (column block cb, V head vh) owns state columns [cb*CB, cb*CB + CB). Warps 0-3 run
-// the epilogues and thread 0 issues the MMAs; warp 4 streams Wk and Kr^T tiles (two stages).
+// the epilogues and thread 0 issues the MMAs; warp 4 streams each chunk's Wk and Kr^T tiles,
+// the CTA's Wv columns and the chunk decay into a two-stage ring.
 //   MMA1: D1[128 x 2CB] = [Wk_hi; Wk_lo] [S_hi | S_lo]   (U = Wv - sum of the 4 quadrants)
 //   MMA2: D2[128 x 2CB] = Kr^T_hi [U_hi | U_lo] + Kr^T_lo [U_hi | U_lo]   (dS = both halves)
 template <int CB>
 struct ScanLayout {
     static constexpr int NB = 2 * CB;
-    static constexpr uint32_t STAGE = 65536;  // Wk 32K | Kr^T hi 16K | Kr^T lo 16K
-    static constexpr uint32_t SB = 2 * STAGE;                 // [S_hi; S_lo] over d: 2 blocks
+    // stage: Wk 32K | Kr^T hi 16K | Kr^T lo 16K | Wv [CB/16][64][16] fp32 | decay (16 B)
+    static constexpr uint32_t ST_WV = 65536;
+    static constexpr uint32_t ST_G = ST_WV + CB * 256;
+    static constexpr uint32_t STAGE_TX = ST_G + 16;
+    static constexpr uint32_t STAGE = ST_G + 1024;
+    static constexpr uint32_t SB = 2 * STAGE;                  // [S_hi; S_lo] over d: 2 blocks
     static constexpr uint32_t UB = SB + 2 * NB * 128;          // [U_hi; U_lo] over t: 1 block
     static constexpr uint32_t XCH = UB + NB * 128;             // float [CB/2][128]
     static constexpr uint32_t BAR = XCH + (CB / 2) * 128 * 4;  // full[2] empty[2] m1 m2
@@ -406,6 +450,7 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
     using Lay = ScanLayout<CB>;
     constexpr int NB = Lay::NB;
     constexpr int HC = CB / 2;
+    constexpr int JS = HC < 16 ? HC : 16;  // TMEM columns per load in the U epilogue
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = align1024(smraw);
     uint8_t *stg = sm, *SB = sm + Lay::SB, *UB = sm + Lay::UB;
@@ -439,10 +484,13 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
                 }
                 const size_t blk = (size_t)vh * n_chunks + c;
                 uint8_t *dst = stg + s * Lay::STAGE;
-                mbar_arrive_expect_tx(&bars[s], Lay::STAGE);
+                mbar_arrive_expect_tx(&bars[s], Lay::STAGE_TX);
                 bulk_g2s(dst, ws.WkA + blk * SZ_WKA, 32768, &bars[s]);
                 bulk_g2s(dst + 32768, ws.KrH + blk * SZ_KR, 16384, &bars[s]);
                 bulk_g2s(dst + 49152, ws.KrL + blk * SZ_KR, 16384, &bars[s]);
+                bulk_g2s(dst + Lay::ST_WV, ws.Wv + blk * (CK * D) + cb * CB * CK, CB * 256,
+                         &bars[s]);
+                bulk_g2s(dst + Lay::ST_G, ws.scal + blk * 128, 16, &bars[s]);
             }
         }
         return;
@@ -502,32 +550,38 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
                 bulk_commit();
             }
         }
-        // Wv (own half of the columns) and the chunk decay, ahead of the MMA
-        float wv[HC];
-        const float *wsrc = ws.Wv + blk * (CK * D) + t * D + cb * CB + jh;
-#pragma unroll
-        for (int j = 0; j < HC; j += 4) {
-            const float4 f = *reinterpret_cast<const float4 *>(wsrc + j);
-            wv[j] = f.x;
-            wv[j + 1] = f.y;
-            wv[j + 2] = f.z;
-            wv[j + 3] = f.w;
-        }
-        const float g63 = ws.scal[blk * 128];
         if (!*abort_ && !mbar_wait(&bars[4], c & 1, status, VX_DEV_TIMEOUT_MMA)) *abort_ = 1;
         tc_fence_after();
-        // quadrant sums: own half kept, the other half handed to the partner thread tid ^ 64
+        // U = Wv - (quadrant sums): own half kept, the other half handed to thread tid ^ 64
+        const float *wv_s = reinterpret_cast<const float *>(stage + Lay::ST_WV);
+        const float g63 = *reinterpret_cast<const float *>(stage + Lay::ST_G);
+        float wv[HC];
 #pragma unroll
-        for (int j0 = 0; j0 < HC; j0 += 16) {
-            float a[16], b2[16];
-            tmem_ld16(tD1 + jo + j0, a);
-            tmem_ld16(tD1 + CB + jo + j0, b2);
+        for (int j = 0; j < HC; j++) {
+            const int col = jh + j;
+            wv[j] = wv_s[(col >> 4) * (CK * 16) + t * 16 + (col & 15)];
+        }
 #pragma unroll
-            for (int j = 0; j < 16; j++) xch[(j0 + j) * 128 + (tid ^ 64)] = a[j] + b2[j];
-            tmem_ld16(tD1 + jh + j0, a);
-            tmem_ld16(tD1 + CB + jh + j0, b2);
+        for (int j0 = 0; j0 < HC; j0 += JS) {
+            float a[JS], b2[JS];
+            if constexpr (JS == 16) {
+                tmem_ld16(tD1 + jo + j0, a);
+                tmem_ld16(tD1 + CB + jo + j0, b2);
+            } else {
+                tmem_ld8(tD1 + jo + j0, a);
+                tmem_ld8(tD1 + CB + jo + j0, b2);
+            }
 #pragma unroll
-            for (int j = 0; j < 16; j++) wv[j0 + j] -= a[j] + b2[j];
+            for (int j = 0; j < JS; j++) xch[(j0 + j) * 128 + (tid ^ 64)] = a[j] + b2[j];
+            if constexpr (JS == 16) {
+                tmem_ld16(tD1 + jh + j0, a);
+                tmem_ld16(tD1 + CB + jh + j0, b2);
+            } else {
+                tmem_ld8(tD1 + jh + j0, a);
+                tmem_ld8(tD1 + CB + jh + j0, b2);
+            }
+#pragma unroll
+            for (int j = 0; j < JS; j++) wv[j0 + j] -= a[j] + b2[j];
         }
         if (tid == 0) bulk_wait_read0();  // the previous U image and this S0 image have left
         named_bar_sync(2, 128);
@@ -706,8 +760,8 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
     const bool g64 = flags & VX27_F_GATES_F64;
     if (!q || !k || !v || !a || !b || !S || !o || !workspace || (!g64 && (!A_log || !dt_bias)))
         return fail(err, errlen, "%s: null pointer argument", fn);
-    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 7)
-        return fail(err, errlen, "%s: q, k and v must be 8-byte aligned", fn);
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15)
+        return fail(err, errlen, "%s: q, k and v must be 16-byte aligned", fn);
     if ((uintptr_t)workspace & 15)
         return fail(err, errlen, "%s: workspace must be 16-byte aligned", fn);
     const size_t need = vx27_deltanet_prefill_workspace_size(T, nqk, nv, hd);
@@ -718,7 +772,15 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
     uint32_t *status = dev_status();
     if (!status) return fail(err, errlen, "%s: device status word unavailable", fn);
     Wsp ws = wsp_views((uint8_t *)workspace, (size_t)n_chunks * nv);
-    const auto *q16 = (const uint16_t *)q, *k16 = (const uint16_t *)k, *v16 = (const uint16_t *)v;
+    // q, k as [T][nqk][128] and v as [T][nv][128]; one box = 64 tokens x 64 dims of one head
+    CUtensorMap tq, tk, tv;
+    if (make_tmap_bf16_3d(&tq, q, D, nqk, T, D * 2, (uint64_t)nqk * D * 2, 64, 1, CK, err,
+                          errlen) ||
+        make_tmap_bf16_3d(&tk, k, D, nqk, T, D * 2, (uint64_t)nqk * D * 2, 64, 1, CK, err,
+                          errlen) ||
+        make_tmap_bf16_3d(&tv, v, D, nv, T, D * 2, (uint64_t)nv * D * 2, 64, 1, CK, err,
+                          errlen))
+        return -1;
 
     if (g64) {
         static bool attr = false;
@@ -727,7 +789,7 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
             attr = true;
         }
         dn_prep_tc<true><<<dim3(n_chunks, nv), 128, PREP_SMEM, st>>>(
-            q16, k16, v16, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
+            tq, tk, tv, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
     } else {
         static bool attr = false;
         if (!attr) {
@@ -735,25 +797,25 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
             attr = true;
         }
         dn_prep_tc<false><<<dim3(n_chunks, nv), 128, PREP_SMEM, st>>>(
-            q16, k16, v16, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
+            tq, tk, tv, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
     }
     VX_CK(cudaGetLastError());
-    // scan: 32 state columns per CTA while that grid fits in one wave, else 64
-    if (nv * (D / 32) <= num_sms()) {
+    // scan: 16 state columns per CTA while that grid fits in one wave, else 32
+    if (nv * (D / 16) <= num_sms()) {
+        static bool attr = false;
+        if (!attr) {
+            if (set_smem(dn_scan_tc<16>, ScanLayout<16>::SMEM, err, errlen)) return -1;
+            attr = true;
+        }
+        dn_scan_tc<16><<<dim3(D / 16, nv), 160, ScanLayout<16>::SMEM, st>>>(ws, S, n_chunks,
+                                                                             status);
+    } else {
         static bool attr = false;
         if (!attr) {
             if (set_smem(dn_scan_tc<32>, ScanLayout<32>::SMEM, err, errlen)) return -1;
             attr = true;
         }
         dn_scan_tc<32><<<dim3(D / 32, nv), 160, ScanLayout<32>::SMEM, st>>>(ws, S, n_chunks,
-                                                                             status);
-    } else {
-        static bool attr = false;
-        if (!attr) {
-            if (set_smem(dn_scan_tc<64>, ScanLayout<64>::SMEM, err, errlen)) return -1;
-            attr = true;
-        }
-        dn_scan_tc<64><<<dim3(D / 64, nv), 160, ScanLayout<64>::SMEM, st>>>(ws, S, n_chunks,
                                                                              status);
     }
     VX_CK(cudaGetLastError());

@@ -473,4 +473,29 @@ int make_tmap_bf16_2d(CUtensorMap *map, const void *base, uint64_t rows, uint64_
     return 0;
 }
 
+int make_tmap_bf16_3d(CUtensorMap *map, const void *base, uint64_t n0, uint64_t n1,
+                      uint64_t n2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1,
+                      uint32_t b2, char *err, size_t errlen) {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess || !p)
+            return fail(err, errlen, "cuTensorMapEncodeTiled unavailable from the driver");
+        fn = (EncodeTiledFn)p;
+    }
+    if (((uintptr_t)base & 15) || (s1 & 15) || (s2 & 15))
+        return fail(err, errlen, "tensor map: base and strides must be 16-byte aligned");
+    const cuuint64_t dims[3] = {n0, n1, n2};
+    const cuuint64_t strides[2] = {s1, s2};
+    const cuuint32_t box[3] = {b0, b1, b2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(err, errlen, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
 }  // namespace vx27

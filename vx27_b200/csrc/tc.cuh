@@ -44,6 +44,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// 8 consecutive fp32 columns (same lane rule as tmem_ld16).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v) {
+    uint32_t r[8];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
 // Store 16 fp32 columns of this thread's TMEM lane; completes before the next
 // tcgen05.wait::st.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float *v) {
@@ -116,5 +129,19 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
 int make_tmap_bf16_2d(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
                       uint64_t row_pitch_bytes, uint32_t box_cols, uint32_t box_rows,
                       char *err, size_t errlen);
+// Host: 3-D bf16 tensor map, dims {n0 (contiguous), n1, n2} with byte strides s1, s2 of
+// dims 1 and 2, box {b0, b1, b2}, 128-byte swizzle, zero fill out of bounds.
+int make_tmap_bf16_3d(CUtensorMap *map, const void *base, uint64_t n0, uint64_t n1,
+                      uint64_t n2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1,
+                      uint32_t b2, char *err, size_t errlen);
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, int x, int y,
+                                            int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_u32(smem_dst)), "l"((uint64_t)map), "r"(x), "r"(y), "r"(z),
+          "r"(smem_u32(bar))
+        : "memory");
+}
 
 }  // namespace vx27
