@@ -53,6 +53,19 @@ __host__ __device__ __forceinline__ uint16_t f32_to_bf16(float x) {
     return (uint16_t)(u >> 16);
 }
 
+// Two floats to a packed bf16x2 word (round to nearest even), lo in bits 0-15.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+// 2^x with the SFU instruction (relative error of a few ulp; 2^-inf = 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // ---- device-side waits ------------------------------------------------------
 // Every spin in this library is bounded; on timeout the kernel records a code in
 // the per-device status word (dev_status(), read by vx27cuda_device_status) and

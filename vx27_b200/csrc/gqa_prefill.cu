@@ -4,13 +4,16 @@
 //                 table), q -> bf16 Qn[nq][T][256], k/v -> the bf16 KV cache slots p0 + t
 //                 (the cache the decode continues from); src/vx27_qfwd.c:339-346 per token
 //   main kernel   one CTA per (128-query tile, query head), flash-attention forward:
-//     warp 0      TMA: the Q tile (128 x 256, resident) and 64-key K / V tiles, two stages
-//     warp 1      tcgen05.mma: S = Q K^T (128 x 64, TMEM, double buffered) and
-//                 O += P V (128 x 256 in TMEM, V read as an MN-major operand)
-//     warps 2-5   one thread per query row (its TMEM lane): causal mask, running max in
-//                 log2 units, p = 2^(x - m) as bf16 rows of P in shared memory; O is
-//                 rescaled in TMEM only when a row's max grows by more than 2^8 (lazy
-//                 rescale); epilogue O / l * sigmoid(gate).
+//     warp 0      TMA: the Q tile (128 x 256, resident); 128-key K tiles as four 64-dim
+//                 chunks and V tiles as four 32-key chunks, through one ring of 16 KB
+//                 slots filled in the order the MMAs consume them
+//     warp 1      tcgen05.mma: S = Q K^T (128 x 128 in TMEM) and O += P V (128 x 256 in
+//                 TMEM, V read as an MN-major operand), issued as S(j+1) then O += P(j) V(j)
+//     warps 2-9   two threads per query row (its TMEM lane), one per half of the keys and of
+//                 the output columns: causal mask, running max in log2 units (the halves
+//                 meet in spare TMEM columns), p = 2^(x - m) as bf16 rows of P in shared
+//                 memory; O is rescaled in TMEM only when a row's max grows by more than
+//                 2^8 (lazy rescale); epilogue O / l * sigmoid(gate).
 // Query tiles are issued longest first; the six query heads of a KV head run on
 // neighbouring CTAs so their K/V tiles are served from L2.
 #include <math.h>
@@ -23,17 +26,16 @@ namespace {
 
 constexpr int HDP = 256;
 constexpr int QT = 128;          // queries per CTA
-constexpr int KT = 64;           // keys per tile
-constexpr int PF_THREADS = 192;
+constexpr int KT = 128;          // keys per tile
+constexpr int NS = 8;            // ring slots of 16 KB (one K tile + one V tile)
+constexpr int PF_THREADS = 320;  // TMA warp, MMA warp, 8 softmax warps
 constexpr float RESCALE_LOG2 = 8.0f;
 
 struct PfSmem {
     uint8_t q[4][QT * 128];      // Q tile, 4 chunks of [128 rows x 64 dims], 128B swizzle
-    uint8_t k[2][4][KT * 128];   // K stages
-    uint8_t v[2][4][KT * 128];   // V stages
-    uint8_t p[2][QT * 128];      // P rows (64 keys, bf16), two buffers
-    uint64_t qfull, kfull[2], kempty[2], vfull[2], vempty[2];
-    uint64_t s_full[2], s_empty[2], p_full[2], pv_done[2], o_final, mma_done;
+    uint8_t ring[NS][16384];     // K chunk [128 keys x 64 dims] or V chunk [32 keys x 256 dims]
+    uint8_t p[2][QT * 128];      // P [128 rows x 128 keys] bf16 as two 64-key column blocks
+    uint64_t qfull, full[NS], empty[NS], s_full, s_empty, p_full, pv_done, o_final, mma_done;
     uint32_t tmem_base;
     int abort;
 };
@@ -154,12 +156,14 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
 
     if (tid == 0) {
         mbar_init(&sm.qfull, 1);
-        for (int i = 0; i < 2; i++) {
-            mbar_init(&sm.kfull[i], 1); mbar_init(&sm.kempty[i], 1);
-            mbar_init(&sm.vfull[i], 1); mbar_init(&sm.vempty[i], 1);
-            mbar_init(&sm.s_full[i], 1); mbar_init(&sm.s_empty[i], 128);
-            mbar_init(&sm.p_full[i], 128); mbar_init(&sm.pv_done[i], 1);
+        for (int i = 0; i < NS; i++) {
+            mbar_init(&sm.full[i], 1);
+            mbar_init(&sm.empty[i], 1);
         }
+        mbar_init(&sm.s_full, 1);
+        mbar_init(&sm.s_empty, 256);
+        mbar_init(&sm.p_full, 256);
+        mbar_init(&sm.pv_done, 1);
         mbar_init(&sm.o_final, 1);
         mbar_init(&sm.mma_done, 1);
         sm.abort = 0;
@@ -173,25 +177,35 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
-    const uint32_t tS = tmem, tO = tmem + 128;
+    const uint32_t tS = tmem, tO = tmem + 128, tX = tmem + 384;
 
     if (warp == 0) {
-        if (lane == 0) {  // ---- TMA producer
+        if (lane == 0) {  // ---- TMA producer: K(m) then V(m-1), as the MMA warp consumes them
             mbar_arrive_expect_tx(&sm.qfull, 4 * QT * 128);
             for (int c = 0; c < 4; c++) tma_load_2d(sm.q[c], &tmq, c * 64, h * T + t0, &sm.qfull);
             const int krow0 = kvh * cap;  // rows of this KV head in the [nkv*cap][256] maps
-            for (int j = 0; j < n_kt; j++) {
-                const int st = j & 1;
-                if (j >= 2 && !pf_wait(&sm.kempty[st], ((j >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
-                    break;
-                mbar_arrive_expect_tx(&sm.kfull[st], 4 * KT * 128);
-                for (int c = 0; c < 4; c++)
-                    tma_load_2d(sm.k[st][c], &tmk, c * 64, krow0 + j * KT, &sm.kfull[st]);
-                if (j >= 2 && !pf_wait(&sm.vempty[st], ((j >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
-                    break;
-                mbar_arrive_expect_tx(&sm.vfull[st], 4 * KT * 128);
-                for (int c = 0; c < 4; c++)
-                    tma_load_2d(sm.v[st][c], &tmv, c * 64, krow0 + j * KT, &sm.vfull[st]);
+            uint32_t n = 0;
+            bool ok = true;
+            for (int m = 0; m <= n_kt && ok; m++) {
+                for (int part = 0; part < 2 && ok; part++) {
+                    if ((part == 0 && m == n_kt) || (part == 1 && m == 0)) continue;
+                    for (int c = 0; c < 4; c++, n++) {
+                        const uint32_t s2 = n % NS;
+                        if (n >= NS && !pf_wait(&sm.empty[s2], ((n / NS) - 1) & 1, sm, status,
+                                                VX_DEV_TIMEOUT_TMA)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&sm.full[s2], 16384);
+                        if (part == 0) {  // K(m): dims [64c, 64c + 64) of 128 keys
+                            tma_load_2d(sm.ring[s2], &tmk, c * 64, krow0 + m * KT, &sm.full[s2]);
+                        } else {          // V(m-1): keys [32c, 32c + 32), all 256 dims
+                            for (int a2 = 0; a2 < 4; a2++)
+                                tma_load_2d(sm.ring[s2] + a2 * 4096, &tmv, a2 * 64,
+                                            krow0 + (m - 1) * KT + 32 * c, &sm.full[s2]);
+                        }
+                    }
+                }
             }
         }
     } else if (warp == 1) {
@@ -199,40 +213,46 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             const uint32_t id1 = idesc_bf16(128, KT, false, false);
             const uint32_t id2 = idesc_bf16(128, HDP, false, true);
             bool ok = pf_wait(&sm.qfull, 0, sm, status, VX_DEV_TIMEOUT_TMA);
-            const uint32_t q0 = smem_u32(sm.q[0]);
-            for (int j = 0; j <= n_kt && ok; j++) {
-                if (j < n_kt) {
-                    const int b = j & 1;
-                    if (j >= 2) ok = pf_wait(&sm.s_empty[b], ((j >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                    ok = ok && pf_wait(&sm.kfull[b], (j >> 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t kb = smem_u32(sm.k[b][0]);
-#pragma unroll
-                    for (int c = 0; c < 4; c++)
+            uint32_t n = 0;
+            for (int m = 0; m <= n_kt && ok; m++) {
+                if (m < n_kt) {  // S = Q K(m)^T once the softmax has read S(m-1)
+                    if (m >= 1) ok = pf_wait(&sm.s_empty, (m - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                    for (int c = 0; c < 4 && ok; c++, n++) {
+                        const uint32_t s2 = n % NS;
+                        ok = pf_wait(&sm.full[s2], (n / NS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint32_t qb = smem_u32(sm.q[c]), kb = smem_u32(sm.ring[s2]);
 #pragma unroll
                         for (int kk = 0; kk < 4; kk++)
-                            mma_bf16(tS + b * KT,
-                                     sdesc_sw128(q0 + c * QT * 128 + kk * 32, 16, 1024),
-                                     sdesc_sw128(kb + c * KT * 128 + kk * 32, 16, 1024), id1,
-                                     (c | kk) != 0);
-                    mma_commit(&sm.kempty[b]);
-                    mma_commit(&sm.s_full[b]);
-                }
-                if (j >= 1) {
-                    const int t = j - 1, b = t & 1;
-                    ok = pf_wait(&sm.p_full[b], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA) &&
-                         pf_wait(&sm.vfull[b], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+                            mma_bf16(tS, sdesc_sw128(qb + kk * 32, 16, 1024),
+                                     sdesc_sw128(kb + kk * 32, 16, 1024), id1, (c | kk) != 0);
+                        mma_commit(&sm.empty[s2]);
+                    }
                     if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t pb = smem_u32(sm.p[b]), vb = smem_u32(sm.v[b][0]);
+                    mma_commit(&sm.s_full);
+                }
+                if (m >= 1) {  // O += P(m-1) V(m-1)
+                    const int t = m - 1;
+                    ok = pf_wait(&sm.p_full, t & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                    for (int c = 0; c < 4 && ok; c++, n++) {
+                        const uint32_t s2 = n % NS;
+                        ok = pf_wait(&sm.full[s2], (n / NS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint32_t vb = smem_u32(sm.ring[s2]);
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++)
-                        mma_bf16(tO, sdesc_sw128(pb + kk * 32, 16, 1024),
-                                 sdesc_sw128(vb + kk * 2048, KT * 128, 1024), id2,
-                                 (t > 0 || kk > 0) ? 1u : 0u);
-                    mma_commit(&sm.vempty[b]);
-                    mma_commit(&sm.pv_done[b]);
+                        for (int k2 = 0; k2 < 2; k2++) {
+                            const int kk = 2 * c + k2;  // 16-key step of the 128-key tile
+                            mma_bf16(tO,
+                                     sdesc_sw128(smem_u32(sm.p[kk >> 2]) + (kk & 3) * 32, 16, 1024),
+                                     sdesc_sw128(vb + k2 * 2048, 32 * 128, 1024), id2,
+                                     (t > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        mma_commit(&sm.empty[s2]);
+                    }
+                    if (!ok) break;
+                    mma_commit(&sm.pv_done);
                     if (t == n_kt - 1) mma_commit(&sm.o_final);
                 }
             }
@@ -240,93 +260,126 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             pf_wait(&sm.mma_done, 0, sm, status, VX_DEV_TIMEOUT_MMA);
         }
     } else {
-        // ---- softmax / rescale / epilogue: thread = query row r of the tile
+        // ---- softmax / rescale / epilogue: two threads per query row r of the tile (its
+        // TMEM lane), one per half of the 128 keys of a tile and of the 256 output columns
         const int q4 = warp & 3;
+        const int hf = (warp - 2) >> 2;
         const int r = q4 * 32 + lane;
         const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
         const int qpos = p0 + t0 + r;
         const float sc2 = 1.4426950408889634f * 0.0625f;  // log2(e) / sqrt(256)
         float m_run = -INFINITY, l_run = 0.0f;
         bool ok = true;
-        for (int j = 0; j < n_kt && ok; j++) {
-            const int b = j & 1;
-            ok = pf_wait(&sm.s_full[b], (j >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+        // every softmax warp runs all n_kt iterations and the named barrier of each, also
+        // after a failed wait (then skipping the tensor-memory work), so none is left waiting
+        for (int j = 0; j < n_kt; j++) {
+            if (ok) ok = pf_wait(&sm.s_full, j & 1, sm, status, VX_DEV_TIMEOUT_MMA);
             ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld/st are warp-wide
-            if (!ok) break;
-            tc_fence_after();
-            float s[KT];
+            constexpr int HK = KT / 2;
+            float s[HK];
+            float mloc = -INFINITY;
+            if (ok) {
+                tc_fence_after();
 #pragma unroll
-            for (int i = 0; i < KT / 16; i++) tmem_ld16(tS + lane_off + b * KT + 16 * i, s + 16 * i);
-            tc_fence_before();
-            mbar_arrive(&sm.s_empty[b]);
-            const int kbase = j * KT;
-            float mt = -INFINITY;
+                for (int i = 0; i < HK / 16; i++)
+                    tmem_ld16(tS + lane_off + hf * HK + 16 * i, s + 16 * i);
+                tc_fence_before();
+                mbar_arrive(&sm.s_empty);
+                const int kbase = j * KT + hf * HK;
+                // causal mask only on tiles reaching past the tile's first query (CTA-uniform)
+                if (j * KT + KT - 1 > p0 + t0) {
 #pragma unroll
-            for (int c = 0; c < KT; c++) {
-                s[c] = (kbase + c <= qpos) ? s[c] * sc2 : -INFINITY;
-                mt = fmaxf(mt, s[c]);
+                    for (int c = 0; c < HK; c++)
+                        if (kbase + c > qpos) s[c] = -INFINITY;
+                }
+                // row max over this half as a tree
+                float mx[16];
+#pragma unroll
+                for (int i = 0; i < 16; i++)
+                    mx[i] = fmaxf(fmaxf(s[4 * i], s[4 * i + 1]), fmaxf(s[4 * i + 2], s[4 * i + 3]));
+#pragma unroll
+                for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+                    for (int i = 0; i < w; i++) mx[i] = fmaxf(mx[i], mx[i + w]);
+                mloc = mx[0];
             }
+            // ... and over both halves: the two threads of a row share its TMEM lane, so the
+            // halves meet in spare columns (tile parity, half) past S and O
+            tmem_st1(tX + lane_off + 2 * (j & 1) + hf, mloc);
+            tmem_st_wait();
+            tc_fence_before();
+            named_bar_sync(1, 256);
+            tc_fence_after();
+            const float mpart = tmem_ld1(tX + lane_off + 2 * (j & 1) + (hf ^ 1));
+            if (!ok) continue;
+            const float mt = fmaxf(mloc, mpart) * sc2;
             float alpha = 1.0f;
             const bool grow = mt > m_run + RESCALE_LOG2;
             if (grow) {
                 alpha = (m_run == -INFINITY) ? 0.0f : exp2f(m_run - mt);
                 m_run = mt;
             }
-            // rescale this warp's O rows when one of its rows raised its max (not on the
-            // first tile of a row, where O holds nothing yet)
+            // P and O are free once O += P(j-1) V(j-1) is done
+            if (j >= 1) {
+                ok = pf_wait(&sm.pv_done, (j - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) continue;
+            }
+            // rescale this warp's half of its O rows when one of its rows raised its max
+            // (not on the first tile of a row, where O holds nothing yet)
             const bool need = grow && alpha > 0.0f;
             if (__any_sync(0xffffffffu, need)) {
-                ok = pf_wait(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, sm, status,
-                             VX_DEV_TIMEOUT_MMA);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
                 tc_fence_after();
 #pragma unroll 1
-                for (int i = 0; i < HDP / 16; i++) {
+                for (int i = 0; i < HDP / 32; i++) {
                     float o[16];
-                    tmem_ld16(tO + lane_off + 16 * i, o);
+                    const uint32_t ta = tO + lane_off + hf * (HDP / 2) + 16 * i;
+                    tmem_ld16(ta, o);
 #pragma unroll
                     for (int e = 0; e < 16; e++) o[e] *= alpha;
-                    tmem_st16(tO + lane_off + 16 * i, o);
+                    tmem_st16(ta, o);
                 }
                 tmem_st_wait();
                 tc_fence_before();
             }
-            if (j >= 2) {  // P buffer b is free once P V of tile j-2 is done
-                ok = pf_wait(&sm.pv_done[b], ((j >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
-            }
-            float lsum = 0.0f;
-            uint8_t *prow = sm.p[b] + r * 128;
+            float ls[4] = {0.f, 0.f, 0.f, 0.f};
+            uint8_t *prow = sm.p[hf] + r * 128;
+            const float nm = -m_run;
 #pragma unroll
             for (int u = 0; u < 8; u++) {
                 uint32_t w4[4];
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const float pa = exp2f(s[u * 8 + 2 * e] - m_run);
-                    const float pb = exp2f(s[u * 8 + 2 * e + 1] - m_run);
-                    lsum += pa + pb;
-                    w4[e] = (uint32_t)f32_to_bf16(pa) | ((uint32_t)f32_to_bf16(pb) << 16);
+                    const float pa = ex2_approx(fmaf(s[u * 8 + 2 * e], sc2, nm));
+                    const float pb = ex2_approx(fmaf(s[u * 8 + 2 * e + 1], sc2, nm));
+                    ls[e] += pa + pb;
+                    w4[e] = pack_bf16x2(pa, pb);
                 }
                 *reinterpret_cast<uint4 *>(prow + (((u ^ (r & 7)) & 7) << 4)) =
                     make_uint4(w4[0], w4[1], w4[2], w4[3]);
             }
-            l_run = fmaf(l_run, alpha, lsum);
+            l_run = fmaf(l_run, alpha, (ls[0] + ls[1]) + (ls[2] + ls[3]));
             fence_proxy_async();
-            mbar_arrive(&sm.p_full[b]);
+            mbar_arrive(&sm.p_full);
         }
+        // the row sum is the sum of both halves' partial sums (same maxima, same rescales)
+        tmem_st1(tX + lane_off + 4 + hf, l_run);
+        tmem_st_wait();
+        tc_fence_before();
+        named_bar_sync(1, 256);
+        tc_fence_after();
+        const float l_row = l_run + tmem_ld1(tX + lane_off + 4 + (hf ^ 1));
         if (ok) ok = pf_wait(&sm.o_final, 0, sm, status, VX_DEV_TIMEOUT_MMA);
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
             tc_fence_after();
             const int t = t0 + r;
-            const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-            const size_t base = ((size_t)t * nq + h) * HDP;
+            const float inv = l_row > 0.0f ? 1.0f / l_row : 0.0f;
+            const size_t base = ((size_t)t * nq + h) * HDP + hf * (HDP / 2);
 #pragma unroll 1
-            for (int i = 0; i < HDP / 16; i++) {
+            for (int i = 0; i < HDP / 32; i++) {
                 float o[16];
-                tmem_ld16(tO + lane_off + 16 * i, o);
+                tmem_ld16(tO + lane_off + hf * (HDP / 2) + 16 * i, o);
                 if (t < T) {
 #pragma unroll
                     for (int e = 0; e < 16; e++) {
@@ -422,7 +475,7 @@ extern "C" int vx27_gqa_prefill(const void *q_in, const void *k_in, const void *
     CUtensorMap mq, mk, mv;
     if (make_tmap_bf16_2d(&mq, qn, (uint64_t)nq * T, HDP, HDP * 2, 64, QT, err, errlen) ||
         make_tmap_bf16_2d(&mk, k_cache, (uint64_t)nkv * cap, HDP, HDP * 2, 64, KT, err, errlen) ||
-        make_tmap_bf16_2d(&mv, v_cache, (uint64_t)nkv * cap, HDP, HDP * 2, 64, KT, err, errlen))
+        make_tmap_bf16_2d(&mv, v_cache, (uint64_t)nkv * cap, HDP, HDP * 2, 64, 32, err, errlen))
         return -1;
     const bool o = flags & VX27_F_OUT_BF16;
     if (a && o) return launch_attn<true, true>(mq, mk, mv, gate, out, T, p0, nq, nkv, cap, st, err, errlen);
