@@ -372,22 +372,78 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
         if (ok) ok = pf_wait(&sm.o_final, 0, sm, status, VX_DEV_TIMEOUT_MMA);
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
+            // O / l into a row-major fp32 staging tile over the (now idle) slot ring, 16-byte
+            // chunks of a row XOR-swizzled by the row so a warp's stores spread over banks
             tc_fence_after();
-            const int t = t0 + r;
             const float inv = l_row > 0.0f ? 1.0f / l_row : 0.0f;
-            const size_t base = ((size_t)t * nq + h) * HDP + hf * (HDP / 2);
+            float4 *row = reinterpret_cast<float4 *>(sm.ring[0]) + r * (HDP / 4);
 #pragma unroll 1
             for (int i = 0; i < HDP / 32; i++) {
                 float o[16];
                 tmem_ld16(tO + lane_off + hf * (HDP / 2) + 16 * i, o);
-                if (t < T) {
 #pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        const float g = act_ld<ACT_BF16>(gate, base + 16 * i + e);
-                        act_st<OUT_BF16>(out, base + 16 * i + e,
-                                         o[e] * inv * (1.0f / (1.0f + expf(-g))));
-                    }
+                for (int k = 0; k < 4; k++) {
+                    const int ch = (hf * (HDP / 2) + 16 * i) / 4 + k;
+                    row[ch ^ (r & 7)] = make_float4(o[4 * k] * inv, o[4 * k + 1] * inv,
+                                                    o[4 * k + 2] * inv, o[4 * k + 3] * inv);
                 }
+            }
+        } else {
+            *(volatile int *)&sm.abort = 1;
+        }
+    }
+    __syncthreads();
+    if (!*(volatile int *)&sm.abort) {
+        // gated output rows with coalesced 16-byte loads of the gate and stores of the output
+        constexpr int VEC = OUT_BF16 ? 8 : 4;
+        constexpr int PER_ROW = HDP / VEC;
+        const float4 *stage = reinterpret_cast<const float4 *>(sm.ring[0]);
+        for (int it = tid; it < QT * PER_ROW; it += PF_THREADS) {
+            const int rr = it / PER_ROW, c0 = (it % PER_ROW) * VEC;
+            const int t = t0 + rr;
+            if (t >= T) continue;
+            float o[VEC], g[VEC];
+#pragma unroll
+            for (int k = 0; k < VEC / 4; k++) {
+                const float4 f = stage[rr * (HDP / 4) + ((c0 / 4 + k) ^ (rr & 7))];
+                o[4 * k] = f.x; o[4 * k + 1] = f.y; o[4 * k + 2] = f.z; o[4 * k + 3] = f.w;
+            }
+            const size_t base = ((size_t)t * nq + h) * HDP + c0;
+            if constexpr (ACT_BF16) {
+                const uint16_t *gp = static_cast<const uint16_t *>(gate) + base;
+                uint32_t w[VEC / 2];
+                if constexpr (VEC == 8) {
+                    const uint4 v4 = *reinterpret_cast<const uint4 *>(gp);
+                    w[0] = v4.x; w[1] = v4.y; w[2] = v4.z; w[3] = v4.w;
+                } else {
+                    const uint2 v2 = *reinterpret_cast<const uint2 *>(gp);
+                    w[0] = v2.x; w[1] = v2.y;
+                }
+#pragma unroll
+                for (int k = 0; k < VEC / 2; k++) {
+                    g[2 * k] = bf16_to_f32(w[k] & 0xffffu);
+                    g[2 * k + 1] = bf16_to_f32(w[k] >> 16);
+                }
+            } else {
+                const float4 *gp = reinterpret_cast<const float4 *>(static_cast<const float *>(gate) + base);
+#pragma unroll
+                for (int k = 0; k < VEC / 4; k++) {
+                    const float4 f = gp[k];
+                    g[4 * k] = f.x; g[4 * k + 1] = f.y; g[4 * k + 2] = f.z; g[4 * k + 3] = f.w;
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < VEC; e++) o[e] = o[e] * (1.0f / (1.0f + expf(-g[e])));
+            if constexpr (OUT_BF16) {
+                uint32_t w[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    w[k] = (uint32_t)f32_to_bf16(o[2 * k]) | ((uint32_t)f32_to_bf16(o[2 * k + 1]) << 16);
+                *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out) + base) =
+                    make_uint4(w[0], w[1], w[2], w[3]);
+            } else {
+                *reinterpret_cast<float4 *>(static_cast<float *>(out) + base) =
+                    make_float4(o[0], o[1], o[2], o[3]);
             }
         }
     }
@@ -447,6 +503,8 @@ extern "C" int vx27_gqa_prefill(const void *q_in, const void *k_in, const void *
     if (!q_in || !k_in || !v_in || !gate || !q_norm_w || !k_norm_w || !k_cache || !v_cache ||
         !out || !workspace || (rope_dim && !rope_table))
         return fail(err, errlen, "%s: null pointer argument", fn);
+    if (((uintptr_t)gate | (uintptr_t)out) & 15)
+        return fail(err, errlen, "%s: gate and out must be 16-byte aligned", fn);
     if (workspace_bytes < vx27_gqa_prefill_workspace_size(T, nq, hd))
         return fail(err, errlen, "%s: workspace of %zu bytes, need %zu", fn, workspace_bytes,
                     vx27_gqa_prefill_workspace_size(T, nq, hd));
