@@ -27,18 +27,29 @@ namespace {
 constexpr int HDP = 256;
 constexpr int QT = 128;          // queries per CTA
 constexpr int KT = 128;          // keys per tile
-constexpr int NS = 8;            // ring slots of 16 KB (one K tile + one V tile)
-constexpr int PF_THREADS = 320;  // TMA warp, MMA warp, 8 softmax warps
+constexpr int NS = 6;            // ring slots of 16 KB
+constexpr int PF_THREADS = 352;  // TMA warp, S-MMA warp, 8 softmax warps, O-MMA warp
 constexpr float RESCALE_LOG2 = 8.0f;
 
 struct PfSmem {
     uint8_t q[4][QT * 128];      // Q tile, 4 chunks of [128 rows x 64 dims], 128B swizzle
     uint8_t ring[NS][16384];     // K chunk [128 keys x 64 dims] or V chunk [32 keys x 256 dims]
-    uint8_t p[2][QT * 128];      // P [128 rows x 128 keys] bf16 as two 64-key column blocks
-    uint64_t qfull, full[NS], empty[NS], s_full, s_empty, p_full, pv_done, o_final, mma_done;
+    uint8_t p[2][2][QT * 128];   // P [128 rows x 128 keys] bf16 as two 64-key column blocks,
+                                 // two buffers (tile parity)
+    uint64_t qfull, full[NS], empty[NS], s_full, s_empty, p_full[2], pv_done[2], o_final,
+        mma_done, qk_done;
     uint32_t tmem_base;
     int abort;
 };
+
+// Ring fill order: K(0), then per step m = 1..n_kt: K(m) (if m < n_kt), V(m-1); four chunks
+// each. Position of chunk c of K(m) and of V(t) in that sequence:
+__device__ __forceinline__ uint32_t ring_pos_k(int m, int c) {
+    return (m == 0 ? 0u : 8u * m - 4u) + c;
+}
+__device__ __forceinline__ uint32_t ring_pos_v(int t, int c, int n_kt) {
+    return 8u * t + (t + 1 < n_kt ? 8u : 4u) + c;
+}
 
 __device__ __forceinline__ uint64_t pf_timer() {
     uint64_t t;
@@ -162,10 +173,13 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
         }
         mbar_init(&sm.s_full, 1);
         mbar_init(&sm.s_empty, 256);
-        mbar_init(&sm.p_full, 256);
-        mbar_init(&sm.pv_done, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&sm.p_full[i], 256);
+            mbar_init(&sm.pv_done[i], 1);
+        }
         mbar_init(&sm.o_final, 1);
         mbar_init(&sm.mma_done, 1);
+        mbar_init(&sm.qk_done, 1);
         sm.abort = 0;
         fence_barrier_init();
     }
@@ -209,52 +223,55 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {  // ---- MMA issuer
+        if (lane == 0) {  // ---- MMA issuer, S stream: S = Q K(m)^T once the softmax has read S(m-1)
             const uint32_t id1 = idesc_bf16(128, KT, false, false);
-            const uint32_t id2 = idesc_bf16(128, HDP, false, true);
             bool ok = pf_wait(&sm.qfull, 0, sm, status, VX_DEV_TIMEOUT_TMA);
-            uint32_t n = 0;
-            for (int m = 0; m <= n_kt && ok; m++) {
-                if (m < n_kt) {  // S = Q K(m)^T once the softmax has read S(m-1)
-                    if (m >= 1) ok = pf_wait(&sm.s_empty, (m - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                    for (int c = 0; c < 4 && ok; c++, n++) {
-                        const uint32_t s2 = n % NS;
-                        ok = pf_wait(&sm.full[s2], (n / NS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
-                        if (!ok) break;
-                        tc_fence_after();
-                        const uint32_t qb = smem_u32(sm.q[c]), kb = smem_u32(sm.ring[s2]);
-#pragma unroll
-                        for (int kk = 0; kk < 4; kk++)
-                            mma_bf16(tS, sdesc_sw128(qb + kk * 32, 16, 1024),
-                                     sdesc_sw128(kb + kk * 32, 16, 1024), id1, (c | kk) != 0);
-                        mma_commit(&sm.empty[s2]);
-                    }
+            for (int m = 0; m < n_kt && ok; m++) {
+                if (m >= 1) ok = pf_wait(&sm.s_empty, (m - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                for (int c = 0; c < 4 && ok; c++) {
+                    const uint32_t pos = ring_pos_k(m, c), s2 = pos % NS;
+                    ok = pf_wait(&sm.full[s2], (pos / NS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
                     if (!ok) break;
-                    mma_commit(&sm.s_full);
-                }
-                if (m >= 1) {  // O += P(m-1) V(m-1)
-                    const int t = m - 1;
-                    ok = pf_wait(&sm.p_full, t & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                    for (int c = 0; c < 4 && ok; c++, n++) {
-                        const uint32_t s2 = n % NS;
-                        ok = pf_wait(&sm.full[s2], (n / NS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
-                        if (!ok) break;
-                        tc_fence_after();
-                        const uint32_t vb = smem_u32(sm.ring[s2]);
+                    tc_fence_after();
+                    const uint32_t qb = smem_u32(sm.q[c]), kb = smem_u32(sm.ring[s2]);
 #pragma unroll
-                        for (int k2 = 0; k2 < 2; k2++) {
-                            const int kk = 2 * c + k2;  // 16-key step of the 128-key tile
-                            mma_bf16(tO,
-                                     sdesc_sw128(smem_u32(sm.p[kk >> 2]) + (kk & 3) * 32, 16, 1024),
-                                     sdesc_sw128(vb + k2 * 2048, 32 * 128, 1024), id2,
-                                     (t > 0 || kk > 0) ? 1u : 0u);
-                        }
-                        mma_commit(&sm.empty[s2]);
-                    }
-                    if (!ok) break;
-                    mma_commit(&sm.pv_done);
-                    if (t == n_kt - 1) mma_commit(&sm.o_final);
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_bf16(tS, sdesc_sw128(qb + kk * 32, 16, 1024),
+                                 sdesc_sw128(kb + kk * 32, 16, 1024), id1, (c | kk) != 0);
+                    mma_commit(&sm.empty[s2]);
                 }
+                if (!ok) break;
+                mma_commit(&sm.s_full);
+            }
+            mma_commit(&sm.qk_done);
+            pf_wait(&sm.qk_done, 0, sm, status, VX_DEV_TIMEOUT_MMA);
+        }
+    } else if (warp == PF_THREADS / 32 - 1) {
+        if (lane == 0) {  // ---- MMA issuer, O stream: O += P(t) V(t) once P(t) is written
+            const uint32_t id2 = idesc_bf16(128, HDP, false, true);
+            bool ok = true;
+            for (int t = 0; t < n_kt && ok; t++) {
+                const int pb = t & 1;
+                ok = pf_wait(&sm.p_full[pb], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                for (int c = 0; c < 4 && ok; c++) {
+                    const uint32_t pos = ring_pos_v(t, c, n_kt), s2 = pos % NS;
+                    ok = pf_wait(&sm.full[s2], (pos / NS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t vb = smem_u32(sm.ring[s2]);
+#pragma unroll
+                    for (int k2 = 0; k2 < 2; k2++) {
+                        const int kk = 2 * c + k2;  // 16-key step of the 128-key tile
+                        mma_bf16(tO,
+                                 sdesc_sw128(smem_u32(sm.p[pb][kk >> 2]) + (kk & 3) * 32, 16, 1024),
+                                 sdesc_sw128(vb + k2 * 2048, 32 * 128, 1024), id2,
+                                 (t > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&sm.empty[s2]);
+                }
+                if (!ok) break;
+                mma_commit(&sm.pv_done[pb]);
+                if (t == n_kt - 1) mma_commit(&sm.o_final);
             }
             mma_commit(&sm.mma_done);
             pf_wait(&sm.mma_done, 0, sm, status, VX_DEV_TIMEOUT_MMA);
@@ -319,16 +336,16 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 alpha = (m_run == -INFINITY) ? 0.0f : exp2f(m_run - mt);
                 m_run = mt;
             }
-            // P and O are free once O += P(j-1) V(j-1) is done
-            if (j >= 1) {
-                ok = pf_wait(&sm.pv_done, (j - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) continue;
-            }
-            // rescale this warp's half of its O rows when one of its rows raised its max
-            // (not on the first tile of a row, where O holds nothing yet)
+            // rescale this warp's half of its O rows when one of its rows raised its max (not
+            // on the first tile of a row, where O holds nothing yet), once O += P(j-1) V(j-1)
+            // is done
+            const int pb = j & 1;
             const bool need = grow && alpha > 0.0f;
             if (__any_sync(0xffffffffu, need)) {
+                ok = pf_wait(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, sm, status,
+                             VX_DEV_TIMEOUT_MMA);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) continue;
                 tc_fence_after();
 #pragma unroll 1
                 for (int i = 0; i < HDP / 32; i++) {
@@ -342,8 +359,14 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 tmem_st_wait();
                 tc_fence_before();
             }
+            // P buffer pb is free once O += P(j-2) V(j-2) is done
+            if (j >= 2) {
+                ok = pf_wait(&sm.pv_done[pb], ((j >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) continue;
+            }
             float ls[4] = {0.f, 0.f, 0.f, 0.f};
-            uint8_t *prow = sm.p[hf] + r * 128;
+            uint8_t *prow = sm.p[pb][hf] + r * 128;
             const float nm = -m_run;
 #pragma unroll
             for (int u = 0; u < 8; u++) {
@@ -360,7 +383,7 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             }
             l_run = fmaf(l_run, alpha, (ls[0] + ls[1]) + (ls[2] + ls[3]));
             fence_proxy_async();
-            mbar_arrive(&sm.p_full);
+            mbar_arrive(&sm.p_full[pb]);
         }
         // the row sum is the sum of both halves' partial sums (same maxima, same rescales)
         tmem_st1(tX + lane_off + 4 + hf, l_run);
