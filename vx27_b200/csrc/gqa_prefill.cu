@@ -17,6 +17,7 @@
 // Query tiles are issued longest first; the six query heads of a KV head run on
 // neighbouring CTAs so their K/V tiles are served from L2.
 #include <math.h>
+#include <algorithm>
 #include "common.cuh"
 #include "tc.cuh"
 #include "../../include/vx27_gqa.h"
@@ -81,57 +82,100 @@ __device__ bool pf_wait(uint64_t *bar, uint32_t parity, PfSmem &sm, uint32_t *st
 }
 
 // ---- prep ----------------------------------------------------------------------------
+// One warp per (token, head) row, 8 consecutive dims per lane (16-byte bf16 accesses).
+// RMSNorm with a double sum of squares, NeoX RoPE on dims [0, rope_dim) (the partner of
+// dim d < rope_dim/2 is d + rope_dim/2, held rope_dim/16 lanes away), bf16 stores.
+template <bool ACT_BF16>
+__device__ __forceinline__ void load8(const void *p, size_t i, float *x) {
+    if constexpr (ACT_BF16) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p) + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            x[2 * k] = bf16_to_f32(w[k] & 0xffffu);
+            x[2 * k + 1] = bf16_to_f32(w[k] >> 16);
+        }
+    } else {
+        const float4 *f = reinterpret_cast<const float4 *>(static_cast<const float *>(p) + i);
+        const float4 a = f[0], b = f[1];
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    }
+}
+__device__ __forceinline__ void store8_bf16(uint16_t *p, const float *x) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        w[k] = (uint32_t)f32_to_bf16(x[2 * k]) | ((uint32_t)f32_to_bf16(x[2 * k + 1]) << 16);
+    *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 template <bool ACT_BF16, bool ONE_P>
-__global__ void __launch_bounds__(HDP)
+__global__ void __launch_bounds__(256)
 prefill_prep_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
                const void *__restrict__ v_in, const float *__restrict__ qw,
                const float *__restrict__ kw, const float *__restrict__ rope, int rope_len,
                int p0, uint16_t *__restrict__ qn, uint16_t *__restrict__ kc,
                uint16_t *__restrict__ vc, int cap, int T, int nq, int nkv, int rope_dim,
                float eps, uint32_t *status) {
-    const int head = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
-    const bool is_q = head < nq;
-    const int h = is_q ? head : head - nq;
-    const size_t row = is_q ? ((size_t)t * nq + h) * HDP : ((size_t)t * nkv + h) * HDP;
-    const float x = act_ld<ACT_BF16>(is_q ? q_in : k_in, row + d);
-    __shared__ double red[HDP / 32];
-    __shared__ float r_s;
-    __shared__ float y_s[HDP];
-    double ss = warp_sum_d((double)x * (double)x);
-    if ((d & 31) == 0) red[d >> 5] = ss;
-    __syncthreads();
-    if (d == 0) {
-        double tt = 0.0;
-        for (int w = 0; w < HDP / 32; w++) tt += red[w];
-        r_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(tt / HDP), eps)));
-    }
-    __syncthreads();
-    float w = is_q ? qw[d] : kw[d];
-    if (ONE_P) w = __fadd_rn(w, 1.0f);
-    const float y = __fmul_rn(__fmul_rn(x, r_s), w);
-    y_s[d] = y;
-    __syncthreads();
-    const int p = p0 + t;
-    const int half = rope_dim / 2;
-    float out = y;
-    if (d < rope_dim) {
-        if (p < 0 || p >= rope_len) {
-            if (d == 0) dev_flag(status, VX_DEV_BAD_ARG);
-        } else {
-            const float *rr = rope + (size_t)p * rope_dim;
-            const int i = d < half ? d : d - half;
-            const float c = rr[i], s = rr[half + i];
-            const float x0 = y_s[i], x1 = y_s[i + half];
-            out = d < half ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s))
-                           : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    const int lane = threadIdx.x & 31;
+    const int nh = nq + nkv;
+    const size_t n_rows = (size_t)T * nh;
+    const int half = rope_dim / 2, hl = half / 8;  // partner lane distance
+    const int d0 = lane * 8;
+    for (size_t item = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; item < n_rows;
+         item += ((size_t)gridDim.x * blockDim.x) >> 5) {
+        const int t = (int)(item / nh), head = (int)(item % nh);
+        const bool is_q = head < nq;
+        const int h = is_q ? head : head - nq;
+        const size_t row = is_q ? ((size_t)t * nq + h) * HDP : ((size_t)t * nkv + h) * HDP;
+        float x[8];
+        load8<ACT_BF16>(is_q ? q_in : k_in, row + d0, x);
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss += (double)x[e] * (double)x[e];
+        ss = warp_sum_d(ss);
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(ss / HDP), eps)));
+        const float *wp = (is_q ? qw : kw) + d0;
+        float y[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            float w = wp[e];
+            if (ONE_P) w = __fadd_rn(w, 1.0f);
+            y[e] = __fmul_rn(__fmul_rn(x[e], r), w);
         }
-    }
-    if (is_q) {
-        qn[((size_t)h * T + t) * HDP + d] = f32_to_bf16(out);
-    } else if (p < cap) {
-        const size_t o = ((size_t)h * cap + p) * HDP + d;
-        kc[o] = f32_to_bf16(out);
-        vc[o] = f32_to_bf16(act_ld<ACT_BF16>(v_in, row + d));
+        const int p = p0 + t;
+        // partner values for the rotation (all lanes take part in the shuffles)
+        const bool rot = d0 < rope_dim;
+        const bool lo = d0 < half;
+        const int src = lo ? lane + hl : lane - hl;
+        float yp[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) yp[e] = __shfl_sync(0xffffffffu, y[e], (src & 31));
+        if (rot) {
+            if (p < 0 || p >= rope_len) {
+                dev_flag(status, VX_DEV_BAD_ARG);
+            } else {
+                const float *rr = rope + (size_t)p * rope_dim;
+                const int i0 = lo ? d0 : d0 - half;
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const float c = rr[i0 + e], sn = rr[half + i0 + e];
+                    const float x0 = lo ? y[e] : yp[e], x1 = lo ? yp[e] : y[e];
+                    y[e] = lo ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn))
+                              : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+                }
+            }
+        }
+        if (is_q) {
+            store8_bf16(qn + ((size_t)h * T + t) * HDP + d0, y);
+        } else if (p < cap) {
+            const size_t o = ((size_t)h * cap + p) * HDP + d0;
+            store8_bf16(kc + o, y);
+            float v[8];
+            load8<ACT_BF16>(v_in, row + d0, v);
+            store8_bf16(vc + o, v);
+        }
     }
 }
 
@@ -520,23 +564,25 @@ extern "C" int vx27_gqa_prefill(const void *q_in, const void *k_in, const void *
     if (p0 < 0 || p0 + T > cap)
         return fail(err, errlen, "%s: positions [%d, %d) exceed the cache capacity %d", fn, p0,
                     p0 + T, cap);
-    if (rope_dim < 0 || rope_dim > hd || (rope_dim & 1) || p0 + T > rope_table_len)
+    if (rope_dim < 0 || rope_dim > hd || (rope_dim & 15) || p0 + T > rope_table_len)
         return fail(err, errlen, "%s: rope_dim=%d / table of %d positions", fn, rope_dim,
                     rope_table_len);
     if (!q_in || !k_in || !v_in || !gate || !q_norm_w || !k_norm_w || !k_cache || !v_cache ||
         !out || !workspace || (rope_dim && !rope_table))
         return fail(err, errlen, "%s: null pointer argument", fn);
-    if (((uintptr_t)gate | (uintptr_t)out) & 15)
-        return fail(err, errlen, "%s: gate and out must be 16-byte aligned", fn);
+    if (((uintptr_t)gate | (uintptr_t)out | (uintptr_t)q_in | (uintptr_t)k_in | (uintptr_t)v_in |
+         (uintptr_t)k_cache | (uintptr_t)v_cache) & 15)
+        return fail(err, errlen, "%s: activations, caches and out must be 16-byte aligned", fn);
     if (workspace_bytes < vx27_gqa_prefill_workspace_size(T, nq, hd))
         return fail(err, errlen, "%s: workspace of %zu bytes, need %zu", fn, workspace_bytes,
                     vx27_gqa_prefill_workspace_size(T, nq, hd));
     cudaStream_t st = (cudaStream_t)stream;
     uint16_t *qn = (uint16_t *)workspace;
     const bool a = flags & VX27_F_ACT_BF16, one = flags & VX27_F_NORM_1P;
-    const dim3 pg(nq + nkv, T);
+    const size_t prep_rows = (size_t)T * (nq + nkv);
+    const int pg = (int)std::min<size_t>((prep_rows + 7) / 8, (size_t)num_sms() * 16);
 #define VX_P(A_, O_)                                                                         \
-    prefill_prep_k<A_, O_><<<pg, HDP, 0, st>>>(q_in, k_in, v_in, q_norm_w, k_norm_w,          \
+    prefill_prep_k<A_, O_><<<pg, 256, 0, st>>>(q_in, k_in, v_in, q_norm_w, k_norm_w,          \
                                                rope_table, rope_table_len, p0, qn,            \
                                                (uint16_t *)k_cache, (uint16_t *)v_cache, cap, \
                                                T, nq, nkv, rope_dim, eps, dev_status())
