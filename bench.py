@@ -308,6 +308,154 @@ def run_layer(args) -> dict:
             "peak_source": peak_src}
 
 
+# ------------------------------------------------- configs 0 and 1 (batch-1 latency)
+def run_batch1(args) -> dict:
+    """Config 0: one DeltaNet layer decoding 2000 tokens of one sequence (16 heads, fp32
+    activations, seed 0); config 1: one gated GQA single-query decode at context 8192
+    (seed 1). Both are latency-bound at batch 1: the line reports microseconds per token,
+    launched one call per token as a decode loop does, and replayed from one CUDA graph."""
+    import torch
+    from oracle import oracle as orc
+    from vx27_b200 import ops
+    torch.cuda.set_device(0)
+    hbm, hbm_src = peaks()
+    bf = torch.bfloat16
+    if args.workload == "config0":
+        n_tok, nqk, nv = 2000, 16, 16
+        C = (2 * nqk + nv) * 128
+        qkv = torch.empty(n_tok, C, device="cuda")
+        a = torch.empty(n_tok, nv, device="cuda")
+        b = torch.empty(n_tok, nv, device="cuda")
+        w = torch.empty(C, 4, device="cuda")
+        dt = torch.empty(nv, device="cuda")
+        A = torch.empty(nv, device="cuda")
+        for n, (t, sd) in enumerate(((qkv, 1.0), (a, 1.0), (b, 1.0), (w, 0.5), (dt, 0.1))):
+            ops.fill_normal(t, 0, n + 1, 0.0, sd)
+        ops.fill_uniform(A, 0, 6, 1.0, 16.0)
+        A.log_()
+        S = torch.zeros(1, nv, 128, 128, device="cuda")
+        ring = torch.zeros(1, 4, C, device="cuda")
+        o = torch.empty(n_tok, nv, 128, device="cuda")
+        pos = torch.arange(n_tok, dtype=torch.int32, device="cuda")
+
+        def run():
+            for t in range(n_tok):
+                ops.deltanet_decode_batch(S, ring, qkv[t:t + 1], a[t:t + 1], b[t:t + 1], A, dt,
+                                          w, pos[t:t + 1], o[t:t + 1], nqk, nv)
+        units, unit_name = n_tok, "token"
+        bytes_per_unit = 2 * nv * 128 * 128 * 4 + 4 * C * 4 + C * 4 + nv * 128 * 4
+        name = "config 0: DeltaNet decode, batch 1, 16 heads, 2000 sequential tokens"
+    else:
+        ctx, nq, nkv, hd = 8192, 24, 4, 256
+        cap = ctx
+        kc = torch.empty(1, nkv, cap, hd, dtype=bf, device="cuda")
+        vc = torch.empty_like(kc)
+        ops.fill_normal(kc, 1, 1)
+        ops.fill_normal(vc, 1, 2)
+        q_in = torch.empty(1, nq, hd, device="cuda")
+        k_in = torch.empty(1, nkv, hd, device="cuda")
+        v_in = torch.empty(1, nkv, hd, device="cuda")
+        gate = torch.empty(1, nq, hd, device="cuda")
+        qw = torch.empty(hd, device="cuda")
+        kw = torch.empty(hd, device="cuda")
+        for n, t in enumerate((q_in, k_in, v_in, gate)):
+            ops.fill_normal(t, 1, 3 + n)
+        ops.fill_normal(qw, 1, 7, 1.0, 0.02)
+        ops.fill_normal(kw, 1, 8, 1.0, 0.02)
+        rope = ops.rope_table(ctx)
+        qn = torch.empty(1, nq, hd, device="cuda")
+        out = torch.empty(1, nq, hd, device="cuda")
+        pos = torch.full((1,), ctx - 1, dtype=torch.int32, device="cuda")
+        ws = torch.empty(ops.gqa_workspace_bytes(1, nq, nkv, hd, cap) // 4 + 1, device="cuda")
+
+        def run():
+            ops.gqa_append(q_in, k_in, v_in, qw, kw, rope, pos, kc, vc, qn)
+            ops.gqa_decode_batch(qn, gate, kc, vc, pos, out, ws)
+        units, unit_name = 1, "decode"
+        bytes_per_unit = nkv * ctx * hd * 2 * 2 + nq * hd * 4 * 3
+        name = "config 1: gated GQA single-query decode, batch 1, context 8192"
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    reps = max(1, args.steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        us_launch = e0.elapsed_time(e1) * 1e3 / (reps * units)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            run()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us_graph = e0.elapsed_time(e1) * 1e3 / (reps * units)
+    del graph
+    if ops.device_status() != 0:
+        raise RuntimeError("device status flag set during the batch-1 run")
+    # the reference's own code on the host (oracle/_ref when built, else the port)
+    import os as _os
+    import time as _time
+    kind = "reference" if orc.use_reference(True) else "port"
+    L, P = orc.lib(), orc.P
+    threads = _os.cpu_count() or 1
+    if args.workload == "config0":
+        n_cpu = 100
+        Sh = np.zeros(nv * 128 * 128, np.float32)
+        rh = np.zeros(4 * C, np.float32)
+        xh = orc.normal(n_cpu * C, 0, 1)
+        ah, bh = orc.normal(n_cpu * nv, 0, 2), orc.normal(n_cpu * nv, 0, 3)
+        wh = orc.normal(C * 4, 0, 4, 0.0, 0.5)
+        dth = orc.normal(nv, 0, 5, 0.0, 0.1)
+        Ah = np.log(orc.uniform(nv, 0, 6, 1.0, 16.0)).astype(np.float32)
+        oh = np.zeros(nv * 128, np.float32)
+        t0 = _time.perf_counter()
+        for t in range(n_cpu):
+            p = np.array([t], np.int32)
+            L.orc_deltanet_decode_batch_mt(P(Sh), P(rh), P(xh[t * C:]), P(ah[t * nv:]),
+                                           P(bh[t * nv:]), P(Ah), P(dth), P(wh), P(p), P(oh),
+                                           1, nqk, nv, 128, 0, threads)
+        cpu_us = (_time.perf_counter() - t0) * 1e6 / n_cpu
+        sample = f"{n_cpu} tokens x 16 heads (step_exact per head, {threads} threads)"
+    else:
+        from oracle.oracle import to_bf16
+        kh = to_bf16(orc.normal(nkv * ctx * hd, 1, 1))
+        vh = to_bf16(orc.normal(nkv * ctx * hd, 1, 2))
+        qh = orc.normal(nq * hd, 1, 3)
+        gh = orc.normal(nq * hd, 1, 6)
+        outh = np.zeros(nq * hd, np.float32)
+        p = np.array([ctx - 1], np.int32)
+        t0 = _time.perf_counter()
+        n_cpu = 5
+        for _ in range(n_cpu):
+            L.orc_gqa_attend_mt(P(qh), P(gh), P(kh), P(vh), ctx, P(p), P(outh), 1, nq, nkv, hd,
+                                0, threads)
+        cpu_us = (_time.perf_counter() - t0) * 1e6 / n_cpu
+        sample = f"{n_cpu} decodes over 8192 positions ({threads} threads)"
+    gbs = bytes_per_unit / (us_graph * 1e-6) / 1e9
+    return {
+        "metric": f"microseconds per {unit_name} ({args.workload}, batch 1)",
+        "value": round(us_graph, 3), "unit": f"us/{unit_name}", "n_gpus": 1,
+        "steps": reps, "warmup": args.warmup, "higher_is_better": False, "dtype": "f32",
+        "data": "synthetic (seeded, BASELINE.json distributions)",
+        "config": {"workload": name},
+        "us_per_unit_launched": round(us_launch, 3), "us_per_unit_graph": round(us_graph, 3),
+        "roofline": {"bound": "hbm (latency at batch 1)", "achieved": round(gbs, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
+                     "algorithmic_bytes_per_unit": bytes_per_unit, "peak_source": hbm_src},
+        "cpu_baseline": {"value": round(cpu_us, 2), "unit": f"us/{unit_name}",
+                         "cores": threads, "kind": kind, "sample": sample},
+        "clocks": clk.summary(),
+    }
+
+
 # ------------------------------------------------- config 4 (prefill)
 def prefill_flops(T: int) -> tuple[float, float]:
     """Algorithmic FLOPs of one config-4 layer of each kind.
@@ -616,8 +764,9 @@ def main() -> None:
     ap.add_argument("--ref-seqs", type=int, default=4)
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["config2", "config3a", "config3b", "config4",
-                                           "dn_layer", "gqa_layer"], default="config2",
+    ap.add_argument("--workload", choices=["config2", "config0", "config1", "config3a",
+                                           "config3b", "config4", "dn_layer", "gqa_layer"],
+                    default="config2",
                     help="config2 (the metric); config3a/3b long context; single-layer "
                          "workloads are for kernel rooflines and profiling")
     ap.add_argument("--ctx3", type=int, default=262144)
@@ -637,6 +786,9 @@ def main() -> None:
         return
     if args.workload == "config4":
         print(json.dumps(run_prefill(args)), flush=True)
+        return
+    if args.workload in ("config0", "config1"):
+        print(json.dumps(run_batch1(args)), flush=True)
         return
 
     if args.impl == "reference":

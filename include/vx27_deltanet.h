@@ -74,6 +74,43 @@ int vx27_deltanet_decode_batch(float *S, float *conv_ring, const void *qkv, cons
                                size_t errlen);
 
 /*
+ * vx27_deltanet_decode_batch followed by the layer's gated RMSNorm output
+ * (src/vx27_qfwd.c:146-151, rmsn_std :42-46, silu1 :48), fused in the kernel's epilogue:
+ *   o[b][vh][i] = (r[i] * s * norm_w[i]) * silu(z[b][vh][i]),
+ *   s = 1 / sqrtf((float)(sum_i r[i]^2 / hd) + 1e-6f)   (sum in double)
+ * with r the delta-rule retrieve output of (b, vh).
+ *   z       [B][nv][hd] (act dtype), the in_proj_z projection
+ *   norm_w  [hd] fp32 (linear_attn.norm.weight, shared by all V heads)
+ * Other arguments and flags as vx27_deltanet_decode_batch. No counterpart in the
+ * reference's headers (the reference does this inline in vx27_qlayer).
+ */
+int vx27_deltanet_decode_batch_gated(float *S, float *conv_ring, const void *qkv,
+                                     const void *a, const void *b, const float *A_log,
+                                     const float *dt_bias, const float *conv_w, const int *pos,
+                                     const void *z, const float *norm_w, void *o, int B,
+                                     int nqk, int nv, int hd, int flags, void *stream,
+                                     char *err, size_t errlen);
+
+/*
+ * T consecutive tokens of ONE sequence through one DeltaNet layer (teacher-forced
+ * verification of speculative drafts), with optional snapshots after every token for a
+ * partial commit: the semantics of vx27_qlayer_batch's Sckpt/Cckpt
+ * (src/vx27_qfwd.h:39-50, src/vx27_qfwd.c:306-307).
+ *   S [nv][hd][hd], conv_ring [4][C] (device, this sequence); qkv [T][C], a, b [T][nv]
+ *   (act dtype); pos [T] device int, the tokens' positions (normally pos0 + t);
+ *   o [T][nv][hd];
+ *   S_ckpt    [T][nv][hd][hd] fp32 or NULL: the state after token t
+ *   conv_ckpt [T][C][3] fp32 or NULL: the conv history after token t in the reference
+ *             layout (oldest first; vx27_deltanet_conv_import restores it)
+ * Flags as vx27_deltanet_decode_batch. Runs on `stream` without synchronising.
+ */
+int vx27_deltanet_decode_tokens(float *S, float *conv_ring, const void *qkv, const void *a,
+                                const void *b, const float *A_log, const float *dt_bias,
+                                const float *conv_w, const int *pos, void *o, float *S_ckpt,
+                                float *conv_ckpt, int T, int nqk, int nv, int hd, int flags,
+                                void *stream, char *err, size_t errlen);
+
+/*
  * Chunked gated delta rule over T prompt tokens (config 4): the token-by-token recurrence
  * of vx27_deltanet_step_exact (l2-normalised q and k, q / sqrt(hd), gates of
  * vx27_deltanet_gate_params) evaluated 64 tokens at a time in the WY/UT form, within

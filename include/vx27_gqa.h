@@ -50,7 +50,8 @@ int vx27_gqa_append(const void *q_in, const void *k_in, const void *v_in,
  * out = att * sigmoid(gate) (src/vx27_qfwd.c:347-371). Split-KV flash decoding: each
  * (sequence, KV head, split) block serves the nq/nkv Q heads of its group; splits are
  * merged with a log-sum-exp combine. n_splits = 0 picks a split count for the device.
- *   gate [B][nq][hd] (act dtype); out [B][nq][hd] (fp32 or bf16 per VX27_F_OUT_BF16)
+ *   gate [B][nq][hd] (act dtype), or NULL for no output gate (the MTP drafter's
+ *        use_gate = 0, src/vx27_mtp.c:249); out [B][nq][hd] (fp32 or bf16 per VX27_F_OUT_BF16)
  *   workspace: vx27_gqa_decode_workspace_size(B, nq, nkv, hd, cap, n_splits) bytes of
  *   device memory; a smaller workspace lowers the automatic split count to what fits.
  *   hd must be 256.
@@ -117,7 +118,8 @@ int vx27_gqa_prefill(const void *q_in, const void *k_in, const void *v_in, const
  *   o [B][nq][hd] followed by ml [B][nq][2]; record size B*nq*(hd+2) floats.
  * An empty range yields m = -inf, l = 0, o = 0. vx27_gqa_combine merges n_parts records
  * placed part_stride floats apart (0: back to back) -- m* = max m_i, l* = sum l_i
- * e^{m_i-m*}, o = sum o_i l_i e^{m_i-m*} / l* -- and applies the sigmoid gate.
+ * e^{m_i-m*}, o = sum o_i l_i e^{m_i-m*} / l* -- and applies the sigmoid gate (none when
+ * gate is NULL).
  * A long range is split across CTAs and merged into the one record; the sub-records need
  * vx27_gqa_partial_workspace_size(B, nq, nkv, hd, p_end - p_begin) bytes of workspace (a
  * smaller or NULL workspace lowers the split count, down to one CTA per KV head).

@@ -48,6 +48,7 @@ _PROTOS = {
     "orc_gqa_partial": (None, [_p, _p, _p, _i, _i, _i, _p, _p, _i, _i, _i]),
     "orc_gqa_combine": (None, [_p, _p, _i, _p, _p, _i, _i, _i]),
     "orc_gate_params_grid": (None, [_p, _p, _p, _p, _i, _i, _p, _p]),
+    "orc_gated_rmsnorm": (None, [_p, _p, _p, _p, _i, _i]),
     "orc_deltanet_recurrent": (None, [_p, _p, _p, _p, C.c_long, _p, _p, _p, _i, _i, _i]),
     "orc_gqa_prefill_rows": (None, [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _f, _f, _p, _i,
                                     _p, _i]),

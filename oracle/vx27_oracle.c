@@ -392,8 +392,9 @@ static void attend_one(const float *q, const void *gate, const uint16_t *kc,
     }
     for (int i = 0; i < hd; i++) {
         size_t idx = ((size_t)bi * nq + h) * hd + i;
-        float gt = act_load(gate, idx, bf);
-        act_store(out, idx, oh[i] * (1.0f / (1.0f + expf(-gt))), obf);
+        /* gate NULL: no output gate (src/vx27_mtp.c:249, use_gate = 0) */
+        const float gf = gate ? 1.0f / (1.0f + expf(-act_load(gate, idx, bf))) : 1.0f;
+        act_store(out, idx, gate ? oh[i] * gf : oh[i], obf);
     }
 }
 
@@ -481,8 +482,26 @@ void orc_gqa_combine(const float *o_parts, const float *ml_parts, int n_parts,
                 acc += w[r] * o_parts[((size_t)r * nq + h) * hd + i];
             float oi = L > 0.0 ? (float)(acc / L) : 0.0f;
             size_t idx = (size_t)h * hd + i;
-            float gt = act_load(gate, idx, bf);
-            act_store(out, idx, oi * (1.0f / (1.0f + expf(-gt))), obf);
+            const float gf = gate ? 1.0f / (1.0f + expf(-act_load(gate, idx, bf))) : 1.0f;
+            act_store(out, idx, gate ? oi * gf : oi, obf);
+        }
+    }
+}
+
+/* Gated RMSNorm output of a DeltaNet layer, src/vx27_qfwd.c:146-151 with rmsn_std
+ * (:42-46, sum of squares in double, eps 1e-6 inside the sqrt, /n) and silu1 (:48):
+ * y[i] = (x[i] * s * w[i]) * (z[i] / (1 + expf(-z[i]))), for each of n_heads heads of hd. */
+void orc_gated_rmsnorm(const float *x, const float *w, const float *z, float *y, int n_heads,
+                       int hd) {
+    for (int h = 0; h < n_heads; h++) {
+        const float *xh = x + (size_t)h * hd, *zh = z + (size_t)h * hd;
+        float *yh = y + (size_t)h * hd;
+        double ss = 0;
+        for (int i = 0; i < hd; i++) ss += (double)xh[i] * xh[i];
+        const float s = 1.0f / sqrtf((float)(ss / hd) + 1e-6f);
+        for (int i = 0; i < hd; i++) {
+            const float tn = xh[i] * s * w[i];
+            yh[i] = tn * (zh[i] / (1.0f + expf(-zh[i])));
         }
     }
 }

@@ -111,6 +111,11 @@ void orc_deltanet_recurrent(float *S, const void *q, const void *k, const void *
                             long ld, const double *beta, const double *g_log,
                             float *o, int T, int hd, int flags);
 
+/* Gated RMSNorm output of a DeltaNet layer (src/vx27_qfwd.c:146-151): per head of hd,
+ * y = rmsn_std(x) * w * silu(z). */
+void orc_gated_rmsnorm(const float *x, const float *w, const float *z, float *y, int n_heads,
+                       int hd);
+
 /* gate_params (the selected implementation) over a [T][nv] grid of fp32 logits. */
 void orc_gate_params_grid(const float *a, const float *b, const float *A_log,
                           const float *dt_bias, int T, int nv, double *beta, double *g_log);

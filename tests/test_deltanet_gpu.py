@@ -125,3 +125,109 @@ def test_conv_ring_import_export_roundtrip(cuda, orc):
     assert lib.vx27_deltanet_conv_export(C.c_void_p(ring.data_ptr()), back.ctypes.data_as(C.c_void_p),
                                          pos.ctypes.data_as(C.c_void_p), B, Cch, st, e, 512) == 0
     assert np.array_equal(back, state)
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_gated_rmsnorm_output(cuda, orc, bf16):
+    """vx27_deltanet_decode_batch_gated == decode step, then the layer's gated RMSNorm
+    output (src/vx27_qfwd.c:146-151) on the oracle's retrieve output; 48 V heads over 16 QK
+    heads as in the real model, 3 tokens."""
+    B, nqk, nv, hd, T = 3, 16, 48, 128, 3
+    lay = make_layer(orc, 31, B, nqk, nv, s_std=0.05)
+    Cch = lay["C"]
+    L = orc.lib()
+    qkv_all = orc.normal(T * B * Cch, 31, 1, bf16=bf16).reshape(T, B * Cch)
+    a_all = orc.normal(T * B * nv, 31, 2, bf16=bf16).reshape(T, B * nv)
+    b_all = orc.normal(T * B * nv, 31, 3, bf16=bf16).reshape(T, B * nv)
+    z_all = orc.normal(T * B * nv * hd, 31, 7, bf16=bf16).reshape(T, B * nv * hd)
+    norm_w = orc.normal(hd, 31, 8, 1.0, 0.1)
+    flags = orc.F_ACT_BF16 if bf16 else 0
+    S, ring = lay["S"].copy(), lay["ring"].copy()
+    dS = dev(lay["S"]).view(B, nv, hd, hd)
+    dring = dev(lay["ring"])
+    from oracle.oracle import from_bf16
+    for t in range(T):
+        pos = np.full(B, t, np.int32)
+        q, a, b = (np.ascontiguousarray(x[t]) for x in (qkv_all, a_all, b_all))
+        r = np.zeros(B * nv * hd, np.float32)
+        L.orc_deltanet_decode_batch_mt(orc.P(S), orc.P(ring), orc.P(q), orc.P(a), orc.P(b),
+                                       orc.P(lay["A_log"]), orc.P(lay["dt_bias"]),
+                                       orc.P(lay["conv_w"]), orc.P(pos), orc.P(r), B, nqk, nv,
+                                       hd, flags, 8)
+        zf = np.ascontiguousarray(from_bf16(z_all[t]) if bf16 else z_all[t])
+        y_ref = np.zeros(B * nv * hd, np.float32)
+        L.orc_gated_rmsnorm(orc.P(r), orc.P(norm_w), orc.P(zf), orc.P(y_ref), B * nv, hd)
+        o = torch.empty(B, nv, hd, device="cuda")
+        ops.deltanet_decode_batch_gated(dS, dring, dev(q, bf16).view(B, Cch),
+                                        dev(a, bf16).view(B, nv), dev(b, bf16).view(B, nv),
+                                        dev(lay["A_log"]), dev(lay["dt_bias"]),
+                                        dev(lay["conv_w"]).view(Cch, 4),
+                                        torch.from_numpy(pos).cuda(),
+                                        dev(z_all[t], bf16).view(B, nv, hd), dev(norm_w), o,
+                                        nqk, nv)
+        torch.cuda.synchronize()
+        assert np.abs(host(o).reshape(-1) - y_ref).max() < TOL
+    assert np.abs(host(dS).reshape(-1) - S).max() < TOL
+    assert ops.device_status() == 0
+
+
+def test_decode_tokens_with_checkpoints(cuda, orc):
+    """vx27_deltanet_decode_tokens: 5 teacher-forced tokens of one sequence with state and
+    conv snapshots after each token (vx27_qlayer_batch's Sckpt/Cckpt), against the oracle
+    stepping token by token; then a partial commit of 3 tokens (restore from the
+    snapshots) continues exactly like a run that only ever saw those 3 tokens."""
+    nqk, nv, hd, T, p0 = 2, 6, 128, 5, 9
+    lay = make_layer(orc, 41, 1, nqk, nv, s_std=0.05)
+    Cch = lay["C"]
+    L = orc.lib()
+    lay["ring"] = orc.normal(4 * Cch, 41, 9)  # some history at position p0
+    qkv = orc.normal(T * Cch, 41, 1, bf16=True).reshape(T, Cch)
+    a = orc.normal(T * nv, 41, 2, bf16=True).reshape(T, nv)
+    b = orc.normal(T * nv, 41, 3, bf16=True).reshape(T, nv)
+    S, ring = lay["S"].copy(), lay["ring"].copy()
+    o_ref, S_ref, c_ref = [], [], []
+    for t in range(T):
+        p = np.array([p0 + t], np.int32)
+        o = np.zeros(nv * hd, np.float32)
+        L.orc_deltanet_decode_batch_mt(orc.P(S), orc.P(ring), orc.P(np.ascontiguousarray(qkv[t])),
+                                       orc.P(np.ascontiguousarray(a[t])),
+                                       orc.P(np.ascontiguousarray(b[t])), orc.P(lay["A_log"]),
+                                       orc.P(lay["dt_bias"]), orc.P(lay["conv_w"]), orc.P(p),
+                                       orc.P(o), 1, nqk, nv, hd, orc.F_ACT_BF16, 4)
+        o_ref.append(o)
+        S_ref.append(S.copy())
+        r4 = ring.reshape(4, Cch)
+        pp = p0 + t
+        c_ref.append(np.stack([r4[(pp - 2) & 3], r4[(pp - 1) & 3], r4[pp & 3]], axis=1))
+    dS = dev(lay["S"]).view(nv, hd, hd)
+    dring = dev(lay["ring"]).view(4, Cch)
+    o = torch.empty(T, nv, hd, device="cuda")
+    S_ck = torch.empty(T, nv, hd, hd, device="cuda")
+    c_ck = torch.empty(T, Cch, 3, device="cuda")
+    pos = torch.arange(p0, p0 + T, dtype=torch.int32, device="cuda")
+    args = (dev(lay["A_log"]), dev(lay["dt_bias"]), dev(lay["conv_w"]).view(Cch, 4))
+    ops.deltanet_decode_tokens(dS, dring, dev(qkv, True), dev(a, True), dev(b, True), *args, pos,
+                               o, nqk, nv, S_ckpt=S_ck, conv_ckpt=c_ck)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    for t in range(T):
+        assert np.abs(host(o[t]).reshape(-1) - o_ref[t]).max() < TOL
+        assert np.abs(host(S_ck[t]).reshape(-1) - S_ref[t]).max() < TOL
+        assert np.array_equal(host(c_ck[t]), c_ref[t])
+    # partial commit: keep 3 tokens, restore state + conv history, decode token 4 again
+    k = 3
+    S2 = S_ck[k - 1].clone()
+    ring2 = torch.zeros(1, 4, Cch, device="cuda")
+    from ctypes import create_string_buffer
+    st = np.ascontiguousarray(host(c_ck[k - 1]).reshape(1, Cch, 3))
+    e = create_string_buffer(512)
+    assert ops.load().vx27_deltanet_conv_import(ops._t(ring2), st.ctypes.data_as(ops.C.c_void_p),
+                                                np.array([p0 + k], np.int32).ctypes.data_as(
+                                                    ops.C.c_void_p), 1, Cch, None, e, 512) == 0
+    o2 = torch.empty(1, nv, hd, device="cuda")
+    ops.deltanet_decode_tokens(S2, ring2.view(4, Cch), dev(qkv[k:k + 1], True),
+                               dev(a[k:k + 1], True), dev(b[k:k + 1], True), *args, pos[k:k + 1],
+                               o2, nqk, nv)
+    torch.cuda.synchronize()
+    assert np.abs(host(o2).reshape(-1) - o_ref[k]).max() < TOL
+    assert np.abs(host(S2).reshape(-1) - S_ref[k]).max() < TOL

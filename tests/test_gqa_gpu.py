@@ -180,3 +180,31 @@ def test_kv_cache_object_roundtrip(cuda, orc):
         assert lib.vx27_kv_store_f32(h, 1, 2, 60, 10, orc.P(k), orc.P(v), e, 512) == -1
     finally:
         lib.vx27_kv_destroy(h)
+
+
+def test_no_output_gate_mtp_drafter(cuda, orc, rope):
+    """gate = NULL: the attention without the sigmoid gate, as the MTP drafter runs it with
+    use_gate = 0 (src/vx27_mtp.c:232-250) over its own cache; two sequences, one split."""
+    B, cap = 2, 700
+    x = setup(orc, 61, B, cap, [333, 699])
+    L, P = orc.lib(), orc.P
+    kc, vc = x["kc"].copy(), x["vc"].copy()
+    qo = np.zeros(B * NQ * HD, np.float32)
+    L.orc_gqa_append(P(x["qi"]), P(x["ki"]), P(x["vi"]), P(x["qw"]), P(x["kw"]), P(x["pos"]),
+                     P(kc), P(vc), cap, P(qo), B, NQ, NKV, HD, 64, 1e7, 1e-6, orc.F_ACT_BF16)
+    ref = np.zeros(B * NQ * HD, np.float32)
+    L.orc_gqa_attend_mt(P(qo), None, P(kc), P(vc), cap, P(x["pos"]), P(ref), B, NQ, NKV, HD,
+                        orc.F_ACT_BF16, 8)
+    dkc = dev(x["kc"], True).view(B, NKV, cap, HD)
+    dvc = dev(x["vc"], True).view(B, NKV, cap, HD)
+    q = torch.empty(B, NQ, HD, device="cuda")
+    pos = dev(x["pos"])
+    ops.gqa_append(dev(x["qi"], True).view(B, NQ, HD), dev(x["ki"], True).view(B, NKV, HD),
+                   dev(x["vi"], True).view(B, NKV, HD), dev(x["qw"]), dev(x["kw"]), rope, pos,
+                   dkc, dvc, q)
+    ws = torch.empty(ops.gqa_workspace_bytes(B, NQ, NKV, HD, cap, 1) // 4 + 1, device="cuda")
+    out = torch.empty(B, NQ, HD, device="cuda")
+    ops.gqa_decode_batch(q, None, dkc, dvc, pos, out, ws, n_splits=1)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert rel_err(host(out).reshape(-1), ref) < REL_TOL

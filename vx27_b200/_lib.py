@@ -43,6 +43,10 @@ PROTOTYPES: dict[str, tuple] = {
     # vx27_deltanet.h -- batched tier
     "vx27_deltanet_decode_batch": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i,
                                         _i, _p, _cp, _sz]),
+    "vx27_deltanet_decode_batch_gated": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                              _i, _i, _i, _i, _i, _p, _cp, _sz]),
+    "vx27_deltanet_decode_tokens": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i,
+                                         _i, _i, _i, _p, _cp, _sz]),
     "vx27_deltanet_prefill_workspace_size": (_sz, [_i, _i, _i, _i]),
     "vx27_deltanet_prefill_chunked": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _i, _i,
                                            _i, _i, _i, _p, _cp, _sz]),

@@ -13,7 +13,9 @@
 //                 (double precision) -> a parameter slot in shared memory;
 //   compute warps (8) state from shared memory into registers (thread = 16 rows x 4
 //                 columns), S' = S*decay, column sums kv = S'^T k, d = (v - kv)*beta,
-//                 S'' = S' + k d^T, o = S''^T q, state stored straight from registers.
+//                 S'' = S' + k d^T, o = S''^T q, state stored straight from registers;
+//                 optionally the layer's gated RMSNorm output o = rmsnorm(o) * w * silu(z)
+//                 (src/vx27_qfwd.c:42-48, 146-151) in the same epilogue.
 // Waits on the mbarriers are bounded (2 s, %globaltimer); in the compute group a single
 // thread waits and publishes the outcome before the group's bar.sync, and a prep warp
 // broadcasts its lane 0's outcome, so a timeout makes a whole group leave together and no
@@ -43,6 +45,7 @@ struct DnSmem {
     Params prm[NPARAM];
     float red[8][HD];
     float d[HD];
+    double gss[HD / 32];
     uint64_t sfull[NSTATE], sempty[NSTATE], pfull[NPARAM], pempty[NPARAM];
     int flag_comp, abort;
 };
@@ -88,12 +91,13 @@ __device__ __forceinline__ void gates_device(double a, double A_log, double b, d
     *g_log = -exp(A_log) * sp;
 }
 
-template <bool ACT_BF16, bool OUT_BF16, bool GATES_F64>
+template <bool ACT_BF16, bool OUT_BF16, bool GATES_F64, bool GATED>
 __global__ void __launch_bounds__(NTHREADS, 1)
 dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restrict__ qkv,
             const void *__restrict__ ga, const void *__restrict__ gb,
             const float *__restrict__ A_log, const float *__restrict__ dt_bias,
-            const float *__restrict__ conv_w, const int *__restrict__ pos, void *__restrict__ o,
+            const float *__restrict__ conv_w, const int *__restrict__ pos,
+            const void *__restrict__ z, const float *__restrict__ norm_w, void *__restrict__ o,
             int B, int nqk, int nv, uint32_t *status) {
     extern __shared__ uint8_t dn_smem_raw[];
     DnSmem &sm = *reinterpret_cast<DnSmem *>(((uintptr_t)dn_smem_raw + 127) & ~(uintptr_t)127);
@@ -282,11 +286,31 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             }
             *reinterpret_cast<float4 *>(&sm.red[warp][lane * 4]) = op;
             named_bar_sync(BAR_COMP, NCOMP);
-            if (tid < HD) {
-                float acc = 0.0f;
+            if constexpr (!GATED) {
+                if (tid < HD) {
+                    float acc = 0.0f;
 #pragma unroll
-                for (int w = 0; w < 8; w++) acc += sm.red[w][tid];
-                act_st<OUT_BF16>(o, (size_t)item * HD + tid, acc);
+                    for (int w = 0; w < 8; w++) acc += sm.red[w][tid];
+                    act_st<OUT_BF16>(o, (size_t)item * HD + tid, acc);
+                }
+            } else {
+                // gated RMSNorm: sum of squares in double over the head, then
+                // y = (o * s) * w, times silu(z) = z / (1 + e^-z)
+                float acc = 0.0f, zv = 0.0f;
+                if (tid < HD) {
+                    zv = act_ld<ACT_BF16>(z, (size_t)item * HD + tid);
+#pragma unroll
+                    for (int w = 0; w < 8; w++) acc += sm.red[w][tid];
+                    const double ss = warp_sum_d((double)acc * (double)acc);
+                    if (lane == 0) sm.gss[warp] = ss;
+                }
+                named_bar_sync(BAR_COMP, NCOMP);
+                if (tid < HD) {
+                    const double ss = (sm.gss[0] + sm.gss[1]) + (sm.gss[2] + sm.gss[3]);
+                    const float sc = 1.0f / sqrtf((float)(ss / HD) + 1e-6f);
+                    const float y = acc * sc * norm_w[tid];
+                    act_st<OUT_BF16>(o, (size_t)item * HD + tid, y * (zv / (1.0f + expf(-zv))));
+                }
             }
             named_bar_sync(BAR_COMP, NCOMP);  // parameter slot and red[] free again
             if (tid == 0) mbar_arrive(&sm.pempty[pslot]);
@@ -295,19 +319,21 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
     __syncthreads();
 }
 
-template <bool A, bool O, bool G>
+template <bool A, bool O, bool G, bool Z>
 int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, const void *a,
            const void *b, const float *A_log, const float *dt_bias, const float *conv_w,
-           const int *pos, void *o, int B, int nqk, int nv, char *err, size_t errlen) {
+           const int *pos, const void *z, const float *norm_w, void *o, int B, int nqk, int nv,
+           char *err, size_t errlen) {
     static bool attr = false;
     const size_t smem = sizeof(DnSmem) + 128;
     if (!attr) {
-        VX_CK(cudaFuncSetAttribute(dn_decode_k<A, O, G>,
+        VX_CK(cudaFuncSetAttribute(dn_decode_k<A, O, G, Z>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attr = true;
     }
-    dn_decode_k<A, O, G><<<grid, NTHREADS, smem, st>>>(S, ring, qkv, a, b, A_log, dt_bias,
-                                                        conv_w, pos, o, B, nqk, nv, dev_status());
+    dn_decode_k<A, O, G, Z><<<grid, NTHREADS, smem, st>>>(S, ring, qkv, a, b, A_log, dt_bias,
+                                                           conv_w, pos, z, norm_w, o, B, nqk, nv,
+                                                           dev_status());
     VX_CK(cudaGetLastError());
     return 0;
 }
@@ -317,41 +343,125 @@ int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, co
 
 using namespace vx27;
 
+static int decode_batch_impl(const char *fn, float *S, float *conv_ring, const void *qkv,
+                             const void *a, const void *b, const float *A_log,
+                             const float *dt_bias, const float *conv_w, const int *pos,
+                             const void *z, const float *norm_w, void *o, int B, int nqk, int nv,
+                             int hd, int flags, void *stream, char *err, size_t errlen) {
+    if (hd != HD) return fail(err, errlen, "%s: hd=%d unsupported (128 only)", fn, hd);
+    if (B <= 0 || nqk <= 0 || nv <= 0 || nv < nqk || (long long)B * nv > (1ll << 30))
+        return fail(err, errlen, "%s: bad shape B=%d nqk=%d nv=%d", fn, B, nqk, nv);
+    if (!S || !conv_ring || !qkv || !a || !b || !conv_w || !pos || !o)
+        return fail(err, errlen, "%s: null pointer argument", fn);
+    const bool g64 = flags & VX27_F_GATES_F64;
+    if (!g64 && (!A_log || !dt_bias)) return fail(err, errlen, "%s: A_log/dt_bias required", fn);
+    if (((uintptr_t)S & 15) || ((uintptr_t)conv_w & 15))
+        return fail(err, errlen, "%s: S and conv_w must be 16-byte aligned", fn);
+    const bool gated = z != nullptr;
+    if (gated && !norm_w) return fail(err, errlen, "%s: norm_w required with z", fn);
+    const int items = B * nv;
+    const int grid = items < num_sms() ? items : num_sms();
+    cudaStream_t st = (cudaStream_t)stream;
+    const int key = (flags & VX27_F_ACT_BF16 ? 1 : 0) | (flags & VX27_F_OUT_BF16 ? 2 : 0) |
+                    (g64 ? 4 : 0) | (gated ? 8 : 0);
+#define VX_L(K, A_, O_, G_, Z_)                                                              \
+    case K:                                                                                  \
+        return launch<A_, O_, G_, Z_>(grid, st, S, conv_ring, qkv, a, b, A_log, dt_bias,     \
+                                      conv_w, pos, z, norm_w, o, B, nqk, nv, err, errlen);
+    switch (key) {
+        VX_L(0, false, false, false, false)
+        VX_L(1, true, false, false, false)
+        VX_L(2, false, true, false, false)
+        VX_L(3, true, true, false, false)
+        VX_L(4, false, false, true, false)
+        VX_L(5, true, false, true, false)
+        VX_L(6, false, true, true, false)
+        VX_L(7, true, true, true, false)
+        VX_L(8, false, false, false, true)
+        VX_L(9, true, false, false, true)
+        VX_L(10, false, true, false, true)
+        VX_L(11, true, true, false, true)
+        VX_L(12, false, false, true, true)
+        VX_L(13, true, false, true, true)
+        VX_L(14, false, true, true, true)
+        VX_L(15, true, true, true, true)
+    }
+#undef VX_L
+    return fail(err, errlen, "%s: bad flags", fn);
+}
+
 extern "C" int vx27_deltanet_decode_batch(float *S, float *conv_ring, const void *qkv,
                                           const void *a, const void *b, const float *A_log,
                                           const float *dt_bias, const float *conv_w,
                                           const int *pos, void *o, int B, int nqk, int nv,
                                           int hd, int flags, void *stream, char *err,
                                           size_t errlen) {
-    if (hd != HD)
-        return fail(err, errlen, "vx27_deltanet_decode_batch: hd=%d unsupported (128 only)", hd);
-    if (B <= 0 || nqk <= 0 || nv <= 0 || nv < nqk || (long long)B * nv > (1ll << 30))
-        return fail(err, errlen, "vx27_deltanet_decode_batch: bad shape B=%d nqk=%d nv=%d", B,
-                    nqk, nv);
-    if (!S || !conv_ring || !qkv || !a || !b || !conv_w || !pos || !o)
-        return fail(err, errlen, "vx27_deltanet_decode_batch: null pointer argument");
-    const bool g64 = flags & VX27_F_GATES_F64;
-    if (!g64 && (!A_log || !dt_bias))
-        return fail(err, errlen, "vx27_deltanet_decode_batch: A_log/dt_bias required");
-    if (((uintptr_t)S & 15) || ((uintptr_t)conv_w & 15))
-        return fail(err, errlen, "vx27_deltanet_decode_batch: S and conv_w must be 16-byte aligned");
-    const int items = B * nv;
-    const int grid = items < num_sms() ? items : num_sms();
-    cudaStream_t st = (cudaStream_t)stream;
-    const int key = (flags & VX27_F_ACT_BF16 ? 1 : 0) | (flags & VX27_F_OUT_BF16 ? 2 : 0) |
-                    (g64 ? 4 : 0);
-#define VX_L(K, A_, O_, G_) \
-    case K: return launch<A_, O_, G_>(grid, st, S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, B, nqk, nv, err, errlen);
-    switch (key) {
-        VX_L(0, false, false, false)
-        VX_L(1, true, false, false)
-        VX_L(2, false, true, false)
-        VX_L(3, true, true, false)
-        VX_L(4, false, false, true)
-        VX_L(5, true, false, true)
-        VX_L(6, false, true, true)
-        VX_L(7, true, true, true)
+    return decode_batch_impl("vx27_deltanet_decode_batch", S, conv_ring, qkv, a, b, A_log,
+                             dt_bias, conv_w, pos, nullptr, nullptr, o, B, nqk, nv, hd, flags,
+                             stream, err, errlen);
+}
+
+extern "C" int vx27_deltanet_decode_batch_gated(float *S, float *conv_ring, const void *qkv,
+                                                const void *a, const void *b,
+                                                const float *A_log, const float *dt_bias,
+                                                const float *conv_w, const int *pos,
+                                                const void *z, const float *norm_w, void *o,
+                                                int B, int nqk, int nv, int hd, int flags,
+                                                void *stream, char *err, size_t errlen) {
+    if (!z) return fail(err, errlen, "vx27_deltanet_decode_batch_gated: z required");
+    return decode_batch_impl("vx27_deltanet_decode_batch_gated", S, conv_ring, qkv, a, b,
+                             A_log, dt_bias, conv_w, pos, z, norm_w, o, B, nqk, nv, hd, flags,
+                             stream, err, errlen);
+}
+
+namespace vx27 {
+namespace {
+// Conv history after the token at device position *pos, in the reference layout
+// state[C][3] (oldest first): the inputs of tokens p-2, p-1, p.
+__global__ void conv_ckpt_k(const float *__restrict__ ring, float *__restrict__ state,
+                            const int *__restrict__ pos, int C) {
+    const int p = *pos;
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < C; c += gridDim.x * blockDim.x) {
+        float *s = state + (size_t)c * 3;
+        s[0] = ring[(size_t)((p - 2) & 3) * C + c];
+        s[1] = ring[(size_t)((p - 1) & 3) * C + c];
+        s[2] = ring[(size_t)(p & 3) * C + c];
     }
-#undef VX_L
-    return fail(err, errlen, "vx27_deltanet_decode_batch: bad flags");
+}
+}  // namespace
+}  // namespace vx27
+
+extern "C" int vx27_deltanet_decode_tokens(float *S, float *conv_ring, const void *qkv,
+                                           const void *a, const void *b, const float *A_log,
+                                           const float *dt_bias, const float *conv_w,
+                                           const int *pos, void *o, float *S_ckpt,
+                                           float *conv_ckpt, int T, int nqk, int nv, int hd,
+                                           int flags, void *stream, char *err,
+                                           size_t errlen) {
+    const char *fn = "vx27_deltanet_decode_tokens";
+    if (T <= 0) return fail(err, errlen, "%s: T=%d", fn, T);
+    if (hd != HD) return fail(err, errlen, "%s: hd=%d unsupported (128 only)", fn, hd);
+    if (nqk <= 0 || nv < nqk) return fail(err, errlen, "%s: bad shape nqk=%d nv=%d", fn, nqk, nv);
+    if (!qkv || !a || !b || !pos || !o) return fail(err, errlen, "%s: null pointer argument", fn);
+    const size_t C = (size_t)(2 * nqk + nv) * HD;
+    const size_t ea = (flags & VX27_F_ACT_BF16) ? 2 : 4, eo = (flags & VX27_F_OUT_BF16) ? 2 : 4;
+    cudaStream_t st = (cudaStream_t)stream;
+    for (int t = 0; t < T; t++) {
+        const int rc = decode_batch_impl(
+            fn, S, conv_ring, (const uint8_t *)qkv + t * C * ea, (const uint8_t *)a + t * nv * ea,
+            (const uint8_t *)b + t * nv * ea, A_log, dt_bias, conv_w, pos + t, nullptr, nullptr,
+            (uint8_t *)o + (size_t)t * nv * HD * eo, 1, nqk, nv, hd, flags, stream, err, errlen);
+        if (rc) return rc;
+        if (S_ckpt)
+            VX_CK(cudaMemcpyAsync(S_ckpt + (size_t)t * nv * HD * HD, S,
+                                  (size_t)nv * HD * HD * sizeof(float), cudaMemcpyDeviceToDevice,
+                                  st));
+        if (conv_ckpt) {
+            conv_ckpt_k<<<(unsigned)((C + 255) / 256), 256, 0, st>>>(conv_ring,
+                                                                    conv_ckpt + (size_t)t * C * 3,
+                                                                    pos + t, (int)C);
+            VX_CK(cudaGetLastError());
+        }
+    }
+    return 0;
 }

@@ -104,8 +104,12 @@ gqa_combine_k(const float *__restrict__ parts, int n_parts, const void *__restri
         }
     }
     const float att = L > 0.0f ? O / L : 0.0f;
-    const float g = act_ld<ACT_BF16>(gate, hq * HD + d);
-    act_st<OUT_BF16>(out, hq * HD + d, att * (1.0f / (1.0f + expf(-g))));
+    if (gate) {
+        const float g = act_ld<ACT_BF16>(gate, hq * HD + d);
+        act_st<OUT_BF16>(out, hq * HD + d, att * (1.0f / (1.0f + expf(-g))));
+    } else {  // no output gate (the MTP drafter's use_gate = 0, src/vx27_mtp.c:249)
+        act_st<OUT_BF16>(out, hq * HD + d, att);
+    }
 }
 
 // Merges n_parts partial records into one partial record (same layout), for a range
@@ -249,7 +253,7 @@ int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
                           int hd, int n_splits, int flags, void *stream, char *err,
                           size_t errlen) {
     if (check_shape("vx27_gqa_decode_batch", B, nq, nkv, hd, err, errlen)) return -1;
-    if (!q || !gate || !k_cache || !v_cache || !pos || !out || !workspace || cap <= 0)
+    if (!q || !k_cache || !v_cache || !pos || !out || !workspace || cap <= 0)
         return fail(err, errlen, "vx27_gqa_decode_batch: null pointer argument");
     const size_t rec = (size_t)B * nq * (hd + 2) * sizeof(float);
     const int fit = (int)(workspace_bytes / rec);
@@ -306,7 +310,7 @@ int vx27_gqa_combine(const float *parts, int n_parts, size_t part_stride, const 
                      void *out, int B, int nq, int hd, int flags, void *stream, char *err,
                      size_t errlen) {
     if (hd != HD) return fail(err, errlen, "vx27_gqa_combine: hd=%d unsupported (256 only)", hd);
-    if (!parts || !gate || !out || n_parts < 1 || B <= 0 || nq <= 0)
+    if (!parts || !out || n_parts < 1 || B <= 0 || nq <= 0)
         return fail(err, errlen, "vx27_gqa_combine: bad arguments");
     const size_t rec = (size_t)B * nq * (hd + 2);
     if (part_stride && part_stride < rec)

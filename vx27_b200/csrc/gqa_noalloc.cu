@@ -61,7 +61,7 @@ extern "C" int vx27_gqa_decode_batch_noalloc(const float *q, const void *gate,
     if (hd != 256) return fail(err, errlen, "%s: hd=%d unsupported (256 only)", fn, hd);
     if (B <= 0 || B > 65535 || nq <= 0 || nkv <= 0 || nkv > 65535 || nq % nkv)
         return fail(err, errlen, "%s: bad shape B=%d nq=%d nkv=%d", fn, B, nq, nkv);
-    if (!q || !gate || !k_cache || !v_cache || !pos || !out || cap <= 0)
+    if (!q || !k_cache || !v_cache || !pos || !out || cap <= 0)
         return fail(err, errlen, "%s: null pointer argument", fn);
     const size_t record = (size_t)B * nq * (hd + 2) * sizeof(float);
     const int fit = (int)((size_t)VX27_GQA_NOALLOC_SCRATCH_BYTES / record);

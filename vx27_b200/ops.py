@@ -157,6 +157,39 @@ def deltanet_decode_batch(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, 
     check(rc, e)
 
 
+def deltanet_decode_tokens(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, nqk: int,
+                           nv: int, S_ckpt=None, conv_ckpt=None, stream=None) -> None:
+    """T tokens of one sequence (vx27_deltanet_decode_tokens); S [nv][128][128],
+    conv_ring [4][C], qkv [T][C], a, b [T][nv], pos [T], o [T][nv][128]; optional
+    S_ckpt [T][nv][128][128] and conv_ckpt [T][C][3] snapshots."""
+    T = qkv.shape[0]
+    flags = (F_ACT_BF16 if _is_bf16(qkv) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0)
+    e = errbuf()
+    rc = load().vx27_deltanet_decode_tokens(_t(S), _t(conv_ring), _t(qkv), _t(a), _t(b),
+                                            _t(A_log), _t(dt_bias), _t(conv_w), _t(pos), _t(o),
+                                            _t(S_ckpt), _t(conv_ckpt), T, nqk, nv, 128, flags,
+                                            _stream(stream), e, 512)
+    check(rc, e)
+
+
+def deltanet_decode_batch_gated(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, z,
+                                norm_w, o, nqk: int, nv: int, gates_f64: bool = False,
+                                stream=None) -> None:
+    """Decode step plus the gated RMSNorm output (vx27_deltanet_decode_batch_gated)."""
+    B = S.shape[0]
+    hd = S.shape[-1]
+    flags = (F_ACT_BF16 if _is_bf16(qkv) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0) | \
+        (F_GATES_F64 if gates_f64 else 0)
+    if _is_bf16(qkv) != _is_bf16(z):
+        raise Vx27Error("z must have the activation dtype of qkv")
+    e = errbuf()
+    rc = load().vx27_deltanet_decode_batch_gated(_t(S), _t(conv_ring), _t(qkv), _t(a), _t(b),
+                                                 _t(A_log), _t(dt_bias), _t(conv_w), _t(pos),
+                                                 _t(z), _t(norm_w), _t(o), B, nqk, nv, hd,
+                                                 flags, _stream(stream), e, 512)
+    check(rc, e)
+
+
 def deltanet_prefill_chunked(q, k, v, a, b, A_log, dt_bias, S, o, workspace=None,
                              gates_f64: bool = False, stream=None) -> None:
     """Chunked gated delta rule over T tokens (vx27_deltanet_prefill_chunked).
@@ -211,7 +244,8 @@ def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: i
                      stream=None) -> None:
     B, nq, hd = q.shape
     nkv, cap = k_cache.shape[1], k_cache.shape[2]
-    flags = (F_ACT_BF16 if _is_bf16(gate) else 0) | (F_OUT_BF16 if _is_bf16(out) else 0)
+    flags = (F_ACT_BF16 if gate is not None and _is_bf16(gate) else 0) | \
+        (F_OUT_BF16 if _is_bf16(out) else 0)
     e = errbuf()
     rc = load().vx27_gqa_decode_batch(_t(q), _t(gate), _t(k_cache), _t(v_cache), cap, _t(pos),
                                       _t(out), _t(workspace),
@@ -238,9 +272,11 @@ def gqa_partial(q, k_cache, v_cache, p_begin: int, p_end: int, part, workspace=N
 
 
 def gqa_combine(parts, n_parts: int, gate, out, part_stride: int = 0, stream=None) -> None:
-    """Merges n_parts partial records placed part_stride floats apart (0: contiguous)."""
-    B, nq, hd = gate.shape
-    flags = (F_ACT_BF16 if _is_bf16(gate) else 0) | (F_OUT_BF16 if _is_bf16(out) else 0)
+    """Merges n_parts partial records placed part_stride floats apart (0: contiguous);
+    gate None: no output gate."""
+    B, nq, hd = out.shape
+    flags = (F_ACT_BF16 if gate is not None and _is_bf16(gate) else 0) | \
+        (F_OUT_BF16 if _is_bf16(out) else 0)
     e = errbuf()
     if parts.is_cuda and not parts.is_contiguous():
         raise Vx27Error("parts must be contiguous")
