@@ -32,6 +32,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "DeltaNet+GQA decode tokens/s at 1/2/4/8 B200; % of HBM roofline"
+# DRAM bytes (read + write) per algorithmic byte of the split-KV GQA decode kernel, from an
+# ncu capture of the same kernel at 32 sequences (the full 256-sequence workload holds
+# 83 GB, too much to profile); the excess is the unused rows of each sequence's last
+# 128-position tile.
+GQA_SPLIT_DRAM_PER_ALGO_BYTE = 1.0297
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -227,7 +232,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "roofline": {
             "bound": "hbm", "kernel": "gqa split-KV decode (per layer, + combine)",
             "achieved": round(gqa_gbs, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(gqa_gbs / peak, 4), "traffic": None, "peak_source": peak_src,
+            "frac": round(gqa_gbs / peak, 4),
+            "traffic": int(GQA_SPLIT_DRAM_PER_ALGO_BYTE * gqa_bytes),
+            "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of gqa_split_tc "
+                               "at B = 32 (same kernel, context and splits per sequence; "
+                               f"{GQA_SPLIT_DRAM_PER_ALGO_BYTE} x its algorithmic bytes), "
+                               "scaled by the sequences of this launch"),
+            "peak_source": peak_src,
             "algorithmic_bytes_per_launch": int(gqa_bytes), "avg_launch_ms": round(gqa_ms, 4),
         },
         "roofline_other": {
