@@ -70,25 +70,25 @@ __device__ __forceinline__ void bulk_wait0() {
 
 // ---- workspace: per (V head, chunk) block, blk = vh * n_chunks + chunk --------------------
 constexpr size_t SZ_WKA = 32768;  // [Wk_hi; Wk_lo] rows t, K-major over d (scan MMA1 A)
-constexpr size_t SZ_KR = 16384;   // Kr^T hi or lo: MN-major image rows t, cols d (scan MMA2 A)
+constexpr size_t SZ_KT = 16384;   // raw K^T: MN-major image rows t, cols d (scan MMA2 A)
 constexpr size_t SZ_QB = 16384;   // raw Q rows t, K-major over d (out MMA1 B)
 constexpr size_t SZ_PM = 16384;   // [Pm_hi; Pm_lo] rows t, K-major over s (out MMA2 B)
 constexpr size_t SZ_SC = 32768;   // S0^T hi or lo: rows v, K-major over d (out MMA1 A)
 constexpr size_t SZ_U = 16384;    // U^T hi or lo: rows v, K-major over t (out MMA2 A)
 constexpr size_t SZ_WV = 32768;   // Wv fp32 in 16-column groups: [d/16][t][16]
-constexpr size_t SZ_SCAL = 512;   // [0] = e^{G_C}; [64 + t] = e^{G_t} rq_t / sqrt(128)
+constexpr size_t SZ_SCAL = 1024;  // [0] = e^{G_C}; [64 + t] = e^{G_t} rq_t / sqrt(128);
+                                  // [128 + t] = e^{G_C - G_t} rk_t
 constexpr size_t BLK_BYTES =
-    SZ_WKA + 2 * SZ_KR + SZ_QB + SZ_PM + 2 * SZ_SC + 2 * SZ_U + SZ_WV + SZ_SCAL;
+    SZ_WKA + SZ_KT + SZ_QB + SZ_PM + 2 * SZ_SC + 2 * SZ_U + SZ_WV + SZ_SCAL;
 
 struct Wsp {
-    uint8_t *WkA, *KrH, *KrL, *QB, *PmB, *ScH, *ScL, *UH, *UL;
+    uint8_t *WkA, *KtA, *QB, *PmB, *ScH, *ScL, *UH, *UL;
     float *Wv, *scal;
 };
 inline Wsp wsp_views(uint8_t *p, size_t nblk) {
     Wsp w;
     w.WkA = p; p += nblk * SZ_WKA;
-    w.KrH = p; p += nblk * SZ_KR;
-    w.KrL = p; p += nblk * SZ_KR;
+    w.KtA = p; p += nblk * SZ_KT;
     w.QB = p; p += nblk * SZ_QB;
     w.PmB = p; p += nblk * SZ_PM;
     w.ScH = p; p += nblk * SZ_SC;
@@ -221,13 +221,17 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         const float gam = (float)exp(G[tid]);
         xs[tid] = gam * rk[tid];
         er[tid] = (float)exp(G[CK - 1] - G[tid]) * rk[tid];
-        ws.scal[blk * 128 + 64 + tid] = gam * __fmul_rn(rq[tid], qscale);
+        ws.scal[blk * 256 + 64 + tid] = gam * __fmul_rn(rq[tid], qscale);
+        ws.scal[blk * 256 + 128 + tid] = er[tid];
     }
     if (tid == 0 && ok) {
-        ws.scal[blk * 128] = (float)exp(G[CK - 1]);
-        // raw Q (rows 64..127 of each column block) -> the out kernel's B operand image
+        ws.scal[blk * 256] = (float)exp(G[CK - 1]);
+        // raw Q (rows 64..127 of each column block) -> the out kernel's B operand image, raw
+        // K (rows 0..63) -> the scan's K^T operand image (MN-major: rows t, columns d)
         bulk_s2g(ws.QB + blk * SZ_QB, AKQ + 8192, 8192);
         bulk_s2g(ws.QB + blk * SZ_QB + 8192, AKQ + 16384 + 8192, 8192);
+        bulk_s2g(ws.KtA + blk * SZ_KT, AKQ, 8192);
+        bulk_s2g(ws.KtA + blk * SZ_KT + 8192, AKQ + 16384, 8192);
         bulk_commit();
         // Gram: D[0:128, 0:64] = [K;Q] K^T
         const uint32_t id = idesc_bf16(128, CK, false, false);
@@ -238,29 +242,6 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             mma_bf16(tbase, de, de, id, kk > 0);
         }
         mma_commit(bar);
-    }
-    __syncthreads();  // er[] visible
-    // 3. Kr^T = K^T diag(e^{G_C - G} rk) as hi/lo MN-major images (rows t, cols d)
-#pragma unroll 1
-    for (int ch = tid; ch < 1024; ch += 128) {
-        const int b = ch >> 9, t = (ch >> 3) & 63, pc = ch & 7;
-        const int d0 = b * 64 + ((pc ^ (t & 7)) << 3);
-        const uint4 raw = *reinterpret_cast<const uint4 *>(AKQ + swz(t, d0, 128));
-        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-        const float s = er[t];
-        uint32_t hw[4], lw[4];
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            uint16_t h0, l0, h1, l1;
-            split_bf16(bf16_to_f32(w[e] & 0xffffu) * s, h0, l0);
-            split_bf16(bf16_to_f32(w[e] >> 16) * s, h1, l1);
-            hw[e] = h0 | ((uint32_t)h1 << 16);
-            lw[e] = l0 | ((uint32_t)l1 << 16);
-        }
-        *reinterpret_cast<uint4 *>(ws.KrH + blk * SZ_KR + ch * 16) =
-            make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4 *>(ws.KrL + blk * SZ_KR + ch * 16) =
-            make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
     if (ok) ok = mbar_wait(bar, 1, status, VX_DEV_TIMEOUT_MMA);
     ok = __syncthreads_and(ok);
@@ -383,7 +364,7 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             mma_commit(bar);
         }
         ok = mbar_wait(bar, 0, status, VX_DEV_TIMEOUT_MMA);  // third phase
-        if (tid == 0) bulk_wait_read0();  // the Q image copy has left AKQ
+        if (tid == 0) bulk_wait_read0();  // the Q and K image copies have left AKQ
         ok = __syncthreads_and(ok);
         tc_fence_after();
         if (ok) {
@@ -425,24 +406,30 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
 
 // ---- phase 2: the sequential state scan ---------------------------------------------------
 // CTA (column block cb, V head vh) owns state columns [cb*CB, cb*CB + CB). Warps 0-3 run
-// the epilogues and thread 0 issues the MMAs; warp 4 streams each chunk's Wk and Kr^T tiles,
-// the CTA's Wv columns and the chunk decay into a two-stage ring.
-//   MMA1: D1[128 x 2CB] = [Wk_hi; Wk_lo] [S_hi | S_lo]   (U = Wv - sum of the 4 quadrants)
-//   MMA2: D2[128 x 2CB] = Kr^T_hi [U_hi | U_lo] + Kr^T_lo [U_hi | U_lo]   (dS = both halves)
+// the epilogues and thread 0 issues the MMAs; warp 4 moves data: each chunk's Wk, raw K^T,
+// Wv columns and scalars into a two-stage ring, and the S0 / U images out to the workspace.
+//   MMA1: D1[128 x 2CB] = [Wk_hi; Wk_lo] [S_hi | S_lo]       (U = Wv - sum of 4 quadrants)
+//   MMA2: D2[128 x 2CB] = K^T [U'_hi | U'_lo], U' = diag(e^{G_C-G} rk) U   (dS = both halves)
+// Per chunk the 160 threads meet at barrier A (state operand ready) and B (U ready); warp 4
+// waits for its bulk stores to finish reading shared memory before it arrives at the next
+// barrier, so the buffers they read are never rewritten under them.
 template <int CB>
 struct ScanLayout {
     static constexpr int NB = 2 * CB;
-    // stage: Wk 32K | Kr^T hi 16K | Kr^T lo 16K | Wv [CB/16][64][16] fp32 | decay (16 B)
-    static constexpr uint32_t ST_WV = 65536;
-    static constexpr uint32_t ST_G = ST_WV + CB * 256;
-    static constexpr uint32_t STAGE_TX = ST_G + 16;
-    static constexpr uint32_t STAGE = ST_G + 1024;
+    // stage: Wk 32K | K^T 16K | Wv [CB/16][64][16] fp32 | scalars (1 KB)
+    static constexpr uint32_t ST_KT = 32768;
+    static constexpr uint32_t ST_WV = 49152;
+    static constexpr uint32_t ST_SC = ST_WV + CB * 256;
+    static constexpr uint32_t STAGE_TX = ST_SC + 1024;
+    static constexpr uint32_t STAGE = STAGE_TX;                // multiple of 1024
     static constexpr uint32_t SB = 2 * STAGE;                  // [S_hi; S_lo] over d: 2 blocks
-    static constexpr uint32_t UB = SB + 2 * NB * 128;          // [U_hi; U_lo] over t: 1 block
-    static constexpr uint32_t XCH = UB + NB * 128;             // float [CB/2][128]
-    static constexpr uint32_t BAR = XCH + (CB / 2) * 128 * 4;  // full[2] empty[2] m1 m2
-    static constexpr uint32_t SMEM = BAR + 6 * 8 + 16 + 1024;
+    static constexpr uint32_t UB = SB + 2 * NB * 128;          // [U_hi; U_lo] over t (image)
+    static constexpr uint32_t UB2 = UB + NB * 128;             // [U'_hi; U'_lo] (MMA2 B)
+    static constexpr uint32_t XCH = UB2 + NB * 128;            // float [CB/2][128]
+    static constexpr uint32_t BAR = XCH + (CB / 2) * 128 * 4;  // full[2] m1 m2
+    static constexpr uint32_t SMEM = BAR + 4 * 8 + 16 + 1024;
 };
+constexpr int SCAN_BAR_A = 1, SCAN_BAR_X = 2, SCAN_BAR_B = 3;
 
 template <int CB>
 __global__ void __launch_bounds__(160, 1)
@@ -453,15 +440,15 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
     constexpr int JS = HC < 16 ? HC : 16;  // TMEM columns per load in the U epilogue
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = align1024(smraw);
-    uint8_t *stg = sm, *SB = sm + Lay::SB, *UB = sm + Lay::UB;
+    uint8_t *stg = sm, *SB = sm + Lay::SB, *UB = sm + Lay::UB, *UB2 = sm + Lay::UB2;
     float *xch = reinterpret_cast<float *>(sm + Lay::XCH);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + Lay::BAR);
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 6);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + Lay::BAR);  // full[2], m1, m2
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 4);
     volatile int *abort_ = reinterpret_cast<volatile int *>(tslot + 1);
     const int cb = blockIdx.x, vh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5,
               lane = tid & 31;
     if (tid == 0) {
-        for (int i = 0; i < 6; i++) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 4; i++) mbar_init(&bars[i], 1);
         *abort_ = 0;
         fence_barrier_init();
     }
@@ -473,26 +460,44 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
     tc_fence_after();
     const uint32_t tbase = *tslot;
 
-    if (warp == 4) {  // producer
-        if (lane == 0) {
-            for (int c = 0; c < n_chunks; c++) {
-                const int s = c & 1;
-                if (c >= 2 && (*abort_ || !mbar_wait(&bars[2 + s], ((c >> 1) - 1) & 1, status,
-                                                     VX_DEV_TIMEOUT_MMA))) {
-                    *abort_ = 1;
-                    break;
+    if (warp == 4) {  // ---- data mover: every lane runs the barrier sequence, lane 0 copies
+        auto load_stage = [&](int c) {
+            const int s = c & 1;
+            const size_t blk = (size_t)vh * n_chunks + c;
+            uint8_t *dst = stg + s * Lay::STAGE;
+            mbar_arrive_expect_tx(&bars[s], Lay::STAGE_TX);
+            bulk_g2s(dst, ws.WkA + blk * SZ_WKA, 32768, &bars[s]);
+            bulk_g2s(dst + Lay::ST_KT, ws.KtA + blk * SZ_KT, 16384, &bars[s]);
+            bulk_g2s(dst + Lay::ST_WV, ws.Wv + blk * (CK * D) + cb * CB * CK, CB * 256, &bars[s]);
+            bulk_g2s(dst + Lay::ST_SC, ws.scal + blk * 256, 1024, &bars[s]);
+        };
+        if (lane == 0) load_stage(0);
+        for (int c = 0; c < n_chunks; c++) {
+            const size_t blk = (size_t)vh * n_chunks + c;
+            named_bar_sync(SCAN_BAR_A, 160);
+            if (lane == 0) {
+                // the state at this chunk's start -> S0^T images for the output kernel
+#pragma unroll
+                for (int b = 0; b < 2; b++) {
+                    bulk_s2g(ws.ScH + blk * SZ_SC + b * 16384 + cb * CB * 128, SB + b * NB * 128,
+                             CB * 128);
+                    bulk_s2g(ws.ScL + blk * SZ_SC + b * 16384 + cb * CB * 128,
+                             SB + b * NB * 128 + CB * 128, CB * 128);
                 }
-                const size_t blk = (size_t)vh * n_chunks + c;
-                uint8_t *dst = stg + s * Lay::STAGE;
-                mbar_arrive_expect_tx(&bars[s], Lay::STAGE_TX);
-                bulk_g2s(dst, ws.WkA + blk * SZ_WKA, 32768, &bars[s]);
-                bulk_g2s(dst + 32768, ws.KrH + blk * SZ_KR, 16384, &bars[s]);
-                bulk_g2s(dst + 49152, ws.KrL + blk * SZ_KR, 16384, &bars[s]);
-                bulk_g2s(dst + Lay::ST_WV, ws.Wv + blk * (CK * D) + cb * CB * CK, CB * 256,
-                         &bars[s]);
-                bulk_g2s(dst + Lay::ST_G, ws.scal + blk * 128, 16, &bars[s]);
+                bulk_commit();
+                // stage (c+1)&1 held chunk c-1, whose MMAs completed before barrier A
+                if (c + 1 < n_chunks && !*abort_) load_stage(c + 1);
+                bulk_wait_read0();  // S0 images out before the state operand is rewritten
+            }
+            named_bar_sync(SCAN_BAR_B, 160);
+            if (lane == 0) {
+                bulk_s2g(ws.UH + blk * SZ_U + cb * CB * 128, UB, CB * 128);
+                bulk_s2g(ws.UL + blk * SZ_U + cb * CB * 128, UB + CB * 128, CB * 128);
+                bulk_commit();
+                bulk_wait_read0();  // U images out before the next chunk rewrites U
             }
         }
+        if (lane == 0) bulk_wait0();
         return;
     }
 
@@ -520,10 +525,9 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
 
     for (int c = 0; c < n_chunks; c++) {
         const int st = c & 1;
-        const size_t blk = (size_t)vh * n_chunks + c;
         uint8_t *stage = stg + st * Lay::STAGE;
         tc_fence_before();
-        named_bar_sync(1, 128);
+        named_bar_sync(SCAN_BAR_A, 160);
         if (tid == 0) {
             if (!*abort_ && !mbar_wait(&bars[st], (c >> 1) & 1, status, VX_DEV_TIMEOUT_TMA))
                 *abort_ = 1;
@@ -538,23 +542,15 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
                              sdesc_sw128(smem_u32(SB) + (kk >> 2) * (NB * 128) + (kk & 3) * 32,
                                          16, 1024),
                              id, kk > 0);
-                mma_commit(&bars[4]);
-                // the state at this chunk's start -> S0^T images for the output kernel
-#pragma unroll
-                for (int b = 0; b < 2; b++) {
-                    bulk_s2g(ws.ScH + blk * SZ_SC + b * 16384 + cb * CB * 128, SB + b * NB * 128,
-                             CB * 128);
-                    bulk_s2g(ws.ScL + blk * SZ_SC + b * 16384 + cb * CB * 128,
-                             SB + b * NB * 128 + CB * 128, CB * 128);
-                }
-                bulk_commit();
+                mma_commit(&bars[2]);
             }
         }
-        if (!*abort_ && !mbar_wait(&bars[4], c & 1, status, VX_DEV_TIMEOUT_MMA)) *abort_ = 1;
+        if (!*abort_ && !mbar_wait(&bars[2], c & 1, status, VX_DEV_TIMEOUT_MMA)) *abort_ = 1;
         tc_fence_after();
         // U = Wv - (quadrant sums): own half kept, the other half handed to thread tid ^ 64
         const float *wv_s = reinterpret_cast<const float *>(stage + Lay::ST_WV);
-        const float g63 = *reinterpret_cast<const float *>(stage + Lay::ST_G);
+        const float *sc = reinterpret_cast<const float *>(stage + Lay::ST_SC);
+        const float g63 = sc[0], er = sc[128 + t];
         float wv[HC];
 #pragma unroll
         for (int j = 0; j < HC; j++) {
@@ -583,8 +579,7 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
 #pragma unroll
             for (int j = 0; j < JS; j++) wv[j0 + j] -= a[j] + b2[j];
         }
-        if (tid == 0) bulk_wait_read0();  // the previous U image and this S0 image have left
-        named_bar_sync(2, 128);
+        named_bar_sync(SCAN_BAR_X, 128);
 #pragma unroll
         for (int j = 0; j < HC; j++) {
             const float u = wv[j] - xch[j * 128 + tid];
@@ -592,30 +587,24 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
             split_bf16(u, h, l);
             st16(UB, swz(jh + j, t, NB), h);
             st16(UB, swz(CB + jh + j, t, NB), l);
+            split_bf16(u * er, h, l);
+            st16(UB2, swz(jh + j, t, NB), h);
+            st16(UB2, swz(CB + jh + j, t, NB), l);
         }
         fence_proxy_async();
         tc_fence_before();
-        named_bar_sync(1, 128);
+        named_bar_sync(SCAN_BAR_B, 160);
         if (tid == 0 && !*abort_) {
             tc_fence_after();
             const uint32_t id = idesc_bf16(128, NB, true, false);
 #pragma unroll
             for (int kk = 0; kk < CK / 16; kk++)
                 mma_bf16(tbase + NB,
-                         sdesc_sw128(smem_u32(stage) + 32768 + kk * 2048, 8192, 1024),
-                         sdesc_sw128(smem_u32(UB) + kk * 32, 16, 1024), id, kk > 0);
-#pragma unroll
-            for (int kk = 0; kk < CK / 16; kk++)
-                mma_bf16(tbase + NB,
-                         sdesc_sw128(smem_u32(stage) + 49152 + kk * 2048, 8192, 1024),
-                         sdesc_sw128(smem_u32(UB) + kk * 32, 16, 1024), id, 1);
-            mma_commit(&bars[5]);
-            mma_commit(&bars[2 + st]);
-            bulk_s2g(ws.UH + blk * SZ_U + cb * CB * 128, UB, CB * 128);
-            bulk_s2g(ws.UL + blk * SZ_U + cb * CB * 128, UB + CB * 128, CB * 128);
-            bulk_commit();
+                         sdesc_sw128(smem_u32(stage) + Lay::ST_KT + kk * 2048, 8192, 1024),
+                         sdesc_sw128(smem_u32(UB2) + kk * 32, 16, 1024), id, kk > 0);
+            mma_commit(&bars[3]);
         }
-        if (!*abort_ && !mbar_wait(&bars[5], c & 1, status, VX_DEV_TIMEOUT_MMA)) *abort_ = 1;
+        if (!*abort_ && !mbar_wait(&bars[3], c & 1, status, VX_DEV_TIMEOUT_MMA)) *abort_ = 1;
         tc_fence_after();
 #pragma unroll
         for (int j0 = 0; j0 < CB; j0 += 16) {
@@ -629,9 +618,8 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
     }
 #pragma unroll
     for (int j = 0; j < CB; j++) Sh[j] = s[j];
-    if (tid == 0) bulk_wait0();
     tc_fence_before();
-    named_bar_sync(1, 128);
+    named_bar_sync(SCAN_BAR_X, 128);
     if (warp == 0) tmem_dealloc(tbase, 2 * NB);
 }
 
@@ -667,7 +655,7 @@ dn_out_tc(Wsp ws, void *__restrict__ o, int T, int nv, int n_chunks, uint32_t *s
         tmem_alloc(tslot, 256);
         tmem_relinquish();
     }
-    if (tid < CK) ct[tid] = ws.scal[blk * 128 + 64 + tid];
+    if (tid < CK) ct[tid] = ws.scal[blk * 256 + 64 + tid];
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;

@@ -83,6 +83,7 @@ __device__ __forceinline__ uint16_t bf16_bits(float x) { return f32_to_bf16(x); 
 template <int G>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+             const __grid_constant__ CUtensorMap tmk32, const __grid_constant__ CUtensorMap tmv32,
              const float *__restrict__ q, const int *__restrict__ pos, float *__restrict__ parts,
              int cap, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
              uint32_t *status) {
@@ -176,9 +177,20 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
                 if (round > 0 && !tc_wait(&sm.empty[slot], (round - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
                     break;
                 const int tile = j >> 3, r = j & 7;
-                mbar_arrive_expect_tx(&sm.full[slot], SLOT_BYTES);
-                tma_load_2d(sm.ring[slot], r < 4 ? &tmk : &tmv, (r & 3) * 64,
-                            row0 + tile * TC_TILE, &sm.full[slot]);
+                // the last tile fetches only the 32-row boxes that hold positions of the
+                // range (the rows past it are masked, and V's are zeroed, by the softmax warps)
+                const int rows_left = p1 - (p0 + tile * TC_TILE);
+                if (rows_left < TC_TILE) {
+                    const int nsub = (rows_left + 31) / 32;
+                    mbar_arrive_expect_tx(&sm.full[slot], nsub * (SLOT_BYTES / 4));
+                    for (int k = 0; k < nsub; k++)
+                        tma_load_2d(sm.ring[slot] + k * (SLOT_BYTES / 4), r < 4 ? &tmk32 : &tmv32,
+                                    (r & 3) * 64, row0 + tile * TC_TILE + 32 * k, &sm.full[slot]);
+                } else {
+                    mbar_arrive_expect_tx(&sm.full[slot], SLOT_BYTES);
+                    tma_load_2d(sm.ring[slot], r < 4 ? &tmk : &tmv, (r & 3) * 64,
+                                row0 + tile * TC_TILE, &sm.full[slot]);
+                }
             }
             if (sm.abort) {  // let the copies already issued land before the CTA exits
                 for (int k = max(0, j - NSLOT); k < j; k++) {
@@ -376,10 +388,12 @@ size_t tc_smem_bytes() { return sizeof(TcSmem) + 1024; }
 int launch_split_tc(const void *kc, const void *vc, const float *q, const int *pos, float *parts,
                     int cap, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
                     cudaStream_t st, char *err, size_t errlen) {
-    CUtensorMap mk, mv;
+    CUtensorMap mk, mv, mk32, mv32;
     const uint64_t rows = (uint64_t)B * nkv * cap;
     if (make_tmap_bf16_2d(&mk, kc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
-        make_tmap_bf16_2d(&mv, vc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen))
+        make_tmap_bf16_2d(&mv, vc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
+        make_tmap_bf16_2d(&mk32, kc, rows, HDIM, HDIM * 2, 64, 32, err, errlen) ||
+        make_tmap_bf16_2d(&mv32, vc, rows, HDIM, HDIM * 2, 64, 32, err, errlen))
         return -1;
     const size_t smem = tc_smem_bytes();
     const dim3 grid(n_splits, nkv, B);
@@ -393,8 +407,9 @@ int launch_split_tc(const void *kc, const void *vc, const float *q, const int *p
                                        (int)smem));                                       \
             attr = true;                                                                  \
         }                                                                                 \
-        gqa_split_tc<GG><<<grid, TC_THREADS, smem, st>>>(mk, mv, q, pos, parts, cap, B, nq, \
-                                                         nkv, n_splits, p_begin, p_end, stw); \
+        gqa_split_tc<GG><<<grid, TC_THREADS, smem, st>>>(mk, mv, mk32, mv32, q, pos, parts, cap, \
+                                                         B, nq, nkv, n_splits, p_begin,    \
+                                                         p_end, stw);                      \
         break;                                                                            \
     }
     switch (nq / nkv) {
@@ -412,10 +427,12 @@ int launch_split_tc(const void *kc, const void *vc, const float *q, const int *p
 int launch_split_tc_status(const void *kc, const void *vc, const float *q, const int *pos,
                            float *parts, int cap, int B, int nq, int nkv, int n_splits,
                            uint32_t *status, cudaStream_t st, char *err, size_t errlen) {
-    CUtensorMap mk, mv;
+    CUtensorMap mk, mv, mk32, mv32;
     const uint64_t rows = (uint64_t)B * nkv * cap;
     if (make_tmap_bf16_2d(&mk, kc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
-        make_tmap_bf16_2d(&mv, vc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen))
+        make_tmap_bf16_2d(&mv, vc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
+        make_tmap_bf16_2d(&mk32, kc, rows, HDIM, HDIM * 2, 64, 32, err, errlen) ||
+        make_tmap_bf16_2d(&mv32, vc, rows, HDIM, HDIM * 2, 64, 32, err, errlen))
         return -1;
     const size_t smem = tc_smem_bytes();
     const dim3 grid(n_splits, nkv, B);
@@ -428,8 +445,9 @@ int launch_split_tc_status(const void *kc, const void *vc, const float *q, const
                                        (int)smem));                                       \
             attr = true;                                                                  \
         }                                                                                 \
-        gqa_split_tc<GG><<<grid, TC_THREADS, smem, st>>>(mk, mv, q, pos, parts, cap, B, nq, \
-                                                         nkv, n_splits, 0, -1, status);   \
+        gqa_split_tc<GG><<<grid, TC_THREADS, smem, st>>>(mk, mv, mk32, mv32, q, pos, parts, cap, \
+                                                         B, nq, nkv, n_splits, 0, -1,      \
+                                                         status);                          \
         break;                                                                            \
     }
     switch (nq / nkv) {
