@@ -49,6 +49,19 @@ __device__ __forceinline__ void split_bf16(float x, uint16_t &h, uint16_t &l) {
     h = f32_to_bf16(x);
     l = f32_to_bf16(x - bf16_to_f32(h));
 }
+// Eight fp32 values -> packed bf16 hi and lo words (x = hi + lo to ~16 significant bits).
+__device__ __forceinline__ void split8(const float *x, uint4 &hi, uint4 &lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        h[e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
+        const float r0 = x[2 * e] - __uint_as_float(h[e] << 16);
+        const float r1 = x[2 * e + 1] - __uint_as_float(h[e] & 0xffff0000u);
+        l[e] = pack_bf16x2(r0, r1);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
 __device__ __forceinline__ void st16(uint8_t *base, uint32_t off, uint16_t v) {
     *reinterpret_cast<uint16_t *>(base + off) = v;
 }
@@ -334,33 +347,50 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             __syncthreads();
         }
         // X = Li diag(beta) (lower triangle) -> [X_hi; X_lo] over L's space, and
-        // X diag(e^G rk) -> its hi/lo pair; a warp covers 32 columns s of one row t
-#pragma unroll 2
-        for (int e = tid; e < CK * CK; e += 128) {
-            const int t2 = e >> 6, sc = e & 63;
-            const float xv = sc <= t2 ? Li[fsw(t2, sc)] * beta[sc] : 0.f;
-            uint16_t h, l;
-            split_bf16(xv, h, l);
-            st16(XV, swz(t2, sc, 128), h);
-            st16(XV, swz(CK + t2, sc, 128), l);
-            split_bf16(xv * xs[sc], h, l);
-            st16(XK, swz(t2, sc, 128), h);
-            st16(XK, swz(CK + t2, sc, 128), l);
+        // X diag(e^G rk) -> its hi/lo pair; one item = 8 consecutive columns s of a row t
+#pragma unroll 1
+        for (int it = tid; it < CK * CK / 8; it += 128) {
+            const int t2 = it >> 3, s0 = (it & 7) * 8;
+            const float4 l0 = *reinterpret_cast<const float4 *>(Li + fsw(t2, s0));
+            const float4 l1 = *reinterpret_cast<const float4 *>(Li + fsw(t2, s0 + 4));
+            const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+            float xv[8], xk[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                xv[e] = s0 + e <= t2 ? lv[e] * beta[s0 + e] : 0.f;
+                xk[e] = xv[e] * xs[s0 + e];
+            }
+            uint4 h, l;
+            split8(xv, h, l);
+            *reinterpret_cast<uint4 *>(XV + swz(t2, s0, 128)) = h;
+            *reinterpret_cast<uint4 *>(XV + swz(CK + t2, s0, 128)) = l;
+            split8(xk, h, l);
+            *reinterpret_cast<uint4 *>(XK + swz(t2, s0, 128)) = h;
+            *reinterpret_cast<uint4 *>(XK + swz(CK + t2, s0, 128)) = l;
         }
         fence_proxy_async();
         __syncthreads();
-        // 6. Wv^T = V^T X^T (cols 0..127) and Wk^T = K^T Xk^T (cols 128..255), hi | lo columns
+        // 6. Wv = X V (cols 0..127) and Wk = Xk K (cols 128..255), rows t in TMEM lanes 0..63:
+        //    [X_hi; X_lo] as A from row 0, then from row 64 (lanes 0..63 add X_lo; lanes 64..127
+        //    take rows past the tile and are not read), V and K as MN-major B
         if (tid == 0) {
             tc_fence_after();
-            const uint32_t id = idesc_bf16(128, 128, true, false);
+            const uint32_t id = idesc_bf16(128, 128, false, true);
 #pragma unroll
-            for (int kk = 0; kk < CK / 16; kk++)
-                mma_bf16(tbase, sdesc_sw128(smem_u32(VT) + kk * 2048, 8192, 1024),
-                         sdesc_sw128(smem_u32(XV) + kk * 32, 16, 1024), id, kk > 0);
+            for (int pass = 0; pass < 2; pass++)
 #pragma unroll
-            for (int kk = 0; kk < CK / 16; kk++)
-                mma_bf16(tbase + 128, sdesc_sw128(smem_u32(AKQ) + kk * 2048, 16384, 1024),
-                         sdesc_sw128(smem_u32(XK) + kk * 32, 16, 1024), id, kk > 0);
+                for (int kk = 0; kk < CK / 16; kk++)
+                    mma_bf16(tbase, sdesc_sw128(smem_u32(XV) + pass * 8192 + kk * 32, 16, 1024),
+                             sdesc_sw128(smem_u32(VT) + kk * 2048, 8192, 1024), id,
+                             (pass | kk) > 0);
+#pragma unroll
+            for (int pass = 0; pass < 2; pass++)
+#pragma unroll
+                for (int kk = 0; kk < CK / 16; kk++)
+                    mma_bf16(tbase + 128,
+                             sdesc_sw128(smem_u32(XK) + pass * 8192 + kk * 32, 16, 1024),
+                             sdesc_sw128(smem_u32(AKQ) + kk * 2048, 16384, 1024), id,
+                             (pass | kk) > 0);
             mma_commit(bar);
         }
         ok = mbar_wait(bar, 0, status, VX_DEV_TIMEOUT_MMA);  // third phase
@@ -368,26 +398,29 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         ok = __syncthreads_and(ok);
         tc_fence_after();
         if (ok) {
-            // 7. Wv -> workspace fp32 [d/16][t][16]; Wk -> [Wk_hi; Wk_lo] staged in AKQ
-            const int d = warp * 32 + lane;
-            const uint32_t ta2 = tbase + ((uint32_t)(warp * 32) << 16);
-            float *Wv = ws.Wv + blk * (CK * D);
+            // 7. warps 0-1 (row t = TMEM lane): Wv -> workspace fp32 [d/16][t][16];
+            //    Wk -> [Wk_hi; Wk_lo] staged in AKQ
+            if (warp < 2) {
+                const int t = warp * 32 + lane;
+                const uint32_t ta2 = tbase + ((uint32_t)(warp * 32) << 16);
+                float *Wv = ws.Wv + blk * (CK * D);
 #pragma unroll 1
-            for (int c16 = 0; c16 < CK; c16 += 16) {
-                float a[16], b2[16];
-                tmem_ld16(ta2 + c16, a);
-                tmem_ld16(ta2 + 64 + c16, b2);
+                for (int g = 0; g < D / 16; g++) {
+                    float w[16];
+                    tmem_ld16(ta2 + g * 16, w);
+                    float4 *dst = reinterpret_cast<float4 *>(Wv + g * (CK * 16) + t * 16);
 #pragma unroll
-                for (int j = 0; j < 16; j++)
-                    Wv[(d >> 4) * (CK * 16) + (c16 + j) * 16 + (d & 15)] = a[j] + b2[j];
-                tmem_ld16(ta2 + 128 + c16, a);
-                tmem_ld16(ta2 + 192 + c16, b2);
+                    for (int q4 = 0; q4 < 4; q4++)
+                        dst[q4] = make_float4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+                    tmem_ld16(ta2 + 128 + g * 16, w);
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    uint16_t h, l;
-                    split_bf16(a[j] + b2[j], h, l);
-                    st16(AKQ, swz(c16 + j, d, 128), h);
-                    st16(AKQ, swz(CK + c16 + j, d, 128), l);
+                    for (int half = 0; half < 2; half++) {
+                        uint4 h, l;
+                        split8(w + half * 8, h, l);
+                        const int d0 = g * 16 + half * 8;
+                        *reinterpret_cast<uint4 *>(AKQ + swz(t, d0, 128)) = h;
+                        *reinterpret_cast<uint4 *>(AKQ + swz(CK + t, d0, 128)) = l;
+                    }
                 }
             }
             fence_proxy_async();
