@@ -136,8 +136,10 @@ constexpr uint32_t P_F = P_G + CK * 8;        // float beta, rk, rq, xs, er [64]
 constexpr uint32_t P_BAR = P_F + 5 * CK * 4;
 constexpr uint32_t PREP_SMEM = P_BAR + 16 + 1024;
 
+constexpr int PREP_THREADS = 256;
+
 template <bool GATES_F64>
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(PREP_THREADS, 2)
 dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
            const __grid_constant__ CUtensorMap tv, const void *__restrict__ ga,
            const void *__restrict__ gb, const float *__restrict__ A_log,
@@ -195,7 +197,7 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     bool ok = mbar_wait(bar, 0, status, VX_DEV_TIMEOUT_TMA);
     // l2 norms from double sums of squares (src/vx27_deltanet.c:51-56), one row per thread:
     // rows 0..63 of AKQ are k, rows 64..127 are q
-    {
+    if (tid < 2 * CK) {
         double ss = 0.0;
 #pragma unroll
         for (int b = 0; b < 2; b++)
@@ -260,16 +262,17 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     ok = __syncthreads_and(ok);
     tc_fence_after();
     if (ok) {
-        // 4. Gram epilogue: rows 0..63 -> L (fp32, shared), rows 64..127 -> Pm (hi/lo image)
-        const int r = warp * 32 + lane;
+        // 4. Gram epilogue: rows 0..63 -> L (fp32, shared), rows 64..127 -> Pm (hi/lo image);
+        //    warps w and w + 4 share a TMEM lane quarter and take one half of the columns each
+        const int r = (warp & 3) * 32 + lane;
         const bool low = r < CK;
         const int t = low ? r : r - CK;
         const double Gt = G[t];
         const float sc_t = low ? beta[t] * rk[t] : __fmul_rn(rq[t], qscale);
-        const uint32_t ta = tbase + ((uint32_t)(warp * 32) << 16);
+        const uint32_t ta = tbase + ((uint32_t)((warp & 3) * 32) << 16);
         uint8_t *pm = ws.PmB + blk * SZ_PM;
 #pragma unroll 1
-        for (int c16 = 0; c16 < CK; c16 += 16) {
+        for (int c16 = (warp >> 2) * 32; c16 < (warp >> 2) * 32 + 32; c16 += 16) {
             float dv[16];
             tmem_ld16(ta + c16, dv);
             float val[16];
@@ -309,7 +312,7 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         // 5. Li = (I + L)^-1 by 16x16 blocks: the diagonal blocks by forward substitution
         //    (warp w, one column per lane), then the off-diagonal blocks one block diagonal
         //    at a time, Li_ij = -Li_ii sum_{k=j}^{i-1} L_ik Li_kj
-        if (lane < 16) {
+        if (warp < 4 && lane < 16) {
             const int o = warp * 16;
             float x[16];
 #pragma unroll
@@ -325,7 +328,7 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
 #pragma unroll 1
         for (int dg = 1; dg < 4; dg++) {
             const int nb = 4 - dg;
-            for (int e = tid; e < nb * 256; e += 128) {
+            for (int e = tid; e < nb * 256; e += PREP_THREADS) {
                 const int j = e >> 8, i = j + dg, r = (e >> 4) & 15, cc = e & 15;
                 float acc = 0.f;
                 for (int kb = j; kb < i; kb++)
@@ -336,7 +339,7 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 Ms[e] = acc;
             }
             __syncthreads();
-            for (int e = tid; e < nb * 256; e += 128) {
+            for (int e = tid; e < nb * 256; e += PREP_THREADS) {
                 const int j = e >> 8, i = j + dg, r = (e >> 4) & 15, cc = e & 15;
                 float acc = 0.f;
 #pragma unroll
@@ -349,7 +352,7 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         // X = Li diag(beta) (lower triangle) -> [X_hi; X_lo] over L's space, and
         // X diag(e^G rk) -> its hi/lo pair; one item = 8 consecutive columns s of a row t
 #pragma unroll 1
-        for (int it = tid; it < CK * CK / 8; it += 128) {
+        for (int it = tid; it < CK * CK / 8; it += PREP_THREADS) {
             const int t2 = it >> 3, s0 = (it & 7) * 8;
             const float4 l0 = *reinterpret_cast<const float4 *>(Li + fsw(t2, s0));
             const float4 l1 = *reinterpret_cast<const float4 *>(Li + fsw(t2, s0 + 4));
@@ -398,14 +401,14 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         ok = __syncthreads_and(ok);
         tc_fence_after();
         if (ok) {
-            // 7. warps 0-1 (row t = TMEM lane): Wv -> workspace fp32 [d/16][t][16];
-            //    Wk -> [Wk_hi; Wk_lo] staged in AKQ
-            if (warp < 2) {
-                const int t = warp * 32 + lane;
-                const uint32_t ta2 = tbase + ((uint32_t)(warp * 32) << 16);
+            // 7. warps on TMEM lanes 0..63 (row t; warps w and w + 4 split the 16-column
+            //    groups): Wv -> workspace fp32 [d/16][t][16]; Wk -> [Wk_hi; Wk_lo] in AKQ
+            if ((warp & 3) < 2) {
+                const int t = (warp & 1) * 32 + lane;
+                const uint32_t ta2 = tbase + ((uint32_t)((warp & 1) * 32) << 16);
                 float *Wv = ws.Wv + blk * (CK * D);
 #pragma unroll 1
-                for (int g = 0; g < D / 16; g++) {
+                for (int g = (warp >> 2) * 4; g < (warp >> 2) * 4 + 4; g++) {
                     float w[16];
                     tmem_ld16(ta2 + g * 16, w);
                     float4 *dst = reinterpret_cast<float4 *>(Wv + g * (CK * 16) + t * 16);
@@ -809,7 +812,7 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
             if (set_smem(dn_prep_tc<true>, PREP_SMEM, err, errlen)) return -1;
             attr = true;
         }
-        dn_prep_tc<true><<<dim3(n_chunks, nv), 128, PREP_SMEM, st>>>(
+        dn_prep_tc<true><<<dim3(n_chunks, nv), PREP_THREADS, PREP_SMEM, st>>>(
             tq, tk, tv, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
     } else {
         static bool attr = false;
@@ -817,7 +820,7 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
             if (set_smem(dn_prep_tc<false>, PREP_SMEM, err, errlen)) return -1;
             attr = true;
         }
-        dn_prep_tc<false><<<dim3(n_chunks, nv), 128, PREP_SMEM, st>>>(
+        dn_prep_tc<false><<<dim3(n_chunks, nv), PREP_THREADS, PREP_SMEM, st>>>(
             tq, tk, tv, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
     }
     VX_CK(cudaGetLastError());
