@@ -34,9 +34,9 @@ sys.path.insert(0, ROOT)
 METRIC = "DeltaNet+GQA decode tokens/s at 1/2/4/8 B200; % of HBM roofline"
 # DRAM bytes (read + write) per algorithmic byte of the split-KV GQA decode kernel, from an
 # ncu capture of the same kernel at 32 sequences (the full 256-sequence workload holds
-# 83 GB, too much to profile); the excess is the unused rows of each sequence's last
-# 128-position tile.
-GQA_SPLIT_DRAM_PER_ALGO_BYTE = 1.0297
+# 83 GB, too much to profile): each K/V byte is read once; the last tile of every
+# (sequence, KV head) fetches only the 32-row boxes it needs.
+GQA_SPLIT_DRAM_PER_ALGO_BYTE = 1.0067
 FALLBACK_HBM_GBS = 6650.0
 
 
