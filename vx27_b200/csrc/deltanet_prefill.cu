@@ -660,32 +660,33 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
 }
 
 // ---- phase 3: outputs ---------------------------------------------------------------------
-constexpr uint32_t O_QB = 0, O_SCH = 16384, O_SCL = 49152, O_UH = 81920, O_UL = 98304,
-                   O_PM = 114688, O_CT = 131072, O_BAR = O_CT + CK * 4;
-constexpr uint32_t OUT_SMEM = O_BAR + 16 + 1024;
+// 80 KB of shared memory so two blocks share an SM: the hi images of S0^T and U^T go
+// through the MMAs first, then their lo images are loaded into the same buffers.
+constexpr uint32_t O_QB = 0, O_SC = 16384, O_U = 49152, O_PM = 65536, O_CT = 81920,
+                   O_BAR = O_CT + CK * 4;
+constexpr uint32_t OUT_SMEM = O_BAR + 2 * 8 + 16 + 1024;
 
 template <bool OUT_BF16>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, 2)
 dn_out_tc(Wsp ws, void *__restrict__ o, int T, int nv, int n_chunks, uint32_t *status) {
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = align1024(smraw);
     float *ct = reinterpret_cast<float *>(sm + O_CT);
-    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + O_BAR);
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar + 1);
+    uint64_t *bar_ld = reinterpret_cast<uint64_t *>(sm + O_BAR), *bar_mma = bar_ld + 1;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bar_ld + 2);
     volatile int *okf = reinterpret_cast<volatile int *>(tslot + 1);
     const int c = blockIdx.x, vh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5,
               lane = tid & 31;
     const size_t blk = (size_t)vh * n_chunks + c;
     if (tid == 0) {
-        mbar_init(bar, 1);
+        mbar_init(bar_ld, 1);
+        mbar_init(bar_mma, 1);
         fence_barrier_init();
-        mbar_arrive_expect_tx(bar, 131072);
-        bulk_g2s(sm + O_QB, ws.QB + blk * SZ_QB, 16384, bar);
-        bulk_g2s(sm + O_SCH, ws.ScH + blk * SZ_SC, 32768, bar);
-        bulk_g2s(sm + O_SCL, ws.ScL + blk * SZ_SC, 32768, bar);
-        bulk_g2s(sm + O_UH, ws.UH + blk * SZ_U, 16384, bar);
-        bulk_g2s(sm + O_UL, ws.UL + blk * SZ_U, 16384, bar);
-        bulk_g2s(sm + O_PM, ws.PmB + blk * SZ_PM, 16384, bar);
+        mbar_arrive_expect_tx(bar_ld, 81920);
+        bulk_g2s(sm + O_QB, ws.QB + blk * SZ_QB, 16384, bar_ld);
+        bulk_g2s(sm + O_SC, ws.ScH + blk * SZ_SC, 32768, bar_ld);
+        bulk_g2s(sm + O_U, ws.UH + blk * SZ_U, 16384, bar_ld);
+        bulk_g2s(sm + O_PM, ws.PmB + blk * SZ_PM, 16384, bar_ld);
     }
     if (warp == 0) {
         tmem_alloc(tslot, 256);
@@ -696,36 +697,40 @@ dn_out_tc(Wsp ws, void *__restrict__ o, int T, int nv, int n_chunks, uint32_t *s
     tc_fence_after();
     const uint32_t tbase = *tslot;
     if (tid == 0) {
-        const bool ok = mbar_wait(bar, 0, status, VX_DEV_TIMEOUT_TMA);
-        *okf = ok ? 1 : 0;
-        if (ok) {
+        const uint32_t b0 = smem_u32(sm);
+        const uint32_t id1 = idesc_bf16(128, CK, false, false);
+        const uint32_t id2 = idesc_bf16(128, 128, false, false);
+        bool ok = true;
+        for (int h = 0; h < 2 && ok; h++) {
+            if (h == 1) {  // the hi passes have read the S0 and U buffers: load the lo images
+                ok = mbar_wait(bar_mma, 0, status, VX_DEV_TIMEOUT_MMA);
+                if (!ok) break;
+                mbar_arrive_expect_tx(bar_ld, 49152);
+                bulk_g2s(sm + O_SC, ws.ScL + blk * SZ_SC, 32768, bar_ld);
+                bulk_g2s(sm + O_U, ws.UL + blk * SZ_U, 16384, bar_ld);
+            }
+            ok = mbar_wait(bar_ld, h, status, VX_DEV_TIMEOUT_TMA);
+            if (!ok) break;
             tc_fence_after();
-            const uint32_t b0 = smem_u32(sm);
-            // D[v][t] cols 0..63: S0^T Q^T (hi and lo passes)
-            const uint32_t id1 = idesc_bf16(128, CK, false, false);
+            // D[v][t] cols 0..63: S0^T Q^T
 #pragma unroll
-            for (int h = 0; h < 2; h++)
+            for (int kk = 0; kk < D / 16; kk++)
+                mma_bf16(tbase,
+                         sdesc_sw128(b0 + O_SC + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                         sdesc_sw128(b0 + O_QB + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
+                         id1, (h | kk) > 0);
+            // D[v][t'] cols 64..191: U^T [Pm_hi | Pm_lo]^T
 #pragma unroll
-                for (int kk = 0; kk < D / 16; kk++)
-                    mma_bf16(tbase,
-                             sdesc_sw128(b0 + (h ? O_SCL : O_SCH) + (kk >> 2) * 16384 +
-                                             (kk & 3) * 32, 16, 1024),
-                             sdesc_sw128(b0 + O_QB + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024),
-                             id1, (h | kk) > 0);
-            // D[v][t'] cols 64..191: U^T [Pm_hi | Pm_lo]^T (hi and lo passes)
-            const uint32_t id2 = idesc_bf16(128, 128, false, false);
-#pragma unroll
-            for (int h = 0; h < 2; h++)
-#pragma unroll
-                for (int kk = 0; kk < CK / 16; kk++)
-                    mma_bf16(tbase + 64, sdesc_sw128(b0 + (h ? O_UL : O_UH) + kk * 32, 16, 1024),
-                             sdesc_sw128(b0 + O_PM + kk * 32, 16, 1024), id2, (h | kk) > 0);
-            mma_commit(bar);
+            for (int kk = 0; kk < CK / 16; kk++)
+                mma_bf16(tbase + 64, sdesc_sw128(b0 + O_U + kk * 32, 16, 1024),
+                         sdesc_sw128(b0 + O_PM + kk * 32, 16, 1024), id2, (h | kk) > 0);
+            mma_commit(bar_mma);
         }
+        *okf = ok ? 1 : 0;
     }
     __syncthreads();
     bool ok = *okf != 0;
-    if (ok) ok = mbar_wait(bar, 1, status, VX_DEV_TIMEOUT_MMA);
+    if (ok) ok = mbar_wait(bar_mma, 1, status, VX_DEV_TIMEOUT_MMA);
     ok = __syncthreads_and(ok);
     tc_fence_after();
     if (ok) {
