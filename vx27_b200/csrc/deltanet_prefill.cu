@@ -88,9 +88,9 @@ constexpr size_t SZ_QB = 16384;   // raw Q rows t, K-major over d (out MMA1 B)
 constexpr size_t SZ_PM = 16384;   // [Pm_hi; Pm_lo] rows t, K-major over s (out MMA2 B)
 constexpr size_t SZ_SC = 32768;   // S0^T hi or lo: rows v, K-major over d (out MMA1 A)
 constexpr size_t SZ_U = 16384;    // U^T hi or lo: rows v, K-major over t (out MMA2 A)
-constexpr size_t SZ_WV = 32768;   // Wv fp32 in 16-column groups: [d/16][t][16]
-constexpr size_t SZ_SCAL = 1024;  // [0] = e^{G_C}; [64 + t] = e^{G_t} rq_t / sqrt(128);
-                                  // [128 + t] = e^{G_C - G_t} rk_t
+constexpr size_t SZ_WV = 32768;   // Wv fp32 in 8-column groups: [d/8][t][8]
+constexpr size_t SZ_SCAL = 1024;  // [0] = e^{G_C}; [64 + t] = e^{G_C - G_t} rk_t;
+                                  // [128 + t] = e^{G_t} rq_t / sqrt(128)
 constexpr size_t BLK_BYTES =
     SZ_WKA + SZ_KT + SZ_QB + SZ_PM + 2 * SZ_SC + 2 * SZ_U + SZ_WV + SZ_SCAL;
 
@@ -236,8 +236,8 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         const float gam = (float)exp(G[tid]);
         xs[tid] = gam * rk[tid];
         er[tid] = (float)exp(G[CK - 1] - G[tid]) * rk[tid];
-        ws.scal[blk * 256 + 64 + tid] = gam * __fmul_rn(rq[tid], qscale);
-        ws.scal[blk * 256 + 128 + tid] = er[tid];
+        ws.scal[blk * 256 + 128 + tid] = gam * __fmul_rn(rq[tid], qscale);
+        ws.scal[blk * 256 + 64 + tid] = er[tid];
     }
     if (tid == 0 && ok) {
         ws.scal[blk * 256] = (float)exp(G[CK - 1]);
@@ -402,7 +402,7 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         tc_fence_after();
         if (ok) {
             // 7. warps on TMEM lanes 0..63 (row t; warps w and w + 4 split the 16-column
-            //    groups): Wv -> workspace fp32 [d/16][t][16]; Wk -> [Wk_hi; Wk_lo] in AKQ
+            //    groups): Wv -> workspace fp32 [d/8][t][8]; Wk -> [Wk_hi; Wk_lo] in AKQ
             if ((warp & 3) < 2) {
                 const int t = (warp & 1) * 32 + lane;
                 const uint32_t ta2 = tbase + ((uint32_t)((warp & 1) * 32) << 16);
@@ -411,10 +411,12 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 for (int g = (warp >> 2) * 4; g < (warp >> 2) * 4 + 4; g++) {
                     float w[16];
                     tmem_ld16(ta2 + g * 16, w);
-                    float4 *dst = reinterpret_cast<float4 *>(Wv + g * (CK * 16) + t * 16);
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; q4++)
-                        dst[q4] = make_float4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+                    for (int q4 = 0; q4 < 4; q4++) {  // 8-column groups 2g, 2g+1
+                        float4 *dst = reinterpret_cast<float4 *>(
+                            Wv + (2 * g + (q4 >> 1)) * (CK * 8) + t * 8 + (q4 & 1) * 4);
+                        *dst = make_float4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+                    }
                     tmem_ld16(ta2 + 128 + g * 16, w);
 #pragma unroll
                     for (int half = 0; half < 2; half++) {
@@ -452,28 +454,29 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
 template <int CB>
 struct ScanLayout {
     static constexpr int NB = 2 * CB;
-    // stage: Wk 32K | K^T 16K | Wv [CB/16][64][16] fp32 | scalars (1 KB)
+    // stage: Wk 32K | K^T 16K | Wv [CB/8][64][8] fp32 (a multiple of 1024 bytes); its
+    // scalars e^{G_C}, e^{G_C-G_t} rk_t (512 B) sit in SC[stage], outside the aligned ring
     static constexpr uint32_t ST_KT = 32768;
     static constexpr uint32_t ST_WV = 49152;
-    static constexpr uint32_t ST_SC = ST_WV + CB * 256;
-    static constexpr uint32_t STAGE_TX = ST_SC + 1024;
-    static constexpr uint32_t STAGE = STAGE_TX;                // multiple of 1024
+    static constexpr uint32_t STAGE = ST_WV + CB * 256;
+    static constexpr uint32_t STAGE_TX = STAGE + 512;
     static constexpr uint32_t SB = 2 * STAGE;                  // [S_hi; S_lo] over d: 2 blocks
     static constexpr uint32_t UB = SB + 2 * NB * 128;          // [U_hi; U_lo] over t (image)
     static constexpr uint32_t UB2 = UB + NB * 128;             // [U'_hi; U'_lo] (MMA2 B)
     static constexpr uint32_t XCH = UB2 + NB * 128;            // float [CB/2][128]
-    static constexpr uint32_t BAR = XCH + (CB / 2) * 128 * 4;  // full[2] m1 m2
+    static constexpr uint32_t SC = XCH + (CB / 2) * 128 * 4;   // scalars of the 2 stages
+    static constexpr uint32_t BAR = SC + 2 * 512;              // full[2] m1 m2
     static constexpr uint32_t SMEM = BAR + 4 * 8 + 16 + 1024;
 };
 constexpr int SCAN_BAR_A = 1, SCAN_BAR_X = 2, SCAN_BAR_B = 3;
 
 template <int CB>
-__global__ void __launch_bounds__(160, 1)
+__global__ void __launch_bounds__(160, CB <= 8 ? 2 : 1)
 dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
     using Lay = ScanLayout<CB>;
     constexpr int NB = Lay::NB;
     constexpr int HC = CB / 2;
-    constexpr int JS = HC < 16 ? HC : 16;  // TMEM columns per load in the U epilogue
+    constexpr int JS = HC < 16 ? HC : 16;  // TMEM columns per load in the U epilogue (4/8/16)
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = align1024(smraw);
     uint8_t *stg = sm, *SB = sm + Lay::SB, *UB = sm + Lay::UB, *UB2 = sm + Lay::UB2;
@@ -505,7 +508,7 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
             bulk_g2s(dst, ws.WkA + blk * SZ_WKA, 32768, &bars[s]);
             bulk_g2s(dst + Lay::ST_KT, ws.KtA + blk * SZ_KT, 16384, &bars[s]);
             bulk_g2s(dst + Lay::ST_WV, ws.Wv + blk * (CK * D) + cb * CB * CK, CB * 256, &bars[s]);
-            bulk_g2s(dst + Lay::ST_SC, ws.scal + blk * 256, 1024, &bars[s]);
+            bulk_g2s(sm + Lay::SC + s * 512, ws.scal + blk * 256, 512, &bars[s]);
         };
         if (lane == 0) load_stage(0);
         for (int c = 0; c < n_chunks; c++) {
@@ -585,13 +588,13 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
         tc_fence_after();
         // U = Wv - (quadrant sums): own half kept, the other half handed to thread tid ^ 64
         const float *wv_s = reinterpret_cast<const float *>(stage + Lay::ST_WV);
-        const float *sc = reinterpret_cast<const float *>(stage + Lay::ST_SC);
-        const float g63 = sc[0], er = sc[128 + t];
+        const float *sc = reinterpret_cast<const float *>(sm + Lay::SC + st * 512);
+        const float g63 = sc[0], er = sc[64 + t];
         float wv[HC];
 #pragma unroll
         for (int j = 0; j < HC; j++) {
             const int col = jh + j;
-            wv[j] = wv_s[(col >> 4) * (CK * 16) + t * 16 + (col & 15)];
+            wv[j] = wv_s[(col >> 3) * (CK * 8) + t * 8 + (col & 7)];
         }
 #pragma unroll
         for (int j0 = 0; j0 < HC; j0 += JS) {
@@ -599,18 +602,24 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
             if constexpr (JS == 16) {
                 tmem_ld16(tD1 + jo + j0, a);
                 tmem_ld16(tD1 + CB + jo + j0, b2);
-            } else {
+            } else if constexpr (JS == 8) {
                 tmem_ld8(tD1 + jo + j0, a);
                 tmem_ld8(tD1 + CB + jo + j0, b2);
+            } else {
+                tmem_ld4(tD1 + jo + j0, a);
+                tmem_ld4(tD1 + CB + jo + j0, b2);
             }
 #pragma unroll
             for (int j = 0; j < JS; j++) xch[(j0 + j) * 128 + (tid ^ 64)] = a[j] + b2[j];
             if constexpr (JS == 16) {
                 tmem_ld16(tD1 + jh + j0, a);
                 tmem_ld16(tD1 + CB + jh + j0, b2);
-            } else {
+            } else if constexpr (JS == 8) {
                 tmem_ld8(tD1 + jh + j0, a);
                 tmem_ld8(tD1 + CB + jh + j0, b2);
+            } else {
+                tmem_ld4(tD1 + jh + j0, a);
+                tmem_ld4(tD1 + CB + jh + j0, b2);
             }
 #pragma unroll
             for (int j = 0; j < JS; j++) wv[j0 + j] -= a[j] + b2[j];
@@ -642,13 +651,19 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
         }
         if (!*abort_ && !mbar_wait(&bars[3], c & 1, status, VX_DEV_TIMEOUT_MMA)) *abort_ = 1;
         tc_fence_after();
+        constexpr int SJ = CB < 16 ? CB : 16;
 #pragma unroll
-        for (int j0 = 0; j0 < CB; j0 += 16) {
-            float a[16], b2[16];
-            tmem_ld16(tD2 + j0, a);
-            tmem_ld16(tD2 + CB + j0, b2);
+        for (int j0 = 0; j0 < CB; j0 += SJ) {
+            float a[SJ], b2[SJ];
+            if constexpr (SJ == 16) {
+                tmem_ld16(tD2 + j0, a);
+                tmem_ld16(tD2 + CB + j0, b2);
+            } else {
+                tmem_ld8(tD2 + j0, a);
+                tmem_ld8(tD2 + CB + j0, b2);
+            }
 #pragma unroll
-            for (int j = 0; j < 16; j++) s[j0 + j] = fmaf(g63, s[j0 + j], a[j] + b2[j]);
+            for (int j = 0; j < SJ; j++) s[j0 + j] = fmaf(g63, s[j0 + j], a[j] + b2[j]);
         }
         write_sb();
     }
@@ -692,7 +707,7 @@ dn_out_tc(Wsp ws, void *__restrict__ o, int T, int nv, int n_chunks, uint32_t *s
         tmem_alloc(tslot, 256);
         tmem_relinquish();
     }
-    if (tid < CK) ct[tid] = ws.scal[blk * 256 + 64 + tid];
+    if (tid < CK) ct[tid] = ws.scal[blk * 256 + 128 + tid];
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *tslot;
@@ -829,8 +844,17 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
             tq, tk, tv, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
     }
     VX_CK(cudaGetLastError());
-    // scan: 16 state columns per CTA while that grid fits in one wave, else 32
-    if (nv * (D / 16) <= num_sms()) {
+    // scan: the narrowest column blocks whose grid still fits the GPU (2 CTAs per SM for 8
+    // columns, 1 for 16), else 32
+    if (nv * (D / 8) <= 2 * num_sms()) {
+        static bool attr = false;
+        if (!attr) {
+            if (set_smem(dn_scan_tc<8>, ScanLayout<8>::SMEM, err, errlen)) return -1;
+            attr = true;
+        }
+        dn_scan_tc<8><<<dim3(D / 8, nv), 160, ScanLayout<8>::SMEM, st>>>(ws, S, n_chunks,
+                                                                         status);
+    } else if (nv * (D / 16) <= num_sms()) {
         static bool attr = false;
         if (!attr) {
             if (set_smem(dn_scan_tc<16>, ScanLayout<16>::SMEM, err, errlen)) return -1;
