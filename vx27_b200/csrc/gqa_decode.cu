@@ -12,10 +12,13 @@
 
 namespace vx27 {
 
-// gqa_tc.cu: the tensor-core split-KV kernel (one CTA per sequence, KV head and split)
+// gqa_tc.cu: the tensor-core split-KV kernel (persistent, one CTA per SM over the
+// (sequence, KV head, split) items). With out != NULL and one split it writes the gated
+// attention output itself (gate/out dtypes from VX27_F_ACT_BF16 / VX27_F_OUT_BF16).
 int launch_split_tc(const void *kc, const void *vc, const float *q, const int *pos, float *parts,
                     int cap, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
-                    cudaStream_t st, char *err, size_t errlen);
+                    cudaStream_t st, char *err, size_t errlen, const void *gate = nullptr,
+                    void *out = nullptr, int flags = 0);
 
 namespace {
 
@@ -146,9 +149,10 @@ gqa_merge_k(const float *__restrict__ parts, int n_parts, float *__restrict__ re
 }
 
 // Split count for B*nkv (sequence, KV head) blocks over max_ctx positions. The split
-// kernel runs one CTA per SM, so a launch takes ceil(CTAs / SMs) waves of
-// (tiles per split + ~2 tiles of pipeline fill and drain); pick the count that minimises
-// that estimate (ties: fewer splits, i.e. fewer partial records to merge).
+// kernel is persistent (one CTA per SM, items streamed back to back), so a launch takes
+// about ceil(items / SMs) x (tiles per split + 1/4 tile of per-item epilogue) plus ~2
+// tiles of pipeline fill and drain; pick the count that minimises that estimate (ties:
+// fewer splits, i.e. fewer partial records to merge).
 int auto_splits(int B, int nkv, int max_ctx) {
     const long long blocks = (long long)B * nkv;
     const long long sms = num_sms();
@@ -162,7 +166,7 @@ int auto_splits(int B, int nkv, int max_ctx) {
         const int active = (tiles + per - 1) / per;   // splits that get work
         if (active < n) continue;                     // same as a smaller n
         const long long waves = (blocks * n + sms - 1) / sms;
-        const long long t = waves * (per + 2);
+        const long long t = waves * (4LL * per + 1) + 8;  // quarter tiles
         if (best_t < 0 || t < best_t) { best_t = t; best = n; }
     }
     return best;
@@ -267,6 +271,9 @@ int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
                     workspace_bytes, fit, n_splits < 1 ? 1 : n_splits);
     cudaStream_t st = (cudaStream_t)stream;
     float *parts = (float *)workspace;
+    if (n_splits == 1)  // the split kernel applies the gate and writes out; no combine pass
+        return launch_split_tc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, 1, 0, -1, st,
+                               err, errlen, gate, out, flags);
     if (launch_split(q, k_cache, v_cache, cap, pos, parts, B, nq, nkv, n_splits, 0, -1, st, err,
                      errlen))
         return -1;

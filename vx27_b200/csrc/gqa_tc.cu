@@ -1,5 +1,7 @@
-// K2 main loop on the 5th-generation tensor cores: split-KV flash decoding for one
-// (sequence, KV head, split) per CTA, serving the G = nq/nkv query heads of the group.
+// K2 main loop on the 5th-generation tensor cores: split-KV flash decoding of work items
+// (sequence, KV head, split), each serving the G = nq/nkv query heads of its group, by a
+// persistent grid of one CTA per SM. A staging warp does the CTA's global loads and stores
+// (q of the next item, gate values, the gated output or the partial record).
 //
 // Data flow per tile of 128 cache positions:
 //   TMA (warp 0)   K and V tiles, bf16 [128 positions x 256 dims], fetched as 16 KB chunks
@@ -24,19 +26,22 @@ namespace vx27 {
 constexpr int TC_TILE = 128;
 constexpr int NSLOT = 12;
 constexpr int SLOT_BYTES = 16384;      // 128 rows x 128 bytes
-constexpr int TC_THREADS = 192;
+constexpr int TC_THREADS = 224;     // TMA, MMA, 4 softmax warps, staging warp
 constexpr int HDIM = 256;
 constexpr uint32_t TMEM_COLS = 128;    // S[2] at 0,16; O[2] (two halves) at 32..95
 
 struct TcSmem {
     uint8_t ring[NSLOT][SLOT_BYTES];
-    uint8_t q[4][2048];                // Q^T operand: 4 chunks of [16 rows x 128 bytes]
+    uint8_t q[2][4][2048];             // Q^T operand per item buffer: 4 chunks of [16 rows x 128 B]
     uint8_t p[2][2][2048];             // P^T operand per buffer: 2 chunks of 64 positions
     uint64_t full[NSLOT], empty[NSLOT];
-    uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2], mma_done;
-    uint64_t grp[2], grp_end;          // softmax-group rendezvous (bounded, unlike bar.sync)
+    uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2], q_full[2], q_empty[2];
+    uint64_t ob_full, ob_empty, mma_done;
+    uint64_t grp[2], grp_end[2];       // softmax-group rendezvous (bounded, unlike bar.sync)
     float red_max[2][4][8];
-    float red_sum[4][8];
+    float red_sum[2][4][8];
+    float ob[8][HDIM];                 // an item's normalised output rows, for the staging warp
+    float ml[8][2];                    // and its (m, l) per head
     uint32_t tmem_base;
     int abort;
 };
@@ -80,47 +85,78 @@ __device__ __forceinline__ uint32_t sw128(int row, int col) {
 
 __device__ __forceinline__ uint16_t bf16_bits(float x) { return f32_to_bf16(x); }
 
+// One work item = (split s, KV head, sequence b), numbered w = s + n_splits * (kvh + nkv * b).
+struct TcItem {
+    int b, kvh, s, p0, p1, n_tiles, row0;
+};
+
+// Range of an item: [p_begin, p_end) (decode: [0, pos[b]]) cut into n_splits pieces on
+// 128-position boundaries, clipped to the cache capacity.
+__device__ __forceinline__ TcItem tc_item(int w, const int *__restrict__ pos, int cap, int nkv,
+                                          int n_splits, int p_begin, int p_end) {
+    TcItem it;
+    it.s = w % n_splits;
+    it.kvh = (w / n_splits) % nkv;
+    it.b = w / (n_splits * nkv);
+    const int rb = p_end >= 0 ? p_begin : 0;
+    const int re = p_end >= 0 ? p_end : pos[it.b] + 1;
+    const int tiles = (re - rb + TC_TILE - 1) / TC_TILE;
+    const int per = (tiles + n_splits - 1) / n_splits;
+    int p0 = rb + it.s * per * TC_TILE;
+    int p1 = min(re, rb + (it.s + 1) * per * TC_TILE);
+    if (p1 < p0) p1 = p0;
+    p0 = max(p0, 0);
+    p1 = min(p1, cap);
+    it.p0 = p0;
+    it.p1 = p1;
+    it.n_tiles = p1 > p0 ? (p1 - p0 + TC_TILE - 1) / TC_TILE : 0;
+    it.row0 = (it.b * nkv + it.kvh) * cap + p0;
+    return it;
+}
+
+// Persistent: CTA c serves items c, c + gridDim.x, ... (one CTA per SM). The three roles
+// walk the same item sequence with CTA-wide counters (ring slot j, tile g, non-empty item
+// k), so the TMA ring keeps streaming across item boundaries; the softmax warps stage the
+// next item's q in the second Q buffer while the current item runs.
 template <int G>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
              const __grid_constant__ CUtensorMap tmk32, const __grid_constant__ CUtensorMap tmv32,
              const float *__restrict__ q, const int *__restrict__ pos, float *__restrict__ parts,
              int cap, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
+             const void *__restrict__ gate, void *__restrict__ out, int flags,
              uint32_t *status) {
     extern __shared__ uint8_t smem_raw[];
     TcSmem &sm = *reinterpret_cast<TcSmem *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    const int s = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h0 = kvh * G;  // the G query heads of this KV head (G = nq / nkv)
-
-    // range of this split: [p_begin, p_end) (decode: [0, pos[b]]) cut into n_splits
-    // pieces on 128-position boundaries
-    int p0, p1;
-    {
-        const int rb = p_end >= 0 ? p_begin : 0;
-        const int re = p_end >= 0 ? p_end : pos[b] + 1;
-        const int tiles = (re - rb + TC_TILE - 1) / TC_TILE;
-        const int per = (tiles + n_splits - 1) / n_splits;
-        p0 = rb + s * per * TC_TILE;
-        p1 = min(re, rb + (s + 1) * per * TC_TILE);
-        if (p1 < p0) p1 = p0;
-    }
-    p0 = max(p0, 0);
-    p1 = min(p1, cap);
+    const int n_items = n_splits * nkv * B, stride = gridDim.x;
     const size_t rec = (size_t)B * nq * (HDIM + 2);
-    float *po = parts + (size_t)s * rec;
-    float *pml = po + (size_t)B * nq * HDIM;
-    const int n_tiles = p1 > p0 ? (p1 - p0 + TC_TILE - 1) / TC_TILE : 0;
-    if (n_tiles == 0) {  // empty range: neutral record
-        for (int e = tid; e < G * HDIM; e += TC_THREADS)
-            po[((size_t)b * nq + h0 + e / HDIM) * HDIM + e % HDIM] = 0.0f;
-        if (tid < G) {
-            pml[((size_t)b * nq + h0 + tid) * 2] = -INFINITY;
-            pml[((size_t)b * nq + h0 + tid) * 2 + 1] = 0.0f;
+    auto item = [&](int w) { return tc_item(w, pos, cap, nkv, n_splits, p_begin, p_end); };
+    auto next_work = [&](int w) {  // first item >= w (in this CTA's sequence) with work
+        for (; w < n_items; w += stride)
+            if (item(w).n_tiles > 0) return w;
+        return n_items;
+    };
+    // q rows of item w as bf16 hi (rows 0..G-1) and lo (rows G..2G-1) into Q buffer qb, by
+    // the staging warp: all loads first, then the conversions
+    auto stage_q = [&](int w, int qb) {
+        const TcItem it = item(w);
+        const float2 *src = reinterpret_cast<const float2 *>(q + ((size_t)it.b * nq + it.kvh * G) * HDIM);
+        float2 v[4 * G];
+#pragma unroll
+        for (int u = 0; u < 4 * G; u++) v[u] = src[lane + 32 * u];
+#pragma unroll
+        for (int u = 0; u < 4 * G; u++) {
+            const int e = lane + 32 * u, g = e / (HDIM / 2), d = (e % (HDIM / 2)) * 2;
+            const uint16_t hx = bf16_bits(v[u].x), hy = bf16_bits(v[u].y);
+            const uint16_t lx = bf16_bits(v[u].x - bf16_to_f32(hx)), ly = bf16_bits(v[u].y - bf16_to_f32(hy));
+            const int c = d >> 6, col = d & 63;
+            *reinterpret_cast<uint32_t *>(&sm.q[qb][c][sw128(g, col)]) = hx | ((uint32_t)hy << 16);
+            *reinterpret_cast<uint32_t *>(&sm.q[qb][c][sw128(g + G, col)]) = lx | ((uint32_t)ly << 16);
         }
-        return;
-    }
-    const int row0 = (b * nkv + kvh) * cap + p0;
+        fence_proxy_async();
+    };
+    const int w_first = next_work(blockIdx.x);
 
     // ---- prologue --------------------------------------------------------------
     if (tid == 0) {
@@ -131,11 +167,14 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
             mbar_init(&sm.p_full[i], 128);
             mbar_init(&sm.o_full[i], 1);
             mbar_init(&sm.o_empty[i], 128);
+            mbar_init(&sm.q_full[i], 32);
+            mbar_init(&sm.q_empty[i], 1);
+            mbar_init(&sm.grp[i], 128);
+            mbar_init(&sm.grp_end[i], 128);
         }
+        mbar_init(&sm.ob_full, 128);
+        mbar_init(&sm.ob_empty, 1);
         mbar_init(&sm.mma_done, 1);
-        mbar_init(&sm.grp[0], 128);
-        mbar_init(&sm.grp[1], 128);
-        mbar_init(&sm.grp_end, 128);
         sm.abort = 0;
         fence_barrier_init();
     }
@@ -144,23 +183,11 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
         tmem_relinquish();
         if (lane == 0) { tma_prefetch_desc(&tmk); tma_prefetch_desc(&tmv); }
     }
-    if (warp >= 2) {
-        const int t = tid - 64;  // 0..127
-        // zero Q and both P operands (rows >= 2G stay zero), then write q hi/lo rows
+    if (warp >= 2 && warp < 6) {
+        // zero both Q buffers and both P operands (rows >= 2G stay zero)
         uint4 z = make_uint4(0, 0, 0, 0);
-        for (int e = t; e < (int)(sizeof(sm.q) + sizeof(sm.p)) / 16; e += 128)
-            reinterpret_cast<uint4 *>(&sm.q[0][0])[e] = z;  // q and p are contiguous
-        named_bar(1, 128);
-        for (int e = t; e < G * (HDIM / 2); e += 128) {
-            const int g = e / (HDIM / 2), d = (e % (HDIM / 2)) * 2;
-            const float2 v = *reinterpret_cast<const float2 *>(
-                q + ((size_t)b * nq + h0 + g) * HDIM + d);
-            const uint16_t hx = bf16_bits(v.x), hy = bf16_bits(v.y);
-            const uint16_t lx = bf16_bits(v.x - bf16_to_f32(hx)), ly = bf16_bits(v.y - bf16_to_f32(hy));
-            const int c = d >> 6, col = d & 63;
-            *reinterpret_cast<uint32_t *>(&sm.q[c][sw128(g, col)]) = hx | ((uint32_t)hy << 16);
-            *reinterpret_cast<uint32_t *>(&sm.q[c][sw128(g + G, col)]) = lx | ((uint32_t)ly << 16);
-        }
+        for (int e = tid - 64; e < (int)(sizeof(sm.q) + sizeof(sm.p)) / 16; e += 128)
+            reinterpret_cast<uint4 *>(&sm.q[0][0][0])[e] = z;  // q and p are contiguous
         fence_proxy_async();
     }
     __syncthreads();
@@ -170,53 +197,65 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
     if (warp == 0) {
         // ---- TMA producer --------------------------------------------------------
         if (lane == 0) {
-            const int n_items = n_tiles * 8;
-            int j = 0;
-            for (; j < n_items; j++) {
-                const int slot = j % NSLOT, round = j / NSLOT;
-                if (round > 0 && !tc_wait(&sm.empty[slot], (round - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
-                    break;
-                const int tile = j >> 3, r = j & 7;
-                // the last tile fetches only the 32-row boxes that hold positions of the
-                // range (the rows past it are masked, and V's are zeroed, by the softmax warps)
-                const int rows_left = p1 - (p0 + tile * TC_TILE);
-                if (rows_left < TC_TILE) {
-                    const int nsub = (rows_left + 31) / 32;
-                    mbar_arrive_expect_tx(&sm.full[slot], nsub * (SLOT_BYTES / 4));
-                    for (int k = 0; k < nsub; k++)
-                        tma_load_2d(sm.ring[slot] + k * (SLOT_BYTES / 4), r < 4 ? &tmk32 : &tmv32,
-                                    (r & 3) * 64, row0 + tile * TC_TILE + 32 * k, &sm.full[slot]);
-                } else {
-                    mbar_arrive_expect_tx(&sm.full[slot], SLOT_BYTES);
-                    tma_load_2d(sm.ring[slot], r < 4 ? &tmk : &tmv, (r & 3) * 64,
-                                row0 + tile * TC_TILE, &sm.full[slot]);
+            int j = 0;  // ring items issued by this CTA
+            bool ok = true;
+            for (int w = w_first; w < n_items && ok; w = next_work(w + stride)) {
+                const TcItem it = item(w);
+                for (int jj = 0; jj < it.n_tiles * 8; jj++, j++) {
+                    const int slot = j % NSLOT, round = j / NSLOT;
+                    if (round > 0 &&
+                        !tc_wait(&sm.empty[slot], (round - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA)) {
+                        ok = false;
+                        break;
+                    }
+                    const int tile = jj >> 3, r = jj & 7;
+                    // the last tile fetches only the 32-row boxes that hold positions of the
+                    // range (the rows past it are masked, and V's are zeroed, by the softmax warps)
+                    const int rows_left = it.p1 - (it.p0 + tile * TC_TILE);
+                    if (rows_left < TC_TILE) {
+                        const int nsub = (rows_left + 31) / 32;
+                        mbar_arrive_expect_tx(&sm.full[slot], nsub * (SLOT_BYTES / 4));
+                        for (int k = 0; k < nsub; k++)
+                            tma_load_2d(sm.ring[slot] + k * (SLOT_BYTES / 4), r < 4 ? &tmk32 : &tmv32,
+                                        (r & 3) * 64, it.row0 + tile * TC_TILE + 32 * k, &sm.full[slot]);
+                    } else {
+                        mbar_arrive_expect_tx(&sm.full[slot], SLOT_BYTES);
+                        tma_load_2d(sm.ring[slot], r < 4 ? &tmk : &tmv, (r & 3) * 64,
+                                    it.row0 + tile * TC_TILE, &sm.full[slot]);
+                    }
                 }
             }
             if (sm.abort) {  // let the copies already issued land before the CTA exits
                 for (int k = max(0, j - NSLOT); k < j; k++) {
                     const uint32_t addr = smem_u32(&sm.full[k % NSLOT]);
                     for (int it = 0; it < (1 << 20); it++) {
-                        uint32_t ok;
+                        uint32_t ok2;
                         asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-                                     : "=r"(ok) : "r"(addr), "r"((uint32_t)((k / NSLOT) & 1)) : "memory");
-                        if (ok) break;
+                                     : "=r"(ok2) : "r"(addr), "r"((uint32_t)((k / NSLOT) & 1)) : "memory");
+                        if (ok2) break;
                     }
                 }
             }
         }
     } else if (warp == 1) {
-        // ---- MMA issuer ----------------------------------------------------------
+        // ---- MMA issuer: S(g) = K_g Q^T, then O(g-1) = V_{g-1}^T P_{g-1}^T -----------
         if (lane == 0) {
             const uint32_t id1 = idesc_bf16(128, 16, false, false);
             const uint32_t id2 = idesc_bf16(128, 16, true, false);
-            const uint32_t ring0 = smem_u32(sm.ring[0]), q0 = smem_u32(sm.q[0]);
-            bool ok = true;
-            for (int i = 0; i <= n_tiles && ok; i++) {
-                if (i < n_tiles) {  // S[i&1] = K_i Q^T
-                    const int bb = i & 1;
-                    if (i >= 2) ok = tc_wait(&sm.s_empty[bb], ((i >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+            const uint32_t ring0 = smem_u32(sm.ring[0]);
+            bool ok = true, prev = false;
+            int w = w_first, n_t = w < n_items ? item(w).n_tiles : 0, i = 0, kq = 0;
+            for (int g = 0; ok && (w < n_items || prev); g++) {
+                const bool cur = w < n_items;
+                if (cur) {
+                    const int bb = g & 1;
+                    if (i == 0)  // this item's q staged
+                        ok = tc_wait(&sm.q_full[kq & 1], (kq >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                    if (ok && g >= 2)
+                        ok = tc_wait(&sm.s_empty[bb], ((g >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                    const uint32_t q0 = smem_u32(sm.q[kq & 1][0]);
                     for (int c = 0; c < 4 && ok; c++) {
-                        const int j = 8 * i + c, slot = j % NSLOT;
+                        const int j = 8 * g + c, slot = j % NSLOT;
                         ok = tc_wait(&sm.full[slot], (j / NSLOT) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
                         if (!ok) break;
                         tc_fence_after();
@@ -230,8 +269,8 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
                     }
                     if (ok) mma_commit(&sm.s_full[bb]);
                 }
-                if (i >= 1 && ok) {  // O[(i-1)&1] = V_{i-1}^T P_{i-1}^T
-                    const int t = i - 1, bb = t & 1;
+                if (prev && ok) {
+                    const int t = g - 1, bb = t & 1;
                     ok = tc_wait(&sm.p_full[bb], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
                     if (ok && t >= 2)
                         ok = tc_wait(&sm.o_empty[bb], ((t >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
@@ -253,127 +292,248 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
                     }
                     if (ok) mma_commit(&sm.o_full[bb]);
                 }
+                prev = cur;
+                if (cur && ++i == n_t) {  // next item with work
+                    if (ok) mma_commit(&sm.q_empty[kq & 1]);  // its S MMAs are all issued
+                    i = 0;
+                    kq++;
+                    w = next_work(w + stride);
+                    n_t = w < n_items ? item(w).n_tiles : 0;
+                }
             }
             mma_commit(&sm.mma_done);
             tc_wait(&sm.mma_done, 0, sm, status, VX_DEV_TIMEOUT_MMA);
         }
-    } else {
-        // ---- softmax / correction / epilogue (warps 2..5) -------------------------
+    } else if (warp < 6) {
+        // ---- softmax / correction / epilogue (warps 2..5); no global memory traffic --
         const int q4 = warp & 3;               // TMEM lane quarter of this warp
         const int r = q4 * 32 + lane;          // position within a tile; output dim r, r+128
         const uint32_t lane_addr = tmem + ((uint32_t)(q4 * 32) << 16);
         const float sc2 = 1.4426950408889634f * 0.0625f;  // log2(e) / sqrt(256)
-        float m2[8], l[8], acc_a[8], acc_b[8], al[8], al_prev[8];
-#pragma unroll
-        for (int h = 0; h < 8; h++) {
-            m2[h] = -INFINITY; l[h] = 0.f; acc_a[h] = 0.f; acc_b[h] = 0.f; al_prev[h] = 0.f;
-        }
         bool ok = true;
-        auto correction = [&](int t) {  // folds O(t) in with alpha_t = al_prev
-            const int bb = t & 1;
-            ok = ok && tc_wait(&sm.o_full[bb], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-            ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is warp-wide
-            if (!ok) return;
-            tc_fence_after();
-            float oa[16], ob[16];
-            tmem_ld16(lane_addr + 32 + bb * 32, oa);
-            tmem_ld16(lane_addr + 48 + bb * 32, ob);
-            tc_fence_before();
-            mbar_arrive(&sm.o_empty[bb]);
+        int g = 0, kq = 0;  // tiles and items with work done so far
+        for (int w = w_first; w < n_items && ok; w = next_work(w + stride)) {
+            const TcItem it = item(w);
+            float m2[8], l[8], acc_a[8], acc_b[8], al[8], al_prev[8];
 #pragma unroll
             for (int h = 0; h < 8; h++) {
-                if (h < G) {
-                    acc_a[h] = fmaf(acc_a[h], al_prev[h], oa[h] + oa[h + G]);
-                    acc_b[h] = fmaf(acc_b[h], al_prev[h], ob[h] + ob[h + G]);
-                }
+                m2[h] = -INFINITY; l[h] = 0.f; acc_a[h] = 0.f; acc_b[h] = 0.f; al_prev[h] = 0.f;
             }
-        };
-        for (int i = 0; i < n_tiles && ok; i++) {
-            const int bb = i & 1;
-            ok = tc_wait(&sm.s_full[bb], (i >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            tc_fence_after();
-            float v[16];
-            tmem_ld16(lane_addr + bb * 16, v);
-            tc_fence_before();
-            mbar_arrive(&sm.s_empty[bb]);
-            const int pabs = p0 + i * TC_TILE + r;
-            const bool valid = pabs < p1;
-            float x[8];
+            auto correction = [&](int t) {  // folds O(t) in with alpha_t = al_prev
+                const int bb = t & 1;
+                ok = ok && tc_wait(&sm.o_full[bb], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld is warp-wide
+                if (!ok) return;
+                tc_fence_after();
+                float oa[16], ob[16];
+                tmem_ld16(lane_addr + 32 + bb * 32, oa);
+                tmem_ld16(lane_addr + 48 + bb * 32, ob);
+                tc_fence_before();
+                mbar_arrive(&sm.o_empty[bb]);
 #pragma unroll
-            for (int h = 0; h < 8; h++) {
-                x[h] = (h < G && valid) ? (v[h] + v[h + G]) * sc2 : -INFINITY;
-                const float t = warp_max(x[h]);
-                if (lane == 0) sm.red_max[bb][q4][h] = t;
-            }
-            // every thread of the group must see all four warps' maxima
-            mbar_arrive(&sm.grp[bb]);
-            ok = tc_wait(&sm.grp[bb], (i >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-            if (!ok) break;
-#pragma unroll
-            for (int h = 0; h < 8; h++) {
-                const float t = fmaxf(fmaxf(sm.red_max[bb][0][h], sm.red_max[bb][1][h]),
-                                      fmaxf(sm.red_max[bb][2][h], sm.red_max[bb][3][h]));
-                const float mn = fmaxf(m2[h], t);
-                al[h] = (h < G) ? exp2f(m2[h] - mn) : 0.f;
-                m2[h] = mn;
-            }
-            uint8_t *pbuf = sm.p[bb][r >> 6];
-#pragma unroll
-            for (int h = 0; h < 8; h++) {
-                if (h < G) {
-                    const float pr = exp2f(x[h] - m2[h]);
-                    l[h] = fmaf(l[h], al[h], pr);
-                    const uint16_t hi = bf16_bits(pr);
-                    const uint16_t lo = bf16_bits(pr - bf16_to_f32(hi));
-                    *reinterpret_cast<uint16_t *>(pbuf + sw128(h, r & 63)) = hi;
-                    *reinterpret_cast<uint16_t *>(pbuf + sw128(h + G, r & 63)) = lo;
-                }
-            }
-            if (i == n_tiles - 1 && p0 + n_tiles * TC_TILE > p1) {
-                // V rows past the range may hold anything: zero them before V^T P^T reads them
-                for (int c = 0; c < 4 && ok; c++) {
-                    const int j = 8 * i + 4 + c;
-                    ok = tc_wait(&sm.full[j % NSLOT], (j / NSLOT) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
-                    if (ok && !valid) {
-                        uint4 *row = reinterpret_cast<uint4 *>(sm.ring[j % NSLOT] + r * 128);
-#pragma unroll
-                        for (int u = 0; u < 8; u++) row[u] = make_uint4(0, 0, 0, 0);
+                for (int h = 0; h < 8; h++) {
+                    if (h < G) {
+                        acc_a[h] = fmaf(acc_a[h], al_prev[h], oa[h] + oa[h + G]);
+                        acc_b[h] = fmaf(acc_b[h], al_prev[h], ob[h] + ob[h + G]);
                     }
                 }
+            };
+            for (int i = 0; i < it.n_tiles && ok; i++) {
+                const int gi = g + i, bb = gi & 1;
+                ok = tc_wait(&sm.s_full[bb], (gi >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                tc_fence_after();
+                float v[16];
+                tmem_ld16(lane_addr + bb * 16, v);
+                tc_fence_before();
+                mbar_arrive(&sm.s_empty[bb]);
+                const int pabs = it.p0 + i * TC_TILE + r;
+                const bool valid = pabs < it.p1;
+                float x[8];
+#pragma unroll
+                for (int h = 0; h < 8; h++) {
+                    x[h] = (h < G && valid) ? (v[h] + v[h + G]) * sc2 : -INFINITY;
+                    const float t = warp_max(x[h]);
+                    if (lane == 0) sm.red_max[bb][q4][h] = t;
+                }
+                // every thread of the group must see all four warps' maxima
+                mbar_arrive(&sm.grp[bb]);
+                ok = tc_wait(&sm.grp[bb], (gi >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+                if (!ok) break;
+#pragma unroll
+                for (int h = 0; h < 8; h++) {
+                    const float t = fmaxf(fmaxf(sm.red_max[bb][0][h], sm.red_max[bb][1][h]),
+                                          fmaxf(sm.red_max[bb][2][h], sm.red_max[bb][3][h]));
+                    const float mn = fmaxf(m2[h], t);
+                    al[h] = (h < G) ? exp2f(m2[h] - mn) : 0.f;
+                    m2[h] = mn;
+                }
+                uint8_t *pbuf = sm.p[bb][r >> 6];
+#pragma unroll
+                for (int h = 0; h < 8; h++) {
+                    if (h < G) {
+                        const float pr = exp2f(x[h] - m2[h]);
+                        l[h] = fmaf(l[h], al[h], pr);
+                        const uint16_t hi = bf16_bits(pr);
+                        const uint16_t lo = bf16_bits(pr - bf16_to_f32(hi));
+                        *reinterpret_cast<uint16_t *>(pbuf + sw128(h, r & 63)) = hi;
+                        *reinterpret_cast<uint16_t *>(pbuf + sw128(h + G, r & 63)) = lo;
+                    }
+                }
+                if (i == it.n_tiles - 1 && it.p0 + it.n_tiles * TC_TILE > it.p1) {
+                    // V rows past the range may hold anything: zero them before V^T P^T reads them
+                    for (int c = 0; c < 4 && ok; c++) {
+                        const int j = 8 * gi + 4 + c;
+                        ok = tc_wait(&sm.full[j % NSLOT], (j / NSLOT) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+                        if (ok && !valid) {
+                            uint4 *row = reinterpret_cast<uint4 *>(sm.ring[j % NSLOT] + r * 128);
+#pragma unroll
+                            for (int u = 0; u < 8; u++) row[u] = make_uint4(0, 0, 0, 0);
+                        }
+                    }
+                }
+                fence_proxy_async();
+                mbar_arrive(&sm.p_full[bb]);
+                if (i >= 1) correction(gi - 1);
+#pragma unroll
+                for (int h = 0; h < 8; h++) al_prev[h] = al[h];
             }
-            fence_proxy_async();
-            mbar_arrive(&sm.p_full[bb]);
-            if (i >= 1) correction(i - 1);
+            if (ok) correction(g + it.n_tiles - 1);
+            // epilogue: total l per head; the normalised rows go to the output buffer, which
+            // the staging warp has emptied of the previous item
+            const int eb = kq & 1;
 #pragma unroll
-            for (int h = 0; h < 8; h++) al_prev[h] = al[h];
-        }
-        if (ok) correction(n_tiles - 1);
-        // epilogue: total l per head, normalised partial output
-#pragma unroll
-        for (int h = 0; h < 8; h++) {
-            const float t = warp_sum(l[h]);
-            if (lane == 0) sm.red_sum[q4][h] = t;
-        }
-        mbar_arrive(&sm.grp_end);
-        const bool all = tc_wait(&sm.grp_end, 0, sm, status, VX_DEV_TIMEOUT_MMA);
-        if (ok && all) {
+            for (int h = 0; h < 8; h++) {
+                const float t = warp_sum(l[h]);
+                if (lane == 0) sm.red_sum[eb][q4][h] = t;
+            }
+            mbar_arrive(&sm.grp_end[eb]);
+            ok = tc_wait(&sm.grp_end[eb], (kq >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA) && ok;
+            if (kq > 0)
+                ok = tc_wait(&sm.ob_empty, (kq - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA) && ok;
 #pragma unroll
             for (int h = 0; h < 8; h++) {
                 if (h < G) {
-                    const float L = sm.red_sum[0][h] + sm.red_sum[1][h] + sm.red_sum[2][h] +
-                                    sm.red_sum[3][h];
-                    const size_t hq = (size_t)b * nq + h0 + h;
+                    const float L = sm.red_sum[eb][0][h] + sm.red_sum[eb][1][h] +
+                                    sm.red_sum[eb][2][h] + sm.red_sum[eb][3][h];
                     const float inv = L > 0.f ? 1.0f / L : 0.f;
-                    po[hq * HDIM + r] = acc_a[h] * inv;
-                    po[hq * HDIM + r + 128] = acc_b[h] * inv;
+                    sm.ob[h][r] = acc_a[h] * inv;
+                    sm.ob[h][r + 128] = acc_b[h] * inv;
                     if (r == 0) {
-                        pml[hq * 2] = L > 0.f ? m2[h] * 0.6931471805599453f : -INFINITY;
-                        pml[hq * 2 + 1] = L;
+                        sm.ml[h][0] = L > 0.f ? m2[h] * 0.6931471805599453f : -INFINITY;
+                        sm.ml[h][1] = L;
                     }
                 }
             }
+            mbar_arrive(&sm.ob_full);
+            g += it.n_tiles;
+            kq++;
+        }
+    } else {
+        // ---- staging warp: every global load and store of the CTA except the TMA ring --
+        // (q of the next item, gate values, the output or the partial record), so that no
+        // release in the softmax warps waits on an HBM round trip
+        const bool bf_gate = flags & VX27_F_ACT_BF16, bf_out = flags & VX27_F_OUT_BF16;
+        bool ok = true;
+        int kq = 0;  // items with work seen so far
+        if (w_first < n_items) {
+            stage_q(w_first, 0);
+            mbar_arrive(&sm.q_full[0]);
+        }
+        for (int w = blockIdx.x; w < n_items && ok; w += stride) {
+            const TcItem it = item(w);
+            const size_t base = ((size_t)it.b * nq + it.kvh * G) * HDIM;  // first of G rows
+            float *po = parts + (size_t)it.s * rec;
+            float *pml = po + (size_t)B * nq * HDIM;
+            float gv[G][8];  // gate of this lane's 8 dims per head
+            auto fetch_gate = [&]() {
+#pragma unroll
+                for (int h = 0; h < G; h++) {
+                    const size_t i = base + (size_t)h * HDIM + 8 * lane;
+                    if (!gate) {
+#pragma unroll
+                        for (int u = 0; u < 8; u++) gv[h][u] = 0.f;
+                    } else if (bf_gate) {
+                        const uint4 raw = *reinterpret_cast<const uint4 *>(
+                            reinterpret_cast<const uint16_t *>(gate) + i);
+                        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            gv[h][2 * u] = bf16_to_f32((uint16_t)(wv[u] & 0xffff));
+                            gv[h][2 * u + 1] = bf16_to_f32((uint16_t)(wv[u] >> 16));
+                        }
+                    } else {
+                        const float4 a = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(gate) + i);
+                        const float4 c = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(gate) + i + 4);
+                        gv[h][0] = a.x; gv[h][1] = a.y; gv[h][2] = a.z; gv[h][3] = a.w;
+                        gv[h][4] = c.x; gv[h][5] = c.y; gv[h][6] = c.z; gv[h][7] = c.w;
+                    }
+                }
+            };
+            // att for this lane's 8 dims of head h -> out (gated, the combine's arithmetic)
+            // or the partial record
+            auto write_rows = [&](auto att_of) {
+#pragma unroll
+                for (int h = 0; h < G; h++) {
+                    float a[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) {
+                        a[u] = att_of(h, 8 * lane + u);
+                        if (out && gate) a[u] = a[u] * (1.0f / (1.0f + expf(-gv[h][u])));
+                    }
+                    const size_t i = base + (size_t)h * HDIM + 8 * lane;
+                    if (!out) {
+                        float4 *d = reinterpret_cast<float4 *>(po + i);
+                        d[0] = make_float4(a[0], a[1], a[2], a[3]);
+                        d[1] = make_float4(a[4], a[5], a[6], a[7]);
+                    } else if (bf_out) {
+                        uint4 o;
+                        o.x = f32_to_bf16(a[0]) | ((uint32_t)f32_to_bf16(a[1]) << 16);
+                        o.y = f32_to_bf16(a[2]) | ((uint32_t)f32_to_bf16(a[3]) << 16);
+                        o.z = f32_to_bf16(a[4]) | ((uint32_t)f32_to_bf16(a[5]) << 16);
+                        o.w = f32_to_bf16(a[6]) | ((uint32_t)f32_to_bf16(a[7]) << 16);
+                        *reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(out) + i) = o;
+                    } else {
+                        float4 *d = reinterpret_cast<float4 *>(reinterpret_cast<float *>(out) + i);
+                        d[0] = make_float4(a[0], a[1], a[2], a[3]);
+                        d[1] = make_float4(a[4], a[5], a[6], a[7]);
+                    }
+                }
+            };
+            if (it.n_tiles == 0) {  // empty range: neutral record, or a zero attention output
+                if (out) fetch_gate();
+                write_rows([&](int, int) { return 0.0f; });
+                if (!out && lane < G) {
+                    pml[((size_t)it.b * nq + it.kvh * G + lane) * 2] = -INFINITY;
+                    pml[((size_t)it.b * nq + it.kvh * G + lane) * 2 + 1] = 0.0f;
+                }
+                continue;
+            }
+            // q of the next item with work into the other buffer, once the S MMAs of the
+            // item before this one (its last reader) are complete
+            const int wn = next_work(w + stride);
+            if (wn < n_items) {
+                if (kq >= 1)
+                    ok = tc_wait(&sm.q_empty[(kq + 1) & 1], ((kq - 1) >> 1) & 1, sm, status,
+                                 VX_DEV_TIMEOUT_MMA);
+                if (ok) {
+                    stage_q(wn, (kq + 1) & 1);
+                    mbar_arrive(&sm.q_full[(kq + 1) & 1]);
+                }
+            }
+            if (out) fetch_gate();
+            ok = ok && tc_wait(&sm.ob_full, kq & 1, sm, status, VX_DEV_TIMEOUT_MMA);
+            if (ok) {
+                write_rows([&](int h, int d) { return sm.ob[h][d]; });
+                if (!out && lane < G) {
+                    pml[((size_t)it.b * nq + it.kvh * G + lane) * 2] = sm.ml[lane][0];
+                    pml[((size_t)it.b * nq + it.kvh * G + lane) * 2 + 1] = sm.ml[lane][1];
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.ob_empty);
+            kq++;
         }
     }
     __syncthreads();
@@ -385,9 +545,23 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
 
 size_t tc_smem_bytes() { return sizeof(TcSmem) + 1024; }
 
+// One CTA per SM (fewer when there are fewer items).
+static int tc_grid(int B, int nkv, int n_splits) {
+    const long long items = (long long)B * nkv * n_splits;
+    return (int)(items < num_sms() ? items : num_sms());
+}
+
 int launch_split_tc(const void *kc, const void *vc, const float *q, const int *pos, float *parts,
                     int cap, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
-                    cudaStream_t st, char *err, size_t errlen) {
+                    cudaStream_t st, char *err, size_t errlen, const void *gate, void *out,
+                    int flags) {
+    if (out && n_splits != 1)
+        return fail(err, errlen, "vx27_gqa: a direct output needs exactly one split");
+    // the staging warp moves rows as 16-byte vectors (q as 8-byte pairs)
+    if (((uintptr_t)parts & 15) || ((uintptr_t)out & 15) || ((uintptr_t)gate & 15) ||
+        ((uintptr_t)q & 7))
+        return fail(err, errlen,
+                    "vx27_gqa: q must be 8-byte aligned, gate, out and the workspace 16-byte aligned");
     CUtensorMap mk, mv, mk32, mv32;
     const uint64_t rows = (uint64_t)B * nkv * cap;
     if (make_tmap_bf16_2d(&mk, kc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
@@ -396,7 +570,7 @@ int launch_split_tc(const void *kc, const void *vc, const float *q, const int *p
         make_tmap_bf16_2d(&mv32, vc, rows, HDIM, HDIM * 2, 64, 32, err, errlen))
         return -1;
     const size_t smem = tc_smem_bytes();
-    const dim3 grid(n_splits, nkv, B);
+    const dim3 grid(tc_grid(B, nkv, n_splits));
     uint32_t *stw = dev_status();
 #define VX_TCG(GG)                                                                        \
     case GG: {                                                                            \
@@ -409,7 +583,7 @@ int launch_split_tc(const void *kc, const void *vc, const float *q, const int *p
         }                                                                                 \
         gqa_split_tc<GG><<<grid, TC_THREADS, smem, st>>>(mk, mv, mk32, mv32, q, pos, parts, cap, \
                                                          B, nq, nkv, n_splits, p_begin,    \
-                                                         p_end, stw);                      \
+                                                         p_end, gate, out, flags, stw);    \
         break;                                                                            \
     }
     switch (nq / nkv) {
@@ -427,6 +601,8 @@ int launch_split_tc(const void *kc, const void *vc, const float *q, const int *p
 int launch_split_tc_status(const void *kc, const void *vc, const float *q, const int *pos,
                            float *parts, int cap, int B, int nq, int nkv, int n_splits,
                            uint32_t *status, cudaStream_t st, char *err, size_t errlen) {
+    if (((uintptr_t)parts & 15) || ((uintptr_t)q & 7))
+        return fail(err, errlen, "vx27_gqa: q must be 8-byte aligned and the records 16-byte aligned");
     CUtensorMap mk, mv, mk32, mv32;
     const uint64_t rows = (uint64_t)B * nkv * cap;
     if (make_tmap_bf16_2d(&mk, kc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
@@ -435,7 +611,7 @@ int launch_split_tc_status(const void *kc, const void *vc, const float *q, const
         make_tmap_bf16_2d(&mv32, vc, rows, HDIM, HDIM * 2, 64, 32, err, errlen))
         return -1;
     const size_t smem = tc_smem_bytes();
-    const dim3 grid(n_splits, nkv, B);
+    const dim3 grid(tc_grid(B, nkv, n_splits));
 #define VX_TCS(GG)                                                                        \
     case GG: {                                                                            \
         static bool attr = false;                                                         \
@@ -447,7 +623,7 @@ int launch_split_tc_status(const void *kc, const void *vc, const float *q, const
         }                                                                                 \
         gqa_split_tc<GG><<<grid, TC_THREADS, smem, st>>>(mk, mv, mk32, mv32, q, pos, parts, cap, \
                                                          B, nq, nkv, n_splits, 0, -1,      \
-                                                         status);                          \
+                                                         nullptr, nullptr, 0, status);     \
         break;                                                                            \
     }
     switch (nq / nkv) {
