@@ -29,6 +29,11 @@ extern "C" {
 #define VX27_F_OUT_BF16  0x2 /* outputs are bf16, else fp32 */
 #define VX27_F_NORM_1P   0x4 /* zero-centred RMSNorm weights: y = x*s*(1+w) */
 #define VX27_F_GATES_F64 0x8 /* DeltaNet: a/b hold host-computed beta/g_log as double */
+/* DeltaNet decode: the kernel may start reading this layer's state S while the kernel
+ * before it on the stream is still running (programmatic dependent launch). Set it only
+ * when that kernel does not write S, e.g. when it belongs to another layer; everything
+ * else the kernel reads still waits for the previous kernel to finish. */
+#define VX27_F_PREFETCH_STATE 0x10
 
 /* Library version, major*10000 + minor*100 + patch. */
 int vx27cuda_version(void);

@@ -98,7 +98,7 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             const float *__restrict__ A_log, const float *__restrict__ dt_bias,
             const float *__restrict__ conv_w, const int *__restrict__ pos,
             const void *__restrict__ z, const float *__restrict__ norm_w, void *__restrict__ o,
-            int B, int nqk, int nv, uint32_t *status) {
+            int B, int nqk, int nv, int prefetch_state, uint32_t *status) {
     extern __shared__ uint8_t dn_smem_raw[];
     DnSmem &sm = *reinterpret_cast<DnSmem *>(((uintptr_t)dn_smem_raw + 127) & ~(uintptr_t)127);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -115,11 +115,24 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
         fence_barrier_init();
     }
     __syncthreads();
+    // Everything below reads the previous kernel's outputs (activations, positions) except,
+    // with prefetch_state, the first state copies, which the TMA warp issues before waiting.
+    // The next kernel may be scheduled once every CTA is past its wait (not earlier: a chain
+    // of early triggers would let a later kernel overtake one that is still running).
+    if (warp != 12) grid_dep_wait();
+    if (tid == 0) grid_dep_launch();
 
     if (warp == 12) {
         // ---- TMA: state of item i -> ring slot i % NSTATE --------------------------
         if (lane == 0) {
             int i = 0;
+            if (prefetch_state)
+                for (; i < n_items && i < NSTATE; i++) {
+                    const int item = blockIdx.x + i * gridDim.x;
+                    mbar_arrive_expect_tx(&sm.sfull[i], STATE_BYTES);
+                    bulk_g2s(sm.state[i], S + (size_t)item * HD * HD, STATE_BYTES, &sm.sfull[i]);
+                }
+            grid_dep_wait();
             for (; i < n_items; i++) {
                 const int slot = i % NSTATE;
                 if (i >= NSTATE &&
@@ -323,7 +336,7 @@ template <bool A, bool O, bool G, bool Z>
 int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, const void *a,
            const void *b, const float *A_log, const float *dt_bias, const float *conv_w,
            const int *pos, const void *z, const float *norm_w, void *o, int B, int nqk, int nv,
-           char *err, size_t errlen) {
+           int prefetch_state, char *err, size_t errlen) {
     static bool attr = false;
     const size_t smem = sizeof(DnSmem) + 128;
     if (!attr) {
@@ -331,10 +344,20 @@ int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, co
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attr = true;
     }
-    dn_decode_k<A, O, G, Z><<<grid, NTHREADS, smem, st>>>(S, ring, qkv, a, b, A_log, dt_bias,
-                                                           conv_w, pos, z, norm_w, o, B, nqk, nv,
-                                                           dev_status());
-    VX_CK(cudaGetLastError());
+    // programmatic dependent launch: the CTAs may start (and, with prefetch_state, begin
+    // streaming state) while the previous kernel on the stream drains
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(NTHREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    VX_CK(cudaLaunchKernelEx(&cfg, dn_decode_k<A, O, G, Z>, S, ring, qkv, a, b, A_log, dt_bias,
+                             conv_w, pos, z, norm_w, o, B, nqk, nv, prefetch_state, dev_status()));
     return 0;
 }
 
@@ -362,12 +385,13 @@ static int decode_batch_impl(const char *fn, float *S, float *conv_ring, const v
     const int items = B * nv;
     const int grid = items < num_sms() ? items : num_sms();
     cudaStream_t st = (cudaStream_t)stream;
+    const int pf = (flags & VX27_F_PREFETCH_STATE) ? 1 : 0;
     const int key = (flags & VX27_F_ACT_BF16 ? 1 : 0) | (flags & VX27_F_OUT_BF16 ? 2 : 0) |
                     (g64 ? 4 : 0) | (gated ? 8 : 0);
 #define VX_L(K, A_, O_, G_, Z_)                                                              \
     case K:                                                                                  \
         return launch<A_, O_, G_, Z_>(grid, st, S, conv_ring, qkv, a, b, A_log, dt_bias,     \
-                                      conv_w, pos, z, norm_w, o, B, nqk, nv, err, errlen);
+                                      conv_w, pos, z, norm_w, o, B, nqk, nv, pf, err, errlen);
     switch (key) {
         VX_L(0, false, false, false, false)
         VX_L(1, true, false, false, false)
@@ -450,7 +474,9 @@ extern "C" int vx27_deltanet_decode_tokens(float *S, float *conv_ring, const voi
         const int rc = decode_batch_impl(
             fn, S, conv_ring, (const uint8_t *)qkv + t * C * ea, (const uint8_t *)a + t * nv * ea,
             (const uint8_t *)b + t * nv * ea, A_log, dt_bias, conv_w, pos + t, nullptr, nullptr,
-            (uint8_t *)o + (size_t)t * nv * HD * eo, 1, nqk, nv, hd, flags, stream, err, errlen);
+            (uint8_t *)o + (size_t)t * nv * HD * eo, 1, nqk, nv, hd,
+            flags & ~VX27_F_PREFETCH_STATE,  // token t reads the state token t-1 wrote
+            stream, err, errlen);
         if (rc) return rc;
         if (S_ckpt)
             VX_CK(cudaMemcpyAsync(S_ckpt + (size_t)t * nv * HD * HD, S,

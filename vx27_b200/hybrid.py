@@ -129,10 +129,12 @@ class HybridDecoder:
             if not full:
                 if on_layer:
                     on_layer("dn", i, "pre")
+                # the kernel before this one belongs to another layer (or is the position
+                # advance), so this layer's state can stream in while it drains
                 ops.deltanet_decode_batch(self.S[i], self.ring[i], self.qkv[i], self.a[i],
                                           self.b[i], self.A_log[i], self.dt_bias[i],
                                           self.conv_w[i], self.pos, self.dn_out[i], c.nqk, c.nv,
-                                          stream=stream)
+                                          stream=stream, prefetch_state=True)
                 if on_layer:
                     on_layer("dn", i, "post")
                 n += 1
@@ -199,7 +201,7 @@ class HybridDecoder:
                 ops.deltanet_decode_batch(self.S[i], self.ring[i], self.qkv[i], self.a[i],
                                           self.b[i], self.A_log[i], self.dt_bias[i],
                                           self.conv_w[i], self.pos, self.dn_out[i], c.nqk, c.nv,
-                                          stream=comp)
+                                          stream=comp, prefetch_state=True)
                 n += 1
             else:
                 ops.gqa_append(self.q_in[i], self.k_in[i], self.v_in[i], self.q_norm_w[i],

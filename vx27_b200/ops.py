@@ -22,6 +22,7 @@ F_ACT_BF16 = 0x1
 F_OUT_BF16 = 0x2
 F_NORM_1P = 0x4
 F_GATES_F64 = 0x8
+F_PREFETCH_STATE = 0x10
 
 
 def _np(a: np.ndarray, dtype=np.float32) -> C.c_void_p:
@@ -144,12 +145,15 @@ def _is_bf16(t) -> bool:
 
 
 def deltanet_decode_batch(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, nqk: int,
-                          nv: int, gates_f64: bool = False, stream=None) -> None:
-    """One DeltaNet decode step for a batch (vx27_deltanet_decode_batch)."""
+                          nv: int, gates_f64: bool = False, stream=None,
+                          prefetch_state: bool = False) -> None:
+    """One DeltaNet decode step for a batch (vx27_deltanet_decode_batch). prefetch_state:
+    the kernel may start reading S while the previous kernel on the stream still runs
+    (VX27_F_PREFETCH_STATE) - only when that kernel does not write S."""
     B = S.shape[0]
     hd = S.shape[-1]
     flags = (F_ACT_BF16 if _is_bf16(qkv) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0) | \
-        (F_GATES_F64 if gates_f64 else 0)
+        (F_GATES_F64 if gates_f64 else 0) | (F_PREFETCH_STATE if prefetch_state else 0)
     e = errbuf()
     rc = load().vx27_deltanet_decode_batch(_t(S), _t(conv_ring), _t(qkv), _t(a), _t(b),
                                            _t(A_log), _t(dt_bias), _t(conv_w), _t(pos), _t(o),
