@@ -36,7 +36,7 @@ METRIC = "DeltaNet+GQA decode tokens/s at 1/2/4/8 B200; % of HBM roofline"
 # ncu capture of the same kernel at 32 sequences (the full 256-sequence workload holds
 # 83 GB, too much to profile): each K/V byte is read once; the last tile of every
 # (sequence, KV head) fetches only the 32-row boxes it needs.
-GQA_SPLIT_DRAM_PER_ALGO_BYTE = 1.0067
+GQA_SPLIT_DRAM_PER_ALGO_BYTE = 1.012
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -242,12 +242,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             "parallelism": f"dp{world} (sequences sharded, no collective)",
         },
         "roofline": {
-            "bound": "hbm", "kernel": "gqa split-KV decode (per layer, + combine)",
+            "bound": "hbm",
+            "kernel": "gqa_split_tc split-KV decode, per layer (one split: it writes the gated "
+                      "output itself, no combine pass)",
             "achieved": round(gqa_gbs, 1), "peak": peak, "unit": "GB/s",
             "frac": round(gqa_gbs / peak, 4),
             "traffic": int(GQA_SPLIT_DRAM_PER_ALGO_BYTE * gqa_bytes),
             "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of gqa_split_tc "
-                               "at B = 32 (same kernel, context and splits per sequence; "
+                               "for one layer at B = 64 (same kernel and per-sequence context; "
                                f"{GQA_SPLIT_DRAM_PER_ALGO_BYTE} x its algorithmic bytes), "
                                "scaled by the sequences of this launch"),
             "peak_source": peak_src,
@@ -313,7 +315,7 @@ def run_layer(args) -> dict:
         pos = torch.full((B,), args.ctx, dtype=torch.int32, device="cuda")
         run = lambda: ops.gqa_decode_batch(q, gate, kc, vc, pos, out, ws)
         nbytes = B * nkv * cap * hd * 2 * 2 + B * nq * hd * (4 + 2 + 2)
-        name = "gqa_split_tc + combine (split-KV decode), one layer"
+        name = "gqa_split_tc (split-KV decode; one split writes the gated output), one layer"
     for _ in range(args.warmup):
         run()
     torch.cuda.synchronize()

@@ -346,18 +346,9 @@ int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, co
     }
     // programmatic dependent launch: the CTAs may start (and, with prefetch_state, begin
     // streaming state) while the previous kernel on the stream drains
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(NTHREADS);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    VX_CK(cudaLaunchKernelEx(&cfg, dn_decode_k<A, O, G, Z>, S, ring, qkv, a, b, A_log, dt_bias,
-                             conv_w, pos, z, norm_w, o, B, nqk, nv, prefetch_state, dev_status()));
+    VX_CK(launch_pdl(dn_decode_k<A, O, G, Z>, dim3(grid), dim3(NTHREADS), smem, st, S, ring, qkv,
+                     a, b, A_log, dt_bias, conv_w, pos, z, norm_w, o, B, nqk, nv, prefetch_state,
+                     dev_status()));
     return 0;
 }
 

@@ -34,6 +34,8 @@ gqa_append_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
              const int *__restrict__ pos, int slot_base, uint16_t *__restrict__ kc,
              uint16_t *__restrict__ vc, int cap, float *__restrict__ q_out, int nq, int nkv,
              int rope_dim, float eps, uint32_t *status) {
+    grid_dep_wait();  // inputs and positions come from the kernels before this one
+    if (threadIdx.x == 0) grid_dep_launch();
     const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const bool is_q = head < nq;
     const int h = is_q ? head : head - nq;
@@ -231,10 +233,10 @@ int vx27_gqa_append(const void *q_in, const void *k_in, const void *v_in,
     cudaStream_t st = (cudaStream_t)stream;
     const bool a = flags & VX27_F_ACT_BF16, one = flags & VX27_F_NORM_1P;
 #define VX_A(A_, O_)                                                                    \
-    gqa_append_k<A_, O_><<<grid, HD, 0, st>>>(q_in, k_in, v_in, q_norm_w, k_norm_w,     \
-                                              rope_table, rope_table_len, pos, slot_base, \
-                                              (uint16_t *)k_cache, (uint16_t *)v_cache, cap, \
-                                              q_out, nq, nkv, rope_dim, eps, dev_status())
+    VX_CK(launch_pdl(gqa_append_k<A_, O_>, grid, dim3(HD), 0, st, q_in, k_in, v_in, q_norm_w, \
+                     k_norm_w, rope_table, rope_table_len, pos, slot_base,                 \
+                     (uint16_t *)k_cache, (uint16_t *)v_cache, cap, q_out, nq, nkv, rope_dim, \
+                     eps, dev_status()))
     if (a && one) VX_A(true, true);
     else if (a) VX_A(true, false);
     else if (one) VX_A(false, true);

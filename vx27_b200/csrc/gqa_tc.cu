@@ -193,6 +193,9 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
+    // q, gate, positions and the newest cache rows come from the kernels before this one
+    grid_dep_wait();
+    if (tid == 0) grid_dep_launch();
 
     if (warp == 0) {
         // ---- TMA producer --------------------------------------------------------
@@ -581,9 +584,9 @@ int launch_split_tc(const void *kc, const void *vc, const float *q, const int *p
                                        (int)smem));                                       \
             attr = true;                                                                  \
         }                                                                                 \
-        gqa_split_tc<GG><<<grid, TC_THREADS, smem, st>>>(mk, mv, mk32, mv32, q, pos, parts, cap, \
-                                                         B, nq, nkv, n_splits, p_begin,    \
-                                                         p_end, gate, out, flags, stw);    \
+        VX_CK(launch_pdl(gqa_split_tc<GG>, grid, dim3(TC_THREADS), smem, st, mk, mv, mk32, mv32, \
+                         q, pos, parts, cap, B, nq, nkv, n_splits, p_begin, p_end, gate, out, \
+                         flags, stw));                                                     \
         break;                                                                            \
     }
     switch (nq / nkv) {
