@@ -48,8 +48,10 @@ int vx27_gqa_append(const void *q_in, const void *k_in, const void *v_in,
  * Decode attention of q (from vx27_gqa_append) over slots [0, pos[b]] of the caches,
  * softmax(q k^T / sqrt(hd)) v per Q head (Q head h reads KV head h*nkv/nq), then
  * out = att * sigmoid(gate) (src/vx27_qfwd.c:347-371). Split-KV flash decoding: each
- * (sequence, KV head, split) block serves the nq/nkv Q heads of its group; splits are
- * merged with a log-sum-exp combine. n_splits = 0 picks a split count for the device.
+ * (sequence, KV head, split) block serves the nq/nkv Q heads of its group; several splits
+ * are merged with a log-sum-exp combine, one split writes out directly. n_splits = 0 picks
+ * a split count for the device. q must be 8-byte aligned; gate, out and the workspace
+ * 16-byte aligned.
  *   gate [B][nq][hd] (act dtype), or NULL for no output gate (the MTP drafter's
  *        use_gate = 0, src/vx27_mtp.c:249); out [B][nq][hd] (fp32 or bf16 per VX27_F_OUT_BF16)
  *   workspace: vx27_gqa_decode_workspace_size(B, nq, nkv, hd, cap, n_splits) bytes of
