@@ -37,7 +37,7 @@ def oracle_step(orc, x, B, cap, bf16=True):
     return qo, kc, vc, out
 
 
-def gpu_step(x, B, cap, rope, n_splits=0, bf16=True):
+def gpu_step(x, B, cap, rope, n_splits=0, bf16=True, out_bf16=False):
     kc = dev(x["kc"], True).view(B, NKV, cap, HD)
     vc = dev(x["vc"], True).view(B, NKV, cap, HD)
     qi = dev(x["qi"], bf16).view(B, NQ, HD)
@@ -49,8 +49,10 @@ def gpu_step(x, B, cap, rope, n_splits=0, bf16=True):
     ops.gqa_append(qi, ki, vi, dev(x["qw"]), dev(x["kw"]), rope, pos, kc, vc, q)
     ws = torch.empty(ops.gqa_workspace_bytes(B, NQ, NKV, HD, cap, n_splits) // 4 + 1,
                      device="cuda")
-    out = torch.empty(B, NQ, HD, device="cuda")
+    out = torch.empty(B, NQ, HD, device="cuda",
+                      dtype=torch.bfloat16 if out_bf16 else torch.float32)
     ops.gqa_decode_batch(q, gate, kc, vc, pos, out, ws, n_splits=n_splits)
+    out = out.float()
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     return host(q).reshape(-1), host(kc).reshape(-1), host(vc).reshape(-1), host(out).reshape(-1)
@@ -107,12 +109,26 @@ def test_config1_ctx8192(cuda, orc, rope):
     assert err < REL_TOL and err < 1e-4
 
 
-def test_fp32_activations(cuda, orc, rope):
+@pytest.mark.parametrize("n_splits", [0, 1])
+def test_fp32_activations(cuda, orc, rope, n_splits):
+    # n_splits = 1: the split kernel applies the fp32 gate and writes the output itself
     B, cap = 2, 300
     x = setup(orc, 31, B, cap, [5, 299], bf16=False)
     qo, kc, vc, ref = oracle_step(orc, x, B, cap, bf16=False)
-    q, _, _, out = gpu_step(x, B, cap, rope, bf16=False)
+    q, _, _, out = gpu_step(x, B, cap, rope, n_splits, bf16=False)
     assert rel_err(out, ref) < 1e-4
+
+
+@pytest.mark.parametrize("n_splits", [1, 4])
+def test_bf16_output(cuda, orc, rope, n_splits):
+    # bf16 gate and bf16 output, written by the split kernel (1) or by the combine (4)
+    B, cap = 3, 700
+    x = setup(orc, 37, B, cap, [0, 300, 699])
+    qo, kc, vc, ref = oracle_step(orc, x, B, cap)
+    q, _, _, out = gpu_step(x, B, cap, rope, n_splits, out_bf16=True)
+    err = rel_err(out, ref)
+    print(f"splits={n_splits}: bf16 output rel err {err:.2e}")
+    assert err < 2e-2
 
 
 def test_partial_combine_context_parallel(cuda, orc, rope):
