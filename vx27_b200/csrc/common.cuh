@@ -125,6 +125,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
 }
 // 1-D bulk copy global -> shared (TMA engine, no tensor map), completion on mbarrier.
 // Both addresses 16-byte aligned and bytes a multiple of 16.
+// Bulk prefetch of [gsrc, gsrc + bytes) into L2 (16-byte aligned, size a multiple of 16):
+// more reads in flight without holding shared memory; a later copy of the range hits L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *gsrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gsrc, uint32_t bytes,
                                          uint64_t *bar) {
     asm volatile(

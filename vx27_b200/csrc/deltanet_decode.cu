@@ -31,6 +31,7 @@ constexpr int NCOMP = 256;                 // compute threads (warps 0-7)
 constexpr int NPREP = 128;                 // prep threads (warps 8-11)
 constexpr int NTHREADS = NCOMP + NPREP + 32;  // + TMA warp (warp 12)
 constexpr int NSTATE = 3;                  // state ring slots
+constexpr int PF_AHEAD = 1;                // L2 prefetch distance in items
 constexpr int NPARAM = 8;                  // parameter ring slots
 constexpr int STATE_BYTES = HD * HD * 4;   // 64 KB
 constexpr int BAR_COMP = 1;                // named barrier id of the compute warps
@@ -141,6 +142,12 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
                 const int item = blockIdx.x + i * gridDim.x;
                 mbar_arrive_expect_tx(&sm.sfull[slot], STATE_BYTES);
                 bulk_g2s(sm.state[slot], S + (size_t)item * HD * HD, STATE_BYTES, &sm.sfull[slot]);
+                // and the next item's state into L2: one more 64 KB read in flight per SM
+                // without shared memory (96.3 us per launch against 101.4 us without; two
+                // items ahead 97.7 us, three or more slower still)
+                if (i + PF_AHEAD < n_items)
+                    bulk_prefetch_l2(S + (size_t)(blockIdx.x + (i + PF_AHEAD) * gridDim.x) * HD * HD,
+                                     STATE_BYTES);
             }
             if (sm.abort) {  // let issued copies land before the CTA exits
                 for (int k = max(0, i - NSTATE); k < i; k++) {
