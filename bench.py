@@ -333,6 +333,105 @@ def run_layer(args) -> dict:
             "peak_source": peak_src}
 
 
+# ------------------------------------------------- K5: projection matvecs
+PMAT_SHAPES = [  # (projection, rows, cols) of one layer (src/vx27_qfwd.c:97-213, H = 5120)
+    ("deltanet.in_proj_qkv", 10240, 5120), ("deltanet.in_proj_z", 6144, 5120),
+    ("deltanet.in_proj_a", 48, 5120), ("deltanet.in_proj_b", 48, 5120),
+    ("deltanet.out_proj", 5120, 6144), ("gqa.q_proj", 12288, 5120), ("gqa.k_proj", 1024, 5120),
+    ("gqa.v_proj", 1024, 5120), ("gqa.o_proj", 5120, 6144)]
+
+
+def run_pmat(args) -> dict:
+    """Packed BP3_128 weights (random codes, fp16 scale 0.02), the projection shapes of one
+    DeltaNet and one GQA layer, B = 1 and 8 tokens. Each shape cycles through enough copies
+    of its weights (>= 512 MB) that every call reads them from HBM, not L2."""
+    import torch
+    from vx27_b200 import ops
+    peak, peak_src = peaks()
+    per = []
+    for B in (1, 8):
+        for name, rows, cols in PMAT_SHAPES:
+            rb = ops.pmat_row_bytes(ops.PMAT_BP3_128, cols)
+            wbytes = rows * rb
+            n_copy = max(2, -(-512 * 2**20 // wbytes))
+            W = torch.randint(0, 256, (n_copy, rows * rb), dtype=torch.uint8, device="cuda")
+            g = W.view(-1, 52)
+            g[:, 48:50] = torch.tensor([0x1F, 0x25], dtype=torch.uint8, device="cuda")  # fp16 0.0200
+            g[:, 50:52] = 0
+            x = torch.randn(B, cols, device="cuda")
+            y = torch.empty(B, rows, device="cuda")
+            for i in range(max(3, args.warmup)):
+                ops.pmat_batch(W[i % n_copy], ops.PMAT_BP3_128, x, y, rows, cols)
+            torch.cuda.synchronize()
+            reps = max(args.steps, 2 * n_copy)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(reps):
+                ops.pmat_batch(W[i % n_copy], ops.PMAT_BP3_128, x, y, rows, cols)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            gbs = (wbytes + B * (rows + cols) * 4) / (us * 1e-6) / 1e9
+            per.append({"projection": name, "rows": rows, "cols": cols, "tokens": B,
+                        "us": round(us, 2), "weight_bytes": wbytes, "GBps": round(gbs, 1),
+                        "frac": round(gbs / peak, 4),
+                        "weights_per_s_T": round(rows * cols / (us * 1e-6) / 1e12, 3)})
+            del W
+    layer = {}
+    for B in (1, 8):
+        for kind in ("deltanet", "gqa"):
+            sel = [r for r in per if r["tokens"] == B and r["projection"].startswith(kind)]
+            us = sum(r["us"] for r in sel)
+            wb = sum(r["weight_bytes"] for r in sel)
+            layer[f"{kind}_B{B}"] = {"us": round(us, 1), "GBps": round(wb / (us * 1e-6) / 1e9, 1),
+                                     "frac": round(wb / (us * 1e-6) / 1e9 / peak, 4)}
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = pmat_cpu_baseline()
+    return {"metric": "projection matvec weight GB/s (BP3_128 packed weights, K5)",
+            "workload": "pmat", "value": layer["deltanet_B1"]["GBps"], "unit": "GB/s",
+            "n_gpus": 1, "higher_is_better": True, "dtype": "f32 (packed 3.25-bit weights)",
+            "data": "synthetic (random 3-bit codes, fp16 scale 0.02; x ~N(0,1))",
+            "config": {"workload": "projections of one DeltaNet and one GQA layer, H = 5120",
+                       "l2": "weights cycled through >= 512 MB of copies"},
+            "roofline": {"bound": "hbm (weights) / CUDA-core unpack", "peak": peak,
+                         "unit": "GB/s", "peak_source": peak_src},
+            "per_layer": layer, "per_projection": per, "cpu_baseline": cpu}
+
+
+def pmat_cpu_baseline() -> dict | None:
+    """The reference's own vx27_pmat (oracle/_ref, AVX2, all host threads) on
+    in_proj_qkv (10240 x 5120, BP3_128), one token."""
+    import ctypes as C
+    import time
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    import oracle.oracle as O
+    if not os.path.exists(O.REF_PMAT_LIB) and not O.build_ref():
+        return None
+    if not os.path.exists(O.REF_PMAT_LIB):
+        return None
+    lib = C.CDLL(O.REF_PMAT_LIB)
+    lib.tp_create.restype = C.c_void_p
+    lib.tp_create.argtypes = [C.c_int, C.c_char_p, C.c_size_t]
+    lib.vx27_pmat.argtypes = [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
+                              C.c_int, C.c_int]
+    threads = os.cpu_count() or 1
+    tp = lib.tp_create(threads, None, 0)
+    rows, cols = 10240, 5120
+    W = O.packed_weights(O.PMAT_BP3, rows, cols, 5)
+    x = np.random.default_rng(1).standard_normal(cols).astype(np.float32)
+    y = np.empty(rows, np.float32)
+    best = 1e9
+    for _ in range(5):
+        t0 = time.perf_counter()
+        lib.vx27_pmat(tp, O.P(W), O.PMAT_BP3, O.P(x), O.P(y), rows, cols)
+        best = min(best, time.perf_counter() - t0)
+    return {"value": round(rows * 52 * (cols // 128) / best / 1e9, 2), "unit": "GB/s",
+            "us": round(best * 1e6, 1), "cores": threads, "kind": "reference",
+            "sample": "vx27_pmat on in_proj_qkv 10240 x 5120 BP3_128, one token, best of 5"}
+
+
 # ------------------------------------------------- configs 0 and 1 (batch-1 latency)
 def run_batch1(args) -> dict:
     """Config 0: one DeltaNet layer decoding 2000 tokens of one sequence (16 heads, fp32
@@ -790,7 +889,7 @@ def main() -> None:
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["config2", "config0", "config1", "config3a",
-                                           "config3b", "config4", "dn_layer", "gqa_layer"],
+                                           "config3b", "config4", "dn_layer", "gqa_layer", "pmat"],
                     default="config2",
                     help="config2 (the metric); config3a/3b long context; single-layer "
                          "workloads are for kernel rooflines and profiling")
@@ -808,6 +907,9 @@ def main() -> None:
 
     if args.workload in ("dn_layer", "gqa_layer"):
         print(json.dumps(run_layer(args)), flush=True)
+        return
+    if args.workload == "pmat":
+        print(json.dumps(run_pmat(args)), flush=True)
         return
     if args.workload == "config4":
         print(json.dumps(run_prefill(args)), flush=True)

@@ -16,6 +16,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "liboracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libvx27ref.so")
+REF_PMAT_LIB = os.path.join(HERE, "_ref", "libvx27ref_pmat.so")
 
 F_ACT_BF16, F_OUT_BF16, F_NORM_1P = 0x1, 0x2, 0x4
 
@@ -55,6 +56,8 @@ _PROTOS = {
     "orc_fill_normal_f32": (None, [_p, _sz, _u64, _u64, _f, _f]),
     "orc_fill_normal_bf16": (None, [_p, _sz, _u64, _u64, _f, _f]),
     "orc_fill_uniform_f32": (None, [_p, _sz, _u64, _u64, _f, _f]),
+    "orc_bp3_scale": (_f, [C.c_uint16]),
+    "orc_pmat_batch": (None, [_p, C.c_uint32, _p, _p, _i, _i, _i]),
     "orc_use_reference": (_i, [C.c_char_p]),
     "orc_impl_is_reference": (_i, []),
 }
@@ -131,3 +134,43 @@ def use_reference(enable: bool = True) -> bool:
     if not os.path.exists(REF_LIB):
         return False
     return lib().orc_use_reference(REF_LIB.encode()) == 0
+
+
+# ---- packed weights (the layouts src/vx27_pmat.c reads) ------------------------------
+PMAT_F32, PMAT_Q8K, PMAT_BP3 = 0, 2, 4
+
+
+def pmat_row_bytes(dtype: int, cols: int) -> int:
+    return cols * 4 if dtype == PMAT_F32 else (cols // 256) * 292 if dtype == PMAT_Q8K \
+        else (cols // 128) * 52
+
+
+def packed_weights(dtype: int, rows: int, cols: int, seed: int) -> np.ndarray:
+    """Random packed weights as raw bytes [rows * row_bytes]: F32 ~N(0, 0.02); Q8_K with
+    d ~ U(1e-4, 1e-3) and uniform int8 codes; BP3_128 with uniform 3-bit codes and fp16
+    scales ~ U(0.005, 0.05), some of them fp16 subnormals (the reference maps those with
+    exponent 1, which the oracle and the device reproduce)."""
+    rng = np.random.default_rng(seed)
+    if dtype == PMAT_F32:
+        return (rng.standard_normal(rows * cols).astype(np.float32) * 0.02).view(np.uint8)
+    if dtype == PMAT_Q8K:
+        nb = rows * (cols // 256)
+        blk = np.zeros((nb, 292), np.uint8)
+        blk[:, 0:4] = rng.uniform(1e-4, 1e-3, nb).astype(np.float32).view(np.uint8).reshape(nb, 4)
+        blk[:, 4:260] = rng.integers(-127, 128, (nb, 256)).astype(np.int8).view(np.uint8)
+        return blk.reshape(-1)
+    ng = rows * (cols // 128)
+    g = np.zeros((ng, 52), np.uint8)
+    g[:, 0:48] = rng.integers(0, 256, (ng, 48), dtype=np.uint8)
+    sc = rng.uniform(0.005, 0.05, ng).astype(np.float16)
+    sub = rng.random(ng) < 0.05
+    sc[sub] = (rng.integers(1, 1024, int(sub.sum())).astype(np.uint16)).view(np.float16)
+    g[:, 48:50] = sc.view(np.uint8).reshape(ng, 2)
+    return g.reshape(-1)
+
+
+def pmat_batch(W: np.ndarray, dtype: int, xb: np.ndarray, rows: int, cols: int, B: int):
+    y = np.empty(B * rows, np.float32)
+    lib().orc_pmat_batch(P(W), dtype, P(np.ascontiguousarray(xb, np.float32)), P(y), rows,
+                         cols, B)
+    return y

@@ -579,6 +579,87 @@ void orc_gqa_prefill_rows(const void *q, const void *k, const void *v, const voi
 
 /* ------------------------------------------------------ synthetic inputs */
 /* splitmix64 (Steele, Lea & Flood 2014), used as a counter-based generator */
+/* ---- packed-weight matvec ------------------------------------------------ */
+/* The group scale's fp16 -> fp32 as src/vx27_pmat.c:38-41 forms it: exponent rebased by
+ * 112, subnormal fp16 values mapped with exponent 1 (not scaled as IEEE would). */
+float orc_bp3_scale(uint16_t h) {
+    const uint32_t u = h, sign = (u & 0x8000u) << 16, ex = (u >> 10) & 0x1Fu, man = u & 0x3FFu;
+    uint32_t bits;
+    if (ex == 0) bits = man ? (sign | ((ex + 1 + 112u) << 23) | (man << 13)) : sign;
+    else if (ex == 31) bits = sign | 0x7F800000u | (man << 13);
+    else bits = sign | ((ex + 112u) << 23) | (man << 13);
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* One BP3_128 row against one vector: eight lanes, lane l = columns l mod 8 of each group
+ * in increasing order, q*scale then fused multiply-add (src/vx27_pmat.c:28-63). */
+static float orc_bp3_row(const uint8_t *row, int ng, const float *x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = 0; k < ng; k++) {
+        const uint8_t *g = row + (size_t)k * 52;
+        uint32_t p[12];
+        uint16_t h;
+        memcpy(p, g, 48);
+        memcpy(&h, g + 48, 2);
+        const float sc = orc_bp3_scale(h);
+        for (int i = 0; i < 128; i += 8)
+            for (int l = 0; l < 8; l++) {
+                const int e = i + l, w = e >> 5, bit = e & 31;
+                const uint32_t u = ((p[w] >> bit) & 1u) | (((p[4 + w] >> bit) & 1u) << 1) |
+                                   (((p[8 + w] >> bit) & 1u) << 2);
+                const int q = u >= 4 ? (int)u - 8 : (int)u;
+                const float qv = (float)q * sc;
+                acc[l] = fmaf(qv, x[k * 128 + e], acc[l]);
+            }
+    }
+    return acc[0] + acc[1] + acc[2] + acc[3] + acc[4] + acc[5] + acc[6] + acc[7];
+}
+
+/* One Q8_K row: per block eight FMA lanes summed left to right, times d in double
+ * (src/vx27_pmat.c:10-24, 100-105). */
+static float orc_q8k_row(const uint8_t *row, int nb, const float *x) {
+    double s = 0;
+    for (int k = 0; k < nb; k++) {
+        const uint8_t *blk = row + (size_t)k * 292;
+        float d;
+        memcpy(&d, blk, 4);
+        const int8_t *qs = (const int8_t *)(blk + 4);
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int i = 0; i < 256; i += 8)
+            for (int l = 0; l < 8; l++) acc[l] = fmaf((float)qs[i + l], x[k * 256 + i + l], acc[l]);
+        const float t = acc[0] + acc[1] + acc[2] + acc[3] + acc[4] + acc[5] + acc[6] + acc[7];
+        s += (double)t * d;
+    }
+    return (float)s;
+}
+
+void orc_pmat_batch(const void *W, uint32_t dtype, const float *xb, float *yb, int rows,
+                    int cols, int B) {
+    const uint8_t *w8 = (const uint8_t *)W;
+    const size_t rb = dtype == 0 ? (size_t)cols * 4
+                    : dtype == 2 ? (size_t)(cols / 256) * 292 : (size_t)(cols / 128) * 52;
+    for (int r = 0; r < rows; r++) {
+        const uint8_t *row = w8 + (size_t)r * rb;
+        for (int b = 0; b < B; b++) {
+            const float *x = xb + (size_t)b * cols;
+            float y;
+            if (dtype == 0) {
+                const float *wr = (const float *)row;
+                double s = 0;
+                for (int c = 0; c < cols; c++) s += (double)wr[c] * (double)x[c];
+                y = (float)s;
+            } else if (dtype == 2) {
+                y = orc_q8k_row(row, cols / 256, x);
+            } else {
+                y = orc_bp3_row(row, cols / 128, x);
+            }
+            yb[(size_t)b * rows + r] = y;
+        }
+    }
+}
+
 uint64_t orc_splitmix64(uint64_t x) {
     x += 0x9E3779B97F4A7C15ull;
     x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;

@@ -127,6 +127,20 @@ void orc_gqa_prefill_rows(const void *q, const void *k, const void *v, const voi
                           int T, int nq, int nkv, int hd, int rope_dim, float theta,
                           float eps, const int *rows, int n_rows, float *out, int flags);
 
+/* ---- packed-weight matvec (src/vx27_pmat.c) ------------------------------- */
+/* yb[b*rows + r] = W[r] . xb[b*cols ..] for b < B, per the reference's arithmetic:
+ * dtype 0 F32 rows, double accumulation over columns (src/vx27_pmat.c:96-99, 196-204);
+ * dtype 2 Q8_K blocks of 256 (float d, int8 qs[256], int16 bsums[16]; 292 B): per block
+ *   eight fp32 FMA lanes (lane l takes columns l, l+8, ...), lanes summed left to right,
+ *   times d in double, accumulated in double (:10-24, :100-105, :187-195);
+ * dtype 4 BP3_128 groups of 128 (three planes of 4 u32 + fp16 scale, 52 B in memory):
+ *   eight fp32 FMA lanes over the whole row with q*scale formed by one multiply, lanes
+ *   summed left to right at the end (:28-63, :133-177).
+ * cols must be a multiple of 256 (Q8_K) or 128 (BP3_128). */
+float orc_bp3_scale(uint16_t h);  /* the reference's fp16 -> fp32 of the group scale */
+void orc_pmat_batch(const void *W, uint32_t dtype, const float *xb, float *yb, int rows,
+                    int cols, int B);
+
 /* ---- seeded synthetic inputs (same formula as vx27_b200/csrc/synth.cu) --- */
 uint64_t orc_splitmix64(uint64_t x);
 void orc_fill_normal_f32(float *x, size_t n, uint64_t seed, uint64_t stream,

@@ -1,0 +1,61 @@
+"""Pins of the packed-weight matvec restatement (oracle/vx27_oracle.c, orc_pmat_batch)
+against the reference's own src/vx27_pmat.c, compiled unmodified into
+oracle/_ref/libvx27ref_pmat.so: bit-identical outputs for F32, Q8_K and BP3_128 rows,
+single-vector (vx27_pmat) and batched (vx27_pmat_batch) entry points."""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+import oracle.oracle as O
+
+
+@pytest.fixture(scope="module")
+def refpmat():
+    if not os.path.exists(O.REF_PMAT_LIB) and not O.build_ref():
+        pytest.skip("reference sources unavailable: oracle/_ref not built")
+    if not os.path.exists(O.REF_PMAT_LIB):
+        pytest.skip("oracle/_ref/libvx27ref_pmat.so not built")
+    lib = C.CDLL(O.REF_PMAT_LIB)
+    lib.vx27_pmat.argtypes = [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
+                              C.c_int, C.c_int]
+    lib.vx27_pmat_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p,
+                                    C.c_void_p, C.c_int, C.c_int, C.c_int]
+    return lib
+
+
+@pytest.mark.parametrize("dtype", [O.PMAT_F32, O.PMAT_Q8K, O.PMAT_BP3])
+@pytest.mark.parametrize("B", [1, 3, 8])
+def test_restatement_equals_reference(refpmat, dtype, B):
+    rows, cols = 37, 1024
+    W = O.packed_weights(dtype, rows, cols, 100 + dtype)
+    x = np.random.default_rng(7 + B).standard_normal(B * cols).astype(np.float32)
+    y_orc = O.pmat_batch(W, dtype, x, rows, cols, B)
+    y_ref = np.empty(B * rows, np.float32)
+    if B == 1:
+        refpmat.vx27_pmat(None, O.P(W), dtype, O.P(x), O.P(y_ref), rows, cols)
+    else:
+        refpmat.vx27_pmat_batch(None, O.P(W), dtype, O.P(x), O.P(y_ref), rows, cols, B)
+    assert np.array_equal(y_orc.view(np.uint32), y_ref.view(np.uint32))
+    # and the batched reference equals B single calls (the reference's own claim)
+    if B > 1:
+        y1 = np.empty(rows, np.float32)
+        for b in range(B):
+            refpmat.vx27_pmat(None, O.P(W), dtype, O.P(x[b * cols:(b + 1) * cols].copy()),
+                              O.P(y1), rows, cols)
+            assert np.array_equal(y1.view(np.uint32), y_ref[b * rows:(b + 1) * rows].view(np.uint32))
+
+
+def test_bp3_scale_conversion(refpmat):
+    # every fp16 bit pattern: normal values convert exactly, subnormals with the
+    # reference's exponent-1 mapping, inf/nan kept
+    h = np.arange(65536, dtype=np.uint16)
+    f = np.array([O.lib().orc_bp3_scale(int(v)) for v in h[::97]], np.float32)
+    ref = h[::97].view(np.float16).astype(np.float32)
+    normal = ((h[::97] >> 10) & 0x1F) != 0
+    finite = ((h[::97] >> 10) & 0x1F) != 31
+    m = normal & finite
+    assert np.array_equal(f[m], ref[m])
+    sub = (~normal) & ((h[::97] & 0x3FF) != 0)
+    assert np.all(np.abs(f[sub]) >= 2.0 ** -14)  # mapped with exponent 1, not scaled down

@@ -289,6 +289,29 @@ def gqa_combine(parts, n_parts: int, gate, out, part_stride: int = 0, stream=Non
     check(rc, e)
 
 
+PMAT_F32, PMAT_Q8_K, PMAT_BP3_128 = 0, 2, 4
+
+
+def pmat_row_bytes(dtype: int, cols: int) -> int:
+    return int(load().vx27_pmat_row_bytes(dtype, cols))
+
+
+def pmat_batch(W, dtype: int, xb, yb, rows: int, cols: int, stream=None) -> None:
+    """Packed-weight matvec (vx27_pmat_batch_dev): yb[b, r] = W[r] . xb[b]; W a uint8
+    tensor holding rows packed rows of pmat_row_bytes(dtype, cols) bytes, xb [B, cols] and
+    yb [B, rows] fp32."""
+    import torch
+    B = xb.shape[0]
+    if xb.dtype != torch.float32 or yb.dtype != torch.float32:
+        raise Vx27Error("pmat_batch: xb and yb must be fp32")
+    if W.numel() * W.element_size() < rows * pmat_row_bytes(dtype, cols):
+        raise Vx27Error("pmat_batch: W holds fewer than rows packed rows")
+    e = errbuf()
+    rc = load().vx27_pmat_batch_dev(_t(W), dtype, _t(xb), _t(yb), rows, cols, B, _stream(stream),
+                                    e, 512)
+    check(rc, e)
+
+
 def gqa_prefill(q_in, k_in, v_in, gate, q_norm_w, k_norm_w, rope, k_cache, v_cache, out,
                 workspace=None, p0: int = 0, eps: float = 1e-6, norm_one_plus: bool = False,
                 stream=None):
