@@ -34,6 +34,10 @@ extern "C" {
  * when that kernel does not write S, e.g. when it belongs to another layer; everything
  * else the kernel reads still waits for the previous kernel to finish. */
 #define VX27_F_PREFETCH_STATE 0x10
+/* DeltaNet decode, gated entry point: the production layer's q/k pre-normalisation
+ * (src/vx27_qfwd.c:118-130): zero-centred RMSNorm with norm_w, y = x*s*(1+w), then l2norm
+ * and q*1/sqrt(hd), before the l2norm and scaling the delta rule itself applies. */
+#define VX27_F_QK_PRENORM 0x20
 
 /* Library version, major*10000 + minor*100 + patch. */
 int vx27cuda_version(void);

@@ -99,7 +99,7 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             const float *__restrict__ A_log, const float *__restrict__ dt_bias,
             const float *__restrict__ conv_w, const int *__restrict__ pos,
             const void *__restrict__ z, const float *__restrict__ norm_w, void *__restrict__ o,
-            int B, int nqk, int nv, int prefetch_state, uint32_t *status) {
+            int B, int nqk, int nv, int prefetch_state, int prenorm, uint32_t *status) {
     extern __shared__ uint8_t dn_smem_raw[];
     DnSmem &sm = *reinterpret_cast<DnSmem *>(((uintptr_t)dn_smem_raw + 127) & ~(uintptr_t)127);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -212,6 +212,32 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
                     y[part][j] = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
                     if (part == 2 || qk_owner) rb[(size_t)slw * C + c] = x;
                 }
+            }
+            if (prenorm) {
+                // production q/k pre-normalisation (src/vx27_qfwd.c:31-39, 118-130):
+                // RMSNorm y*s*(1+w) with the fp64 sum of squares, then l2norm, q/sqrt(hd)
+#pragma unroll
+                for (int part = 0; part < 2; part++) {
+                    double ss = 0.0;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) ss += (double)y[part][j] * (double)y[part][j];
+                    ss = warp_sum_d(ss);
+                    const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(ss / HD), 1e-6f)));
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        y[part][j] = __fmul_rn(__fmul_rn(y[part][j], s),
+                                               __fadd_rn(norm_w[lane + 32 * j], 1.0f));
+                    double sl = 0.0;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) sl += (double)y[part][j] * (double)y[part][j];
+                    sl = warp_sum_d(sl);
+                    const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)sl, 1e-6f)));
+#pragma unroll
+                    for (int j = 0; j < 4; j++) y[part][j] = __fmul_rn(y[part][j], rs);
+                }
+                const float qs0 = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+#pragma unroll
+                for (int j = 0; j < 4; j++) y[0][j] = __fmul_rn(y[0][j], qs0);
             }
             double sq = 0.0, sk = 0.0;
 #pragma unroll
@@ -343,7 +369,7 @@ template <bool A, bool O, bool G, bool Z>
 int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, const void *a,
            const void *b, const float *A_log, const float *dt_bias, const float *conv_w,
            const int *pos, const void *z, const float *norm_w, void *o, int B, int nqk, int nv,
-           int prefetch_state, char *err, size_t errlen) {
+           int prefetch_state, int prenorm, char *err, size_t errlen) {
     static bool attr = false;
     const size_t smem = sizeof(DnSmem) + 128;
     if (!attr) {
@@ -355,7 +381,7 @@ int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, co
     // streaming state) while the previous kernel on the stream drains
     VX_CK(launch_pdl(dn_decode_k<A, O, G, Z>, dim3(grid), dim3(NTHREADS), smem, st, S, ring, qkv,
                      a, b, A_log, dt_bias, conv_w, pos, z, norm_w, o, B, nqk, nv, prefetch_state,
-                     dev_status()));
+                     prenorm, dev_status()));
     return 0;
 }
 
@@ -384,12 +410,15 @@ static int decode_batch_impl(const char *fn, float *S, float *conv_ring, const v
     const int grid = items < num_sms() ? items : num_sms();
     cudaStream_t st = (cudaStream_t)stream;
     const int pf = (flags & VX27_F_PREFETCH_STATE) ? 1 : 0;
+    const int pn = (flags & VX27_F_QK_PRENORM) ? 1 : 0;
+    if (pn && !gated)
+        return fail(err, errlen, "%s: VX27_F_QK_PRENORM needs the gated entry point (norm_w)", fn);
     const int key = (flags & VX27_F_ACT_BF16 ? 1 : 0) | (flags & VX27_F_OUT_BF16 ? 2 : 0) |
                     (g64 ? 4 : 0) | (gated ? 8 : 0);
 #define VX_L(K, A_, O_, G_, Z_)                                                              \
     case K:                                                                                  \
         return launch<A_, O_, G_, Z_>(grid, st, S, conv_ring, qkv, a, b, A_log, dt_bias,     \
-                                      conv_w, pos, z, norm_w, o, B, nqk, nv, pf, err, errlen);
+                                      conv_w, pos, z, norm_w, o, B, nqk, nv, pf, pn, err, errlen);
     switch (key) {
         VX_L(0, false, false, false, false)
         VX_L(1, true, false, false, false)

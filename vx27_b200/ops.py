@@ -23,6 +23,7 @@ F_OUT_BF16 = 0x2
 F_NORM_1P = 0x4
 F_GATES_F64 = 0x8
 F_PREFETCH_STATE = 0x10
+F_QK_PRENORM = 0x20
 
 
 def _np(a: np.ndarray, dtype=np.float32) -> C.c_void_p:
@@ -178,12 +179,16 @@ def deltanet_decode_tokens(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos,
 
 def deltanet_decode_batch_gated(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, z,
                                 norm_w, o, nqk: int, nv: int, gates_f64: bool = False,
-                                stream=None) -> None:
-    """Decode step plus the gated RMSNorm output (vx27_deltanet_decode_batch_gated)."""
+                                stream=None, qk_prenorm: bool = False,
+                                prefetch_state: bool = False) -> None:
+    """Decode step plus the gated RMSNorm output (vx27_deltanet_decode_batch_gated).
+    qk_prenorm: the production layer's q/k RMSNorm (1+norm_w), l2norm and 1/sqrt(hd)
+    before the delta rule's own normalisation (VX27_F_QK_PRENORM)."""
     B = S.shape[0]
     hd = S.shape[-1]
     flags = (F_ACT_BF16 if _is_bf16(qkv) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0) | \
-        (F_GATES_F64 if gates_f64 else 0)
+        (F_GATES_F64 if gates_f64 else 0) | (F_QK_PRENORM if qk_prenorm else 0) | \
+        (F_PREFETCH_STATE if prefetch_state else 0)
     if _is_bf16(qkv) != _is_bf16(z):
         raise Vx27Error("z must have the activation dtype of qkv")
     e = errbuf()
