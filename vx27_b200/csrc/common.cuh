@@ -171,6 +171,9 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 int num_sms();
+// Sets a kernel's dynamic shared-memory limit on the current device once per (kernel,
+// device, size); -1 with the CUDA error in err.
+int ensure_smem_attr(const void *kernel, size_t bytes, char *err, size_t errlen);
 
 // Launch with programmatic stream serialization: the grid may be scheduled while the
 // previous kernel on the stream drains; the kernel calls grid_dep_wait() before it reads

@@ -370,13 +370,8 @@ int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, co
            const void *b, const float *A_log, const float *dt_bias, const float *conv_w,
            const int *pos, const void *z, const float *norm_w, void *o, int B, int nqk, int nv,
            int prefetch_state, int prenorm, char *err, size_t errlen) {
-    static bool attr = false;
     const size_t smem = sizeof(DnSmem) + 128;
-    if (!attr) {
-        VX_CK(cudaFuncSetAttribute(dn_decode_k<A, O, G, Z>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr = true;
-    }
+    if (ensure_smem_attr((const void *)dn_decode_k<A, O, G, Z>, smem, err, errlen)) return -1;
     // programmatic dependent launch: the CTAs may start (and, with prefetch_state, begin
     // streaming state) while the previous kernel on the stream drains
     VX_CK(launch_pdl(dn_decode_k<A, O, G, Z>, dim3(grid), dim3(NTHREADS), smem, st, S, ring, qkv,

@@ -773,8 +773,7 @@ dn_out_tc(Wsp ws, void *__restrict__ o, int T, int nv, int n_chunks, uint32_t *s
 
 template <typename K>
 int set_smem(K kernel, uint32_t bytes, char *err, size_t errlen) {
-    VX_CK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-    return 0;
+    return ensure_smem_attr((const void *)kernel, bytes, err, errlen);
 }
 
 }  // namespace
@@ -827,19 +826,11 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
         return -1;
 
     if (g64) {
-        static bool attr = false;
-        if (!attr) {
-            if (set_smem(dn_prep_tc<true>, PREP_SMEM, err, errlen)) return -1;
-            attr = true;
-        }
+        if (set_smem(dn_prep_tc<true>, PREP_SMEM, err, errlen)) return -1;
         dn_prep_tc<true><<<dim3(n_chunks, nv), PREP_THREADS, PREP_SMEM, st>>>(
             tq, tk, tv, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
     } else {
-        static bool attr = false;
-        if (!attr) {
-            if (set_smem(dn_prep_tc<false>, PREP_SMEM, err, errlen)) return -1;
-            attr = true;
-        }
+        if (set_smem(dn_prep_tc<false>, PREP_SMEM, err, errlen)) return -1;
         dn_prep_tc<false><<<dim3(n_chunks, nv), PREP_THREADS, PREP_SMEM, st>>>(
             tq, tk, tv, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
     }
@@ -847,44 +838,24 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
     // scan: the narrowest column blocks whose grid still fits the GPU (2 CTAs per SM for 8
     // columns, 1 for 16), else 32
     if (nv * (D / 8) <= 2 * num_sms()) {
-        static bool attr = false;
-        if (!attr) {
-            if (set_smem(dn_scan_tc<8>, ScanLayout<8>::SMEM, err, errlen)) return -1;
-            attr = true;
-        }
+        if (set_smem(dn_scan_tc<8>, ScanLayout<8>::SMEM, err, errlen)) return -1;
         dn_scan_tc<8><<<dim3(D / 8, nv), 160, ScanLayout<8>::SMEM, st>>>(ws, S, n_chunks,
                                                                          status);
     } else if (nv * (D / 16) <= num_sms()) {
-        static bool attr = false;
-        if (!attr) {
-            if (set_smem(dn_scan_tc<16>, ScanLayout<16>::SMEM, err, errlen)) return -1;
-            attr = true;
-        }
+        if (set_smem(dn_scan_tc<16>, ScanLayout<16>::SMEM, err, errlen)) return -1;
         dn_scan_tc<16><<<dim3(D / 16, nv), 160, ScanLayout<16>::SMEM, st>>>(ws, S, n_chunks,
                                                                              status);
     } else {
-        static bool attr = false;
-        if (!attr) {
-            if (set_smem(dn_scan_tc<32>, ScanLayout<32>::SMEM, err, errlen)) return -1;
-            attr = true;
-        }
+        if (set_smem(dn_scan_tc<32>, ScanLayout<32>::SMEM, err, errlen)) return -1;
         dn_scan_tc<32><<<dim3(D / 32, nv), 160, ScanLayout<32>::SMEM, st>>>(ws, S, n_chunks,
                                                                              status);
     }
     VX_CK(cudaGetLastError());
     if (flags & VX27_F_OUT_BF16) {
-        static bool attr = false;
-        if (!attr) {
-            if (set_smem(dn_out_tc<true>, OUT_SMEM, err, errlen)) return -1;
-            attr = true;
-        }
+        if (set_smem(dn_out_tc<true>, OUT_SMEM, err, errlen)) return -1;
         dn_out_tc<true><<<dim3(n_chunks, nv), 128, OUT_SMEM, st>>>(ws, o, T, nv, n_chunks, status);
     } else {
-        static bool attr = false;
-        if (!attr) {
-            if (set_smem(dn_out_tc<false>, OUT_SMEM, err, errlen)) return -1;
-            attr = true;
-        }
+        if (set_smem(dn_out_tc<false>, OUT_SMEM, err, errlen)) return -1;
         dn_out_tc<false><<<dim3(n_chunks, nv), 128, OUT_SMEM, st>>>(ws, o, T, nv, n_chunks,
                                                                     status);
     }

@@ -525,13 +525,8 @@ template <bool A, bool O>
 int launch_attn(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
                 const void *gate, void *out, int T, int p0, int nq, int nkv, int cap,
                 cudaStream_t st, char *err, size_t errlen) {
-    static bool attr = false;
     const size_t smem = sizeof(PfSmem) + 1024;
-    if (!attr) {
-        VX_CK(cudaFuncSetAttribute(prefill_attn_tc<A, O>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr = true;
-    }
+    if (ensure_smem_attr((const void *)prefill_attn_tc<A, O>, smem, err, errlen)) return -1;
     const int n_qt = (T + QT - 1) / QT;
     prefill_attn_tc<A, O><<<n_qt * nq, PF_THREADS, smem, st>>>(mq, mk, mv, gate, out, T, p0, nq,
                                                                  nkv, cap, dev_status());

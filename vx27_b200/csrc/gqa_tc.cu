@@ -577,13 +577,8 @@ int launch_split_tc(const void *kc, const void *vc, const float *q, const int *p
     uint32_t *stw = dev_status();
 #define VX_TCG(GG)                                                                        \
     case GG: {                                                                            \
-        static bool attr = false;                                                         \
-        if (!attr) {                                                                      \
-            VX_CK(cudaFuncSetAttribute(gqa_split_tc<GG>,                                  \
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,       \
-                                       (int)smem));                                       \
-            attr = true;                                                                  \
-        }                                                                                 \
+        if (ensure_smem_attr((const void *)gqa_split_tc<GG>, smem, err, errlen))          \
+            return -1;                                                                    \
         VX_CK(launch_pdl(gqa_split_tc<GG>, grid, dim3(TC_THREADS), smem, st, mk, mv, mk32, mv32, \
                          q, pos, parts, cap, B, nq, nkv, n_splits, p_begin, p_end, gate, out, \
                          flags, stw));                                                     \
@@ -617,13 +612,8 @@ int launch_split_tc_status(const void *kc, const void *vc, const float *q, const
     const dim3 grid(tc_grid(B, nkv, n_splits));
 #define VX_TCS(GG)                                                                        \
     case GG: {                                                                            \
-        static bool attr = false;                                                         \
-        if (!attr) {                                                                      \
-            VX_CK(cudaFuncSetAttribute(gqa_split_tc<GG>,                                  \
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,       \
-                                       (int)smem));                                       \
-            attr = true;                                                                  \
-        }                                                                                 \
+        if (ensure_smem_attr((const void *)gqa_split_tc<GG>, smem, err, errlen))          \
+            return -1;                                                                    \
         gqa_split_tc<GG><<<grid, TC_THREADS, smem, st>>>(mk, mv, mk32, mv32, q, pos, parts, cap, \
                                                          B, nq, nkv, n_splits, 0, -1,      \
                                                          nullptr, nullptr, 0, status);     \

@@ -247,12 +247,7 @@ int launch_pmat(const void *W, uint32_t dtype, const float *xb, float *yb, int r
         const size_t smem = bp3_w_bytes(cols) + bp3_xs_bytes(TB);
         if (smem > 220 * 1024)
             return fail(err, errlen, "vx27_pmat_batch_dev: cols=%d too wide for one CTA", cols);
-        static int attr = 0;
-        if ((size_t)attr < smem) {
-            VX_CK(cudaFuncSetAttribute(pmat_bp3_k<TB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem));
-            attr = (int)smem;
-        }
+        if (ensure_smem_attr((const void *)pmat_bp3_k<TB>, smem, err, errlen)) return -1;
         VX_CK(launch_pdl(pmat_bp3_k<TB>, grid, dim3(BP3_THREADS), smem, st,
                          (const uint8_t *)W, xb, yb, rows, cols, B, dev_status()));
     } else if (dtype == VX27_PMAT_Q8_K) {

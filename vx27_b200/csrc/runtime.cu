@@ -3,6 +3,7 @@
 #include <stdarg.h>
 #include <stdlib.h>
 #include <string.h>
+#include <mutex>
 #include <vector>
 #include "common.cuh"
 #include "../../include/vx27_deltanet.h"
@@ -12,10 +13,13 @@
 
 namespace vx27 {
 
+static std::mutex g_rt_mu;  // guards the per-device caches below
+
 uint32_t *dev_status() {
     static uint32_t *ptrs[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_rt_mu);
     if (!ptrs[dev]) {
         uint32_t *p = nullptr;
         if (cudaMalloc((void **)&p, sizeof(uint32_t)) != cudaSuccess) return nullptr;
@@ -47,17 +51,35 @@ void compat_fail(const char *fn, const char *msg) {
     if (!(na && na[0] == '1')) abort();
 }
 
+// The dynamic shared-memory limit of a kernel is a per-device attribute: set it once per
+// (kernel, device, size) and remember that, so a process driving several GPUs (or
+// several host threads) launches correctly on each.
+int ensure_smem_attr(const void *kernel, size_t bytes, char *err, size_t errlen) {
+    struct Done { const void *k; int dev; size_t bytes; };
+    static std::vector<Done> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return check_cuda(e, "cudaGetDevice", err, errlen);
+    std::lock_guard<std::mutex> lock(g_rt_mu);
+    for (const Done &d : done)
+        if (d.k == kernel && d.dev == dev && d.bytes >= bytes) return 0;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute", err, errlen);
+    done.push_back({kernel, dev, bytes});
+    return 0;
+}
+
 int num_sms() {
-    static int cached = 0;
-    if (!cached) {
-        int dev = 0, n = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess &&
-            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
-            cached = n;
-        else
+    static int cached[64] = {};
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    std::lock_guard<std::mutex> lock(g_rt_mu);
+    if (!cached[dev]) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
             return 148;
+        cached[dev] = n;
     }
-    return cached;
+    return cached[dev];
 }
 
 // ---- synthetic inputs: same formula as oracle/vx27_oracle.c (splitmix64 + Box-Muller)
