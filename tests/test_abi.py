@@ -125,3 +125,36 @@ def test_ddmath_host_matches_c_library_nearly_always():
             _, x, mine, libc = line.split()
             exact = Decimal(float.fromhex(x)).ln()
             assert float(Fraction(exact)).hex() == float.fromhex(mine).hex()
+
+
+def test_wrappers_reject_wrong_dtypes_and_sizes_before_any_launch():
+    """The Python wrappers check dtype, size and device of every tensor before its pointer
+    reaches a kernel (which would otherwise read or write past it). CPU tensors here: the
+    checks run first or _t() rejects the host tensor, so nothing is launched."""
+    import pytest
+    import torch
+    from vx27_b200 import ops
+    B, nq, nkv, hd, cap = 2, 24, 4, 256, 64
+    q = torch.zeros(B, nq, hd)
+    kc = torch.zeros(B, nkv, cap, hd, dtype=torch.bfloat16)
+    pos = torch.zeros(B, dtype=torch.int32)
+    out = torch.zeros(B, nq, hd)
+    ws = torch.zeros(16)
+    with pytest.raises(ops.Vx27Error, match="k_cache: dtype"):
+        ops.gqa_decode_batch(q, None, kc.float(), kc, pos, out, ws)
+    with pytest.raises(ops.Vx27Error, match="pos: dtype"):
+        ops.gqa_decode_batch(q, None, kc, kc, pos.long(), out, ws)
+    with pytest.raises(ops.Vx27Error, match="out: .* elements"):
+        ops.gqa_decode_batch(q, None, kc, kc, pos, out[:1], ws)
+    nqk = nv = 16
+    C_ = (2 * nqk + nv) * 128
+    S = torch.zeros(B, nv, 128, 128)
+    ring = torch.zeros(B, 4, C_)
+    qkv = torch.zeros(B, C_, dtype=torch.float16)  # neither fp32 nor bf16
+    a = torch.zeros(B, nv)
+    with pytest.raises(ops.Vx27Error, match="qkv: dtype"):
+        ops.deltanet_decode_batch(S, ring, qkv, a, a, torch.zeros(nv), torch.zeros(nv),
+                                  torch.zeros(C_, 4), pos, torch.zeros(B, nv, 128), nqk, nv)
+    with pytest.raises(ops.Vx27Error, match="expected a contiguous CUDA tensor"):
+        ops.deltanet_decode_batch(S, ring, qkv.float(), a, a, torch.zeros(nv), torch.zeros(nv),
+                                  torch.zeros(C_, 4), pos, torch.zeros(B, nv, 128), nqk, nv)

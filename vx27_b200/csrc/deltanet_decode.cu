@@ -92,14 +92,14 @@ __device__ __forceinline__ void gates_device(double a, double A_log, double b, d
     *g_log = -exp(A_log) * sp;
 }
 
-template <bool ACT_BF16, bool OUT_BF16, bool GATES_F64, bool GATED>
+template <bool ACT_BF16, bool OUT_BF16, bool GATES_F64, bool GATED, bool PRENORM>
 __global__ void __launch_bounds__(NTHREADS, 1)
 dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restrict__ qkv,
             const void *__restrict__ ga, const void *__restrict__ gb,
             const float *__restrict__ A_log, const float *__restrict__ dt_bias,
             const float *__restrict__ conv_w, const int *__restrict__ pos,
             const void *__restrict__ z, const float *__restrict__ norm_w, void *__restrict__ o,
-            int B, int nqk, int nv, int prefetch_state, int prenorm, uint32_t *status) {
+            int B, int nqk, int nv, int prefetch_state, uint32_t *status) {
     extern __shared__ uint8_t dn_smem_raw[];
     DnSmem &sm = *reinterpret_cast<DnSmem *>(((uintptr_t)dn_smem_raw + 127) & ~(uintptr_t)127);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -213,7 +213,7 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
                     if (part == 2 || qk_owner) rb[(size_t)slw * C + c] = x;
                 }
             }
-            if (prenorm) {
+            if constexpr (PRENORM) {
                 // production q/k pre-normalisation (src/vx27_qfwd.c:31-39, 118-130):
                 // RMSNorm y*s*(1+w) with the fp64 sum of squares, then l2norm, q/sqrt(hd)
 #pragma unroll
@@ -365,18 +365,18 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
     __syncthreads();
 }
 
-template <bool A, bool O, bool G, bool Z>
+template <bool A, bool O, bool G, bool Z, bool PN>
 int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, const void *a,
            const void *b, const float *A_log, const float *dt_bias, const float *conv_w,
            const int *pos, const void *z, const float *norm_w, void *o, int B, int nqk, int nv,
-           int prefetch_state, int prenorm, char *err, size_t errlen) {
+           int prefetch_state, char *err, size_t errlen) {
     const size_t smem = sizeof(DnSmem) + 128;
-    if (ensure_smem_attr((const void *)dn_decode_k<A, O, G, Z>, smem, err, errlen)) return -1;
+    if (ensure_smem_attr((const void *)dn_decode_k<A, O, G, Z, PN>, smem, err, errlen)) return -1;
     // programmatic dependent launch: the CTAs may start (and, with prefetch_state, begin
     // streaming state) while the previous kernel on the stream drains
-    VX_CK(launch_pdl(dn_decode_k<A, O, G, Z>, dim3(grid), dim3(NTHREADS), smem, st, S, ring, qkv,
+    VX_CK(launch_pdl(dn_decode_k<A, O, G, Z, PN>, dim3(grid), dim3(NTHREADS), smem, st, S, ring, qkv,
                      a, b, A_log, dt_bias, conv_w, pos, z, norm_w, o, B, nqk, nv, prefetch_state,
-                     prenorm, dev_status()));
+                     dev_status()));
     return 0;
 }
 
@@ -410,27 +410,35 @@ static int decode_batch_impl(const char *fn, float *S, float *conv_ring, const v
         return fail(err, errlen, "%s: VX27_F_QK_PRENORM needs the gated entry point (norm_w)", fn);
     const int key = (flags & VX27_F_ACT_BF16 ? 1 : 0) | (flags & VX27_F_OUT_BF16 ? 2 : 0) |
                     (g64 ? 4 : 0) | (gated ? 8 : 0);
-#define VX_L(K, A_, O_, G_, Z_)                                                              \
+#define VX_L(K, A_, O_, G_, Z_, P_)                                                          \
     case K:                                                                                  \
-        return launch<A_, O_, G_, Z_>(grid, st, S, conv_ring, qkv, a, b, A_log, dt_bias,     \
-                                      conv_w, pos, z, norm_w, o, B, nqk, nv, pf, pn, err, errlen);
-    switch (key) {
-        VX_L(0, false, false, false, false)
-        VX_L(1, true, false, false, false)
-        VX_L(2, false, true, false, false)
-        VX_L(3, true, true, false, false)
-        VX_L(4, false, false, true, false)
-        VX_L(5, true, false, true, false)
-        VX_L(6, false, true, true, false)
-        VX_L(7, true, true, true, false)
-        VX_L(8, false, false, false, true)
-        VX_L(9, true, false, false, true)
-        VX_L(10, false, true, false, true)
-        VX_L(11, true, true, false, true)
-        VX_L(12, false, false, true, true)
-        VX_L(13, true, false, true, true)
-        VX_L(14, false, true, true, true)
-        VX_L(15, true, true, true, true)
+        return launch<A_, O_, G_, Z_, P_>(grid, st, S, conv_ring, qkv, a, b, A_log, dt_bias, \
+                                          conv_w, pos, z, norm_w, o, B, nqk, nv, pf, err, errlen);
+    switch (key | (pn ? 16 : 0)) {
+        VX_L(0, false, false, false, false, false)
+        VX_L(1, true, false, false, false, false)
+        VX_L(2, false, true, false, false, false)
+        VX_L(3, true, true, false, false, false)
+        VX_L(4, false, false, true, false, false)
+        VX_L(5, true, false, true, false, false)
+        VX_L(6, false, true, true, false, false)
+        VX_L(7, true, true, true, false, false)
+        VX_L(8, false, false, false, true, false)
+        VX_L(9, true, false, false, true, false)
+        VX_L(10, false, true, false, true, false)
+        VX_L(11, true, true, false, true, false)
+        VX_L(12, false, false, true, true, false)
+        VX_L(13, true, false, true, true, false)
+        VX_L(14, false, true, true, true, false)
+        VX_L(15, true, true, true, true, false)
+        VX_L(24, false, false, false, true, true)
+        VX_L(25, true, false, false, true, true)
+        VX_L(26, false, true, false, true, true)
+        VX_L(27, true, true, false, true, true)
+        VX_L(28, false, false, true, true, true)
+        VX_L(29, true, false, true, true, true)
+        VX_L(30, false, true, true, true, true)
+        VX_L(31, true, true, true, true, true)
     }
 #undef VX_L
     return fail(err, errlen, "%s: bad flags", fn);

@@ -130,7 +130,45 @@ def _t(t) -> C.c_void_p:
         return C.c_void_p(0)
     if not t.is_cuda or not t.is_contiguous():
         raise Vx27Error("expected a contiguous CUDA tensor")
+    if t.device.index != torch.cuda.current_device():
+        raise Vx27Error(f"tensor on {t.device}, but the current device is "
+                        f"cuda:{torch.cuda.current_device()}")
     return C.c_void_p(t.data_ptr())
+
+
+def _need(t, name: str, numel: int, dtypes, optional: bool = False) -> None:
+    """Checks a tensor argument before its pointer reaches a kernel, which trusts sizes:
+    a dtype from dtypes and at least numel elements (None allowed when optional)."""
+    if t is None:
+        if optional:
+            return
+        raise Vx27Error(f"{name}: required")
+    if t.dtype not in dtypes:
+        raise Vx27Error(f"{name}: dtype {t.dtype} not one of {', '.join(map(str, dtypes))}")
+    if t.numel() < numel:
+        raise Vx27Error(f"{name}: {t.numel()} elements, the call needs {numel}")
+
+
+def _dt():
+    import torch
+    return torch.float32, torch.bfloat16, torch.int32, torch.float64, torch.uint8
+
+
+def _check_deltanet(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, B, nqk, nv, hd,
+                    gates_f64, T=None):
+    f32, bf16, i32, f64, _ = _dt()
+    C_ = (2 * nqk + nv) * hd
+    n = T if T is not None else B                       # tokens (rows of the activations)
+    _need(S, "S", (1 if T is not None else B) * nv * hd * hd, (f32,))
+    _need(conv_ring, "conv_ring", (1 if T is not None else B) * 4 * C_, (f32,))
+    _need(qkv, "qkv", n * C_, (f32, bf16))
+    for t, nm in ((a, "a"), (b, "b")):
+        _need(t, nm, n * nv, (f64,) if gates_f64 else (qkv.dtype,))
+    _need(A_log, "A_log", nv, (f32,), optional=gates_f64)
+    _need(dt_bias, "dt_bias", nv, (f32,), optional=gates_f64)
+    _need(conv_w, "conv_w", C_ * 4, (f32,))
+    _need(pos, "pos", n, (i32,))
+    _need(o, "o", n * nv * hd, (f32, bf16))
 
 
 def _stream(stream) -> C.c_void_p:
@@ -153,6 +191,8 @@ def deltanet_decode_batch(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, 
     (VX27_F_PREFETCH_STATE) - only when that kernel does not write S."""
     B = S.shape[0]
     hd = S.shape[-1]
+    _check_deltanet(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, B, nqk, nv, hd,
+                    gates_f64)
     flags = (F_ACT_BF16 if _is_bf16(qkv) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0) | \
         (F_GATES_F64 if gates_f64 else 0) | (F_PREFETCH_STATE if prefetch_state else 0)
     e = errbuf()
@@ -168,6 +208,11 @@ def deltanet_decode_tokens(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos,
     conv_ring [4][C], qkv [T][C], a, b [T][nv], pos [T], o [T][nv][128]; optional
     S_ckpt [T][nv][128][128] and conv_ckpt [T][C][3] snapshots."""
     T = qkv.shape[0]
+    _check_deltanet(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, 1, nqk, nv, 128,
+                    False, T=T)
+    f32 = _dt()[0]
+    _need(S_ckpt, "S_ckpt", T * nv * 128 * 128, (f32,), optional=True)
+    _need(conv_ckpt, "conv_ckpt", T * (2 * nqk + nv) * 128 * 3, (f32,), optional=True)
     flags = (F_ACT_BF16 if _is_bf16(qkv) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0)
     e = errbuf()
     rc = load().vx27_deltanet_decode_tokens(_t(S), _t(conv_ring), _t(qkv), _t(a), _t(b),
@@ -189,8 +234,10 @@ def deltanet_decode_batch_gated(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w,
     flags = (F_ACT_BF16 if _is_bf16(qkv) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0) | \
         (F_GATES_F64 if gates_f64 else 0) | (F_QK_PRENORM if qk_prenorm else 0) | \
         (F_PREFETCH_STATE if prefetch_state else 0)
-    if _is_bf16(qkv) != _is_bf16(z):
-        raise Vx27Error("z must have the activation dtype of qkv")
+    _check_deltanet(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, B, nqk, nv, hd,
+                    gates_f64)
+    _need(z, "z", B * nv * hd, (qkv.dtype,))
+    _need(norm_w, "norm_w", hd, (_dt()[0],))
     e = errbuf()
     rc = load().vx27_deltanet_decode_batch_gated(_t(S), _t(conv_ring), _t(qkv), _t(a), _t(b),
                                                  _t(A_log), _t(dt_bias), _t(conv_w), _t(pos),
@@ -206,6 +253,16 @@ def deltanet_prefill_chunked(q, k, v, a, b, A_log, dt_bias, S, o, workspace=None
     import torch
     T, nqk, hd = q.shape
     nv = v.shape[1]
+    f32, bf16, _, f64, _ = _dt()
+    _need(q, "q", T * nqk * hd, (f32, bf16))
+    _need(k, "k", T * nqk * hd, (q.dtype,))
+    _need(v, "v", T * nv * hd, (q.dtype,))
+    for t, nm in ((a, "a"), (b, "b")):  # the library requires bf16 (or f64 gates) itself
+        _need(t, nm, T * nv, (f64,) if gates_f64 else (f32, bf16))
+    _need(A_log, "A_log", nv, (f32,), optional=gates_f64)
+    _need(dt_bias, "dt_bias", nv, (f32,), optional=gates_f64)
+    _need(S, "S", nv * hd * hd, (f32,))
+    _need(o, "o", T * nv * hd, (f32, bf16))
     need = load().vx27_deltanet_prefill_workspace_size(T, nqk, nv, hd)
     if workspace is None:
         workspace = torch.empty(need // 4 + 1, dtype=torch.float32, device=q.device)
@@ -235,6 +292,17 @@ def gqa_append(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, pos, k_cache, v_cache
     B, nq, hd = q_in.shape
     nkv = k_in.shape[1]
     cap = k_cache.shape[2] if k_cache is not None else 0
+    f32, bf16, i32, _, _ = _dt()
+    _need(q_in, "q_in", B * nq * hd, (f32, bf16))
+    _need(k_in, "k_in", B * nkv * hd, (q_in.dtype,))
+    _need(v_in, "v_in", B * nkv * hd, (q_in.dtype,))
+    _need(q_norm_w, "q_norm_w", hd, (f32,))
+    _need(k_norm_w, "k_norm_w", hd, (f32,))
+    _need(rope, "rope", 1, (f32,))
+    _need(pos, "pos", B, (i32,))
+    _need(k_cache, "k_cache", B * nkv * cap * hd, (bf16,), optional=True)
+    _need(v_cache, "v_cache", B * nkv * cap * hd, (bf16,), optional=True)
+    _need(q_out, "q_out", B * nq * hd, (f32,))
     flags = (F_ACT_BF16 if _is_bf16(q_in) else 0) | (F_NORM_1P if norm_one_plus else 0)
     e = errbuf()
     rc = load().vx27_gqa_append(_t(q_in), _t(k_in), _t(v_in), _t(q_norm_w), _t(k_norm_w),
@@ -253,6 +321,13 @@ def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: i
                      stream=None) -> None:
     B, nq, hd = q.shape
     nkv, cap = k_cache.shape[1], k_cache.shape[2]
+    f32, bf16, i32, _, _ = _dt()
+    _need(q, "q", B * nq * hd, (f32,))
+    _need(gate, "gate", B * nq * hd, (f32, bf16), optional=True)
+    _need(k_cache, "k_cache", B * nkv * cap * hd, (bf16,))
+    _need(v_cache, "v_cache", B * nkv * cap * hd, (bf16,))
+    _need(pos, "pos", B, (i32,))
+    _need(out, "out", B * nq * hd, (f32, bf16))
     flags = (F_ACT_BF16 if gate is not None and _is_bf16(gate) else 0) | \
         (F_OUT_BF16 if _is_bf16(out) else 0)
     e = errbuf()
@@ -273,6 +348,11 @@ def gqa_partial(q, k_cache, v_cache, p_begin: int, p_end: int, part, workspace=N
     workspace is given)."""
     B, nq, hd = q.shape
     nkv, cap = k_cache.shape[1], k_cache.shape[2]
+    f32, bf16 = _dt()[:2]
+    _need(q, "q", B * nq * hd, (f32,))
+    _need(k_cache, "k_cache", B * nkv * cap * hd, (bf16,))
+    _need(v_cache, "v_cache", B * nkv * cap * hd, (bf16,))
+    _need(part, "part", B * nq * (hd + 2), (f32,))
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     e = errbuf()
     rc = load().vx27_gqa_partial(_t(q), _t(k_cache), _t(v_cache), cap, p_begin, p_end, _t(part),
@@ -284,6 +364,11 @@ def gqa_combine(parts, n_parts: int, gate, out, part_stride: int = 0, stream=Non
     """Merges n_parts partial records placed part_stride floats apart (0: contiguous);
     gate None: no output gate."""
     B, nq, hd = out.shape
+    f32, bf16 = _dt()[:2]
+    rec = B * nq * (hd + 2)
+    _need(parts, "parts", (n_parts - 1) * (part_stride or rec) + rec, (f32,))
+    _need(gate, "gate", B * nq * hd, (f32, bf16), optional=True)
+    _need(out, "out", B * nq * hd, (f32, bf16))
     flags = (F_ACT_BF16 if gate is not None and _is_bf16(gate) else 0) | \
         (F_OUT_BF16 if _is_bf16(out) else 0)
     e = errbuf()
@@ -311,6 +396,8 @@ def pmat_batch(W, dtype: int, xb, yb, rows: int, cols: int, stream=None) -> None
         raise Vx27Error("pmat_batch: xb and yb must be fp32")
     if W.numel() * W.element_size() < rows * pmat_row_bytes(dtype, cols):
         raise Vx27Error("pmat_batch: W holds fewer than rows packed rows")
+    _need(xb, "xb", B * cols, (torch.float32,))
+    _need(yb, "yb", B * rows, (torch.float32,))
     e = errbuf()
     rc = load().vx27_pmat_batch_dev(_t(W), dtype, _t(xb), _t(yb), rows, cols, B, _stream(stream),
                                     e, 512)
@@ -325,6 +412,17 @@ def gqa_prefill(q_in, k_in, v_in, gate, q_norm_w, k_norm_w, rope, k_cache, v_cac
     T, nq, hd = q_in.shape
     nkv = k_in.shape[1]
     cap = k_cache.shape[1]
+    f32, bf16 = _dt()[:2]
+    _need(q_in, "q_in", T * nq * hd, (f32, bf16))
+    for t, nm, n in ((k_in, "k_in", T * nkv * hd), (v_in, "v_in", T * nkv * hd),
+                     (gate, "gate", T * nq * hd)):
+        _need(t, nm, n, (q_in.dtype,))
+    _need(q_norm_w, "q_norm_w", hd, (f32,))
+    _need(k_norm_w, "k_norm_w", hd, (f32,))
+    _need(rope, "rope", 1, (f32,))
+    _need(k_cache, "k_cache", nkv * cap * hd, (bf16,))
+    _need(v_cache, "v_cache", nkv * cap * hd, (bf16,))
+    _need(out, "out", T * nq * hd, (f32, bf16))
     need = load().vx27_gqa_prefill_workspace_size(T, nq, hd)
     if workspace is None:
         workspace = torch.empty(need // 2 + 1, dtype=torch.int16, device=q_in.device)
