@@ -34,11 +34,23 @@ size_t vx27_pmat_row_bytes(uint32_t dtype, int cols);
 
 /*
  * yb[b*rows + r] = sum_c W[r][c] * xb[b*cols + c] for r < rows, b < B (device pointers).
- * cols: a multiple of 256 for Q8_K, of 128 for BP3_128. W 4-byte aligned; xb 16-byte
- * aligned for Q8_K and BP3_128. Asynchronous on stream.
+ * cols: a multiple of 256 for Q8_K, of 128 for BP3_128. W 4-byte aligned (BP3_128:
+ * 16-byte); xb 16-byte aligned for Q8_K and BP3_128. Asynchronous on stream.
  */
 int vx27_pmat_batch_dev(const void *W, uint32_t dtype, const float *xb, float *yb, int rows,
                         int cols, int B, void *stream, char *err, size_t errlen);
+
+#define VX27_PMAT_MAX_GROUPS 4
+
+/*
+ * n (1..VX27_PMAT_MAX_GROUPS) projections of the same inputs in one launch, e.g. a
+ * DeltaNet layer's in_proj_qkv / z / a / b: for each i < n, yb[i][b*rows[i] + r] =
+ * W[i][r] . xb[b] with the same dtype and cols (host arrays of device pointers; each
+ * output as vx27_pmat_batch_dev writes it, bit-identical to the reference's vx27_pmat).
+ */
+int vx27_pmat_multi_dev(int n, const void *const *W, uint32_t dtype, const float *xb,
+                        float *const *yb, const int *rows, int cols, int B, void *stream,
+                        char *err, size_t errlen);
 
 #ifdef __cplusplus
 }

@@ -59,3 +59,30 @@ def test_bp3_scale_conversion(refpmat):
     assert np.array_equal(f[m], ref[m])
     sub = (~normal) & ((h[::97] & 0x3FF) != 0)
     assert np.all(np.abs(f[sub]) >= 2.0 ** -14)  # mapped with exponent 1, not scaled down
+
+
+@pytest.mark.parametrize("B", [1, 4])
+def test_bp3_special_scales_and_inputs(refpmat, B):
+    # zero, negative, largest, subnormal, infinite and NaN group scales; inputs with zeros
+    # of both signs and subnormals: bit-identical (a NaN only has to be a NaN)
+    rows, cols = 40, 1024
+    g = O.packed_weights(O.PMAT_BP3, rows, cols, 55).reshape(-1, 52)
+    rng = np.random.default_rng(56)
+    specials = np.array([0x0000, 0x8000, 0xA51F, 0x7BFF, 0xFBFF, 0x8001, 0x83FF, 0x0001,
+                         0x7C00, 0xFC00, 0x7E00], np.uint16)
+    pick = rng.random(len(g)) < 0.15
+    g[pick, 48:50] = rng.choice(specials, int(pick.sum())).view(np.uint8).reshape(-1, 2)
+    W = g.reshape(-1)
+    x = rng.standard_normal(B * cols).astype(np.float32)
+    x[rng.random(x.size) < 0.05] = -0.0
+    x[rng.random(x.size) < 0.05] = np.float32(-1e-40)
+    y_orc = O.pmat_batch(W, O.PMAT_BP3, x, rows, cols, B)
+    y_ref = np.empty(B * rows, np.float32)
+    if B == 1:
+        refpmat.vx27_pmat(None, O.P(W), O.PMAT_BP3, O.P(x), O.P(y_ref), rows, cols)
+    else:
+        refpmat.vx27_pmat_batch(None, O.P(W), O.PMAT_BP3, O.P(x), O.P(y_ref), rows, cols, B)
+    on, rn = np.isnan(y_orc), np.isnan(y_ref)
+    assert np.array_equal(on, rn)
+    assert np.array_equal(y_orc[~on].view(np.uint32), y_ref[~rn].view(np.uint32))
+    assert np.isfinite(y_ref).sum() > rows * B // 3

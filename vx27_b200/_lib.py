@@ -73,6 +73,7 @@ PROTOTYPES: dict[str, tuple] = {
     # vx27_pmat.h
     "vx27_pmat_row_bytes": (_sz, [C.c_uint32, _i]),
     "vx27_pmat_batch_dev": (_i, [_p, C.c_uint32, _p, _p, _i, _i, _i, _p, _cp, _sz]),
+    "vx27_pmat_multi_dev": (_i, [_i, _p, C.c_uint32, _p, _p, _p, _i, _i, _p, _cp, _sz]),
     # vx27_kv.h
     "vx27_kv_elems": (_u64, [_i]),
     "vx27_kv_gb": (_d, [_i, _d]),

@@ -8,14 +8,18 @@
 //            multiply-add; the lanes summed left to right at the end
 //            (src/vx27_pmat.c:28-63, 133-177). Eight threads per row, thread = lane, so a
 //            row's lanes run in parallel; x is staged in shared memory transposed by lane
-//            so each thread reads its 16 values of a group as four float4.
+//            so each thread reads its 16 values of a group as four float4. q*scale costs
+//            two instructions per weight (bp3_codes).
 //   Q8_K    (dtype 2; blocks of 256: float d, int8 qs[256], int16 bsums[16], 292 B): per
 //            block eight FMA lanes summed left to right, times d in double, accumulated
 //            in double (:10-24, :100-105, :187-195). One thread per row.
 //   F32     (dtype 0): double products accumulated in column order (:96-99, :196-204).
 //            One thread per row.
 // Tokens run in passes of up to 8 (blockIdx.y), each thread keeping its accumulators
-// for all of them, so a weight byte is read from HBM once per 8 tokens.
+// for all of them, so a weight byte is read from HBM once per 8 tokens. One launch serves
+// up to VX27_PMAT_MAX_GROUPS projections of the same x (a layer's input projections):
+// their row blocks share the grid, so a small projection (48 rows) runs beside the large
+// ones instead of as a launch of three CTAs.
 #include "common.cuh"
 #include "../../include/vx27_pmat.h"
 
@@ -24,10 +28,28 @@ namespace {
 
 constexpr int BP3_THREADS = 128;
 constexpr int BP3_ROWS = BP3_THREADS / 8;  // 8 lanes per row; 16 rows (16 * 52 B = 832 B)
-constexpr int BP3_KC = 8;                  // groups of 128 columns staged per chunk
 constexpr int XS_LANE = 20;                // floats per lane slot: 16 used, 4 pad (banks)
 constexpr int ROW_THREADS = 128;           // Q8_K / F32: one thread per row
 constexpr unsigned FULL = 0xffffffffu;
+constexpr int MAXG = VX27_PMAT_MAX_GROUPS;
+
+// The projections of one launch (same x, dtype and cols): CTAs blk0[i] .. blk0[i+1]-1
+// along x serve group i.
+struct PmatGroups {
+    const uint8_t *W[MAXG];
+    float *y[MAXG];
+    int rows[MAXG];
+    int blk0[MAXG + 1];
+    int n;
+};
+
+__device__ __forceinline__ int pm_group(const PmatGroups &g, int bx) {
+    int i = 0;
+#pragma unroll
+    for (int j = 1; j < MAXG; j++)
+        if (j < g.n && bx >= g.blk0[j]) i = j;
+    return i;
+}
 
 // The group scale's fp16 -> fp32 exactly as the reference forms it (src/vx27_pmat.c:38-41):
 // exponent rebased by 112; an fp16 subnormal keeps exponent field 1 instead of scaling.
@@ -40,11 +62,84 @@ __device__ __forceinline__ float bp3_scale(uint16_t h) {
     return __uint_as_float(bits);
 }
 
-// Shared memory of a BP3 CTA: its block of packed rows (one bulk copy), then the staged
-// x chunk: element e of group kk of token b at xs[((b * BP3_KC + kk) * 8 + (e & 7)) *
-// XS_LANE + (e >> 3)].
+// Four codes of a lane, bytes c' = q + 4 (0..7) of v4, to q * scale. Placed in the
+// mantissa of 2.0 a code gives a = 2 + c'/64 exactly. With EXACT_FMA (a finite positive
+// scale, s1 = 64 sc, s2 = -132 sc, both exact) one fused multiply-add gives
+// a * 64 sc - 132 sc = q * sc: the exact value has at most 14 significant bits, so its one
+// rounding is exact and the result equals the reference's rounded product, signed zeros
+// included (+0 for q = 0, as 0.0f * sc is for sc > 0). Otherwise (zero, negative, infinite
+// or NaN scale; s1 = sc) q is formed exactly first and multiplied as the reference does.
+template <bool EXACT_FMA>
+__device__ __forceinline__ void bp3_codes(uint32_t v4, float s1, float s2, float (&qv)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float a = __uint_as_float(__byte_perm(v4, 0x40000000u, 0x7044u | (j << 8)));
+        if (EXACT_FMA) qv[j] = __fmaf_rn(a, s1, s2);
+        else qv[j] = __fmul_rn(__fmaf_rn(a, 64.f, -132.f), s1);
+    }
+}
+
+// Groups of 128 columns of x staged per chunk (two chunk buffers of 5-10 KB).
+__host__ __device__ constexpr int bp3_kc(int tb) { return tb == 1 ? 8 : 16 / tb; }
+
+// One 128-column group of a row for this lane: its 16 weights against TB tokens' x.
+template <int TB, int KC, bool EXACT_FMA>
+__device__ __forceinline__ void bp3_group(const uint32_t *gw, int l, float s1, float s2,
+                                          const float *xk, float (&acc)[TB]) {
+    uint32_t p[12];
+#pragma unroll
+    for (int i = 0; i < 12; i++) p[i] = gw[i];
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+        // this lane's columns of word w: 32w + 8j + l, j = 0..3, one code per byte,
+        // bit 2 flipped so that code ^ 4 = q + 4 in 0..7
+        const uint32_t v4 = (((p[w] >> l) & 0x01010101u) |
+                             (((p[4 + w] >> l) & 0x01010101u) << 1) |
+                             (((p[8 + w] >> l) & 0x01010101u) << 2)) ^ 0x04040404u;
+        float qv[4];
+        bp3_codes<EXACT_FMA>(v4, s1, s2, qv);
+#pragma unroll
+        for (int b = 0; b < TB; b++) {
+            const float4 xv = *reinterpret_cast<const float4 *>(
+                xk + (size_t)b * KC * 8 * XS_LANE + 4 * w);
+            acc[b] = fmaf(qv[0], xv.x, acc[b]);
+            acc[b] = fmaf(qv[1], xv.y, acc[b]);
+            acc[b] = fmaf(qv[2], xv.z, acc[b]);
+            acc[b] = fmaf(qv[3], xv.w, acc[b]);
+        }
+    }
+}
+
+// Shared memory of a BP3 CTA: its block of packed rows (one bulk copy), then two x chunk
+// buffers: element e of group kk of token b at xs[((b * KC + kk) * 8 + (e & 7)) * XS_LANE +
+// (e >> 3)].
 __host__ __device__ constexpr size_t bp3_xs_bytes(int tb) {
-    return (size_t)tb * BP3_KC * 8 * XS_LANE * 4;
+    return (size_t)2 * tb * bp3_kc(tb) * 8 * XS_LANE * 4;
+}
+
+__device__ __forceinline__ void cp_async_4(float *dst, const float *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Groups k0 .. k0+kn-1 of the nb tokens' x into a chunk buffer, transposed by lane, as
+// asynchronous 4-byte copies: thread t copies element t of each group (coalesced reads;
+// the 32 stores of a warp hit 32 different banks).
+template <int KC>
+__device__ __forceinline__ void bp3_stage_x(float *xsb, const float *xb, int b0, int nb,
+                                            int cols, int k0, int kn, int tid) {
+    float *d = xsb + (tid & 7) * XS_LANE + (tid >> 3);
+    for (int b = 0; b < nb; b++)
+        for (int kk = 0; kk < kn; kk++)
+            cp_async_4(d + (b * KC + kk) * 8 * XS_LANE,
+                       xb + (size_t)(b0 + b) * cols + (size_t)(k0 + kk) * 128 + tid);
 }
 __host__ __device__ inline size_t bp3_w_bytes(int cols) {
     return ((size_t)BP3_ROWS * (size_t)(cols >> 7) * 52 + 15) & ~(size_t)15;
@@ -52,17 +147,22 @@ __host__ __device__ inline size_t bp3_w_bytes(int cols) {
 
 template <int TB>
 __global__ void __launch_bounds__(BP3_THREADS)
-pmat_bp3_k(const uint8_t *__restrict__ W, const float *__restrict__ xb, float *__restrict__ yb,
-           int rows, int cols, int B, uint32_t *status) {
+pmat_bp3_k(const __grid_constant__ PmatGroups g, const float *__restrict__ xb, int cols, int B,
+           uint32_t *status) {
     extern __shared__ __align__(128) uint8_t pm_smem[];
     __shared__ uint64_t wbar;
-    const int tid = threadIdx.x, l = tid & 7, rl = tid >> 3;
-    const int r0 = blockIdx.x * BP3_ROWS, nr = min(BP3_ROWS, rows - r0);
+    const int tid = threadIdx.x, l = tid & 7, rl = tid >> 3, base = (tid & 31) & ~7;
+    const int gi = pm_group(g, blockIdx.x), rows = g.rows[gi];
+    const uint8_t *W = g.W[gi];
+    float *yb = g.y[gi];
+    const int r0 = (blockIdx.x - g.blk0[gi]) * BP3_ROWS, nr = min(BP3_ROWS, rows - r0);
     const int b0 = blockIdx.y * TB, nb = min(TB, B - b0);
     const int ng = cols >> 7;
     const size_t rb = (size_t)ng * 52;
+    constexpr int KC = bp3_kc(TB);
     uint8_t *wsm = pm_smem;
-    float *xs = reinterpret_cast<float *>(pm_smem + bp3_w_bytes(cols));
+    float *xs0 = reinterpret_cast<float *>(pm_smem + bp3_w_bytes(cols));
+    float *xs1 = xs0 + TB * KC * 8 * XS_LANE;
     // the CTA's rows are contiguous in W and start on a 16-byte boundary (BP3_ROWS * 52 is
     // a multiple of 16): one bulk copy of the 16-byte-aligned part, the tail by plain loads
     const size_t blk = (size_t)nr * rb, blk16 = blk & ~(size_t)15;
@@ -79,30 +179,26 @@ pmat_bp3_k(const uint8_t *__restrict__ W, const float *__restrict__ xb, float *_
         for (size_t off = 0; off < blk16; off += 65536)
             bulk_g2s(wsm + off, src + off, (uint32_t)min((size_t)65536, blk16 - off), &wbar);
     }
+    bp3_stage_x<KC>(xs0, xb, b0, nb, cols, 0, min(KC, ng), tid);
+    cp_async_commit();
     for (size_t i = blk16 + tid; i < blk; i += BP3_THREADS) wsm[i] = src[i];
     float acc[TB];
 #pragma unroll
     for (int b = 0; b < TB; b++) acc[b] = 0.f;
     const uint8_t *wr = wsm + (size_t)(rl < nr ? rl : 0) * rb;
     bool ok = true;
-    for (int k0 = 0; k0 < ng; k0 += BP3_KC) {
-        const int kn = min(BP3_KC, ng - k0);
-        __syncthreads();  // the previous chunk has been read
-        for (int idx = tid; idx < TB * kn * 32; idx += BP3_THREADS) {
-            const int b = idx / (kn * 32), rem = idx - b * kn * 32, kk = rem >> 5;
-            const int e4 = (rem & 31) * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (b < nb)
-                v = __ldg(reinterpret_cast<const float4 *>(xb + (size_t)(b0 + b) * cols +
-                                                           (size_t)(k0 + kk) * 128 + e4));
-            float *d = xs + ((size_t)(b * BP3_KC + kk) * 8 + (e4 & 7)) * XS_LANE + (e4 >> 3);
-            d[0] = v.x;
-            d[XS_LANE] = v.y;
-            d[2 * XS_LANE] = v.z;
-            d[3 * XS_LANE] = v.w;
-        }
-        __syncthreads();
-        if (k0 == 0) {  // the weights: every thread waits (bounded), outcome made uniform
+    // x chunk c + 1 is copied in while chunk c is used; slots of tokens past nb are left
+    // as they are (their sums are never stored)
+    for (int k0 = 0, c = 0; k0 < ng; k0 += KC, c++) {
+        const int kn = min(KC, ng - k0);
+        const float *xc = (c & 1) ? xs1 : xs0;
+        if (k0 + KC < ng)
+            bp3_stage_x<KC>((c & 1) ? xs0 : xs1, xb, b0, nb, cols, k0 + KC,
+                            min(KC, ng - k0 - KC), tid);
+        cp_async_commit();
+        cp_async_wait<1>();  // this thread's copies of chunk c have landed
+        if (k0 > 0) __syncthreads();
+        else {  // the weights: every thread waits (bounded), outcome made uniform
             uint32_t done = 0;
             for (uint32_t it = 0; it < (1u << 26) && !done; it++)
                 asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0; selp.u32 %0, 1, 0, p; }"
@@ -111,42 +207,24 @@ pmat_bp3_k(const uint8_t *__restrict__ W, const float *__restrict__ xb, float *_
             if (!ok && tid == 0) dev_flag(status, VX_DEV_TIMEOUT_TMA);
         }
         if (!ok) break;
+        // the chunk's group scales of this row: lane l converts group k0 + l's, the row's
+        // other lanes receive it by shuffle
+        const float sc_l = l < kn ? bp3_scale(*reinterpret_cast<const unsigned short *>(
+                                        wr + (size_t)(k0 + l) * 52 + 48))
+                                  : 0.f;
         for (int kk = 0; kk < kn; kk++) {
+            const float sc = __shfl_sync(FULL, sc_l, base + kk);
             const uint32_t *gw = reinterpret_cast<const uint32_t *>(wr + (size_t)(k0 + kk) * 52);
-            uint32_t p[12];
-#pragma unroll
-            for (int i = 0; i < 12; i++) p[i] = gw[i];
-            const float sc = bp3_scale(*reinterpret_cast<const unsigned short *>(gw + 12));
-            const float *xk = xs + ((size_t)kk * 8 + l) * XS_LANE;
-#pragma unroll
-            for (int w = 0; w < 4; w++) {
-                // this lane's columns of word w: 32w + 8j + l, j = 0..3, one code per byte,
-                // bit 2 flipped so that code ^ 4 = q + 4 in 0..7
-                const uint32_t v4 = (((p[w] >> l) & 0x01010101u) |
-                                     (((p[4 + w] >> l) & 0x01010101u) << 1) |
-                                     (((p[8 + w] >> l) & 0x01010101u) << 2)) ^ 0x04040404u;
-                float qv[4];
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    // 2^23 + (q + 4) minus 2^23 + 4 = q exactly, then q * scale rounded once
-                    const float qf = __fsub_rn(__uint_as_float(0x4B000000u | ((v4 >> (8 * j)) & 7u)),
-                                               8388612.0f);
-                    qv[j] = __fmul_rn(qf, sc);
-                }
-#pragma unroll
-                for (int b = 0; b < TB; b++) {
-                    const float4 xv = *reinterpret_cast<const float4 *>(
-                        xk + (size_t)b * BP3_KC * 8 * XS_LANE + 4 * w);
-                    acc[b] = fmaf(qv[0], xv.x, acc[b]);
-                    acc[b] = fmaf(qv[1], xv.y, acc[b]);
-                    acc[b] = fmaf(qv[2], xv.z, acc[b]);
-                    acc[b] = fmaf(qv[3], xv.w, acc[b]);
-                }
-            }
+            const float *xk = xc + ((size_t)kk * 8 + l) * XS_LANE;
+            if (sc > 0.f && sc <= 3.40282347e38f)
+                bp3_group<TB, KC, true>(gw, l, sc * 64.f, sc * -132.f, xk, acc);
+            else
+                bp3_group<TB, KC, false>(gw, l, sc, 0.f, xk, acc);
         }
+        __syncthreads();  // chunk c's buffer is refilled two chunks on
     }
+    cp_async_wait<0>();
     // lanes 0..7 of the row summed left to right
-    const int base = (tid & 31) & ~7;
 #pragma unroll
     for (int b = 0; b < TB; b++) {
         float t = __shfl_sync(FULL, acc[b], base);
@@ -158,9 +236,11 @@ pmat_bp3_k(const uint8_t *__restrict__ W, const float *__restrict__ xb, float *_
 
 template <int TB>
 __global__ void __launch_bounds__(ROW_THREADS)
-pmat_q8k_k(const uint8_t *__restrict__ W, const float *__restrict__ xb, float *__restrict__ yb,
-           int rows, int cols, int B) {
-    const int r = blockIdx.x * ROW_THREADS + threadIdx.x;
+pmat_q8k_k(const __grid_constant__ PmatGroups g, const float *__restrict__ xb, int cols, int B) {
+    const int gi = pm_group(g, blockIdx.x), rows = g.rows[gi];
+    const uint8_t *W = g.W[gi];
+    float *yb = g.y[gi];
+    const int r = (blockIdx.x - g.blk0[gi]) * ROW_THREADS + threadIdx.x;
     if (r >= rows) return;
     const int b0 = blockIdx.y * TB, nb = min(TB, B - b0);
     const int nblk = cols >> 8;
@@ -216,9 +296,11 @@ pmat_q8k_k(const uint8_t *__restrict__ W, const float *__restrict__ xb, float *_
 
 template <int TB>
 __global__ void __launch_bounds__(ROW_THREADS)
-pmat_f32_k(const float *__restrict__ W, const float *__restrict__ xb, float *__restrict__ yb,
-           int rows, int cols, int B) {
-    const int r = blockIdx.x * ROW_THREADS + threadIdx.x;
+pmat_f32_k(const __grid_constant__ PmatGroups g, const float *__restrict__ xb, int cols, int B) {
+    const int gi = pm_group(g, blockIdx.x), rows = g.rows[gi];
+    const float *W = reinterpret_cast<const float *>(g.W[gi]);
+    float *yb = g.y[gi];
+    const int r = (blockIdx.x - g.blk0[gi]) * ROW_THREADS + threadIdx.x;
     if (r >= rows) return;
     const int b0 = blockIdx.y * TB, nb = min(TB, B - b0);
     const float *row = W + (size_t)r * cols;
@@ -239,25 +321,28 @@ pmat_f32_k(const float *__restrict__ W, const float *__restrict__ xb, float *__r
 }
 
 template <int TB>
-int launch_pmat(const void *W, uint32_t dtype, const float *xb, float *yb, int rows, int cols,
-                int B, cudaStream_t st, char *err, size_t errlen) {
+int launch_pmat(PmatGroups g, uint32_t dtype, const float *xb, int cols, int B,
+                cudaStream_t st, char *err, size_t errlen) {
     const unsigned passes = (unsigned)((B + TB - 1) / TB);
+    const int per = dtype == VX27_PMAT_BP3_128 ? BP3_ROWS : ROW_THREADS;
+    int nblk = 0;
+    for (int i = 0; i < MAXG; i++) {
+        g.blk0[i] = nblk;
+        if (i < g.n) nblk += (g.rows[i] + per - 1) / per;
+    }
+    g.blk0[MAXG] = nblk;
+    const dim3 grid((unsigned)nblk, passes);
     if (dtype == VX27_PMAT_BP3_128) {
-        const dim3 grid((unsigned)((rows + BP3_ROWS - 1) / BP3_ROWS), passes);
         const size_t smem = bp3_w_bytes(cols) + bp3_xs_bytes(TB);
         if (smem > 220 * 1024)
-            return fail(err, errlen, "vx27_pmat_batch_dev: cols=%d too wide for one CTA", cols);
+            return fail(err, errlen, "vx27_pmat: cols=%d too wide for one CTA", cols);
         if (ensure_smem_attr((const void *)pmat_bp3_k<TB>, smem, err, errlen)) return -1;
-        VX_CK(launch_pdl(pmat_bp3_k<TB>, grid, dim3(BP3_THREADS), smem, st,
-                         (const uint8_t *)W, xb, yb, rows, cols, B, dev_status()));
+        VX_CK(launch_pdl(pmat_bp3_k<TB>, grid, dim3(BP3_THREADS), smem, st, g, xb, cols, B,
+                         dev_status()));
     } else if (dtype == VX27_PMAT_Q8_K) {
-        const dim3 grid((unsigned)((rows + ROW_THREADS - 1) / ROW_THREADS), passes);
-        VX_CK(launch_pdl(pmat_q8k_k<TB>, grid, dim3(ROW_THREADS), 0, st,
-                         (const uint8_t *)W, xb, yb, rows, cols, B));
+        VX_CK(launch_pdl(pmat_q8k_k<TB>, grid, dim3(ROW_THREADS), 0, st, g, xb, cols, B));
     } else {
-        const dim3 grid((unsigned)((rows + ROW_THREADS - 1) / ROW_THREADS), passes);
-        VX_CK(launch_pdl(pmat_f32_k<TB>, grid, dim3(ROW_THREADS), 0, st,
-                         (const float *)W, xb, yb, rows, cols, B));
+        VX_CK(launch_pdl(pmat_f32_k<TB>, grid, dim3(ROW_THREADS), 0, st, g, xb, cols, B));
     }
     return 0;
 }
@@ -275,24 +360,46 @@ extern "C" size_t vx27_pmat_row_bytes(uint32_t dtype, int cols) {
     return 0;
 }
 
+extern "C" int vx27_pmat_multi_dev(int n, const void *const *W, uint32_t dtype,
+                                   const float *xb, float *const *yb, const int *rows, int cols,
+                                   int B, void *stream, char *err, size_t errlen) {
+    if (n < 1 || n > MAXG || !W || !yb || !rows)
+        return fail(err, errlen, "vx27_pmat: n=%d projections (1..%d) or null arrays", n, MAXG);
+    if (!xb) return fail(err, errlen, "vx27_pmat: null x");
+    if (cols <= 0 || B <= 0 || (long long)B > 65535ll * 8)
+        return fail(err, errlen, "vx27_pmat: bad shape cols=%d B=%d", cols, B);
+    if (dtype != VX27_PMAT_F32 && dtype != VX27_PMAT_Q8_K && dtype != VX27_PMAT_BP3_128)
+        return fail(err, errlen, "vx27_pmat: dtype %u unsupported (0, 2 or 4)", dtype);
+    if ((dtype == VX27_PMAT_Q8_K && cols % 256) || (dtype == VX27_PMAT_BP3_128 && cols % 128))
+        return fail(err, errlen, "vx27_pmat: cols=%d not a whole number of blocks", cols);
+    if (dtype != VX27_PMAT_F32 && ((uintptr_t)xb & 15))
+        return fail(err, errlen, "vx27_pmat: xb must be 16-byte aligned");
+    PmatGroups g = {};
+    g.n = n;
+    long long blocks = 0;
+    for (int i = 0; i < n; i++) {
+        if (!W[i] || !yb[i] || rows[i] <= 0)
+            return fail(err, errlen, "vx27_pmat: projection %d: null pointer or rows=%d", i,
+                        rows[i]);
+        if ((uintptr_t)W[i] & (dtype == VX27_PMAT_BP3_128 ? 15 : 3))
+            return fail(err, errlen,
+                        "vx27_pmat: projection %d: W must be 4-byte (BP3_128: 16-byte) aligned",
+                        i);
+        blocks += rows[i] / 16 + 1;
+        g.W[i] = (const uint8_t *)W[i];
+        g.y[i] = yb[i];
+        g.rows[i] = rows[i];
+    }
+    if (blocks > 0x7fffffffll) return fail(err, errlen, "vx27_pmat: too many rows");
+    cudaStream_t st = (cudaStream_t)stream;
+    if (B == 1) return launch_pmat<1>(g, dtype, xb, cols, B, st, err, errlen);
+    if (B == 2) return launch_pmat<2>(g, dtype, xb, cols, B, st, err, errlen);
+    if (B <= 4) return launch_pmat<4>(g, dtype, xb, cols, B, st, err, errlen);
+    return launch_pmat<8>(g, dtype, xb, cols, B, st, err, errlen);
+}
+
 extern "C" int vx27_pmat_batch_dev(const void *W, uint32_t dtype, const float *xb, float *yb,
                                    int rows, int cols, int B, void *stream, char *err,
                                    size_t errlen) {
-    if (!W || !xb || !yb) return fail(err, errlen, "vx27_pmat_batch_dev: null pointer argument");
-    if (rows <= 0 || cols <= 0 || B <= 0 || (long long)B > 65535ll * 8)
-        return fail(err, errlen, "vx27_pmat_batch_dev: bad shape rows=%d cols=%d B=%d", rows, cols, B);
-    if (dtype != VX27_PMAT_F32 && dtype != VX27_PMAT_Q8_K && dtype != VX27_PMAT_BP3_128)
-        return fail(err, errlen, "vx27_pmat_batch_dev: dtype %u unsupported (0, 2 or 4)", dtype);
-    if ((dtype == VX27_PMAT_Q8_K && cols % 256) || (dtype == VX27_PMAT_BP3_128 && cols % 128))
-        return fail(err, errlen, "vx27_pmat_batch_dev: cols=%d not a whole number of blocks", cols);
-    if (((uintptr_t)W & (dtype == VX27_PMAT_BP3_128 ? 15 : 3)) ||
-        (dtype != VX27_PMAT_F32 && ((uintptr_t)xb & 15)))
-        return fail(err, errlen,
-                    "vx27_pmat_batch_dev: W must be 4-byte (BP3_128: 16-byte) aligned, xb "
-                    "16-byte aligned");
-    cudaStream_t st = (cudaStream_t)stream;
-    if (B == 1) return launch_pmat<1>(W, dtype, xb, yb, rows, cols, B, st, err, errlen);
-    if (B == 2) return launch_pmat<2>(W, dtype, xb, yb, rows, cols, B, st, err, errlen);
-    if (B <= 4) return launch_pmat<4>(W, dtype, xb, yb, rows, cols, B, st, err, errlen);
-    return launch_pmat<8>(W, dtype, xb, yb, rows, cols, B, st, err, errlen);
+    return vx27_pmat_multi_dev(1, &W, dtype, xb, &yb, &rows, cols, B, stream, err, errlen);
 }

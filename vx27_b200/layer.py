@@ -15,9 +15,11 @@ GQA layer (src/vx27_qfwd.c:156-214):
   softmax(q k^T / 16) v * sigmoid(gate)                                 (K2)
   out = W_o att                                                          (K5)
 
-The input x is the layer's normalised hidden state, fp32 [B, H]. Every tensor lives on the
-device; the only non-library operation is the split of the interleaved q_proj output
-into q and gate, which the reference does with memcpy (src/vx27_qfwd.c:163-166).
+The input x is the layer's normalised hidden state, fp32 [B, H]. The input projections
+of a layer read the same x, so they run as one K5 launch (``vx27_pmat_multi_dev``); each
+output is bit-identical to its own ``vx27_pmat``. Every tensor lives on the device; the
+only non-library operation is the split of the interleaved q_proj output into q and
+gate, which the reference does with memcpy (src/vx27_qfwd.c:163-166).
 """
 from __future__ import annotations
 
@@ -45,6 +47,14 @@ class PackedLinear:
         return out
 
 
+def project(x: torch.Tensor, *lins: PackedLinear, stream=None) -> list[torch.Tensor]:
+    """The projections lins (same dtype and cols) of x [B, cols] in one launch."""
+    outs = [torch.empty(x.shape[0], m.rows, device=x.device) for m in lins]
+    ops.pmat_multi([m.W for m in lins], lins[0].dtype, x, outs, [m.rows for m in lins],
+                   lins[0].cols, stream=stream)
+    return outs
+
+
 @dataclass
 class DeltaNetLayer:
     qkv: PackedLinear
@@ -65,8 +75,7 @@ class DeltaNetLayer:
         """x [B, H] fp32; S [B, nv, hd, hd] and ring [B, 4, C] updated in place; pos [B]
         int32 (the token's position). Returns the layer output [B, H] fp32."""
         B = x.shape[0]
-        qkv, z = self.qkv(x, stream=stream), self.z(x, stream=stream)
-        a, b = self.a(x, stream=stream), self.b(x, stream=stream)
+        qkv, z, a, b = project(x, self.qkv, self.z, self.a, self.b, stream=stream)
         o = torch.empty(B, self.nv, self.hd, device=x.device)
         ops.deltanet_decode_batch_gated(S, ring, qkv, a, b, self.A_log, self.dt_bias,
                                         self.conv_w, pos, z, self.norm_w, o, self.nqk, self.nv,
@@ -94,10 +103,10 @@ class GQALayer:
         """x [B, H] fp32; caches bf16 [B, nkv, cap, hd] (this token's K/V appended at
         pos[b]); workspace: ops.gqa_workspace_bytes(...). Returns [B, H] fp32."""
         B = x.shape[0]
-        qg = self.q(x, stream=stream).view(B, self.nq, 2, self.hd)
+        qg, k_in, v_in = project(x, self.q, self.k, self.v, stream=stream)
+        qg = qg.view(B, self.nq, 2, self.hd)
         q_in, gate = qg[:, :, 0].contiguous(), qg[:, :, 1].contiguous()
-        k_in = self.k(x, stream=stream).view(B, self.nkv, self.hd)
-        v_in = self.v(x, stream=stream).view(B, self.nkv, self.hd)
+        k_in, v_in = k_in.view(B, self.nkv, self.hd), v_in.view(B, self.nkv, self.hd)
         qn = torch.empty(B, self.nq, self.hd, device=x.device)
         ops.gqa_append(q_in, k_in, v_in, self.q_norm_w, self.k_norm_w, self.rope, pos,
                        k_cache, v_cache, qn, eps=self.eps, norm_one_plus=True, stream=stream)

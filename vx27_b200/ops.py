@@ -404,6 +404,32 @@ def pmat_batch(W, dtype: int, xb, yb, rows: int, cols: int, stream=None) -> None
     check(rc, e)
 
 
+PMAT_MAX_GROUPS = 4
+
+
+def pmat_multi(Ws, dtype: int, xb, ys, rows, cols: int, stream=None) -> None:
+    """Several projections of the same xb [B, cols] in one launch (vx27_pmat_multi_dev):
+    ys[i][b, r] = Ws[i][r] . xb[b] for each i, with the same dtype and cols; each output as
+    pmat_batch writes it."""
+    import torch
+    n, B = len(Ws), xb.shape[0]
+    if not 1 <= n <= PMAT_MAX_GROUPS or len(ys) != n or len(rows) != n:
+        raise Vx27Error(f"pmat_multi: 1..{PMAT_MAX_GROUPS} projections with one output and "
+                        f"one row count each")
+    _need(xb, "xb", B * cols, (torch.float32,))
+    for i in range(n):
+        if Ws[i].numel() * Ws[i].element_size() < rows[i] * pmat_row_bytes(dtype, cols):
+            raise Vx27Error(f"pmat_multi: W[{i}] holds fewer than {rows[i]} packed rows")
+        _need(ys[i], f"y[{i}]", B * rows[i], (torch.float32,))
+    Wp = (C.c_void_p * n)(*[_t(w).value for w in Ws])
+    yp = (C.c_void_p * n)(*[_t(y).value for y in ys])
+    rp = (C.c_int * n)(*rows)
+    e = errbuf()
+    rc = load().vx27_pmat_multi_dev(n, Wp, dtype, _t(xb), yp, rp, cols, B, _stream(stream), e,
+                                    512)
+    check(rc, e)
+
+
 def gqa_prefill(q_in, k_in, v_in, gate, q_norm_w, k_norm_w, rope, k_cache, v_cache, out,
                 workspace=None, p0: int = 0, eps: float = 1e-6, norm_one_plus: bool = False,
                 stream=None):
