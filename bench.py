@@ -61,14 +61,24 @@ def tensor_peak() -> tuple[float, str]:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi samples every 200 ms while the timed region runs."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi samples every 200 ms while the timed region runs. Started before the
+    warm-up, with begin() / end() marking the timed region on the host clock, the summary
+    keeps the samples taken inside it (or, for a region shorter than the sampling period,
+    the samples within 0.5 s of it)."""
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.t_begin = self.t_end = None
+
+    def begin(self) -> None:
+        self.t_begin = time.time()
+
+    def end(self) -> None:
+        self.t_end = time.time()
 
     def __enter__(self):
         try:
@@ -91,23 +101,33 @@ class ClockSampler:
                 out = ""
             self.lines = [l for l in out.splitlines() if l.strip()]
 
-    def summary(self) -> dict:
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    def _rows(self) -> list:
+        import datetime
+        rows = []
         for l in getattr(self, "lines", []):
             f = [x.strip() for x in l.split(",")]
             try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
+                t = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((t, float(f[2]), float(f[3]), f[6:10]))
             except (ValueError, IndexError):
                 continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+        return rows
+
+    def summary(self) -> dict:
+        rows, window = self._rows(), "timed region"
+        if self.t_begin is not None and self.t_end is not None:
+            inside = [r for r in rows if self.t_begin <= r[0] <= self.t_end]
+            if not inside:
+                inside = [r for r in rows if self.t_begin - 0.5 <= r[0] <= self.t_end + 0.5]
+                window = "within 0.5 s of the timed region (shorter than the 200 ms period)"
+            rows = inside
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = {n for r in rows for n, v in zip(names, r[3]) if v.lower() == "active"}
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(r[1] for r in rows),
+                "sm_max_mhz": max(r[2] for r in rows), "reasons": sorted(reasons),
+                "samples": len(rows), "window": window}
 
 
 # ---------------------------------------------------------------- our arm
@@ -127,7 +147,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    # warm-up, then the device-resident timed region
+    # warm-up, then the device-resident timed region; the clock sampler starts before the
+    # warm-up so that it is running when the timed region begins
+    clk = ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ
+                       else int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank]))
+    clk.__enter__()
     for _ in range(args.warmup):
         dec.step()
     barrier()
@@ -146,16 +170,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         ev[kind].append(e)
 
     ctx0 = int(dec.pos[0].item())
-    with ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ
-                      else int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local_rank])) as clk:
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        launches = 0
-        for _ in range(args.steps):
-            launches += dec.step(on_layer=on_layer)
-        t1.record(stream)
-        barrier()
+    clk.begin()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    launches = 0
+    for _ in range(args.steps):
+        launches += dec.step(on_layer=on_layer)
+    t1.record(stream)
+    barrier()
+    clk.end()
+    clk.__exit__(None, None, None)
     ms = t0.elapsed_time(t1)
     if world > 1:
         tt = torch.tensor([ms], device="cuda")
