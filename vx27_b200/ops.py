@@ -124,16 +124,28 @@ def vx27_kv_fits(ctx: int, bytes_per_elem: float, budget_gb: float) -> int:
 
 
 # ------------------------------------------------------------- batched tier
-def _t(t) -> C.c_void_p:
-    import torch
+# The wrappers run once per launch in an eager decode loop, so their checks use the
+# cheapest torch queries (an int device index, the raw current stream).
+_cur_dev = None
+
+
+def _device() -> int:
+    global _cur_dev
+    if _cur_dev is None:
+        import torch
+        _cur_dev = torch.cuda.current_device
+    return _cur_dev()
+
+
+def _t(t) -> int | None:
+    """Device address of a contiguous tensor on the current device (None for None)."""
     if t is None:
-        return C.c_void_p(0)
-    if not t.is_cuda or not t.is_contiguous():
+        return None
+    if not (t.is_cuda and t.is_contiguous()):
         raise Vx27Error("expected a contiguous CUDA tensor")
-    if t.device.index != torch.cuda.current_device():
-        raise Vx27Error(f"tensor on {t.device}, but the current device is "
-                        f"cuda:{torch.cuda.current_device()}")
-    return C.c_void_p(t.data_ptr())
+    if t.get_device() != _device():
+        raise Vx27Error(f"tensor on {t.device}, but the current device is cuda:{_device()}")
+    return t.data_ptr()
 
 
 def _need(t, name: str, numel: int, dtypes, optional: bool = False) -> None:
@@ -171,11 +183,12 @@ def _check_deltanet(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, B, 
     _need(o, "o", n * nv * hd, (f32, bf16))
 
 
-def _stream(stream) -> C.c_void_p:
-    import torch
+def _stream(stream) -> int:
+    """cudaStream_t of stream, or of the current stream of the current device."""
     if stream is None:
-        stream = torch.cuda.current_stream()
-    return C.c_void_p(stream.cuda_stream)
+        import torch
+        return torch._C._cuda_getCurrentRawStream(_device())
+    return stream.cuda_stream
 
 
 def _is_bf16(t) -> bool:
@@ -421,8 +434,8 @@ def pmat_multi(Ws, dtype: int, xb, ys, rows, cols: int, stream=None) -> None:
         if Ws[i].numel() * Ws[i].element_size() < rows[i] * pmat_row_bytes(dtype, cols):
             raise Vx27Error(f"pmat_multi: W[{i}] holds fewer than {rows[i]} packed rows")
         _need(ys[i], f"y[{i}]", B * rows[i], (torch.float32,))
-    Wp = (C.c_void_p * n)(*[_t(w).value for w in Ws])
-    yp = (C.c_void_p * n)(*[_t(y).value for y in ys])
+    Wp = (C.c_void_p * n)(*[_t(w) for w in Ws])
+    yp = (C.c_void_p * n)(*[_t(y) for y in ys])
     rp = (C.c_int * n)(*rows)
     e = errbuf()
     rc = load().vx27_pmat_multi_dev(n, Wp, dtype, _t(xb), yp, rp, cols, B, _stream(stream), e,
