@@ -144,11 +144,10 @@ class HybridDecoder:
                                self.qn, eps=c.eps, stream=stream)
                 if on_layer:
                     on_layer("gqa", i, "pre")
-                ops.gqa_decode_batch(self.qn, self.gate[i], self.kc[i], self.vc[i], self.pos,
-                                     self.att_out[i], self.ws, stream=stream)
+                n += 1 + ops.gqa_decode_batch(self.qn, self.gate[i], self.kc[i], self.vc[i],
+                                              self.pos, self.att_out[i], self.ws, stream=stream)
                 if on_layer:
                     on_layer("gqa", i, "post")
-                n += 3  # append, split, combine
         ops.add_int(self.pos, 1, stream=stream)
         return n + 1
 
@@ -207,9 +206,8 @@ class HybridDecoder:
                 ops.gqa_append(self.q_in[i], self.k_in[i], self.v_in[i], self.q_norm_w[i],
                                self.k_norm_w[i], self.rope, self.pos, self.kc[i], self.vc[i],
                                self.qn, eps=c.eps, stream=comp)
-                ops.gqa_decode_batch(self.qn, self.gate[i], self.kc[i], self.vc[i], self.pos,
-                                     self.att_out[i], self.ws, stream=comp)
-                n += 3
+                n += 1 + ops.gqa_decode_batch(self.qn, self.gate[i], self.kc[i], self.vc[i],
+                                              self.pos, self.att_out[i], self.ws, stream=comp)
             done = torch.cuda.Event()
             done.record(comp)
             self._done[L] = done

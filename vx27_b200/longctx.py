@@ -75,9 +75,8 @@ class LongContextGQA:
                 ops.gqa_append(self.q_in[l], self.k_in[l], self.v_in[l], self.q_norm_w[l],
                                self.k_norm_w[l], self.rope, self.pos, self.kc[l], self.vc[l],
                                self.qn[l], stream=stream)
-                ops.gqa_decode_batch(self.qn[l], self.gate[l], self.kc[l], self.vc[l],
-                                     self.pos, self.out[l], self.ws, stream=stream)
-                n += 3
+                n += 1 + ops.gqa_decode_batch(self.qn[l], self.gate[l], self.kc[l], self.vc[l],
+                                              self.pos, self.out[l], self.ws, stream=stream)
             return n
         n += self.local_partials(stream)
         gathered = gather_records(self.parts, self.world)  # [world, layers*rec]
@@ -86,13 +85,14 @@ class LongContextGQA:
     def local_partials(self, stream=None) -> int:
         """KV-sharded step, local half: q for every layer (the new token's K/V land on the
         shard owning position P-1) and this shard's partial record per layer."""
+        n = 0
         for l in range(self.layers):
             ops.gqa_append(self.q_in[l], self.k_in[l], self.v_in[l], self.q_norm_w[l],
                            self.k_norm_w[l], self.rope, self.pos, self.kc[l], self.vc[l],
                            self.qn[l], slot_base=self.begin, stream=stream)
-            ops.gqa_partial(self.qn[l], self.kc[l], self.vc[l], 0, self.cap, self.parts[l],
-                            self.ws, stream=stream)
-        return 2 * self.layers
+            n += 1 + ops.gqa_partial(self.qn[l], self.kc[l], self.vc[l], 0, self.cap,
+                                     self.parts[l], self.ws, stream=stream)
+        return n
 
     def combine(self, gathered, stream=None) -> int:
         """Merges the all-gathered records ([world, layers*rec]) into self.out."""

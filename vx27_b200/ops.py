@@ -331,7 +331,10 @@ def gqa_workspace_bytes(B: int, nq: int, nkv: int, hd: int, max_ctx: int,
 
 
 def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: int = 0,
-                     stream=None) -> None:
+                     stream=None) -> int:
+    """Split-KV decode of one token per sequence (vx27_gqa_decode_batch); returns the
+    kernels it launched: 1 with one split (the split kernel writes the gated output), 2
+    with several (split kernel + combine)."""
     B, nq, hd = q.shape
     nkv, cap = k_cache.shape[1], k_cache.shape[2]
     f32, bf16, i32, _, _ = _dt()
@@ -344,11 +347,15 @@ def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: i
     flags = (F_ACT_BF16 if gate is not None and _is_bf16(gate) else 0) | \
         (F_OUT_BF16 if _is_bf16(out) else 0)
     e = errbuf()
+    ws_bytes = workspace.numel() * workspace.element_size()
     rc = load().vx27_gqa_decode_batch(_t(q), _t(gate), _t(k_cache), _t(v_cache), cap, _t(pos),
-                                      _t(out), _t(workspace),
-                                      workspace.numel() * workspace.element_size(), B, nq, nkv,
-                                      hd, n_splits, flags, _stream(stream), e, 512)
+                                      _t(out), _t(workspace), ws_bytes, B, nq, nkv, hd, n_splits,
+                                      flags, _stream(stream), e, 512)
     check(rc, e)
+    if n_splits <= 0:  # the library's own choice, capped by the workspace
+        rec = B * nq * (hd + 2) * 4
+        n_splits = min(gqa_workspace_bytes(B, nq, nkv, hd, cap) // rec, ws_bytes // rec)
+    return 1 if n_splits == 1 else 2
 
 
 def gqa_partial_workspace_bytes(B: int, nq: int, nkv: int, hd: int, max_range: int) -> int:
@@ -356,9 +363,9 @@ def gqa_partial_workspace_bytes(B: int, nq: int, nkv: int, hd: int, max_range: i
 
 
 def gqa_partial(q, k_cache, v_cache, p_begin: int, p_end: int, part, workspace=None,
-                stream=None) -> None:
+                stream=None) -> int:
     """Partial record over cache slots [p_begin, p_end) (split across CTAs when a
-    workspace is given)."""
+    workspace is given); returns the kernels launched (1, or 2 with a merge of splits)."""
     B, nq, hd = q.shape
     nkv, cap = k_cache.shape[1], k_cache.shape[2]
     f32, bf16 = _dt()[:2]
@@ -371,6 +378,9 @@ def gqa_partial(q, k_cache, v_cache, p_begin: int, p_end: int, part, workspace=N
     rc = load().vx27_gqa_partial(_t(q), _t(k_cache), _t(v_cache), cap, p_begin, p_end, _t(part),
                                  B, nq, nkv, hd, _t(workspace), ws_bytes, _stream(stream), e, 512)
     check(rc, e)
+    rec = B * nq * (hd + 2) * 4
+    n = min(gqa_partial_workspace_bytes(B, nq, nkv, hd, p_end - p_begin) // rec, ws_bytes // rec)
+    return 2 if n > 1 else 1
 
 
 def gqa_combine(parts, n_parts: int, gate, out, part_stride: int = 0, stream=None) -> None:
