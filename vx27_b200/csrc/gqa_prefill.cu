@@ -5,8 +5,12 @@
 //                 (the cache the decode continues from); src/vx27_qfwd.c:339-346 per token
 //   main kernel   one CTA per (128-query tile, query head), flash-attention forward:
 //     warp 0      TMA: the Q tile (128 x 256, resident); 128-key K tiles as four 64-dim
-//                 chunks and V tiles as four 32-key chunks, through one ring of 16 KB
-//                 slots filled in the order the MMAs consume them
+//                 chunks and V tiles as four 32-key chunks through two rings of 16 KB
+//                 slots, one for K (read by the S-MMA warp) and one for V (the O-MMA
+//                 warp), each refilled as soon as a slot frees. A slot has one consumer,
+//                 which waits for every phase of its barriers in order; with a shared ring
+//                 a consumer that ran ahead of a slot's previous load (the other warp's)
+//                 could take that load's pending phase for its own
 //     warp 1      tcgen05.mma: S = Q K^T (128 x 128 in TMEM) and O += P V (128 x 256 in
 //                 TMEM, V read as an MN-major operand), issued as S(j+1) then O += P(j) V(j)
 //     warps 2-9   two threads per query row (its TMEM lane), one per half of the keys and of
@@ -28,7 +32,9 @@ namespace {
 constexpr int HDP = 256;
 constexpr int QT = 128;          // queries per CTA
 constexpr int KT = 128;          // keys per tile
-constexpr int NS = 6;            // ring slots of 16 KB
+constexpr int NKS = 3;           // K ring slots of 16 KB
+constexpr int NVS = 3;           // V ring slots of 16 KB
+constexpr int NS = NKS + NVS;    // slots 0..NKS-1 hold K chunks, NKS.. V chunks
 constexpr int PF_THREADS = 352;  // TMA warp, S-MMA warp, 8 softmax warps, O-MMA warp
 constexpr float RESCALE_LOG2 = 8.0f;
 
@@ -43,13 +49,30 @@ struct PfSmem {
     int abort;
 };
 
-// Ring fill order: K(0), then per step m = 1..n_kt: K(m) (if m < n_kt), V(m-1); four chunks
-// each. Position of chunk c of K(m) and of V(t) in that sequence:
-__device__ __forceinline__ uint32_t ring_pos_k(int m, int c) {
-    return (m == 0 ? 0u : 8u * m - 4u) + c;
+// Chunk c of K(m) is the (4m + c)-th load of the K ring, chunk c of V(t) the (4t + c)-th
+// of the V ring: slot i % NKS (NKS + i % NVS), barrier phase i / NKS (i / NVS).
+
+__device__ __forceinline__ bool pf_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; "
+        "selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok;
 }
-__device__ __forceinline__ uint32_t ring_pos_v(int t, int c, int n_kt) {
-    return 8u * t + (t + 1 < n_kt ? 8u : 4u) + c;
+
+// Bounded wait for a phase, without the abort check: for copies that must land before the
+// CTA may exit.
+__device__ __forceinline__ void pf_drain(uint64_t *bar, uint32_t parity) {
+    const uint32_t addr = smem_u32(bar);
+    for (int it = 0; it < (1 << 20); it++) {
+        uint32_t ok;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
+            "selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+        if (ok) return;
+    }
 }
 
 __device__ __forceinline__ uint64_t pf_timer() {
@@ -238,33 +261,54 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     const uint32_t tS = tmem, tO = tmem + 128, tX = tmem + 384;
 
     if (warp == 0) {
-        if (lane == 0) {  // ---- TMA producer: K(m) then V(m-1), as the MMA warp consumes them
+        if (lane == 0) {  // ---- TMA producer: each ring refilled as soon as a slot frees
             mbar_arrive_expect_tx(&sm.qfull, 4 * QT * 128);
             for (int c = 0; c < 4; c++) tma_load_2d(sm.q[c], &tmq, c * 64, h * T + t0, &sm.qfull);
             const int krow0 = kvh * cap;  // rows of this KV head in the [nkv*cap][256] maps
-            uint32_t n = 0;
-            bool ok = true;
-            for (int m = 0; m <= n_kt && ok; m++) {
-                for (int part = 0; part < 2 && ok; part++) {
-                    if ((part == 0 && m == n_kt) || (part == 1 && m == 0)) continue;
-                    for (int c = 0; c < 4; c++, n++) {
-                        const uint32_t s2 = n % NS;
-                        if (n >= NS && !pf_wait(&sm.empty[s2], ((n / NS) - 1) & 1, sm, status,
-                                                VX_DEV_TIMEOUT_TMA)) {
-                            ok = false;
+            const uint32_t n_all = 4u * n_kt;  // chunks per ring
+            uint32_t nk = 0, nv = 0;           // loads issued into the K and V rings
+            uint32_t spins = 0;
+            uint64_t tw0 = 0;
+            while (nk < n_all || nv < n_all) {
+                bool did = false;
+                if (nk < n_all && (nk < NKS || pf_test(&sm.empty[nk % NKS], ((nk / NKS) - 1) & 1))) {
+                    const uint32_t s2 = nk % NKS;  // K(m): dims [64c, 64c + 64) of 128 keys
+                    mbar_arrive_expect_tx(&sm.full[s2], 16384);
+                    tma_load_2d(sm.ring[s2], &tmk, (nk & 3) * 64, krow0 + (nk >> 2) * KT, &sm.full[s2]);
+                    nk++;
+                    did = true;
+                }
+                if (nv < n_all && (nv < NVS || pf_test(&sm.empty[NKS + nv % NVS], ((nv / NVS) - 1) & 1))) {
+                    const uint32_t s2 = NKS + nv % NVS;  // V(t): keys [32c, 32c + 32), all dims
+                    mbar_arrive_expect_tx(&sm.full[s2], 16384);
+                    for (int a2 = 0; a2 < 4; a2++)
+                        tma_load_2d(sm.ring[s2] + a2 * 4096, &tmv, a2 * 64,
+                                    krow0 + (nv >> 2) * KT + 32 * (nv & 3), &sm.full[s2]);
+                    nv++;
+                    did = true;
+                }
+                if (did) {
+                    spins = 0;
+                } else {  // bounded like every wait: ~2 s without a free slot aborts the CTA
+                    if ((spins++ & 255) == 0) {
+                        if (*(volatile int *)&sm.abort) break;
+                        const uint64_t now = pf_timer();
+                        if (spins == 1) tw0 = now;
+                        else if (now - tw0 > 2000000000ull) {
+                            *(volatile int *)&sm.abort = 1;
+                            dev_flag(status, VX_DEV_TIMEOUT_TMA);
                             break;
-                        }
-                        mbar_arrive_expect_tx(&sm.full[s2], 16384);
-                        if (part == 0) {  // K(m): dims [64c, 64c + 64) of 128 keys
-                            tma_load_2d(sm.ring[s2], &tmk, c * 64, krow0 + m * KT, &sm.full[s2]);
-                        } else {          // V(m-1): keys [32c, 32c + 32), all 256 dims
-                            for (int a2 = 0; a2 < 4; a2++)
-                                tma_load_2d(sm.ring[s2] + a2 * 4096, &tmv, a2 * 64,
-                                            krow0 + (m - 1) * KT + 32 * c, &sm.full[s2]);
                         }
                     }
                 }
             }
+            // every copy issued lands before the CTA can exit, also when a role has aborted
+            // (on the normal path all have been consumed, so these return at once)
+            for (uint32_t i = nk > NKS ? nk - NKS : 0; i < nk; i++)
+                pf_drain(&sm.full[i % NKS], (i / NKS) & 1);
+            for (uint32_t i = nv > NVS ? nv - NVS : 0; i < nv; i++)
+                pf_drain(&sm.full[NKS + i % NVS], (i / NVS) & 1);
+            pf_drain(&sm.qfull, 0);
         }
     } else if (warp == 1) {
         if (lane == 0) {  // ---- MMA issuer, S stream: S = Q K(m)^T once the softmax has read S(m-1)
@@ -273,8 +317,8 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             for (int m = 0; m < n_kt && ok; m++) {
                 if (m >= 1) ok = pf_wait(&sm.s_empty, (m - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
                 for (int c = 0; c < 4 && ok; c++) {
-                    const uint32_t pos = ring_pos_k(m, c), s2 = pos % NS;
-                    ok = pf_wait(&sm.full[s2], (pos / NS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+                    const uint32_t i = 4u * m + c, s2 = i % NKS;
+                    ok = pf_wait(&sm.full[s2], (i / NKS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t qb = smem_u32(sm.q[c]), kb = smem_u32(sm.ring[s2]);
@@ -298,8 +342,8 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                 const int pb = t & 1;
                 ok = pf_wait(&sm.p_full[pb], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
                 for (int c = 0; c < 4 && ok; c++) {
-                    const uint32_t pos = ring_pos_v(t, c, n_kt), s2 = pos % NS;
-                    ok = pf_wait(&sm.full[s2], (pos / NS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+                    const uint32_t i = 4u * t + c, s2 = NKS + i % NVS;
+                    ok = pf_wait(&sm.full[s2], (i / NVS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
                     if (!ok) break;
                     tc_fence_after();
                     const uint32_t vb = smem_u32(sm.ring[s2]);
