@@ -82,33 +82,48 @@ __device__ __forceinline__ void bp3_codes(uint32_t v4, float s1, float s2, float
 // Groups of 128 columns of x staged per chunk (two chunk buffers of 5-10 KB).
 __host__ __device__ constexpr int bp3_kc(int tb) { return tb == 1 ? 8 : 16 / tb; }
 
-// One 128-column group of a row for this lane: its 16 weights against TB tokens' x.
-template <int TB, int KC, bool EXACT_FMA>
-__device__ __forceinline__ void bp3_group(const uint32_t *gw, int l, float s1, float s2,
-                                          const float *xk, float (&acc)[TB]) {
-    uint32_t p[12];
+// One 128-column group of R rows for this lane: each row's 16 weights against TB tokens'
+// x, every x value read from shared memory once for the R rows.
+template <int TB, int KC, int R, bool EXACT_FMA>
+__device__ __forceinline__ void bp3_group(const uint32_t *const (&gw)[R], int l,
+                                          const float (&s1)[R], const float (&s2)[R],
+                                          const float *xk, float (&acc)[R][TB]) {
+    uint32_t p[R][12];
 #pragma unroll
-    for (int i = 0; i < 12; i++) p[i] = gw[i];
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int i = 0; i < 12; i++) p[r][i] = gw[r][i];
 #pragma unroll
     for (int w = 0; w < 4; w++) {
-        // this lane's columns of word w: 32w + 8j + l, j = 0..3, one code per byte,
-        // bit 2 flipped so that code ^ 4 = q + 4 in 0..7
-        const uint32_t v4 = (((p[w] >> l) & 0x01010101u) |
-                             (((p[4 + w] >> l) & 0x01010101u) << 1) |
-                             (((p[8 + w] >> l) & 0x01010101u) << 2)) ^ 0x04040404u;
-        float qv[4];
-        bp3_codes<EXACT_FMA>(v4, s1, s2, qv);
+        float qv[R][4];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            // this lane's columns of word w: 32w + 8j + l, j = 0..3, one code per byte,
+            // bit 2 flipped so that code ^ 4 = q + 4 in 0..7
+            const uint32_t v4 = (((p[r][w] >> l) & 0x01010101u) |
+                                 (((p[r][4 + w] >> l) & 0x01010101u) << 1) |
+                                 (((p[r][8 + w] >> l) & 0x01010101u) << 2)) ^ 0x04040404u;
+            bp3_codes<EXACT_FMA>(v4, s1[r], s2[r], qv[r]);
+        }
 #pragma unroll
         for (int b = 0; b < TB; b++) {
             const float4 xv = *reinterpret_cast<const float4 *>(
                 xk + (size_t)b * KC * 8 * XS_LANE + 4 * w);
-            acc[b] = fmaf(qv[0], xv.x, acc[b]);
-            acc[b] = fmaf(qv[1], xv.y, acc[b]);
-            acc[b] = fmaf(qv[2], xv.z, acc[b]);
-            acc[b] = fmaf(qv[3], xv.w, acc[b]);
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                acc[r][b] = fmaf(qv[r][0], xv.x, acc[r][b]);
+                acc[r][b] = fmaf(qv[r][1], xv.y, acc[r][b]);
+                acc[r][b] = fmaf(qv[r][2], xv.z, acc[r][b]);
+                acc[r][b] = fmaf(qv[r][3], xv.w, acc[r][b]);
+            }
         }
     }
 }
+
+// Rows per thread: two when a pass has 4 or 8 tokens, so that each x value read from shared
+// memory feeds two rows' FMAs (the 8 lanes of a row read 8 different x float4s, so a
+// warp's x load takes one shared-memory wavefront per row it serves).
+__host__ __device__ constexpr int bp3_rows_per_thread(int tb) { return tb >= 4 ? 2 : 1; }
 
 // Shared memory of a BP3 CTA: its block of packed rows (one bulk copy), then two x chunk
 // buffers: element e of group kk of token b at xs[((b * KC + kk) * 8 + (e & 7)) * XS_LANE +
@@ -141,8 +156,8 @@ __device__ __forceinline__ void bp3_stage_x(float *xsb, const float *xb, int b0,
             cp_async_4(d + (b * KC + kk) * 8 * XS_LANE,
                        xb + (size_t)(b0 + b) * cols + (size_t)(k0 + kk) * 128 + tid);
 }
-__host__ __device__ inline size_t bp3_w_bytes(int cols) {
-    return ((size_t)BP3_ROWS * (size_t)(cols >> 7) * 52 + 15) & ~(size_t)15;
+__host__ __device__ inline size_t bp3_w_bytes(int cols, int R) {
+    return ((size_t)BP3_ROWS * R * (size_t)(cols >> 7) * 52 + 15) & ~(size_t)15;
 }
 
 template <int TB>
@@ -151,20 +166,22 @@ pmat_bp3_k(const __grid_constant__ PmatGroups g, const float *__restrict__ xb, i
            uint32_t *status) {
     extern __shared__ __align__(128) uint8_t pm_smem[];
     __shared__ uint64_t wbar;
+    constexpr int R = bp3_rows_per_thread(TB), ROWS = BP3_ROWS * R;
     const int tid = threadIdx.x, l = tid & 7, rl = tid >> 3, base = (tid & 31) & ~7;
     const int gi = pm_group(g, blockIdx.x), rows = g.rows[gi];
     const uint8_t *W = g.W[gi];
     float *yb = g.y[gi];
-    const int r0 = (blockIdx.x - g.blk0[gi]) * BP3_ROWS, nr = min(BP3_ROWS, rows - r0);
+    const int r0 = (blockIdx.x - g.blk0[gi]) * ROWS, nr = min(ROWS, rows - r0);
     const int b0 = blockIdx.y * TB, nb = min(TB, B - b0);
     const int ng = cols >> 7;
     const size_t rb = (size_t)ng * 52;
     constexpr int KC = bp3_kc(TB);
     uint8_t *wsm = pm_smem;
-    float *xs0 = reinterpret_cast<float *>(pm_smem + bp3_w_bytes(cols));
+    float *xs0 = reinterpret_cast<float *>(pm_smem + bp3_w_bytes(cols, R));
     float *xs1 = xs0 + TB * KC * 8 * XS_LANE;
-    // the CTA's rows are contiguous in W and start on a 16-byte boundary (BP3_ROWS * 52 is
-    // a multiple of 16): one bulk copy of the 16-byte-aligned part, the tail by plain loads
+    // the CTA's rows (thread row rl serves rows rl, rl + 16, ...) are contiguous in W and
+    // start on a 16-byte boundary (16 * 52 is a multiple of 16): one bulk copy of the
+    // 16-byte-aligned part, the tail by plain loads
     const size_t blk = (size_t)nr * rb, blk16 = blk & ~(size_t)15;
     const uint8_t *src = W + (size_t)r0 * rb;
     if (tid == 0) {
@@ -182,10 +199,15 @@ pmat_bp3_k(const __grid_constant__ PmatGroups g, const float *__restrict__ xb, i
     bp3_stage_x<KC>(xs0, xb, b0, nb, cols, 0, min(KC, ng), tid);
     cp_async_commit();
     for (size_t i = blk16 + tid; i < blk; i += BP3_THREADS) wsm[i] = src[i];
-    float acc[TB];
+    float acc[R][TB];
+    const uint8_t *wr[R];
 #pragma unroll
-    for (int b = 0; b < TB; b++) acc[b] = 0.f;
-    const uint8_t *wr = wsm + (size_t)(rl < nr ? rl : 0) * rb;
+    for (int r = 0; r < R; r++) {
+#pragma unroll
+        for (int b = 0; b < TB; b++) acc[r][b] = 0.f;
+        const int row = rl + BP3_ROWS * r;
+        wr[r] = wsm + (size_t)(row < nr ? row : 0) * rb;
+    }
     bool ok = true;
     // x chunk c + 1 is copied in while chunk c is used; slots of tokens past nb are left
     // as they are (their sums are never stored)
@@ -207,30 +229,46 @@ pmat_bp3_k(const __grid_constant__ PmatGroups g, const float *__restrict__ xb, i
             if (!ok && tid == 0) dev_flag(status, VX_DEV_TIMEOUT_TMA);
         }
         if (!ok) break;
-        // the chunk's group scales of this row: lane l converts group k0 + l's, the row's
+        // the chunk's group scales of each row: lane l converts group k0 + l's, the row's
         // other lanes receive it by shuffle
-        const float sc_l = l < kn ? bp3_scale(*reinterpret_cast<const unsigned short *>(
-                                        wr + (size_t)(k0 + l) * 52 + 48))
-                                  : 0.f;
+        float sc_l[R];
+#pragma unroll
+        for (int r = 0; r < R; r++)
+            sc_l[r] = l < kn ? bp3_scale(*reinterpret_cast<const unsigned short *>(
+                                   wr[r] + (size_t)(k0 + l) * 52 + 48))
+                             : 0.f;
         for (int kk = 0; kk < kn; kk++) {
-            const float sc = __shfl_sync(FULL, sc_l, base + kk);
-            const uint32_t *gw = reinterpret_cast<const uint32_t *>(wr + (size_t)(k0 + kk) * 52);
+            float sc[R], s64[R], s132[R];
+            const uint32_t *gw[R];
+            bool fast = true;  // every row's scale positive and finite
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                sc[r] = __shfl_sync(FULL, sc_l[r], base + kk);
+                s64[r] = sc[r] * 64.f;
+                s132[r] = sc[r] * -132.f;
+                fast = fast && sc[r] > 0.f && sc[r] <= 3.40282347e38f;
+                gw[r] = reinterpret_cast<const uint32_t *>(wr[r] + (size_t)(k0 + kk) * 52);
+            }
             const float *xk = xc + ((size_t)kk * 8 + l) * XS_LANE;
-            if (sc > 0.f && sc <= 3.40282347e38f)
-                bp3_group<TB, KC, true>(gw, l, sc * 64.f, sc * -132.f, xk, acc);
+            if (fast)
+                bp3_group<TB, KC, R, true>(gw, l, s64, s132, xk, acc);
             else
-                bp3_group<TB, KC, false>(gw, l, sc, 0.f, xk, acc);
+                bp3_group<TB, KC, R, false>(gw, l, sc, sc, xk, acc);
         }
         __syncthreads();  // chunk c's buffer is refilled two chunks on
     }
     cp_async_wait<0>();
-    // lanes 0..7 of the row summed left to right
+    // lanes 0..7 of each row summed left to right
 #pragma unroll
-    for (int b = 0; b < TB; b++) {
-        float t = __shfl_sync(FULL, acc[b], base);
+    for (int r = 0; r < R; r++) {
+        const int row = rl + BP3_ROWS * r;
 #pragma unroll
-        for (int j = 1; j < 8; j++) t = __fadd_rn(t, __shfl_sync(FULL, acc[b], base + j));
-        if (ok && l == 0 && rl < nr && b < nb) yb[(size_t)(b0 + b) * rows + r0 + rl] = t;
+        for (int b = 0; b < TB; b++) {
+            float t = __shfl_sync(FULL, acc[r][b], base);
+#pragma unroll
+            for (int j = 1; j < 8; j++) t = __fadd_rn(t, __shfl_sync(FULL, acc[r][b], base + j));
+            if (ok && l == 0 && row < nr && b < nb) yb[(size_t)(b0 + b) * rows + r0 + row] = t;
+        }
     }
 }
 
@@ -324,7 +362,7 @@ template <int TB>
 int launch_pmat(PmatGroups g, uint32_t dtype, const float *xb, int cols, int B,
                 cudaStream_t st, char *err, size_t errlen) {
     const unsigned passes = (unsigned)((B + TB - 1) / TB);
-    const int per = dtype == VX27_PMAT_BP3_128 ? BP3_ROWS : ROW_THREADS;
+    const int per = dtype == VX27_PMAT_BP3_128 ? BP3_ROWS * bp3_rows_per_thread(TB) : ROW_THREADS;
     int nblk = 0;
     for (int i = 0; i < MAXG; i++) {
         g.blk0[i] = nblk;
@@ -333,7 +371,7 @@ int launch_pmat(PmatGroups g, uint32_t dtype, const float *xb, int cols, int B,
     g.blk0[MAXG] = nblk;
     const dim3 grid((unsigned)nblk, passes);
     if (dtype == VX27_PMAT_BP3_128) {
-        const size_t smem = bp3_w_bytes(cols) + bp3_xs_bytes(TB);
+        const size_t smem = bp3_w_bytes(cols, bp3_rows_per_thread(TB)) + bp3_xs_bytes(TB);
         if (smem > 220 * 1024)
             return fail(err, errlen, "vx27_pmat: cols=%d too wide for one CTA", cols);
         if (ensure_smem_attr((const void *)pmat_bp3_k<TB>, smem, err, errlen)) return -1;
