@@ -138,6 +138,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
     torch.cuda.set_device(local_rank)
     cfg = HybridConfig(batch=args.batch, ctx=args.ctx, steps=args.warmup + args.steps + 2,
+                       fused_gqa=args.fused_gqa,
                        seed=2 + rank * 1000)
     dec = HybridDecoder(cfg)
     stream = torch.cuda.current_stream()
@@ -201,7 +202,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     ctx_avg = ctx0 + 1 + (args.steps - 1) / 2.0
     by = dec.bytes_per_step(ctx_avg)
     c = cfg
-    gqa_bytes = by["kv"] / N_FULL + (c.batch * c.nq * c.hd * 2 * 2) + c.batch * c.nq * c.hd * 4
+    if args.fused_gqa:  # the fused kernel: K/V, q/k/v in, gate, out, the new K/V rows
+        gqa_bytes = (by["kv"] + by["gqa_act"]) / N_FULL
+    else:  # the split kernel: K/V, the normalised fp32 q, gate and out
+        gqa_bytes = by["kv"] / N_FULL + c.batch * c.nq * c.hd * (4 + 2 + 2)
     dn_bytes = (by["dn_state"] + by["dn_conv"] + by["dn_act"]) / N_LIN
     peak, peak_src = peaks()
     gqa_ms, dn_ms = avg_ms("gqa"), avg_ms("dn")
@@ -265,11 +269,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                   (sum(t.numel() * t.element_size() for t in (dec.S, dec.ring, dec.kc, dec.vc))
                    / 1e9),
             "parallelism": f"dp{world} (sequences sharded, no collective)",
+            "gqa_layer": ("one fused kernel (vx27_gqa_decode_fused)" if args.fused_gqa
+                          else "vx27_gqa_append + vx27_gqa_decode_batch"),
         },
         "roofline": {
             "bound": "hbm",
-            "kernel": "gqa_split_tc split-KV decode, per layer (one split: it writes the gated "
-                      "output itself, no combine pass)",
+            "kernel": ("gqa_split_tc split-KV decode" +
+                       (" with the QK norm, RoPE and K/V append fused in" if args.fused_gqa
+                        else "") +
+                       ", per layer (one split: it writes the gated output itself, no "
+                       "combine pass)"),
             "achieved": round(gqa_gbs, 1), "peak": peak, "unit": "GB/s",
             "frac": round(gqa_gbs / peak, 4),
             "traffic": int(GQA_SPLIT_DRAM_PER_ALGO_BYTE * gqa_bytes),
@@ -974,6 +983,9 @@ def main() -> None:
     ap.add_argument("--ref-seqs", type=int, default=4)
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fused-gqa", action="store_true",
+                    help="config 2: GQA layers as one fused kernel (vx27_gqa_decode_fused) "
+                         "instead of append + split-KV decode")
     ap.add_argument("--workload", choices=["config2", "config0", "config1", "config3a",
                                            "config3b", "config4", "dn_layer", "gqa_layer", "pmat"],
                     default="config2",

@@ -67,6 +67,27 @@ int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
                           size_t errlen);
 
 /*
+ * vx27_gqa_append + vx27_gqa_decode_batch in one kernel: the split kernel forms each
+ * (sequence, KV head) group's q from the raw activations (QK RMSNorm, partial RoPE at
+ * pos[b], the arithmetic of vx27_gqa_append) and writes the token's normalised, rotated K
+ * and raw V rows into the caches at slot pos[b] before its tensor-core loads read that
+ * slot; then the same attention and gate as vx27_gqa_decode_batch. Replaces one launch
+ * per layer (src/vx27_qfwd.c:339-371 per token).
+ *   q_in, gate [B][nq][hd], k_in, v_in [B][nkv][hd] (act dtype, 16-byte aligned);
+ *   q_norm_w, k_norm_w [hd] (VX27_F_NORM_1P: zero-centred); rope_table [rope_table_len]
+ *   [rope_dim] (vx27_rope_table_build), rope_dim a multiple of 16; caches as for
+ *   vx27_gqa_decode_batch; workspace: vx27_gqa_decode_workspace_size(...) bytes.
+ * The normalised q is not written out (vx27_gqa_append does that).
+ */
+int vx27_gqa_decode_fused(const void *q_in, const void *k_in, const void *v_in,
+                          const float *q_norm_w, const float *k_norm_w, const float *rope_table,
+                          int rope_table_len, const void *gate, void *k_cache, void *v_cache,
+                          int cap, const int *pos, void *out, void *workspace,
+                          size_t workspace_bytes, int B, int nq, int nkv, int hd, int rope_dim,
+                          float eps, int n_splits, int flags, void *stream, char *err,
+                          size_t errlen);
+
+/*
  * No counterpart in the reference. vx27_gqa_decode_batch without the workspace: same
  * arguments, same kernels and results, but the split partial records go to a fixed
  * array of VX27_GQA_NOALLOC_SCRATCH_BYTES in the library's own device memory, and the

@@ -58,6 +58,27 @@ def gpu_step(x, B, cap, rope, n_splits=0, bf16=True, out_bf16=False):
     return host(q).reshape(-1), host(kc).reshape(-1), host(vc).reshape(-1), host(out).reshape(-1)
 
 
+def gpu_step_fused(x, B, cap, rope, n_splits=0, bf16=True, out_bf16=False):
+    """vx27_gqa_decode_fused: append and attention in one kernel."""
+    kc = dev(x["kc"], True).view(B, NKV, cap, HD)
+    vc = dev(x["vc"], True).view(B, NKV, cap, HD)
+    qi = dev(x["qi"], bf16).view(B, NQ, HD)
+    ki = dev(x["ki"], bf16).view(B, NKV, HD)
+    vi = dev(x["vi"], bf16).view(B, NKV, HD)
+    gate = dev(x["gate"], bf16).view(B, NQ, HD)
+    pos = dev(x["pos"])
+    ws = torch.empty(ops.gqa_workspace_bytes(B, NQ, NKV, HD, cap, n_splits) // 4 + 1,
+                     device="cuda")
+    out = torch.empty(B, NQ, HD, device="cuda",
+                      dtype=torch.bfloat16 if out_bf16 else torch.float32)
+    ops.gqa_decode_fused(qi, ki, vi, dev(x["qw"]), dev(x["kw"]), rope, gate, kc, vc, pos, out, ws,
+                         n_splits=n_splits)
+    out = out.float()
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    return host(kc).reshape(-1), host(vc).reshape(-1), host(out).reshape(-1)
+
+
 @pytest.fixture(scope="module")
 def rope(cuda):
     return ops.rope_table(300000)
@@ -224,3 +245,52 @@ def test_no_output_gate_mtp_drafter(cuda, orc, rope):
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     assert rel_err(host(out).reshape(-1), ref) < REL_TOL
+
+
+@pytest.mark.parametrize("n_splits", [0, 1, 3, 7])
+def test_fused_decode_ragged_batch(cuda, orc, rope, n_splits):
+    """The fused kernel (vx27_gqa_decode_fused) on the ragged batch: the appended rows equal
+    the separate append kernel's bit for bit, the output the oracle's."""
+    B, cap = 5, 1024
+    x = setup(orc, 21, B, cap, [0, 1, 127, 128, 1000])
+    qo, kc, vc, ref = oracle_step(orc, x, B, cap)
+    _, kc_sep, vc_sep, out_sep = gpu_step(x, B, cap, rope, n_splits)
+    kcg, vcg, out = gpu_step_fused(x, B, cap, rope, n_splits)
+    assert np.array_equal(vcg, vc_sep) and np.array_equal(vcg, vc)
+    krow_f = kcg.reshape(B, NKV, cap, HD)[np.arange(B), :, x["pos"]]
+    krow_s = kc_sep.reshape(B, NKV, cap, HD)[np.arange(B), :, x["pos"]]
+    # the norm's double sum runs in another order: a 1-ulp difference may flip a bf16 rounding
+    assert np.count_nonzero(krow_f != krow_s) <= krow_f.size // 1000
+    # every other cache row is untouched
+    keep = np.ones((B, NKV, cap), bool)
+    keep[np.arange(B), :, x["pos"]] = False
+    assert np.array_equal(kcg.reshape(B, NKV, cap, HD)[keep], x["kc"].reshape(B, NKV, cap, HD)[keep])
+    err = rel_err(out, ref)
+    print(f"fused splits={n_splits}: rel err {err:.2e} (separate kernels {rel_err(out_sep, ref):.2e})")
+    assert err < 1e-4 < REL_TOL
+
+
+def test_fused_decode_golden_and_config1(cuda, orc, golden, rope):
+    """Golden driver inputs (pos 10 and 37) and config 1 (ctx 8192) through the fused kernel."""
+    B, cap = 2, 48
+    x = setup(orc, 8, B, cap, golden["gq_pos"])
+    kc, vc, out = gpu_step_fused(x, B, cap, rope)
+    krow = kc.reshape(B, NKV, cap, HD)[np.arange(B), :, golden["gq_pos"]]
+    assert np.count_nonzero(krow != golden["gq_krow"]) <= krow.size // 1000
+    vrow = vc.reshape(B, NKV, cap, HD)[np.arange(B), :, golden["gq_pos"]]
+    assert np.array_equal(vrow, golden["gq_vrow"])
+    assert rel_err(out, golden["gq_out"]) < 1e-4
+    B, cap = 1, 8192
+    x = setup(orc, 1, B, cap, [8191])
+    _, _, _, ref = oracle_step(orc, x, B, cap)
+    _, _, out = gpu_step_fused(x, B, cap, rope)
+    assert rel_err(out, ref) < 1e-4
+
+
+@pytest.mark.parametrize("bf16,out_bf16", [(False, False), (True, True)])
+def test_fused_decode_dtypes(cuda, orc, rope, bf16, out_bf16):
+    B, cap = 3, 700
+    x = setup(orc, 37, B, cap, [0, 300, 699], bf16=bf16)
+    _, _, _, ref = oracle_step(orc, x, B, cap, bf16=bf16)
+    _, _, out = gpu_step_fused(x, B, cap, rope, 1, bf16=bf16, out_bf16=out_bf16)
+    assert rel_err(out, ref) < (2e-2 if out_bf16 else 1e-4)

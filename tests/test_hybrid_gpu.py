@@ -18,8 +18,9 @@ def test_layer_order_is_three_deltanet_then_one_gqa():
     assert kinds[63] == (True, 15) and kinds[62] == (False, 47)
 
 
-def test_step_layers_match_oracle(cuda, orc):
-    cfg = HybridConfig(batch=3, ctx=200, steps=2, seed=7)
+@pytest.mark.parametrize("fused_gqa", [False, True])
+def test_step_layers_match_oracle(cuda, orc, fused_gqa):
+    cfg = HybridConfig(batch=3, ctx=200, steps=2, seed=7, fused_gqa=fused_gqa)
     dec = HybridDecoder(cfg)
     # snapshot layer 0 (DeltaNet) and GQA layer 0 (model layer 3) before the step
     S0, ring0 = host(dec.S[0]).copy(), host(dec.ring[0]).copy()

@@ -19,6 +19,11 @@ int launch_split_tc(const void *kc, const void *vc, const float *q, const int *p
                     int cap, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
                     cudaStream_t st, char *err, size_t errlen, const void *gate = nullptr,
                     void *out = nullptr, int flags = 0);
+int launch_split_tc_fused(const void *q_in, const void *k_in, const void *v_in,
+                          const float *qw, const float *kw, const float *rope, int rope_len,
+                          int rope_dim, float eps, void *kc, void *vc, int cap, const int *pos,
+                          float *parts, int B, int nq, int nkv, int n_splits, const void *gate,
+                          void *out, int flags, cudaStream_t st, char *err, size_t errlen);
 
 namespace {
 
@@ -279,6 +284,39 @@ int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
     if (launch_split(q, k_cache, v_cache, cap, pos, parts, B, nq, nkv, n_splits, 0, -1, st, err,
                      errlen))
         return -1;
+    return launch_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen);
+}
+
+int vx27_gqa_decode_fused(const void *q_in, const void *k_in, const void *v_in,
+                          const float *q_norm_w, const float *k_norm_w, const float *rope_table,
+                          int rope_table_len, const void *gate, void *k_cache, void *v_cache,
+                          int cap, const int *pos, void *out, void *workspace,
+                          size_t workspace_bytes, int B, int nq, int nkv, int hd, int rope_dim,
+                          float eps, int n_splits, int flags, void *stream, char *err,
+                          size_t errlen) {
+    if (check_shape("vx27_gqa_decode_fused", B, nq, nkv, hd, err, errlen)) return -1;
+    if (!q_in || !k_in || !v_in || !q_norm_w || !k_norm_w || !k_cache || !v_cache || !pos ||
+        !out || !workspace || cap <= 0 || (rope_dim && !rope_table))
+        return fail(err, errlen, "vx27_gqa_decode_fused: null pointer argument");
+    const size_t rec = (size_t)B * nq * (hd + 2) * sizeof(float);
+    const int fit = (int)(workspace_bytes / rec);
+    if (n_splits <= 0) {
+        n_splits = auto_splits(B, nkv, cap);
+        if (n_splits > fit) n_splits = fit;
+    }
+    if (n_splits < 1 || n_splits > fit || n_splits > 65535)
+        return fail(err, errlen,
+                    "vx27_gqa_decode_fused: workspace of %zu bytes holds %d splits, need %d",
+                    workspace_bytes, fit, n_splits < 1 ? 1 : n_splits);
+    cudaStream_t st = (cudaStream_t)stream;
+    float *parts = (float *)workspace;
+    const bool direct = n_splits == 1;  // the split kernel applies the gate and writes out
+    if (launch_split_tc_fused(q_in, k_in, v_in, q_norm_w, k_norm_w, rope_table, rope_table_len,
+                              rope_dim, eps, k_cache, v_cache, cap, pos, parts, B, nq, nkv,
+                              n_splits, direct ? gate : nullptr, direct ? out : nullptr, flags,
+                              st, err, errlen))
+        return -1;
+    if (direct) return 0;
     return launch_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen);
 }
 

@@ -37,6 +37,8 @@ struct TcSmem {
     uint64_t full[NSLOT], empty[NSLOT];
     uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2], q_full[2], q_empty[2];
     uint64_t ob_full, ob_empty, mma_done;
+    uint64_t kv_ready[2];              // fused prologue: an item's new K/V row is in the cache
+    alignas(16) uint8_t kvrow[2][HDIM * 2];  // ... staged here, stored by a bulk copy
     uint64_t grp[2], grp_end[2];       // softmax-group rendezvous (bounded, unlike bar.sync)
     float red_max[2][4][8];
     float red_sum[2][4][8];
@@ -85,6 +87,83 @@ __device__ __forceinline__ uint32_t sw128(int row, int col) {
 
 __device__ __forceinline__ uint16_t bf16_bits(float x) { return f32_to_bf16(x); }
 
+// The token prologue fused into the split kernel (decode): the staging warp forms each
+// item's q from the raw activations, and the CTA whose range ends at the token's slot
+// appends its K/V row to the cache (the arithmetic of gqa_append_k: QK RMSNorm with a
+// double sum of squares, NeoX RoPE on dims < rope_dim, bf16 store). q_in == NULL: q is the
+// normalised q of vx27_gqa_append instead.
+struct TcAppend {
+    const void *q_in, *k_in, *v_in;   // [B][nq][hd], [B][nkv][hd] (act dtype)
+    const float *qw, *kw, *rope;      // norm weights [hd]; rope table [rope_len][rope_dim]
+    uint16_t *kc, *vc;                // the caches the tensor maps read
+    int rope_len, rope_dim;
+    float eps;
+    int one_p;                        // zero-centred (1 + w) norm weights
+};
+
+__device__ __forceinline__ void load8f(const void *p, size_t i, bool bf, float (&x)[8]) {
+    if (bf) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p) + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            x[2 * k] = bf16_to_f32(w[k] & 0xffffu);
+            x[2 * k + 1] = bf16_to_f32(w[k] >> 16);
+        }
+    } else {
+        const float4 *f = reinterpret_cast<const float4 *>(static_cast<const float *>(p) + i);
+        const float4 a = f[0], b = f[1];
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    }
+}
+__device__ __forceinline__ uint4 pack8_bf16(const float (&x)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        w[k] = (uint32_t)f32_to_bf16(x[2 * k]) | ((uint32_t)f32_to_bf16(x[2 * k + 1]) << 16);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// One 256-dim row held 8 dims per lane (dims 8*lane ..): RMSNorm then the rotation, as
+// gqa_append_k rounds them; rr = the position's rope row, NULL for none (bad position).
+// Not inlined: one copy of this code serves all rows, which keeps the staging warp's code
+// from crowding the instruction cache the other roles' loops share (measured: inlined
+// eight times it slowed a config 2 layer by 1.5%).
+__device__ __noinline__ void tc_norm_rope(float (&y)[8], const float (&x)[8],
+                                             const float *w, const TcAppend &ap,
+                                             const float *rr, int lane) {
+    double ss = 0.0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) ss += (double)x[e] * (double)x[e];
+    ss = warp_sum_d(ss);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(ss / HDIM), ap.eps)));
+    const int d0 = 8 * lane;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        float wv = w[d0 + e];
+        if (ap.one_p) wv = __fadd_rn(wv, 1.0f);
+        y[e] = __fmul_rn(__fmul_rn(x[e], r), wv);
+    }
+    // the partner of dim d < half is d + half, held half / 8 lanes away
+    const int half = ap.rope_dim / 2, hl = half / 8;
+    const bool lo = d0 < half;
+    float yp[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        yp[e] = __shfl_sync(0xffffffffu, y[e], (lo ? lane + hl : lane - hl) & 31);
+    if (rr && d0 < ap.rope_dim) {
+        const int i0 = lo ? d0 : d0 - half;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float c = rr[i0 + e], s = rr[half + i0 + e];
+            const float x0 = lo ? y[e] : yp[e], x1 = lo ? yp[e] : y[e];
+            y[e] = lo ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s))
+                      : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        }
+    }
+}
+
 // One work item = (split s, KV head, sequence b), numbered w = s + n_splits * (kvh + nkv * b).
 struct TcItem {
     int b, kvh, s, p0, p1, n_tiles, row0;
@@ -118,16 +197,17 @@ __device__ __forceinline__ TcItem tc_item(int w, const int *__restrict__ pos, in
 // walk the same item sequence with CTA-wide counters (ring slot j, tile g, non-empty item
 // k), so the TMA ring keeps streaming across item boundaries; the softmax warps stage the
 // next item's q in the second Q buffer while the current item runs.
-template <int G>
+template <int G, bool FUSED>
 __global__ void __launch_bounds__(TC_THREADS, 1)
 gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
              const __grid_constant__ CUtensorMap tmk32, const __grid_constant__ CUtensorMap tmv32,
              const float *__restrict__ q, const int *__restrict__ pos, float *__restrict__ parts,
              int cap, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
              const void *__restrict__ gate, void *__restrict__ out, int flags,
-             uint32_t *status) {
+             const __grid_constant__ TcAppend ap, uint32_t *status) {
     extern __shared__ uint8_t smem_raw[];
     TcSmem &sm = *reinterpret_cast<TcSmem *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    constexpr bool fused = FUSED;  // the token prologue runs in this kernel (ap is set)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n_items = n_splits * nkv * B, stride = gridDim.x;
     const size_t rec = (size_t)B * nq * (HDIM + 2);
@@ -139,7 +219,7 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
     };
     // q rows of item w as bf16 hi (rows 0..G-1) and lo (rows G..2G-1) into Q buffer qb, by
     // the staging warp: all loads first, then the conversions
-    auto stage_q = [&](int w, int qb) {
+    auto stage_q_plain = [&](int w, int qb) {
         const TcItem it = item(w);
         const float2 *src = reinterpret_cast<const float2 *>(q + ((size_t)it.b * nq + it.kvh * G) * HDIM);
         float2 v[4 * G];
@@ -156,6 +236,108 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
         }
         fence_proxy_async();
     };
+    // fused prologue: q of item w normalised and rotated from q_in into Q buffer qb (then
+    // q_full[qb]); the new token's K/V row into the cache when its slot ends this item's
+    // range, then kv_ready[qb] (after a proxy fence: the TMA loads read that row). All rows
+    // are loaded before any arithmetic, so their latencies overlap.
+    auto stage_q_fused = [&](int w, int qb) {
+        const TcItem it = item(w);
+        const int p = pos[it.b];
+        const bool bf = flags & VX27_F_ACT_BF16;
+        const bool p_ok = p >= 0 && p < ap.rope_len;
+        const float *rr = ap.rope_dim > 0 && p_ok ? ap.rope + (size_t)p * ap.rope_dim : nullptr;
+        if (ap.rope_dim > 0 && !p_ok && lane == 0) dev_flag(status, VX_DEV_BAD_ARG);
+        const bool app = p >= it.p0 && p < it.p1;  // this item's range ends at the token's slot
+        const int d0 = 8 * lane, c = d0 >> 6, col = d0 & 63;
+        const size_t q_row = ((size_t)it.b * nq + it.kvh * G) * HDIM + d0;
+        const size_t kv_row = ((size_t)it.b * nkv + it.kvh) * HDIM + d0;
+        float x[G + 2][8];  // q rows of the group, then k and v
+        if (bf) {
+            uint4 raw[G + 2];
+#pragma unroll
+            for (int h = 0; h < G; h++)
+                raw[h] = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(ap.q_in) +
+                                                          q_row + (size_t)h * HDIM);
+            if (app) {
+                raw[G] = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(ap.k_in) + kv_row);
+                raw[G + 1] = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(ap.v_in) + kv_row);
+            } else {
+                raw[G] = raw[G + 1] = make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int h = 0; h < G + 2; h++) {
+                const uint32_t wv[4] = {raw[h].x, raw[h].y, raw[h].z, raw[h].w};
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    x[h][2 * k] = bf16_to_f32(wv[k] & 0xffffu);
+                    x[h][2 * k + 1] = bf16_to_f32(wv[k] >> 16);
+                }
+            }
+        } else {
+            float4 raw[G + 2][2];
+#pragma unroll
+            for (int h = 0; h < G; h++) {
+                const float4 *f = reinterpret_cast<const float4 *>(static_cast<const float *>(ap.q_in) +
+                                                                   q_row + (size_t)h * HDIM);
+                raw[h][0] = f[0];
+                raw[h][1] = f[1];
+            }
+            if (app) {
+                const float4 *fk = reinterpret_cast<const float4 *>(static_cast<const float *>(ap.k_in) + kv_row);
+                const float4 *fv = reinterpret_cast<const float4 *>(static_cast<const float *>(ap.v_in) + kv_row);
+                raw[G][0] = fk[0]; raw[G][1] = fk[1];
+                raw[G + 1][0] = fv[0]; raw[G + 1][1] = fv[1];
+            } else {
+                raw[G][0] = raw[G][1] = raw[G + 1][0] = raw[G + 1][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int h = 0; h < G + 2; h++) {
+                x[h][0] = raw[h][0].x; x[h][1] = raw[h][0].y; x[h][2] = raw[h][0].z; x[h][3] = raw[h][0].w;
+                x[h][4] = raw[h][1].x; x[h][5] = raw[h][1].y; x[h][6] = raw[h][1].z; x[h][7] = raw[h][1].w;
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < G; h++) {
+            float y[8], lo8[8];
+            tc_norm_rope(y, x[h], ap.qw, ap, rr, lane);
+#pragma unroll
+            for (int e = 0; e < 8; e++) lo8[e] = y[e] - bf16_to_f32(f32_to_bf16(y[e]));
+            *reinterpret_cast<uint4 *>(&sm.q[qb][c][sw128(h, col)]) = pack8_bf16(y);
+            *reinterpret_cast<uint4 *>(&sm.q[qb][c][sw128(h + G, col)]) = pack8_bf16(lo8);
+        }
+        fence_proxy_async();
+        mbar_arrive(&sm.q_full[qb]);
+        if (app) {
+            // the rows go out as bulk copies (async proxy, like the TMA loads that read them
+            // back), staged in shared memory
+            float y[8];
+            tc_norm_rope(y, x[G], ap.kw, ap, rr, lane);
+            *reinterpret_cast<uint4 *>(&sm.kvrow[0][16 * lane]) = pack8_bf16(y);
+            *reinterpret_cast<uint4 *>(&sm.kvrow[1][16 * lane]) = pack8_bf16(x[G + 1]);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+                const size_t o = (((size_t)it.b * nkv + it.kvh) * cap + p) * HDIM;
+                asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                             ::"l"(ap.kc + o), "r"(smem_u32(sm.kvrow[0])), "r"(HDIM * 2) : "memory");
+                asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                             ::"l"(ap.vc + o), "r"(smem_u32(sm.kvrow[1])), "r"(HDIM * 2) : "memory");
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // stores complete
+            }
+            __syncwarp();
+        }
+        mbar_arrive(&sm.kv_ready[qb]);
+    };
+    // q of item w into Q buffer qb, then q_full[qb]
+    auto stage_q = [&](int w, int qb) {
+        if constexpr (FUSED) {
+            stage_q_fused(w, qb);
+        } else {
+            stage_q_plain(w, qb);
+            mbar_arrive(&sm.q_full[qb]);
+        }
+    };
     const int w_first = next_work(blockIdx.x);
 
     // ---- prologue --------------------------------------------------------------
@@ -171,6 +353,7 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
             mbar_init(&sm.q_empty[i], 1);
             mbar_init(&sm.grp[i], 128);
             mbar_init(&sm.grp_end[i], 128);
+            mbar_init(&sm.kv_ready[i], 32);
         }
         mbar_init(&sm.ob_full, 128);
         mbar_init(&sm.ob_empty, 1);
@@ -200,11 +383,19 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
     if (warp == 0) {
         // ---- TMA producer --------------------------------------------------------
         if (lane == 0) {
-            int j = 0;  // ring items issued by this CTA
+            int j = 0;   // ring items issued by this CTA
+            int kp = 0;  // items with work seen
             bool ok = true;
-            for (int w = w_first; w < n_items && ok; w = next_work(w + stride)) {
+            for (int w = w_first; w < n_items && ok; w = next_work(w + stride), kp++) {
                 const TcItem it = item(w);
                 for (int jj = 0; jj < it.n_tiles * 8; jj++, j++) {
+                    // fused prologue: the last tile may hold the new token's row, written by
+                    // the staging warp when it staged this item's q
+                    if (fused && jj == (it.n_tiles - 1) * 8 &&
+                        !tc_wait(&sm.kv_ready[kp & 1], (kp >> 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA)) {
+                        ok = false;
+                        break;
+                    }
                     const int slot = j % NSLOT, round = j / NSLOT;
                     if (round > 0 &&
                         !tc_wait(&sm.empty[slot], (round - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA)) {
@@ -442,7 +633,6 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
         int kq = 0;  // items with work seen so far
         if (w_first < n_items) {
             stage_q(w_first, 0);
-            mbar_arrive(&sm.q_full[0]);
         }
         for (int w = blockIdx.x; w < n_items && ok; w += stride) {
             const TcItem it = item(w);
@@ -520,10 +710,7 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
                 if (kq >= 1)
                     ok = tc_wait(&sm.q_empty[(kq + 1) & 1], ((kq - 1) >> 1) & 1, sm, status,
                                  VX_DEV_TIMEOUT_MMA);
-                if (ok) {
-                    stage_q(wn, (kq + 1) & 1);
-                    mbar_arrive(&sm.q_full[(kq + 1) & 1]);
-                }
+                if (ok) stage_q(wn, (kq + 1) & 1);
             }
             if (out) fetch_gate();
             ok = ok && tc_wait(&sm.ob_full, kq & 1, sm, status, VX_DEV_TIMEOUT_MMA);
@@ -546,12 +733,58 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
     }
 }
 
+// one CTA per SM: the struct, aligned to 1024 B, within the 227 KB a CTA may opt into
+static_assert(sizeof(TcSmem) + 1024 <= 232448, "split kernel shared memory over 227 KB");
 size_t tc_smem_bytes() { return sizeof(TcSmem) + 1024; }
 
 // One CTA per SM (fewer when there are fewer items).
 static int tc_grid(int B, int nkv, int n_splits) {
     const long long items = (long long)B * nkv * n_splits;
     return (int)(items < num_sms() ? items : num_sms());
+}
+
+// The split kernel's launch: tensor maps over both caches, one CTA per SM; with pdl the
+// launch may overlap its predecessor's tail (programmatic dependent launch), else a plain
+// launch reporting to the status word given.
+static int launch_tc(const void *kc, const void *vc, const float *q, const int *pos,
+                     float *parts, int cap, int B, int nq, int nkv, int n_splits, int p_begin,
+                     int p_end, const void *gate, void *out, int flags, const TcAppend &ap,
+                     uint32_t *stw, bool pdl, cudaStream_t st, char *err, size_t errlen) {
+    CUtensorMap mk, mv, mk32, mv32;
+    const uint64_t rows = (uint64_t)B * nkv * cap;
+    if (make_tmap_bf16_2d(&mk, kc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
+        make_tmap_bf16_2d(&mv, vc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
+        make_tmap_bf16_2d(&mk32, kc, rows, HDIM, HDIM * 2, 64, 32, err, errlen) ||
+        make_tmap_bf16_2d(&mv32, vc, rows, HDIM, HDIM * 2, 64, 32, err, errlen))
+        return -1;
+    const size_t smem = tc_smem_bytes();
+    const dim3 grid(tc_grid(B, nkv, n_splits));
+#define VX_TCK(GG, FF)                                                                    \
+    {                                                                                     \
+        if (ensure_smem_attr((const void *)gqa_split_tc<GG, FF>, smem, err, errlen))      \
+            return -1;                                                                    \
+        if (pdl)                                                                          \
+            VX_CK(launch_pdl(gqa_split_tc<GG, FF>, grid, dim3(TC_THREADS), smem, st, mk, mv, \
+                             mk32, mv32, q, pos, parts, cap, B, nq, nkv, n_splits, p_begin, \
+                             p_end, gate, out, flags, ap, stw));                           \
+        else                                                                              \
+            gqa_split_tc<GG, FF><<<grid, TC_THREADS, smem, st>>>(                          \
+                mk, mv, mk32, mv32, q, pos, parts, cap, B, nq, nkv, n_splits, p_begin, p_end, \
+                gate, out, flags, ap, stw);                                                \
+    }
+#define VX_TCG(GG)                                                                        \
+    case GG:                                                                              \
+        if (ap.q_in) VX_TCK(GG, true) else VX_TCK(GG, false)                              \
+        break;
+    switch (nq / nkv) {
+        VX_TCG(1) VX_TCG(2) VX_TCG(4) VX_TCG(6) VX_TCG(8)
+        default:
+            return fail(err, errlen, "vx27_gqa: group size %d (nq/nkv) unsupported", nq / nkv);
+    }
+#undef VX_TCG
+#undef VX_TCK
+    VX_CK(cudaGetLastError());
+    return 0;
 }
 
 int launch_split_tc(const void *kc, const void *vc, const float *q, const int *pos, float *parts,
@@ -565,33 +798,42 @@ int launch_split_tc(const void *kc, const void *vc, const float *q, const int *p
         ((uintptr_t)q & 7))
         return fail(err, errlen,
                     "vx27_gqa: q must be 8-byte aligned, gate, out and the workspace 16-byte aligned");
-    CUtensorMap mk, mv, mk32, mv32;
-    const uint64_t rows = (uint64_t)B * nkv * cap;
-    if (make_tmap_bf16_2d(&mk, kc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
-        make_tmap_bf16_2d(&mv, vc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
-        make_tmap_bf16_2d(&mk32, kc, rows, HDIM, HDIM * 2, 64, 32, err, errlen) ||
-        make_tmap_bf16_2d(&mv32, vc, rows, HDIM, HDIM * 2, 64, 32, err, errlen))
-        return -1;
-    const size_t smem = tc_smem_bytes();
-    const dim3 grid(tc_grid(B, nkv, n_splits));
-    uint32_t *stw = dev_status();
-#define VX_TCG(GG)                                                                        \
-    case GG: {                                                                            \
-        if (ensure_smem_attr((const void *)gqa_split_tc<GG>, smem, err, errlen))          \
-            return -1;                                                                    \
-        VX_CK(launch_pdl(gqa_split_tc<GG>, grid, dim3(TC_THREADS), smem, st, mk, mv, mk32, mv32, \
-                         q, pos, parts, cap, B, nq, nkv, n_splits, p_begin, p_end, gate, out, \
-                         flags, stw));                                                     \
-        break;                                                                            \
-    }
-    switch (nq / nkv) {
-        VX_TCG(1) VX_TCG(2) VX_TCG(4) VX_TCG(6) VX_TCG(8)
-        default:
-            return fail(err, errlen, "vx27_gqa: group size %d (nq/nkv) unsupported", nq / nkv);
-    }
-#undef VX_TCG
-    VX_CK(cudaGetLastError());
-    return 0;
+    return launch_tc(kc, vc, q, pos, parts, cap, B, nq, nkv, n_splits, p_begin, p_end, gate, out,
+                     flags, TcAppend{}, dev_status(), true, st, err, errlen);
+}
+
+// Decode with the token prologue fused in (q_in/k_in/v_in raw activations; the new K/V rows
+// are appended at slot pos[b] by the kernel itself).
+int launch_split_tc_fused(const void *q_in, const void *k_in, const void *v_in,
+                          const float *qw, const float *kw, const float *rope, int rope_len,
+                          int rope_dim, float eps, void *kc, void *vc, int cap, const int *pos,
+                          float *parts, int B, int nq, int nkv, int n_splits, const void *gate,
+                          void *out, int flags, cudaStream_t st, char *err, size_t errlen) {
+    if (out && n_splits != 1)
+        return fail(err, errlen, "vx27_gqa: a direct output needs exactly one split");
+    if (((uintptr_t)parts & 15) || ((uintptr_t)out & 15) || ((uintptr_t)gate & 15) ||
+        ((uintptr_t)q_in & 15) || ((uintptr_t)k_in & 15) || ((uintptr_t)v_in & 15))
+        return fail(err, errlen,
+                    "vx27_gqa_decode_fused: q_in, k_in, v_in, gate, out and the workspace must be "
+                    "16-byte aligned");
+    if (rope_dim < 0 || rope_dim > HDIM || (rope_dim & 15))
+        return fail(err, errlen, "vx27_gqa_decode_fused: rope_dim=%d (a multiple of 16 up to 256)",
+                    rope_dim);
+    TcAppend ap{};
+    ap.q_in = q_in;
+    ap.k_in = k_in;
+    ap.v_in = v_in;
+    ap.qw = qw;
+    ap.kw = kw;
+    ap.rope = rope;
+    ap.kc = (uint16_t *)kc;
+    ap.vc = (uint16_t *)vc;
+    ap.rope_len = rope_len;
+    ap.rope_dim = rope_dim;
+    ap.eps = eps;
+    ap.one_p = (flags & VX27_F_NORM_1P) ? 1 : 0;
+    return launch_tc(kc, vc, nullptr, pos, parts, cap, B, nq, nkv, n_splits, 0, -1, gate, out,
+                     flags, ap, dev_status(), true, st, err, errlen);
 }
 
 // Same launch with an explicit device status word (null: timeouts end the waits without
@@ -601,32 +843,8 @@ int launch_split_tc_status(const void *kc, const void *vc, const float *q, const
                            uint32_t *status, cudaStream_t st, char *err, size_t errlen) {
     if (((uintptr_t)parts & 15) || ((uintptr_t)q & 7))
         return fail(err, errlen, "vx27_gqa: q must be 8-byte aligned and the records 16-byte aligned");
-    CUtensorMap mk, mv, mk32, mv32;
-    const uint64_t rows = (uint64_t)B * nkv * cap;
-    if (make_tmap_bf16_2d(&mk, kc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
-        make_tmap_bf16_2d(&mv, vc, rows, HDIM, HDIM * 2, 64, TC_TILE, err, errlen) ||
-        make_tmap_bf16_2d(&mk32, kc, rows, HDIM, HDIM * 2, 64, 32, err, errlen) ||
-        make_tmap_bf16_2d(&mv32, vc, rows, HDIM, HDIM * 2, 64, 32, err, errlen))
-        return -1;
-    const size_t smem = tc_smem_bytes();
-    const dim3 grid(tc_grid(B, nkv, n_splits));
-#define VX_TCS(GG)                                                                        \
-    case GG: {                                                                            \
-        if (ensure_smem_attr((const void *)gqa_split_tc<GG>, smem, err, errlen))          \
-            return -1;                                                                    \
-        gqa_split_tc<GG><<<grid, TC_THREADS, smem, st>>>(mk, mv, mk32, mv32, q, pos, parts, cap, \
-                                                         B, nq, nkv, n_splits, 0, -1,      \
-                                                         nullptr, nullptr, 0, status);     \
-        break;                                                                            \
-    }
-    switch (nq / nkv) {
-        VX_TCS(1) VX_TCS(2) VX_TCS(4) VX_TCS(6) VX_TCS(8)
-        default:
-            return fail(err, errlen, "vx27_gqa: group size %d (nq/nkv) unsupported", nq / nkv);
-    }
-#undef VX_TCS
-    VX_CK(cudaGetLastError());
-    return 0;
+    return launch_tc(kc, vc, q, pos, parts, cap, B, nq, nkv, n_splits, 0, -1, nullptr, nullptr, 0,
+                     TcAppend{}, status, false, st, err, errlen);
 }
 
 // ---- host: tensor maps ---------------------------------------------------------------

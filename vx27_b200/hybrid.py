@@ -39,6 +39,9 @@ class HybridConfig:
     theta: float = 1e7
     eps: float = 1e-6
     seed: int = 2
+    # GQA layers: QK norm + RoPE + K/V append as their own kernel before the split-KV
+    # decode (False), or fused into it (vx27_gqa_decode_fused, True)
+    fused_gqa: bool = False
 
     @property
     def cap(self) -> int:
@@ -139,15 +142,7 @@ class HybridDecoder:
                     on_layer("dn", i, "post")
                 n += 1
             else:
-                ops.gqa_append(self.q_in[i], self.k_in[i], self.v_in[i], self.q_norm_w[i],
-                               self.k_norm_w[i], self.rope, self.pos, self.kc[i], self.vc[i],
-                               self.qn, eps=c.eps, stream=stream)
-                if on_layer:
-                    on_layer("gqa", i, "pre")
-                n += 1 + ops.gqa_decode_batch(self.qn, self.gate[i], self.kc[i], self.vc[i],
-                                              self.pos, self.att_out[i], self.ws, stream=stream)
-                if on_layer:
-                    on_layer("gqa", i, "post")
+                n += self._gqa_layer(i, stream, on_layer)
         ops.add_int(self.pos, 1, stream=stream)
         return n + 1
 
@@ -203,11 +198,7 @@ class HybridDecoder:
                                           stream=comp, prefetch_state=True)
                 n += 1
             else:
-                ops.gqa_append(self.q_in[i], self.k_in[i], self.v_in[i], self.q_norm_w[i],
-                               self.k_norm_w[i], self.rope, self.pos, self.kc[i], self.vc[i],
-                               self.qn, eps=c.eps, stream=comp)
-                n += 1 + ops.gqa_decode_batch(self.qn, self.gate[i], self.kc[i], self.vc[i],
-                                              self.pos, self.att_out[i], self.ws, stream=comp)
+                n += self._gqa_layer(i, comp)
             done = torch.cuda.Event()
             done.record(comp)
             self._done[L] = done
@@ -223,6 +214,30 @@ class HybridDecoder:
         return n + 1
 
     # -------------------------------------------------------------- accounting
+    def _gqa_layer(self, i: int, stream, on_layer=None) -> int:
+        """One GQA layer's decode; returns the kernels launched. on_layer brackets the
+        split-KV decode kernel (with the prologue fused in, that is the whole layer)."""
+        c = self.cfg
+        n = 0
+        if not c.fused_gqa:
+            ops.gqa_append(self.q_in[i], self.k_in[i], self.v_in[i], self.q_norm_w[i],
+                           self.k_norm_w[i], self.rope, self.pos, self.kc[i], self.vc[i],
+                           self.qn, eps=c.eps, stream=stream)
+            n += 1
+        if on_layer:
+            on_layer("gqa", i, "pre")
+        if c.fused_gqa:
+            n += ops.gqa_decode_fused(self.q_in[i], self.k_in[i], self.v_in[i], self.q_norm_w[i],
+                                      self.k_norm_w[i], self.rope, self.gate[i], self.kc[i],
+                                      self.vc[i], self.pos, self.att_out[i], self.ws, eps=c.eps,
+                                      stream=stream)
+        else:
+            n += ops.gqa_decode_batch(self.qn, self.gate[i], self.kc[i], self.vc[i], self.pos,
+                                      self.att_out[i], self.ws, stream=stream)
+        if on_layer:
+            on_layer("gqa", i, "post")
+        return n
+
     def bytes_per_step(self, ctx_attended: float) -> dict[str, float]:
         """Algorithmic HBM bytes of one step when each sequence attends ctx_attended
         positions: state read+write, conv history, KV read, activations in/out."""

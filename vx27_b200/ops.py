@@ -358,6 +358,42 @@ def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: i
     return 1 if n_splits == 1 else 2
 
 
+def gqa_decode_fused(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, gate, k_cache, v_cache, pos,
+                     out, workspace, eps: float = 1e-6, norm_one_plus: bool = False,
+                     n_splits: int = 0, stream=None) -> int:
+    """gqa_append + gqa_decode_batch as one kernel (vx27_gqa_decode_fused): the new token's
+    K/V rows land in the caches at pos[b] and out gets the gated attention; returns the
+    kernels launched (1 with one split, 2 with a combine)."""
+    B, nq, hd = q_in.shape
+    nkv, cap = k_cache.shape[1], k_cache.shape[2]
+    f32, bf16, i32, _, _ = _dt()
+    _need(q_in, "q_in", B * nq * hd, (f32, bf16))
+    _need(k_in, "k_in", B * nkv * hd, (q_in.dtype,))
+    _need(v_in, "v_in", B * nkv * hd, (q_in.dtype,))
+    _need(gate, "gate", B * nq * hd, (q_in.dtype,), optional=True)
+    _need(q_norm_w, "q_norm_w", hd, (f32,))
+    _need(k_norm_w, "k_norm_w", hd, (f32,))
+    _need(rope, "rope", 1, (f32,))
+    _need(pos, "pos", B, (i32,))
+    _need(k_cache, "k_cache", B * nkv * cap * hd, (bf16,))
+    _need(v_cache, "v_cache", B * nkv * cap * hd, (bf16,))
+    _need(out, "out", B * nq * hd, (f32, bf16))
+    flags = (F_ACT_BF16 if _is_bf16(q_in) else 0) | (F_OUT_BF16 if _is_bf16(out) else 0) | \
+        (F_NORM_1P if norm_one_plus else 0)
+    ws_bytes = workspace.numel() * workspace.element_size()
+    e = errbuf()
+    rc = load().vx27_gqa_decode_fused(_t(q_in), _t(k_in), _t(v_in), _t(q_norm_w), _t(k_norm_w),
+                                      _t(rope), rope.shape[0], _t(gate), _t(k_cache),
+                                      _t(v_cache), cap, _t(pos), _t(out), _t(workspace),
+                                      ws_bytes, B, nq, nkv, hd, rope.shape[1], eps, n_splits,
+                                      flags, _stream(stream), e, 512)
+    check(rc, e)
+    if n_splits <= 0:
+        rec = B * nq * (hd + 2) * 4
+        n_splits = min(gqa_workspace_bytes(B, nq, nkv, hd, cap) // rec, ws_bytes // rec)
+    return 1 if n_splits == 1 else 2
+
+
 def gqa_partial_workspace_bytes(B: int, nq: int, nkv: int, hd: int, max_range: int) -> int:
     return load().vx27_gqa_partial_workspace_size(B, nq, nkv, hd, max_range)
 
