@@ -36,7 +36,7 @@ METRIC = "DeltaNet+GQA decode tokens/s at 1/2/4/8 B200; % of HBM roofline"
 # ncu capture of the same kernel at 32 sequences (the full 256-sequence workload holds
 # 83 GB, too much to profile): each K/V byte is read once; the last tile of every
 # (sequence, KV head) fetches only the 32-row boxes it needs.
-GQA_SPLIT_DRAM_PER_ALGO_BYTE = 1.012
+GQA_SPLIT_DRAM_PER_ALGO_BYTE = 1.011
 FALLBACK_HBM_GBS = 6650.0
 
 
