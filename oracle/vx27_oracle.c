@@ -248,7 +248,7 @@ static void dn_conv_seq(const dn_job *j, int bi, float *y) {
     const int t = j->pos[bi];
     float *ring = j->ring + (size_t)bi * 4 * C;
     float *st = (float *)malloc((size_t)C * 3 * sizeof(float));
-    float *x = (float *)malloc((size_t)C * sizeof(float));
+    float *x = (float *)calloc((size_t)C, sizeof(float));
     for (int c = 0; c < C; c++) {
         st[(size_t)c * 3 + 0] = ring[(size_t)((t - 3) & 3) * C + c];
         st[(size_t)c * 3 + 1] = ring[(size_t)((t - 2) & 3) * C + c];
