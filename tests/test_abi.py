@@ -97,6 +97,14 @@ def test_batched_entry_points_reject_bad_shapes_without_gpu(vxlib):
                                      256, 0, 0, None, err, 256)
     assert rc == -1 and b"bad shape" in err.value
     assert vxlib.vx27_gqa_decode_workspace_size(2, 24, 4, 256, 4096, 3) == 3 * 2 * 24 * 258 * 4
+    rc = vxlib.vx27_pmat_multi_dev(5, None, 4, None, None, None, 128, 1, None, err, 256)
+    assert rc == -1 and b"n=5 projections" in err.value
+    # the fused decode: a RoPE width that 8-dim lanes cannot pair up (checked before any
+    # CUDA call; the pointers are never dereferenced)
+    rec = 1 * 24 * 258 * 4
+    rc = vxlib.vx27_gqa_decode_fused(16, 16, 16, 16, 16, 16, 64, None, 16, 16, 64, 16, 16, 16, rec,
+                                     1, 24, 4, 256, 20, 1e-6, 1, 0, None, err, 256)
+    assert rc == -1 and b"rope_dim=20" in err.value
 
 
 def test_ddmath_host_matches_c_library_nearly_always():
@@ -158,3 +166,26 @@ def test_wrappers_reject_wrong_dtypes_and_sizes_before_any_launch():
     with pytest.raises(ops.Vx27Error, match="expected a contiguous CUDA tensor"):
         ops.deltanet_decode_batch(S, ring, qkv.float(), a, a, torch.zeros(nv), torch.zeros(nv),
                                   torch.zeros(C_, 4), pos, torch.zeros(B, nv, 128), nqk, nv)
+    # the fused GQA decode: activations of one dtype, caches bf16
+    q_in = torch.zeros(B, nq, hd, dtype=torch.bfloat16)
+    kv_in = torch.zeros(B, nkv, hd, dtype=torch.bfloat16)
+    w = torch.zeros(hd)
+    rope = torch.zeros(cap, 64)
+    with pytest.raises(ops.Vx27Error, match="k_in: dtype"):
+        ops.gqa_decode_fused(q_in, kv_in.float(), kv_in, w, w, rope, q_in, kc, kc, pos, out, ws)
+    with pytest.raises(ops.Vx27Error, match="gate: dtype"):
+        ops.gqa_decode_fused(q_in, kv_in, kv_in, w, w, rope, q_in.float(), kc, kc, pos, out, ws)
+    with pytest.raises(ops.Vx27Error, match="v_cache: .* elements"):
+        ops.gqa_decode_fused(q_in, kv_in, kv_in, w, w, rope, q_in, kc, kc[:1], pos, out, ws)
+    # grouped projections: one output and one row count per weight set, at most four
+    x = torch.zeros(B, 1024)
+    Wb = torch.zeros(10 * 8 * 52, dtype=torch.uint8)
+    y = torch.zeros(B, 10)
+    with pytest.raises(ops.Vx27Error, match="1..4 projections"):
+        ops.pmat_multi([Wb] * 5, ops.PMAT_BP3_128, x, [y] * 5, [10] * 5, 1024)
+    with pytest.raises(ops.Vx27Error, match="1..4 projections"):
+        ops.pmat_multi([Wb, Wb], ops.PMAT_BP3_128, x, [y], [10, 10], 1024)
+    with pytest.raises(ops.Vx27Error, match="fewer than 11 packed rows"):
+        ops.pmat_multi([Wb], ops.PMAT_BP3_128, x, [torch.zeros(B, 11)], [11], 1024)
+    with pytest.raises(ops.Vx27Error, match=r"y\[0\]: .* elements"):
+        ops.pmat_multi([Wb], ops.PMAT_BP3_128, x, [y[:1]], [10], 1024)
