@@ -127,10 +127,11 @@ __device__ __forceinline__ uint4 pack8_bf16(const float (&x)[8]) {
 
 // One 256-dim row held 8 dims per lane (dims 8*lane ..): RMSNorm then the rotation, as
 // gqa_append_k rounds them; rr = the position's rope row, NULL for none (bad position).
-// Not inlined: one copy of this code serves all rows, which keeps the staging warp's code
-// from crowding the instruction cache the other roles' loops share (measured: inlined
-// eight times it slowed a config 2 layer by 1.5%).
-__device__ __noinline__ void tc_norm_rope(float (&y)[8], const float (&x)[8],
+// Inlined into a row loop that is not unrolled: one copy of the code serves all rows, so
+// the staging warp's code does not crowd the instruction cache the other roles' loops
+// share (inlined and unrolled eight times it slowed a config 2 layer by 1.5%), and no call
+// saves and restores registers (as a called function it took ~14 us per item).
+__device__ __forceinline__ void tc_norm_rope(float (&y)[8], const float (&x)[8],
                                              const float *w, const TcAppend &ap,
                                              const float *rr, int lane) {
     double ss = 0.0;
@@ -296,7 +297,7 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
                 x[h][4] = raw[h][1].x; x[h][5] = raw[h][1].y; x[h][6] = raw[h][1].z; x[h][7] = raw[h][1].w;
             }
         }
-#pragma unroll
+#pragma unroll 1
         for (int h = 0; h < G; h++) {
             float y[8], lo8[8];
             tc_norm_rope(y, x[h], ap.qw, ap, rr, lane);
