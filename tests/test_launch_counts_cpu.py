@@ -1,0 +1,33 @@
+"""Kernel counts the GQA wrappers report (they feed bench.py's gpu_launches): derived from
+the library's own split choice (vx27_gqa_decode_workspace_size and
+vx27_gqa_partial_workspace_size), so no GPU is needed."""
+from vx27_b200 import ops
+
+NQ, NKV, HD = 24, 4, 256
+REC = lambda B: B * NQ * (HD + 2) * 4
+
+
+def test_config2_decode_is_one_launch():
+    # 256 sequences x 4 KV heads fill the SMs: one split, the split kernel writes out
+    ws = ops.gqa_workspace_bytes(256, NQ, NKV, HD, 4160)
+    assert ws == REC(256)
+    assert ops.gqa_decode_launches(256, NQ, NKV, HD, 4160, ws) == 1
+
+
+def test_long_single_sequence_splits_and_combines():
+    ws = ops.gqa_workspace_bytes(1, NQ, NKV, HD, 8192)
+    assert ws > REC(1)  # several splits
+    assert ops.gqa_decode_launches(1, NQ, NKV, HD, 8192, ws) == 2
+    # a workspace of one record caps the library's choice at one split
+    assert ops.gqa_decode_launches(1, NQ, NKV, HD, 8192, REC(1)) == 1
+    # an explicit split count wins
+    assert ops.gqa_decode_launches(1, NQ, NKV, HD, 8192, ws, n_splits=1) == 1
+    assert ops.gqa_decode_launches(1, NQ, NKV, HD, 8192, ws, n_splits=3) == 2
+
+
+def test_partial_launches():
+    span = 131072
+    ws = ops.gqa_partial_workspace_bytes(1, NQ, NKV, HD, span)
+    assert ws > 0
+    assert ops.gqa_partial_launches(1, NQ, NKV, HD, span, ws) == 2
+    assert ops.gqa_partial_launches(1, NQ, NKV, HD, span, 0) == 1

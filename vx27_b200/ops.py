@@ -330,6 +330,25 @@ def gqa_workspace_bytes(B: int, nq: int, nkv: int, hd: int, max_ctx: int,
     return load().vx27_gqa_decode_workspace_size(B, nq, nkv, hd, max_ctx, n_splits)
 
 
+def gqa_decode_launches(B: int, nq: int, nkv: int, hd: int, cap: int, ws_bytes: int,
+                        n_splits: int = 0) -> int:
+    """Kernels one decode call launches: the library's split count (its own choice when
+    n_splits <= 0, capped by the workspace), then 1 for one split (the split kernel writes
+    the gated output) or 2 (split kernel + combine)."""
+    if n_splits <= 0:
+        rec = B * nq * (hd + 2) * 4
+        n_splits = min(gqa_workspace_bytes(B, nq, nkv, hd, cap) // rec, ws_bytes // rec)
+    return 1 if n_splits == 1 else 2
+
+
+def gqa_partial_launches(B: int, nq: int, nkv: int, hd: int, span: int, ws_bytes: int) -> int:
+    """Kernels one vx27_gqa_partial call over span slots launches: 2 when the workspace
+    lets it split the range (split kernel + merge), else 1."""
+    rec = B * nq * (hd + 2) * 4
+    n = min(gqa_partial_workspace_bytes(B, nq, nkv, hd, span) // rec, ws_bytes // rec)
+    return 2 if n > 1 else 1
+
+
 def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: int = 0,
                      stream=None) -> int:
     """Split-KV decode of one token per sequence (vx27_gqa_decode_batch); returns the
@@ -352,10 +371,7 @@ def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: i
                                       _t(out), _t(workspace), ws_bytes, B, nq, nkv, hd, n_splits,
                                       flags, _stream(stream), e, 512)
     check(rc, e)
-    if n_splits <= 0:  # the library's own choice, capped by the workspace
-        rec = B * nq * (hd + 2) * 4
-        n_splits = min(gqa_workspace_bytes(B, nq, nkv, hd, cap) // rec, ws_bytes // rec)
-    return 1 if n_splits == 1 else 2
+    return gqa_decode_launches(B, nq, nkv, hd, cap, ws_bytes, n_splits)
 
 
 def gqa_decode_fused(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, gate, k_cache, v_cache, pos,
@@ -388,10 +404,7 @@ def gqa_decode_fused(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, gate, k_cache, 
                                       ws_bytes, B, nq, nkv, hd, rope.shape[1], eps, n_splits,
                                       flags, _stream(stream), e, 512)
     check(rc, e)
-    if n_splits <= 0:
-        rec = B * nq * (hd + 2) * 4
-        n_splits = min(gqa_workspace_bytes(B, nq, nkv, hd, cap) // rec, ws_bytes // rec)
-    return 1 if n_splits == 1 else 2
+    return gqa_decode_launches(B, nq, nkv, hd, cap, ws_bytes, n_splits)
 
 
 def gqa_partial_workspace_bytes(B: int, nq: int, nkv: int, hd: int, max_range: int) -> int:
@@ -414,9 +427,7 @@ def gqa_partial(q, k_cache, v_cache, p_begin: int, p_end: int, part, workspace=N
     rc = load().vx27_gqa_partial(_t(q), _t(k_cache), _t(v_cache), cap, p_begin, p_end, _t(part),
                                  B, nq, nkv, hd, _t(workspace), ws_bytes, _stream(stream), e, 512)
     check(rc, e)
-    rec = B * nq * (hd + 2) * 4
-    n = min(gqa_partial_workspace_bytes(B, nq, nkv, hd, p_end - p_begin) // rec, ws_bytes // rec)
-    return 2 if n > 1 else 1
+    return gqa_partial_launches(B, nq, nkv, hd, p_end - p_begin, ws_bytes)
 
 
 def gqa_combine(parts, n_parts: int, gate, out, part_stride: int = 0, stream=None) -> None:
