@@ -76,3 +76,41 @@ def test_split_kv_exchange_on_two_cpu_ranks(tmp_path):
     for r in range(world):
         out, full = np.load(tmp_path / f"r{r}.npy")
         assert np.abs(out - full).max() <= 1e-5 * np.abs(full).max()
+
+
+def _leaving_rank_main(rank, world, port, out_dir):
+    import time
+    import torch
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    from vx27_b200.dist import gather_records, init_from_env
+    init_from_env("gloo", timeout_s=5)
+    if rank == 1:
+        os._exit(0)  # leaves between steps, with no collective of its own in flight
+    t0 = time.time()
+    try:
+        gather_records(torch.zeros(8), world)
+        res = "no-error"
+    except Exception as e:  # the collective must end with an error, not hang
+        res = type(e).__name__
+    with open(os.path.join(out_dir, "r0.txt"), "w") as f:
+        f.write(f"{res} {time.time() - t0:.1f}")
+    os._exit(0)
+
+
+def test_a_rank_that_leaves_ends_the_others_collective_with_an_error(tmp_path):
+    """Failure detection on the host: a rank exits between steps; the surviving rank's
+    next all-gather (the config 3b exchange) fails within the short process-group timeout
+    instead of waiting forever."""
+    import time
+    import torch.multiprocessing as mp
+    ctx = mp.start_processes(_leaving_rank_main, args=(2, _free_port(), str(tmp_path)),
+                             nprocs=2, join=False, start_method="spawn")
+    deadline = time.time() + 120
+    while not ctx.join(timeout=1):
+        if time.time() > deadline:
+            for p in ctx.processes:
+                p.kill()
+            pytest.fail("the surviving rank did not return")
+    res, secs = (tmp_path / "r0.txt").read_text().split()
+    assert res != "no-error" and float(secs) < 60, (res, secs)
