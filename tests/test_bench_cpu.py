@@ -41,3 +41,20 @@ def test_clock_window_and_reasons():
     assert s["samples"] == 4 and s["reasons"] == ["sw_power_cap", "sw_thermal_slowdown"]
     c.lines = []
     assert c.summary()["reasons"] == ["unsampled"]
+
+
+def test_reference_arm_line():
+    """`bench.py --impl reference` (the reference's own CPU code, on the host cores) prints
+    one JSON line with the metric of our arm and its CPU-baseline description."""
+    import json
+    import subprocess
+    import sys
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                          "--steps", "1", "--warmup", "0", "--ref-seqs", "1"],
+                         capture_output=True, text=True, timeout=600, cwd=ROOT, check=True).stdout
+    d = json.loads([ln for ln in out.splitlines() if ln.startswith("{")][-1])
+    assert d["impl"] == "reference" and d["metric"].startswith("DeltaNet+GQA decode tokens/s")
+    assert d["value"] > 0 and d["unit"] == "tokens/s" and d["higher_is_better"] is True
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["kind"] in ("reference", "port") and cb["cores"] >= 1
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["value"] == d["value"]
