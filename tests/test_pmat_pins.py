@@ -86,3 +86,32 @@ def test_bp3_special_scales_and_inputs(refpmat, B):
     assert np.array_equal(on, rn)
     assert np.array_equal(y_orc[~on].view(np.uint32), y_ref[~rn].view(np.uint32))
     assert np.isfinite(y_ref).sum() > rows * B // 3
+
+
+@pytest.mark.parametrize("dtype", [O.PMAT_F32, O.PMAT_Q8K])
+def test_special_values_other_formats(refpmat, dtype):
+    # Q8_K block scales d of zero, negative, huge, infinite and NaN; F32 weights with the
+    # same specials; inputs with signed zeros and subnormals: bit-identical (NaN as NaN)
+    rows, cols, B = 24, 1024, 3
+    W = O.packed_weights(dtype, rows, cols, 66).copy()
+    rng = np.random.default_rng(67)
+    specials = np.array([0.0, -0.0, -1e-3, 3e38, -3e38, np.inf, -np.inf, np.nan], np.float32)
+    if dtype == O.PMAT_Q8K:
+        blk = W.reshape(-1, 292)
+        pick = rng.random(len(blk)) < 0.3
+        d = rng.choice(specials, int(pick.sum())).astype(np.float32)
+        blk[pick, 0:4] = d.view(np.uint8).reshape(-1, 4)
+    else:
+        w = W.view(np.float32)
+        pick = rng.random(w.size) < 0.001
+        w[pick] = rng.choice(specials, int(pick.sum()))
+    x = rng.standard_normal(B * cols).astype(np.float32)
+    x[rng.random(x.size) < 0.05] = -0.0
+    x[rng.random(x.size) < 0.05] = np.float32(1e-40)
+    y_orc = O.pmat_batch(W, dtype, x, rows, cols, B)
+    y_ref = np.empty(B * rows, np.float32)
+    refpmat.vx27_pmat_batch(None, O.P(W), dtype, O.P(x), O.P(y_ref), rows, cols, B)
+    on, rn = np.isnan(y_orc), np.isnan(y_ref)
+    assert np.array_equal(on, rn)
+    assert np.array_equal(y_orc[~on].view(np.uint32), y_ref[~rn].view(np.uint32))
+    assert np.isfinite(y_ref).sum() > rows * B // 4
