@@ -89,21 +89,26 @@ int vx27_gqa_decode_fused(const void *q_in, const void *k_in, const void *v_in,
 
 /*
  * No counterpart in the reference. vx27_gqa_decode_batch without the workspace: same
- * arguments, same kernels and results, but the split partial records go to a fixed
- * array of VX27_GQA_NOALLOC_SCRATCH_BYTES in the library's own device memory, and the
- * call itself allocates nothing (no cudaMalloc, no cudaFree, no allocating library call).
+ * arguments, same split count (n_splits = 0 picks vx27_gqa_decode_batch's automatic count,
+ * capped by the array below), same kernels and results, but the split partial records go
+ * to a fixed array of VX27_GQA_NOALLOC_SCRATCH_BYTES in the library's own device memory,
+ * and the call itself allocates nothing (no cudaMalloc, no cudaFree, no allocating library
+ * call). A bounded wait that times out is recorded in the device status word
+ * (vx27cuda_device_status), which is a module global as well.
  * It is for callers that cannot provide device scratch: an engine that has already
  * handed all free device memory to its KV cache and weights, or a host that reaches this
  * library through a fixed C interface (such as the reference's) that has no workspace
  * argument and no way to own a device buffer.
  * Limits and rules:
- *  - the array is 8 MiB and is reserved on every GPU that loads the library, until the
- *    process exits; one split's records take B*nq*(hd+2)*4 bytes, so a call needs
- *    n_splits*B*nq*(hd+2)*4 <= 8 MiB (n_splits = 0 picks the largest automatic count
- *    that fits; a batch whose single record does not fit is rejected with an error);
+ *  - the array is 8 MiB and is held on every GPU where the library's module is loaded,
+ *    until the process exits; one split's records take B*nq*(hd+2)*4 bytes, so a call
+ *    needs n_splits*B*nq*(hd+2)*4 <= 8 MiB (a batch whose single record does not fit, or
+ *    an explicit n_splits beyond the array, is rejected with an error);
  *  - the first call on a device, made with that device current, looks up the array's
- *    device address (cudaGetSymbolAddress); make that first call before any stream
- *    capture;
+ *    device address (cudaGetSymbolAddress); with CUDA's lazy module loading (the default)
+ *    that lookup may also be what loads the module and reserves the 8 MiB, so it can fail
+ *    for lack of device memory: make the first call during set-up, before the KV cache
+ *    takes the remaining memory, and before any stream capture;
  *  - all calls on a device share the array and it keeps the last call's contents: two
  *    calls whose kernels overlap on the GPU (different streams, no ordering) race and
  *    both results are undefined; calls ordered on one stream are safe.

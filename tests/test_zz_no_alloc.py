@@ -1,9 +1,10 @@
 """vx27_gqa_decode_batch_noalloc, the decode entry point for callers that cannot give the
 library device scratch (their device memory is already spoken for, or they reach the
 library through a C interface with no workspace argument). Called through the C ABI and
-checked against vx27_gqa_decode_batch, which takes a caller workspace, on two calls in a
-row with different inputs, so contents left in the shared static scratch by the first
-call cannot leak into the second. This file sorts last so a run that stops at the first
+checked on three calls in a row with different inputs against vx27_gqa_decode_batch, which
+takes a caller workspace (bit for bit: same split count, same kernels), and against the
+CPU oracle, so contents left in the shared static scratch by one call cannot leak into the
+next. This file sorts last so a run that stops at the first
 failure has run every other test before it."""
 import ctypes as C
 
@@ -11,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import dev, rel_err
+from gpu_util import dev, host, rel_err
 from vx27_b200 import ops
 from vx27_b200._lib import errbuf, load
 
@@ -48,12 +49,24 @@ def _noalloc(q, gate, kc, vc, pos, n_splits, out):
     return rc, e.value.decode(), out
 
 
+def _oracle(orc, q, gate, kc, vc, pos):
+    """The reference's decode attention (src/vx27_qfwd.c:347-371) over the same bf16 cache."""
+    L, P = orc.lib(), orc.P
+    B, cap = q.shape[0], kc.shape[2]
+    h = lambda t: host(t).reshape(-1)
+    out = np.zeros(B * NQ * HD, np.float32)
+    L.orc_gqa_attend_mt(P(h(q)), P(h(gate)), P(h(kc)), P(h(vc)), cap, P(h(pos)), P(out), B, NQ,
+                        NKV, HD, orc.F_ACT_BF16, 8)
+    return out
+
+
 def test_noalloc_matches_workspace_entry_point_twice(cuda, orc):
     calls = [(71, 3, 700, [699, 5, 300], 4),    # first call: 4 splits, ragged positions
-             (72, 2, 1100, [1099, 0], 0)]       # second: other shapes, automatic splits
+             (72, 2, 1100, [1099, 0], 0),       # second: other shapes, automatic splits
+             (74, 1, 200, [150], 1)]            # one split: the kernel writes out directly
     for n, (seed, B, cap, pos, n_splits) in enumerate(calls):
         x = _inputs(orc, seed, B, cap, pos)
-        ref = _with_workspace(*x, n_splits).cpu().numpy()
+        ref = _with_workspace(*x, n_splits).cpu().numpy().reshape(-1)
         out = torch.empty(x[0].shape[0], NQ, HD, device="cuda")
         torch.cuda.synchronize()
         free_before = torch.cuda.mem_get_info()[0]
@@ -62,7 +75,11 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda, orc):
         assert rc == 0, msg
         if n > 0:  # the device symbol is resolved on the first call; later calls allocate nothing
             assert torch.cuda.mem_get_info()[0] == free_before
-        assert rel_err(out.cpu().numpy().reshape(-1), ref.reshape(-1)) < TOL
+        got = out.cpu().numpy().reshape(-1)
+        # same split count and kernels as the workspace entry point: the same bits
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        assert rel_err(got, _oracle(orc, *x)) < TOL
+        assert ops.device_status() == 0
 
 
 def test_noalloc_rejects_batches_beyond_the_static_scratch(cuda, orc):

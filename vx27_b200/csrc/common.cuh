@@ -73,7 +73,8 @@ __device__ __forceinline__ float ex2_approx(float x) {
 #define VX_SPIN_LIMIT (1u << 26)
 enum : uint32_t { VX_DEV_OK = 0, VX_DEV_TIMEOUT_TMA = 1, VX_DEV_TIMEOUT_MMA = 2,
                   VX_DEV_BAD_ARG = 3 };
-// Device pointer of the status word of the current device (allocated on first use).
+// Device pointer of the status word of the current device: a module global, its address
+// looked up on first use (no allocation).
 uint32_t *dev_status();
 
 __device__ __forceinline__ void dev_flag(uint32_t *st, uint32_t code) {

@@ -18,7 +18,7 @@
 //    within a few ulps works): log y = l0 + log1p(y e^-l0 - 1), with the correction
 //    computed in double-double.
 // Results in the subnormal range (x < -708.39 for exp) may be double-rounded.
-// Constants: ln2 split and 1/n! as double-double pairs, produced by gen_ddconst.py.
+// Constants: ln2 split and 1/n! as double-double pairs, produced by tests/gen_ddconst.py.
 //
 // Every operation goes through the macros below so that no compiler contraction into
 // FMA changes rounding between the host and the device builds.

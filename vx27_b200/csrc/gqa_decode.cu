@@ -208,7 +208,10 @@ int check_shape(const char *fn, int B, int nq, int nkv, int hd, char *err, size_
 
 }  // namespace
 
-// The combine launch for other translation units (gqa_noalloc.cu); no allocation.
+// The split-count choice and the combine launch for other translation units
+// (gqa_noalloc.cu); neither allocates.
+int gqa_auto_splits(int B, int nkv, int max_ctx) { return auto_splits(B, nkv, max_ctx); }
+
 int launch_gqa_combine(const float *parts, int n_parts, const void *gate, void *out, int B,
                        int nq, int flags, cudaStream_t st, char *err, size_t errlen) {
     return launch_combine(parts, n_parts, gate, out, B, nq, flags, st, err, errlen);

@@ -3,20 +3,26 @@
 // allocate one. Its partial (m, l, o) records live in a fixed array in the module's own
 // global memory instead of a caller workspace or a cudaMalloc.
 //
-// The array below is reserved on every GPU that loads this library and stays reserved
-// until the process exits. In host code its name is only a host-side stand-in for the
-// device symbol, so the device address is looked up once per device with
-// cudaGetSymbolAddress (on the first call made while that device is current) and that
-// address is what the kernels receive.
+// The array below is held on every GPU where this library's module is loaded, until the
+// process exits. With CUDA's lazy module loading (the default since CUDA 12) the module,
+// and with it the array, may be loaded only by the first call on a device, so that call
+// can fail for lack of device memory; callers make it during their set-up, before they
+// hand the rest of the memory to a KV cache. In host code the array's name is only a
+// host-side stand-in for the device symbol, so the device address is looked up once per
+// device with cudaGetSymbolAddress (on the first call made while that device is current)
+// and that address is what the kernels receive.
+#include <mutex>
 #include "common.cuh"
 #include "../../include/vx27_gqa.h"
 
 namespace vx27 {
-int launch_split_tc_status(const void *kc, const void *vc, const float *q, const int *pos,
-                           float *parts, int cap, int B, int nq, int nkv, int n_splits,
-                           uint32_t *status, cudaStream_t st, char *err, size_t errlen);
+int launch_split_tc(const void *kc, const void *vc, const float *q, const int *pos, float *parts,
+                    int cap, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
+                    cudaStream_t st, char *err, size_t errlen, const void *gate, void *out,
+                    int flags);
 int launch_gqa_combine(const float *parts, int n_parts, const void *gate, void *out, int B,
                        int nq, int flags, cudaStream_t st, char *err, size_t errlen);
+int gqa_auto_splits(int B, int nkv, int max_ctx);
 }  // namespace vx27
 
 namespace {
@@ -25,7 +31,7 @@ namespace {
 static __device__ __align__(256) unsigned char g_gqa_scratch[VX27_GQA_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-constexpr int kTile = 128;  // split boundaries fall on multiples of 128 cache slots
+std::mutex g_scratch_mu;  // guards addr[] below: several host threads may make first calls
 
 // Device address of g_gqa_scratch on the current device, looked up on first use.
 float *scratch_on_current_device(char *err, size_t errlen) {
@@ -38,6 +44,7 @@ float *scratch_on_current_device(char *err, size_t errlen) {
     if (dev < 0 || dev >= kMaxDevices)
         return (vx27::fail(err, errlen, "vx27_gqa_decode_batch_noalloc: device %d out of range",
                            dev), nullptr);
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
     if (!addr[dev]) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_gqa_scratch);
@@ -71,14 +78,9 @@ extern "C" int vx27_gqa_decode_batch_noalloc(const float *q, const void *gate,
                     "scratch (B*nq*(hd+2)*4 must be <= %u)",
                     fn, record, (unsigned)VX27_GQA_NOALLOC_SCRATCH_BYTES,
                     (unsigned)VX27_GQA_NOALLOC_SCRATCH_BYTES);
-    if (n_splits <= 0) {
-        const int blocks = B * nkv;
-        n_splits = (2 * num_sms() + blocks - 1) / blocks;
-        const int by_ctx = (cap + kTile - 1) / kTile;
-        if (n_splits > by_ctx) n_splits = by_ctx;
-        if (n_splits > 128) n_splits = 128;
+    if (n_splits <= 0) {  // the workspace entry point's choice, capped by the array
+        n_splits = gqa_auto_splits(B, nkv, cap);
         if (n_splits > fit) n_splits = fit;
-        if (n_splits < 1) n_splits = 1;
     } else if (n_splits > fit || n_splits > 65535) {
         return fail(err, errlen,
                     "%s: %d splits need %zu bytes of partial records, more than the %u-byte "
@@ -89,10 +91,14 @@ extern "C" int vx27_gqa_decode_batch_noalloc(const float *q, const void *gate,
     float *parts = scratch_on_current_device(err, errlen);
     if (!parts) return -1;
     // Every record the combine reads is written by the split kernel first (empty ranges
-    // write a neutral record), so nothing left from an earlier call needs clearing.
+    // write a neutral record), so nothing left from an earlier call needs clearing. With
+    // one split the kernel writes the gated output itself, as vx27_gqa_decode_batch does.
     cudaStream_t st = (cudaStream_t)stream;
-    if (launch_split_tc_status(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, n_splits,
-                               nullptr, st, err, errlen))
+    if (n_splits == 1)
+        return launch_split_tc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, 1, 0, -1, st,
+                               err, errlen, gate, out, flags);
+    if (launch_split_tc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, n_splits, 0, -1, st,
+                        err, errlen, nullptr, nullptr, 0))
         return -1;
     return launch_gqa_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen);
 }

@@ -837,17 +837,6 @@ int launch_split_tc_fused(const void *q_in, const void *k_in, const void *v_in,
                      flags, ap, dev_status(), true, st, err, errlen);
 }
 
-// Same launch with an explicit device status word (null: timeouts end the waits without
-// being recorded). Touches no allocator, for the entry point that allocates nothing.
-int launch_split_tc_status(const void *kc, const void *vc, const float *q, const int *pos,
-                           float *parts, int cap, int B, int nq, int nkv, int n_splits,
-                           uint32_t *status, cudaStream_t st, char *err, size_t errlen) {
-    if (((uintptr_t)parts & 15) || ((uintptr_t)q & 7))
-        return fail(err, errlen, "vx27_gqa: q must be 8-byte aligned and the records 16-byte aligned");
-    return launch_tc(kc, vc, q, pos, parts, cap, B, nq, nkv, n_splits, 0, -1, nullptr, nullptr, 0,
-                     TcAppend{}, status, false, st, err, errlen);
-}
-
 // ---- host: tensor maps ---------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,

@@ -15,16 +15,20 @@ namespace vx27 {
 
 static std::mutex g_rt_mu;  // guards the per-device caches below
 
+// The status word lives in the module's own global memory (zero at module load), one per
+// device, so reading its address allocates nothing: entry points that must not allocate
+// report their timeouts here too.
+static __device__ uint32_t g_dev_status;
+
 uint32_t *dev_status() {
     static uint32_t *ptrs[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
     std::lock_guard<std::mutex> lock(g_rt_mu);
     if (!ptrs[dev]) {
-        uint32_t *p = nullptr;
-        if (cudaMalloc((void **)&p, sizeof(uint32_t)) != cudaSuccess) return nullptr;
-        if (cudaMemset(p, 0, sizeof(uint32_t)) != cudaSuccess) return nullptr;
-        ptrs[dev] = p;
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_dev_status) != cudaSuccess || !p) return nullptr;
+        ptrs[dev] = (uint32_t *)p;
     }
     return ptrs[dev];
 }
