@@ -528,7 +528,7 @@ def pmat_cpu_baseline() -> dict | None:
 
 
 # ------------------------------------------------- configs 0 and 1 (batch-1 latency)
-def run_batch1(args) -> dict:
+def run_batch1(args, cpu: bool = True) -> dict:
     """Config 0: one DeltaNet layer decoding 2000 tokens of one sequence (16 heads, fp32
     activations, seed 0); config 1: one gated GQA single-query decode at context 8192
     (seed 1). Both are latency-bound at batch 1: the line reports microseconds per token,
@@ -619,6 +619,21 @@ def run_batch1(args) -> dict:
     del graph
     if ops.device_status() != 0:
         raise RuntimeError("device status flag set during the batch-1 run")
+    gbs = bytes_per_unit / (us_graph * 1e-6) / 1e9
+    line = {
+        "metric": f"microseconds per {unit_name} ({args.workload}, batch 1)",
+        "value": round(us_graph, 3), "unit": f"us/{unit_name}", "n_gpus": 1,
+        "steps": reps, "warmup": args.warmup, "higher_is_better": False, "dtype": "f32",
+        "data": "synthetic (seeded, BASELINE.json distributions)",
+        "config": {"workload": name},
+        "us_per_unit_launched": round(us_launch, 3), "us_per_unit_graph": round(us_graph, 3),
+        "roofline": {"bound": "hbm (latency at batch 1)", "achieved": round(gbs, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
+                     "algorithmic_bytes_per_unit": bytes_per_unit, "peak_source": hbm_src},
+        "clocks": clk.summary(),
+    }
+    if not cpu:
+        return line
     # the reference's own code on the host (oracle/_ref when built, else the port)
     import os as _os
     import time as _time
@@ -658,21 +673,9 @@ def run_batch1(args) -> dict:
                                 0, threads)
         cpu_us = (_time.perf_counter() - t0) * 1e6 / n_cpu
         sample = f"{n_cpu} decodes over 8192 positions ({threads} threads)"
-    gbs = bytes_per_unit / (us_graph * 1e-6) / 1e9
-    return {
-        "metric": f"microseconds per {unit_name} ({args.workload}, batch 1)",
-        "value": round(us_graph, 3), "unit": f"us/{unit_name}", "n_gpus": 1,
-        "steps": reps, "warmup": args.warmup, "higher_is_better": False, "dtype": "f32",
-        "data": "synthetic (seeded, BASELINE.json distributions)",
-        "config": {"workload": name},
-        "us_per_unit_launched": round(us_launch, 3), "us_per_unit_graph": round(us_graph, 3),
-        "roofline": {"bound": "hbm (latency at batch 1)", "achieved": round(gbs, 1),
-                     "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
-                     "algorithmic_bytes_per_unit": bytes_per_unit, "peak_source": hbm_src},
-        "cpu_baseline": {"value": round(cpu_us, 2), "unit": f"us/{unit_name}",
-                         "cores": threads, "kind": kind, "sample": sample},
-        "clocks": clk.summary(),
-    }
+    line["cpu_baseline"] = {"value": round(cpu_us, 2), "unit": f"us/{unit_name}",
+                            "cores": threads, "kind": kind, "sample": sample}
+    return line
 
 
 # ------------------------------------------------- config 4 (prefill)
@@ -869,6 +872,39 @@ def run_longctx(args, rank: int, world: int, local: int) -> dict | None:
             "gpu_launches": launches, "cuda_graph": bool(args.graph)}
 
 
+# ------------------------------------------------- the other configs, briefly
+def other_configs(args) -> dict:
+    """Configs 1 and 4 on the same GPU after the config 2 timed region (its buffers freed):
+    the batch-1 GQA decode at context 8192 (replayed from a CUDA graph) and the 32768-token
+    prefill of one layer of each kind, each with its own clock samples."""
+    import copy
+    import torch
+    torch.cuda.empty_cache()
+    a1 = copy.copy(args)
+    a1.workload, a1.steps, a1.warmup = "config1", 200, 10
+    c1 = run_batch1(a1, cpu=False)
+    a4 = copy.copy(args)
+    a4.workload, a4.steps, a4.warmup = "config4", 5, 2
+    c4 = run_prefill(a4)
+    torch.cuda.empty_cache()
+    return {
+        "config1_decode_us": c1["value"],
+        "config1": {"us_per_decode_graph": c1["us_per_unit_graph"],
+                    "us_per_decode_launched": c1["us_per_unit_launched"],
+                    "roofline": c1["roofline"], "clocks": c1["clocks"]},
+        "config4_gqa_prefill": {"ms": c4["gqa_prefill"]["ms"],
+                                "tflops": c4["gqa_prefill"]["tflops"],
+                                "frac": c4["gqa_prefill"]["roofline"]["frac"],
+                                "peak": c4["gqa_prefill"]["roofline"]["peak"],
+                                "peak_source": c4["gqa_prefill"]["roofline"]["peak_source"]},
+        "config4_deltanet_prefill": {"ms": c4["deltanet_prefill"]["ms"],
+                                     "tflops": c4["deltanet_prefill"]["tflops"],
+                                     "hbm_frac": c4["deltanet_prefill"]["hbm_frac"]},
+        "config4_prompt_tokens_per_s": c4["value"],
+        "config4_clocks": c4["clocks"],
+    }
+
+
 # ------------------------------------------------------------ CPU reference
 def cpu_reference_step_sampler(n_seq: int, ctx: int, threads: int):
     """Builds host buffers for n_seq sequences of config 2 and returns (run_step, kind).
@@ -983,6 +1019,9 @@ def main() -> None:
     ap.add_argument("--ref-seqs", type=int, default=4)
     ap.add_argument("--cpu-seqs", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="config 2 at N = 1: skip the config 1 and config 4 figures added "
+                         "after its timed region")
     ap.add_argument("--fused-gqa", action="store_true",
                     help="config 2: GQA layers as one fused kernel (vx27_gqa_decode_fused) "
                          "instead of append + split-KV decode")
@@ -1037,6 +1076,8 @@ def main() -> None:
             return
         line = run_ours(args, rank, world, local_rank)
         if line is not None:
+            if world == 1 and not args.no_other_configs:
+                line["other_configs"] = other_configs(args)
             if world == 1 and not args.no_cpu_baseline:
                 line["cpu_baseline"] = cpu_baseline(args.cpu_seqs, args.ctx)
             print(json.dumps(line), flush=True)

@@ -92,6 +92,22 @@ int vx27_deltanet_decode_batch_gated(float *S, float *conv_ring, const void *qkv
                                      char *err, size_t errlen);
 
 /*
+ * The gates of vx27_deltanet_decode_batch / _prefill_chunked as the device computes them
+ * (no counterpart in the reference; it exists to measure them against
+ * vx27_deltanet_gate_params, src/vx27_deltanet.c:58-69). For item i with head vh = i % nv:
+ * beta[i], g_log[i] in double from a[i], b[i] (act dtype), A_log[vh], dt_bias[vh] with
+ * the device exp/log, and beta_f32[i] = (float)beta[i], decay_f32[i] = (float)exp(g_log[i]),
+ * the two values the fp32 update uses. Any output may be NULL. The double values can
+ * differ from the host function's in the last bit (neither side's exp/log is correctly
+ * rounded on every input); VX27_F_GATES_F64 feeds the host's bits to the kernels instead.
+ * Flags: VX27_F_ACT_BF16.
+ */
+int vx27_deltanet_gate_params_dev(const void *a, const void *b, const float *A_log,
+                                  const float *dt_bias, double *beta, double *g_log,
+                                  float *beta_f32, float *decay_f32, int n, int nv, int flags,
+                                  void *stream, char *err, size_t errlen);
+
+/*
  * T consecutive tokens of ONE sequence through one DeltaNet layer (teacher-forced
  * verification of speculative drafts), with optional snapshots after every token for a
  * partial commit: the semantics of vx27_qlayer_batch's Sckpt/Cckpt

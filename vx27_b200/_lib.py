@@ -45,6 +45,8 @@ PROTOTYPES: dict[str, tuple] = {
                                         _i, _p, _cp, _sz]),
     "vx27_deltanet_decode_batch_gated": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                                               _i, _i, _i, _i, _i, _p, _cp, _sz]),
+    "vx27_deltanet_gate_params_dev": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p, _cp,
+                                           _sz]),
     "vx27_deltanet_decode_tokens": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i,
                                          _i, _i, _i, _p, _cp, _sz]),
     "vx27_deltanet_prefill_workspace_size": (_sz, [_i, _i, _i, _i]),

@@ -155,6 +155,19 @@ __device__ __forceinline__ void act_st(void *p, size_t i, float x) {
     else ((float *)p)[i] = x;
 }
 
+// The gate mapping of src/vx27_deltanet.c:58-69 (three-regime softplus, beta without
+// dt_bias) in double with CUDA's device exp/log, which are within 1 ulp of the correctly
+// rounded value; the C library's exp/log are not always correctly rounded either, so the
+// double results can differ from vx27_deltanet_gate_params's in the last bit. The
+// decode and prefill kernels use this, and vx27_deltanet_gate_params_dev exports it.
+__device__ __forceinline__ void dn_gates_device(double a, double A_log, double b, double dt,
+                                                double *beta, double *g_log) {
+    *beta = 1.0 / (1.0 + exp(-b));
+    const double x = a + dt;
+    const double sp = x > 20.0 ? x : (x < -20.0 ? exp(x) : log(1.0 + exp(x)));
+    *g_log = -exp(A_log) * sp;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -81,17 +81,6 @@ __device__ bool dn_wait(uint64_t *bar, uint32_t parity, DnSmem &sm, uint32_t *st
     }
 }
 
-// The gate mapping of src/vx27_deltanet.c:58-69 in double with the device exp/log.
-// Callers that need the C library's exact bits pass host-computed gates
-// (VX27_F_GATES_F64).
-__device__ __forceinline__ void gates_device(double a, double A_log, double b, double dt,
-                                             double *beta, double *g_log) {
-    *beta = 1.0 / (1.0 + exp(-b));
-    const double x = a + dt;
-    const double sp = x > 20.0 ? x : (x < -20.0 ? exp(x) : log(1.0 + exp(x)));
-    *g_log = -exp(A_log) * sp;
-}
-
 template <bool ACT_BF16, bool OUT_BF16, bool GATES_F64, bool GATED, bool PRENORM>
 __global__ void __launch_bounds__(NTHREADS, 1)
 dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restrict__ qkv,
@@ -264,7 +253,7 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
                     beta = ga_v;
                     g = gb_v;
                 } else {
-                    gates_device(ga_v, (double)al, gb_v, (double)dtb, &beta, &g);
+                    dn_gates_device(ga_v, (double)al, gb_v, (double)dtb, &beta, &g);
                 }
                 P.beta = (float)beta;
                 P.decay = (float)exp(g);
@@ -380,10 +369,52 @@ int launch(int grid, cudaStream_t st, float *S, float *ring, const void *qkv, co
     return 0;
 }
 
+// The gates exactly as the decode kernel's prep warps form them: double beta and g_log
+// from dn_gates_device, and the fp32 beta and decay = exp(g_log) that the update uses.
+template <bool ACT_BF16>
+__global__ void gate_params_k(const void *__restrict__ a, const void *__restrict__ b,
+                              const float *__restrict__ A_log, const float *__restrict__ dt_bias,
+                              double *beta, double *g_log, float *beta_f32, float *decay_f32,
+                              int n, int nv) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int vh = i % nv;
+        double be, g;
+        dn_gates_device((double)act_ld<ACT_BF16>(a, i), (double)A_log[vh],
+                        (double)act_ld<ACT_BF16>(b, i), (double)dt_bias[vh], &be, &g);
+        if (beta) beta[i] = be;
+        if (g_log) g_log[i] = g;
+        if (beta_f32) beta_f32[i] = (float)be;
+        if (decay_f32) decay_f32[i] = (float)exp(g);
+    }
+}
+
 }  // namespace
 }  // namespace vx27
 
 using namespace vx27;
+
+extern "C" int vx27_deltanet_gate_params_dev(const void *a, const void *b, const float *A_log,
+                                             const float *dt_bias, double *beta, double *g_log,
+                                             float *beta_f32, float *decay_f32, int n, int nv,
+                                             int flags, void *stream, char *err,
+                                             size_t errlen) {
+    if (n < 0 || nv <= 0) return fail(err, errlen, "vx27_deltanet_gate_params_dev: n=%d nv=%d", n, nv);
+    if (n == 0) return 0;
+    if (!a || !b || !A_log || !dt_bias)
+        return fail(err, errlen, "vx27_deltanet_gate_params_dev: null pointer argument");
+    const int threads = 256;
+    long long blocks = ((long long)n + threads - 1) / threads;
+    if (blocks > 8LL * num_sms()) blocks = 8LL * num_sms();
+    cudaStream_t st = (cudaStream_t)stream;
+    if (flags & VX27_F_ACT_BF16)
+        gate_params_k<true><<<(int)blocks, threads, 0, st>>>(a, b, A_log, dt_bias, beta, g_log,
+                                                           beta_f32, decay_f32, n, nv);
+    else
+        gate_params_k<false><<<(int)blocks, threads, 0, st>>>(a, b, A_log, dt_bias, beta, g_log,
+                                                            beta_f32, decay_f32, n, nv);
+    VX_CK(cudaGetLastError());
+    return 0;
+}
 
 static int decode_batch_impl(const char *fn, float *S, float *conv_ring, const void *qkv,
                              const void *a, const void *b, const float *A_log,

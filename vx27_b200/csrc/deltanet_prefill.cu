@@ -113,15 +113,6 @@ inline Wsp wsp_views(uint8_t *p, size_t nblk) {
     return w;
 }
 
-// src/vx27_deltanet.c:65-69 in double, with the three-regime softplus of :58-63
-__device__ __forceinline__ void gates_dev(double a, double A_log, double b, double dt,
-                                          double *beta, double *g_log) {
-    *beta = 1.0 / (1.0 + exp(-b));
-    const double x = a + dt;
-    const double sp = x > 20.0 ? x : (x < -20.0 ? exp(x) : log(1.0 + exp(x)));
-    *g_log = -exp(A_log) * sp;
-}
-
 // ---- phase 1: per-chunk preparation ------------------------------------------------------
 // shared memory (after 1024-byte alignment)
 constexpr uint32_t P_AKQ = 0;        // [K;Q] raw, K-major 128 rows x 128; later [Wk_hi;Wk_lo]
@@ -186,7 +177,7 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
                 bt = static_cast<const double *>(ga)[gi];
                 gl = static_cast<const double *>(gb)[gi];
             } else {
-                gates_dev((double)act_ld<true>(ga, gi), (double)A_log[vh],
+                dn_gates_device((double)act_ld<true>(ga, gi), (double)A_log[vh],
                           (double)act_ld<true>(gb, gi), (double)dt_bias[vh], &bt, &gl);
             }
         }
