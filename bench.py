@@ -564,6 +564,7 @@ def run_batch1(args, cpu: bool = True) -> dict:
         units, unit_name = n_tok, "token"
         bytes_per_unit = 2 * nv * 128 * 128 * 4 + 4 * C * 4 + C * 4 + nv * 128 * 4
         name = "config 0: DeltaNet decode, batch 1, 16 heads, 2000 sequential tokens"
+        others = {}
     else:
         ctx, nq, nkv, hd = 8192, 24, 4, 256
         cap = ctx
@@ -587,9 +588,18 @@ def run_batch1(args, cpu: bool = True) -> dict:
         pos = torch.full((1,), ctx - 1, dtype=torch.int32, device="cuda")
         ws = torch.empty(ops.gqa_workspace_bytes(1, nq, nkv, hd, cap) // 4 + 1, device="cuda")
 
-        def run():
+        def run():  # the library's choice for one sequence: the fused CUDA-core decode
+            ops.gqa_decode_fused(q_in, k_in, v_in, qw, kw, rope, gate, kc, vc, pos, out, ws,
+                                 prefetch_kv=True)
+
+        def run_tc():  # append + the tensor-core split-KV decode
             ops.gqa_append(q_in, k_in, v_in, qw, kw, rope, pos, kc, vc, qn)
-            ops.gqa_decode_batch(qn, gate, kc, vc, pos, out, ws)
+            ops.gqa_decode_batch(qn, gate, kc, vc, pos, out, ws, kernel="tc")
+
+        def run_cc2():  # append + the CUDA-core decode, cache rows requested early
+            ops.gqa_append(q_in, k_in, v_in, qw, kw, rope, pos, kc, vc, qn)
+            ops.gqa_decode_batch(qn, gate, kc, vc, pos, out, ws, kernel="cc", prefetch_kv=True)
+        others = {"append + tensor-core decode": run_tc, "append + CUDA-core decode": run_cc2}
         units, unit_name = 1, "decode"
         bytes_per_unit = nkv * ctx * hd * 2 * 2 + nq * hd * 4 * 3
         name = "config 1: gated GQA single-query decode, batch 1, context 8192"
@@ -616,7 +626,23 @@ def run_batch1(args, cpu: bool = True) -> dict:
         e1.record()
         torch.cuda.synchronize()
         us_graph = e0.elapsed_time(e1) * 1e3 / (reps * units)
-    del graph
+        del graph
+        other_us = {}
+        for label, fn in others.items():
+            for _ in range(args.warmup):
+                fn()
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2):
+                fn()
+            g2.replay()
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(reps):
+                g2.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            other_us[label] = round(e0.elapsed_time(e1) * 1e3 / (reps * units), 3)
+            del g2
     if ops.device_status() != 0:
         raise RuntimeError("device status flag set during the batch-1 run")
     gbs = bytes_per_unit / (us_graph * 1e-6) / 1e9
@@ -627,6 +653,7 @@ def run_batch1(args, cpu: bool = True) -> dict:
         "data": "synthetic (seeded, BASELINE.json distributions)",
         "config": {"workload": name},
         "us_per_unit_launched": round(us_launch, 3), "us_per_unit_graph": round(us_graph, 3),
+        "other_forms_us_graph": other_us,
         "roofline": {"bound": "hbm (latency at batch 1)", "achieved": round(gbs, 1),
                      "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4),
                      "algorithmic_bytes_per_unit": bytes_per_unit, "peak_source": hbm_src},
@@ -891,6 +918,8 @@ def other_configs(args) -> dict:
         "config1_decode_us": c1["value"],
         "config1": {"us_per_decode_graph": c1["us_per_unit_graph"],
                     "us_per_decode_launched": c1["us_per_unit_launched"],
+                    "form": "vx27_gqa_decode_fused, the library's choice (CUDA-core split-KV)",
+                    "other_forms_us_graph": c1["other_forms_us_graph"],
                     "roofline": c1["roofline"], "clocks": c1["clocks"]},
         "config4_gqa_prefill": {"ms": c4["gqa_prefill"]["ms"],
                                 "tflops": c4["gqa_prefill"]["tflops"],

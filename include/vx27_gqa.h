@@ -67,6 +67,17 @@ int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
                           size_t errlen);
 
 /*
+ * The kernel and split count a vx27_gqa_decode_batch / vx27_gqa_decode_fused call with
+ * these arguments runs: *kernel = 0 for the tensor-core split-KV kernel, 1 for the
+ * CUDA-core one (small batches, or per VX27_F_DECODE_CC / VX27_F_DECODE_TC); *splits the
+ * split count. Returns the number of kernels the call launches (1: the split kernel
+ * writes the gated output; 2: split kernel + combine), or -1 for bad arguments. No
+ * counterpart in the reference.
+ */
+int vx27_gqa_decode_plan(int B, int nq, int nkv, int hd, int cap, size_t workspace_bytes,
+                         int n_splits, int flags, int *kernel, int *splits);
+
+/*
  * vx27_gqa_append + vx27_gqa_decode_batch in one kernel: the split kernel forms each
  * (sequence, KV head) group's q from the raw activations (QK RMSNorm, partial RoPE at
  * pos[b], the arithmetic of vx27_gqa_append) and writes the token's normalised, rotated K

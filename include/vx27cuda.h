@@ -38,6 +38,17 @@ extern "C" {
  * (src/vx27_qfwd.c:118-130): zero-centred RMSNorm with norm_w, y = x*s*(1+w), then l2norm
  * and q*1/sqrt(hd), before the l2norm and scaling the delta rule itself applies. */
 #define VX27_F_QK_PRENORM 0x20
+/* GQA decode (vx27_gqa_decode_batch, vx27_gqa_decode_fused): the kernel may request cache
+ * rows below the token's slot, and read pos, while the kernel before it on the stream is
+ * still running (programmatic dependent launch). Set it only when that kernel writes
+ * neither pos nor any cache row other than row pos[b] (e.g. vx27_gqa_append for the same
+ * layer, or another layer's kernel); honoured by the CUDA-core decode. */
+#define VX27_F_PREFETCH_KV 0x40
+/* GQA decode: which kernel runs the attention. Neither flag: the library chooses by
+ * batch shape (the CUDA-core split-KV kernel for a few (sequence, KV head) streams, the
+ * tensor-core kernel otherwise; vx27_gqa_decode_plan reports the choice). */
+#define VX27_F_DECODE_CC 0x80 /* CUDA-core split-KV kernel */
+#define VX27_F_DECODE_TC 0x100 /* tensor-core (tcgen05) split-KV kernel */
 
 /* Library version, major*10000 + minor*100 + patch. */
 int vx27cuda_version(void);

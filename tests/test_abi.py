@@ -99,12 +99,16 @@ def test_batched_entry_points_reject_bad_shapes_without_gpu(vxlib):
     assert vxlib.vx27_gqa_decode_workspace_size(2, 24, 4, 256, 4096, 3) == 3 * 2 * 24 * 258 * 4
     rc = vxlib.vx27_pmat_multi_dev(5, None, 4, None, None, None, 128, 1, None, err, 256)
     assert rc == -1 and b"n=5 projections" in err.value
-    # the fused decode: a RoPE width that 8-dim lanes cannot pair up (checked before any
-    # CUDA call; the pointers are never dereferenced)
+    # the fused decode on the tensor cores: a RoPE width that 8-dim lanes cannot pair up;
+    # on the CUDA cores (one thread per dim): an odd one (checked before any CUDA call; the
+    # pointers are never dereferenced)
     rec = 1 * 24 * 258 * 4
     rc = vxlib.vx27_gqa_decode_fused(16, 16, 16, 16, 16, 16, 64, None, 16, 16, 64, 16, 16, 16, rec,
-                                     1, 24, 4, 256, 20, 1e-6, 1, 0, None, err, 256)
+                                     1, 24, 4, 256, 20, 1e-6, 1, 0x100, None, err, 256)
     assert rc == -1 and b"rope_dim=20" in err.value
+    rc = vxlib.vx27_gqa_decode_fused(16, 16, 16, 16, 16, 16, 64, None, 16, 16, 64, 16, 16, 16, rec,
+                                     1, 24, 4, 256, 21, 1e-6, 1, 0x80, None, err, 256)
+    assert rc == -1 and b"rope_dim=21" in err.value
 
 
 def test_ddmath_host_matches_c_library_nearly_always():

@@ -7,8 +7,12 @@ evaluate the same formula on the device, in double with CUDA's exp/log; this tes
 those device gates (vx27_deltanet_gate_params_dev) and measures them against the host
 bits on the reference's six pins, 200,000 random cases across the softplus regimes, and
 every bf16 logit below 700 in magnitude at config 2's heads:
-  * the double beta and g_log are at most 1 ulp from the host's, and differ on a small
-    fraction of inputs (the measured rate is printed and bounded here);
+  * the double beta and g_log are NOT the host's bits on every input: CUDA's and the C
+    library's exp/log each round a few percent of results differently (measured on a
+    B200: 2.8% of beta and 6.9% of g_log values differ in the random set, by 1-2 ulp;
+    in softplus's range where log(1 + e^x) cancels, a 1-ulp difference of 1 + e^x is
+    a few thousand ulp of the result, 8e-13 relative). The test bounds the relative
+    difference and the rate and prints both;
   * the fp32 beta and decay = exp(g_log) that the kernels' update uses are identical to
     the host values rounded the same way, on every case.
 Bit-exact double gates on the device path come from VX27_F_GATES_F64 (host-computed
@@ -71,10 +75,15 @@ def _compare(name, d, h):
     ub, ug = _ulps(bd, bh), _ulps(gd, gh)
     n = bd.shape[0]
     rate = (np.count_nonzero(ub) + np.count_nonzero(ug)) / (2 * n)
+    rel = max(float(np.max(np.abs(bd - bh) / np.abs(bh))),
+              float(np.max(np.abs(gd - gh) / np.maximum(np.abs(gh), 1e-300))))
+    near = np.percentile(np.maximum(ub, ug), 99.9)
     print(f"{name}: {n} cases, double beta/g_log differ in {np.count_nonzero(ub)}/"
-          f"{np.count_nonzero(ug)} ({100 * rate:.3f}%), max {max(ub.max(), ug.max())} ulp")
-    assert ub.max() <= 1 and ug.max() <= 1
-    assert rate < 0.01
+          f"{np.count_nonzero(ug)} ({100 * rate:.3f}%), 99.9th percentile {near:.0f} ulp, "
+          f"max {max(ub.max(), ug.max())} ulp, max relative {rel:.2e}")
+    assert rel < 1e-11
+    assert near <= 2
+    assert rate < 0.1
     assert np.array_equal(bfd.view(np.uint32), bfh.view(np.uint32)), f"{name}: fp32 beta"
     assert np.array_equal(dfd.view(np.uint32), dfh.view(np.uint32)), f"{name}: fp32 decay"
     return rate

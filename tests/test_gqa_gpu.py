@@ -37,7 +37,7 @@ def oracle_step(orc, x, B, cap, bf16=True):
     return qo, kc, vc, out
 
 
-def gpu_step(x, B, cap, rope, n_splits=0, bf16=True, out_bf16=False):
+def gpu_step(x, B, cap, rope, n_splits=0, bf16=True, out_bf16=False, kernel="auto"):
     kc = dev(x["kc"], True).view(B, NKV, cap, HD)
     vc = dev(x["vc"], True).view(B, NKV, cap, HD)
     qi = dev(x["qi"], bf16).view(B, NQ, HD)
@@ -51,14 +51,14 @@ def gpu_step(x, B, cap, rope, n_splits=0, bf16=True, out_bf16=False):
                      device="cuda")
     out = torch.empty(B, NQ, HD, device="cuda",
                       dtype=torch.bfloat16 if out_bf16 else torch.float32)
-    ops.gqa_decode_batch(q, gate, kc, vc, pos, out, ws, n_splits=n_splits)
+    ops.gqa_decode_batch(q, gate, kc, vc, pos, out, ws, n_splits=n_splits, kernel=kernel)
     out = out.float()
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     return host(q).reshape(-1), host(kc).reshape(-1), host(vc).reshape(-1), host(out).reshape(-1)
 
 
-def gpu_step_fused(x, B, cap, rope, n_splits=0, bf16=True, out_bf16=False):
+def gpu_step_fused(x, B, cap, rope, n_splits=0, bf16=True, out_bf16=False, kernel="auto"):
     """vx27_gqa_decode_fused: append and attention in one kernel."""
     kc = dev(x["kc"], True).view(B, NKV, cap, HD)
     vc = dev(x["vc"], True).view(B, NKV, cap, HD)
@@ -72,7 +72,7 @@ def gpu_step_fused(x, B, cap, rope, n_splits=0, bf16=True, out_bf16=False):
     out = torch.empty(B, NQ, HD, device="cuda",
                       dtype=torch.bfloat16 if out_bf16 else torch.float32)
     ops.gqa_decode_fused(qi, ki, vi, dev(x["qw"]), dev(x["kw"]), rope, gate, kc, vc, pos, out, ws,
-                         n_splits=n_splits)
+                         n_splits=n_splits, kernel=kernel)
     out = out.float()
     torch.cuda.synchronize()
     assert ops.device_status() == 0
@@ -108,45 +108,49 @@ def test_golden_driver_inputs(cuda, orc, golden, rope):
 
 
 @pytest.mark.parametrize("n_splits", [0, 1, 3, 7])
-def test_ragged_batch(cuda, orc, rope, n_splits):
+@pytest.mark.parametrize("kernel", ["tc", "cc"])
+def test_ragged_batch(cuda, orc, rope, n_splits, kernel):
     """Sequences at positions 0 (a single key), 1, 127, 128 (tile edges) and 1000."""
     B, cap = 5, 1024
     x = setup(orc, 21, B, cap, [0, 1, 127, 128, 1000])
     qo, kc, vc, ref = oracle_step(orc, x, B, cap)
-    q, kcg, vcg, out = gpu_step(x, B, cap, rope, n_splits)
+    q, kcg, vcg, out = gpu_step(x, B, cap, rope, n_splits, kernel=kernel)
     assert rel_err(q, qo) < 1e-6
     assert rel_err(out, ref) < 1e-4 < REL_TOL
     print(f"splits={n_splits}: rel err {rel_err(out, ref):.2e}")
 
 
-def test_config1_ctx8192(cuda, orc, rope):
+@pytest.mark.parametrize("kernel", ["tc", "cc"])
+def test_config1_ctx8192(cuda, orc, rope, kernel):
     """Config 1: batch 1, ctx 8192 (cache 0..8190 ~N(0,1) bf16, token at 8191), seed 1."""
     B, cap = 1, 8192
     x = setup(orc, 1, B, cap, [8191])
     qo, kc, vc, ref = oracle_step(orc, x, B, cap)
-    q, kcg, vcg, out = gpu_step(x, B, cap, rope)
+    q, kcg, vcg, out = gpu_step(x, B, cap, rope, kernel=kernel)
     err = rel_err(out, ref)
     print(f"config1 rel err {err:.3e}")
     assert err < REL_TOL and err < 1e-4
 
 
 @pytest.mark.parametrize("n_splits", [0, 1])
-def test_fp32_activations(cuda, orc, rope, n_splits):
+@pytest.mark.parametrize("kernel", ["tc", "cc"])
+def test_fp32_activations(cuda, orc, rope, n_splits, kernel):
     # n_splits = 1: the split kernel applies the fp32 gate and writes the output itself
     B, cap = 2, 300
     x = setup(orc, 31, B, cap, [5, 299], bf16=False)
     qo, kc, vc, ref = oracle_step(orc, x, B, cap, bf16=False)
-    q, _, _, out = gpu_step(x, B, cap, rope, n_splits, bf16=False)
+    q, _, _, out = gpu_step(x, B, cap, rope, n_splits, bf16=False, kernel=kernel)
     assert rel_err(out, ref) < 1e-4
 
 
 @pytest.mark.parametrize("n_splits", [1, 4])
-def test_bf16_output(cuda, orc, rope, n_splits):
+@pytest.mark.parametrize("kernel", ["tc", "cc"])
+def test_bf16_output(cuda, orc, rope, n_splits, kernel):
     # bf16 gate and bf16 output, written by the split kernel (1) or by the combine (4)
     B, cap = 3, 700
     x = setup(orc, 37, B, cap, [0, 300, 699])
     qo, kc, vc, ref = oracle_step(orc, x, B, cap)
-    q, _, _, out = gpu_step(x, B, cap, rope, n_splits, out_bf16=True)
+    q, _, _, out = gpu_step(x, B, cap, rope, n_splits, out_bf16=True, kernel=kernel)
     err = rel_err(out, ref)
     print(f"splits={n_splits}: bf16 output rel err {err:.2e}")
     assert err < 2e-2
@@ -248,14 +252,15 @@ def test_no_output_gate_mtp_drafter(cuda, orc, rope):
 
 
 @pytest.mark.parametrize("n_splits", [0, 1, 3, 7])
-def test_fused_decode_ragged_batch(cuda, orc, rope, n_splits):
+@pytest.mark.parametrize("kernel", ["tc", "cc"])
+def test_fused_decode_ragged_batch(cuda, orc, rope, n_splits, kernel):
     """The fused kernel (vx27_gqa_decode_fused) on the ragged batch: the appended rows equal
     the separate append kernel's bit for bit, the output the oracle's."""
     B, cap = 5, 1024
     x = setup(orc, 21, B, cap, [0, 1, 127, 128, 1000])
     qo, kc, vc, ref = oracle_step(orc, x, B, cap)
     _, kc_sep, vc_sep, out_sep = gpu_step(x, B, cap, rope, n_splits)
-    kcg, vcg, out = gpu_step_fused(x, B, cap, rope, n_splits)
+    kcg, vcg, out = gpu_step_fused(x, B, cap, rope, n_splits, kernel=kernel)
     assert np.array_equal(vcg, vc_sep) and np.array_equal(vcg, vc)
     krow_f = kcg.reshape(B, NKV, cap, HD)[np.arange(B), :, x["pos"]]
     krow_s = kc_sep.reshape(B, NKV, cap, HD)[np.arange(B), :, x["pos"]]
@@ -270,11 +275,12 @@ def test_fused_decode_ragged_batch(cuda, orc, rope, n_splits):
     assert err < 1e-4 < REL_TOL
 
 
-def test_fused_decode_golden_and_config1(cuda, orc, golden, rope):
+@pytest.mark.parametrize("kernel", ["tc", "cc"])
+def test_fused_decode_golden_and_config1(cuda, orc, golden, rope, kernel):
     """Golden driver inputs (pos 10 and 37) and config 1 (ctx 8192) through the fused kernel."""
     B, cap = 2, 48
     x = setup(orc, 8, B, cap, golden["gq_pos"])
-    kc, vc, out = gpu_step_fused(x, B, cap, rope)
+    kc, vc, out = gpu_step_fused(x, B, cap, rope, kernel=kernel)
     krow = kc.reshape(B, NKV, cap, HD)[np.arange(B), :, golden["gq_pos"]]
     assert np.count_nonzero(krow != golden["gq_krow"]) <= krow.size // 1000
     vrow = vc.reshape(B, NKV, cap, HD)[np.arange(B), :, golden["gq_pos"]]
@@ -283,14 +289,15 @@ def test_fused_decode_golden_and_config1(cuda, orc, golden, rope):
     B, cap = 1, 8192
     x = setup(orc, 1, B, cap, [8191])
     _, _, _, ref = oracle_step(orc, x, B, cap)
-    _, _, out = gpu_step_fused(x, B, cap, rope)
+    _, _, out = gpu_step_fused(x, B, cap, rope, kernel=kernel)
     assert rel_err(out, ref) < 1e-4
 
 
 @pytest.mark.parametrize("bf16,out_bf16", [(False, False), (True, True)])
-def test_fused_decode_dtypes(cuda, orc, rope, bf16, out_bf16):
+@pytest.mark.parametrize("kernel", ["tc", "cc"])
+def test_fused_decode_dtypes(cuda, orc, rope, bf16, out_bf16, kernel):
     B, cap = 3, 700
     x = setup(orc, 37, B, cap, [0, 300, 699], bf16=bf16)
     _, _, _, ref = oracle_step(orc, x, B, cap, bf16=bf16)
-    _, _, out = gpu_step_fused(x, B, cap, rope, 1, bf16=bf16, out_bf16=out_bf16)
+    _, _, out = gpu_step_fused(x, B, cap, rope, 1, bf16=bf16, out_bf16=out_bf16, kernel=kernel)
     assert rel_err(out, ref) < (2e-2 if out_bf16 else 1e-4)

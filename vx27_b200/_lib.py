@@ -63,6 +63,7 @@ PROTOTYPES: dict[str, tuple] = {
     "vx27_gqa_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),
     "vx27_gqa_decode_batch": (_i, [_p, _p, _p, _p, _i, _p, _p, _p, _sz, _i, _i, _i, _i, _i, _i,
                                    _p, _cp, _sz]),
+    "vx27_gqa_decode_plan": (_i, [_i, _i, _i, _i, _i, _sz, _i, _i, _ip, _ip]),
     "vx27_gqa_decode_fused": (_i, [_p, _p, _p, _p, _p, _p, _i, _p, _p, _p, _i, _p, _p, _p, _sz,
                                    _i, _i, _i, _i, _i, _f, _i, _i, _p, _cp, _sz]),
     "vx27_gqa_decode_batch_noalloc": (_i, [_p, _p, _p, _p, _i, _p, _p, _i, _i, _i, _i, _i, _i,

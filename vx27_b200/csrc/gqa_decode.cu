@@ -25,6 +25,16 @@ int launch_split_tc_fused(const void *q_in, const void *k_in, const void *v_in,
                           float *parts, int B, int nq, int nkv, int n_splits, const void *gate,
                           void *out, int flags, cudaStream_t st, char *err, size_t errlen);
 
+// gqa_cc.cu: the CUDA-core split-KV kernel for small batches (+ its combine); q_in != NULL
+// selects its fused prologue. Returns the kernels launched or -1.
+int launch_decode_cc(const void *kc, const void *vc, const float *q, const int *pos,
+                     float *parts, int cap, int B, int nq, int nkv, int n_splits,
+                     const void *gate, void *out, int flags, const void *q_in, const void *k_in,
+                     const void *v_in, const float *qw, const float *kw, const float *rope,
+                     int rope_len, int rope_dim, float eps, cudaStream_t st, char *err,
+                     size_t errlen);
+int cc_auto_splits(int B, int nkv, int max_ctx);
+
 namespace {
 
 constexpr int HD = 256;
@@ -179,6 +189,23 @@ int auto_splits(int B, int nkv, int max_ctx) {
     return best;
 }
 
+// Which decode kernel a call uses: the flags' choice, else the CUDA-core kernel while the
+// (sequence, KV head) streams are few enough that the tensor-core kernel's per-CTA
+// pipeline start-up, not HBM, would bound it.
+bool use_cc(int B, int nkv, int flags) {
+    if (flags & VX27_F_DECODE_CC) return true;
+    if (flags & VX27_F_DECODE_TC) return false;
+    return (long long)B * nkv <= 16;
+}
+
+// The split count a decode call runs with: n_splits when given, else the chosen kernel's
+// own count capped by the workspace (fit records).
+int plan_splits(int B, int nkv, int cap, int n_splits, int fit, bool cc) {
+    if (n_splits > 0) return n_splits;
+    n_splits = cc ? cc_auto_splits(B, nkv, cap) : auto_splits(B, nkv, cap);
+    return n_splits > fit ? fit : n_splits;
+}
+
 int launch_split(const float *q, const void *kc, const void *vc, int cap, const int *pos,
                  float *parts, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
                  cudaStream_t st, char *err, size_t errlen) {
@@ -257,8 +284,24 @@ int vx27_gqa_append(const void *q_in, const void *k_in, const void *v_in,
 size_t vx27_gqa_decode_workspace_size(int B, int nq, int nkv, int hd, int max_ctx,
                                       int n_splits) {
     if (B <= 0 || nq <= 0 || nkv <= 0 || hd <= 0) return 0;
-    if (n_splits <= 0) n_splits = auto_splits(B, nkv, max_ctx);
+    if (n_splits <= 0) {  // enough for either kernel's automatic count
+        n_splits = auto_splits(B, nkv, max_ctx);
+        const int c = cc_auto_splits(B, nkv, max_ctx);
+        if (use_cc(B, nkv, 0) && c > n_splits) n_splits = c;
+    }
     return (size_t)n_splits * B * nq * (hd + 2) * sizeof(float);
+}
+
+int vx27_gqa_decode_plan(int B, int nq, int nkv, int hd, int cap, size_t workspace_bytes,
+                         int n_splits, int flags, int *kernel, int *splits) {
+    if (B <= 0 || nq <= 0 || nkv <= 0 || hd != HD || cap <= 0) return -1;
+    const bool cc = use_cc(B, nkv, flags);
+    const size_t rec = (size_t)B * nq * (hd + 2) * sizeof(float);
+    const int n = plan_splits(B, nkv, cap, n_splits, (int)(workspace_bytes / rec), cc);
+    if (n < 1) return -1;
+    if (kernel) *kernel = cc ? 1 : 0;
+    if (splits) *splits = n;
+    return n == 1 ? 1 : 2;
 }
 
 int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
@@ -271,16 +314,18 @@ int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
         return fail(err, errlen, "vx27_gqa_decode_batch: null pointer argument");
     const size_t rec = (size_t)B * nq * (hd + 2) * sizeof(float);
     const int fit = (int)(workspace_bytes / rec);
-    if (n_splits <= 0) {
-        n_splits = auto_splits(B, nkv, cap);
-        if (n_splits > fit) n_splits = fit;
-    }
+    const bool cc = use_cc(B, nkv, flags);
+    n_splits = plan_splits(B, nkv, cap, n_splits, fit, cc);
     if (n_splits < 1 || n_splits > fit || n_splits > 65535)
         return fail(err, errlen,
                     "vx27_gqa_decode_batch: workspace of %zu bytes holds %d splits, need %d",
                     workspace_bytes, fit, n_splits < 1 ? 1 : n_splits);
     cudaStream_t st = (cudaStream_t)stream;
     float *parts = (float *)workspace;
+    if (cc)
+        return launch_decode_cc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, n_splits, gate,
+                                out, flags, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                0, 0, 0.0f, st, err, errlen) < 0 ? -1 : 0;
     if (n_splits == 1)  // the split kernel applies the gate and writes out; no combine pass
         return launch_split_tc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, 1, 0, -1, st,
                                err, errlen, gate, out, flags);
@@ -303,16 +348,19 @@ int vx27_gqa_decode_fused(const void *q_in, const void *k_in, const void *v_in,
         return fail(err, errlen, "vx27_gqa_decode_fused: null pointer argument");
     const size_t rec = (size_t)B * nq * (hd + 2) * sizeof(float);
     const int fit = (int)(workspace_bytes / rec);
-    if (n_splits <= 0) {
-        n_splits = auto_splits(B, nkv, cap);
-        if (n_splits > fit) n_splits = fit;
-    }
+    const bool cc = use_cc(B, nkv, flags);
+    n_splits = plan_splits(B, nkv, cap, n_splits, fit, cc);
     if (n_splits < 1 || n_splits > fit || n_splits > 65535)
         return fail(err, errlen,
                     "vx27_gqa_decode_fused: workspace of %zu bytes holds %d splits, need %d",
                     workspace_bytes, fit, n_splits < 1 ? 1 : n_splits);
     cudaStream_t st = (cudaStream_t)stream;
     float *parts = (float *)workspace;
+    if (cc)
+        return launch_decode_cc(k_cache, v_cache, nullptr, pos, parts, cap, B, nq, nkv, n_splits,
+                                gate, out, flags, q_in, k_in, v_in, q_norm_w, k_norm_w,
+                                rope_table, rope_table_len, rope_dim, eps, st, err, errlen) < 0
+                   ? -1 : 0;
     const bool direct = n_splits == 1;  // the split kernel applies the gate and writes out
     if (launch_split_tc_fused(q_in, k_in, v_in, q_norm_w, k_norm_w, rope_table, rope_table_len,
                               rope_dim, eps, k_cache, v_cache, cap, pos, parts, B, nq, nkv,

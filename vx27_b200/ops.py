@@ -24,6 +24,10 @@ F_NORM_1P = 0x4
 F_GATES_F64 = 0x8
 F_PREFETCH_STATE = 0x10
 F_QK_PRENORM = 0x20
+F_PREFETCH_KV = 0x40
+F_DECODE_CC = 0x80
+F_DECODE_TC = 0x100
+_KERNEL_FLAGS = {"auto": 0, "cc": F_DECODE_CC, "tc": F_DECODE_TC}
 
 
 def _np(a: np.ndarray, dtype=np.float32) -> C.c_void_p:
@@ -330,15 +334,24 @@ def gqa_workspace_bytes(B: int, nq: int, nkv: int, hd: int, max_ctx: int,
     return load().vx27_gqa_decode_workspace_size(B, nq, nkv, hd, max_ctx, n_splits)
 
 
+def gqa_decode_plan(B: int, nq: int, nkv: int, hd: int, cap: int, ws_bytes: int,
+                    n_splits: int = 0, kernel: str = "auto") -> tuple[str, int, int]:
+    """The library's choice for a decode call (vx27_gqa_decode_plan): ("tc" | "cc", split
+    count, kernels launched: 1 when one split writes the gated output, 2 with a combine)."""
+    k, n = C.c_int(), C.c_int()
+    launches = load().vx27_gqa_decode_plan(B, nq, nkv, hd, cap, ws_bytes, n_splits,
+                                           _KERNEL_FLAGS[kernel], C.byref(k), C.byref(n))
+    if launches < 0:
+        raise Vx27Error(f"vx27_gqa_decode_plan: bad arguments B={B} nq={nq} nkv={nkv}")
+    return ("cc" if k.value else "tc"), n.value, launches
+
+
 def gqa_decode_launches(B: int, nq: int, nkv: int, hd: int, cap: int, ws_bytes: int,
-                        n_splits: int = 0) -> int:
+                        n_splits: int = 0, kernel: str = "auto") -> int:
     """Kernels one decode call launches: the library's split count (its own choice when
     n_splits <= 0, capped by the workspace), then 1 for one split (the split kernel writes
     the gated output) or 2 (split kernel + combine)."""
-    if n_splits <= 0:
-        rec = B * nq * (hd + 2) * 4
-        n_splits = min(gqa_workspace_bytes(B, nq, nkv, hd, cap) // rec, ws_bytes // rec)
-    return 1 if n_splits == 1 else 2
+    return gqa_decode_plan(B, nq, nkv, hd, cap, ws_bytes, n_splits, kernel)[2]
 
 
 def gqa_partial_launches(B: int, nq: int, nkv: int, hd: int, span: int, ws_bytes: int) -> int:
@@ -350,10 +363,11 @@ def gqa_partial_launches(B: int, nq: int, nkv: int, hd: int, span: int, ws_bytes
 
 
 def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: int = 0,
-                     stream=None) -> int:
+                     stream=None, kernel: str = "auto", prefetch_kv: bool = False) -> int:
     """Split-KV decode of one token per sequence (vx27_gqa_decode_batch); returns the
     kernels it launched: 1 with one split (the split kernel writes the gated output), 2
-    with several (split kernel + combine)."""
+    with several (split kernel + combine). kernel: "auto" (the library's choice by batch
+    shape), "tc" (tensor cores) or "cc" (CUDA cores); prefetch_kv: VX27_F_PREFETCH_KV."""
     B, nq, hd = q.shape
     nkv, cap = k_cache.shape[1], k_cache.shape[2]
     f32, bf16, i32, _, _ = _dt()
@@ -364,22 +378,25 @@ def gqa_decode_batch(q, gate, k_cache, v_cache, pos, out, workspace, n_splits: i
     _need(pos, "pos", B, (i32,))
     _need(out, "out", B * nq * hd, (f32, bf16))
     flags = (F_ACT_BF16 if gate is not None and _is_bf16(gate) else 0) | \
-        (F_OUT_BF16 if _is_bf16(out) else 0)
+        (F_OUT_BF16 if _is_bf16(out) else 0) | _KERNEL_FLAGS[kernel] | \
+        (F_PREFETCH_KV if prefetch_kv else 0)
     e = errbuf()
     ws_bytes = workspace.numel() * workspace.element_size()
     rc = load().vx27_gqa_decode_batch(_t(q), _t(gate), _t(k_cache), _t(v_cache), cap, _t(pos),
                                       _t(out), _t(workspace), ws_bytes, B, nq, nkv, hd, n_splits,
                                       flags, _stream(stream), e, 512)
     check(rc, e)
-    return gqa_decode_launches(B, nq, nkv, hd, cap, ws_bytes, n_splits)
+    return gqa_decode_launches(B, nq, nkv, hd, cap, ws_bytes, n_splits, kernel)
 
 
 def gqa_decode_fused(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, gate, k_cache, v_cache, pos,
                      out, workspace, eps: float = 1e-6, norm_one_plus: bool = False,
-                     n_splits: int = 0, stream=None) -> int:
+                     n_splits: int = 0, stream=None, kernel: str = "auto",
+                     prefetch_kv: bool = False) -> int:
     """gqa_append + gqa_decode_batch as one kernel (vx27_gqa_decode_fused): the new token's
     K/V rows land in the caches at pos[b] and out gets the gated attention; returns the
-    kernels launched (1 with one split, 2 with a combine)."""
+    kernels launched (1 with one split, 2 with a combine). kernel and prefetch_kv as for
+    gqa_decode_batch."""
     B, nq, hd = q_in.shape
     nkv, cap = k_cache.shape[1], k_cache.shape[2]
     f32, bf16, i32, _, _ = _dt()
@@ -395,7 +412,8 @@ def gqa_decode_fused(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, gate, k_cache, 
     _need(v_cache, "v_cache", B * nkv * cap * hd, (bf16,))
     _need(out, "out", B * nq * hd, (f32, bf16))
     flags = (F_ACT_BF16 if _is_bf16(q_in) else 0) | (F_OUT_BF16 if _is_bf16(out) else 0) | \
-        (F_NORM_1P if norm_one_plus else 0)
+        (F_NORM_1P if norm_one_plus else 0) | _KERNEL_FLAGS[kernel] | \
+        (F_PREFETCH_KV if prefetch_kv else 0)
     ws_bytes = workspace.numel() * workspace.element_size()
     e = errbuf()
     rc = load().vx27_gqa_decode_fused(_t(q_in), _t(k_in), _t(v_in), _t(q_norm_w), _t(k_norm_w),
@@ -404,7 +422,7 @@ def gqa_decode_fused(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, gate, k_cache, 
                                       ws_bytes, B, nq, nkv, hd, rope.shape[1], eps, n_splits,
                                       flags, _stream(stream), e, 512)
     check(rc, e)
-    return gqa_decode_launches(B, nq, nkv, hd, cap, ws_bytes, n_splits)
+    return gqa_decode_launches(B, nq, nkv, hd, cap, ws_bytes, n_splits, kernel)
 
 
 def gqa_partial_workspace_bytes(B: int, nq: int, nkv: int, hd: int, max_range: int) -> int:
