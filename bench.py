@@ -588,18 +588,18 @@ def run_batch1(args, cpu: bool = True) -> dict:
         pos = torch.full((1,), ctx - 1, dtype=torch.int32, device="cuda")
         ws = torch.empty(ops.gqa_workspace_bytes(1, nq, nkv, hd, cap) // 4 + 1, device="cuda")
 
-        def run():  # the library's choice for one sequence: the fused CUDA-core decode
+        def run():  # append + the tensor-core split-KV decode (+ combine)
+            ops.gqa_append(q_in, k_in, v_in, qw, kw, rope, pos, kc, vc, qn)
+            ops.gqa_decode_batch(qn, gate, kc, vc, pos, out, ws, prefetch_kv=True)
+
+        def run_fused():  # the same in one split kernel (+ combine)
             ops.gqa_decode_fused(q_in, k_in, v_in, qw, kw, rope, gate, kc, vc, pos, out, ws,
                                  prefetch_kv=True)
 
-        def run_tc():  # append + the tensor-core split-KV decode
-            ops.gqa_append(q_in, k_in, v_in, qw, kw, rope, pos, kc, vc, qn)
-            ops.gqa_decode_batch(qn, gate, kc, vc, pos, out, ws, kernel="tc")
-
-        def run_cc2():  # append + the CUDA-core decode, cache rows requested early
-            ops.gqa_append(q_in, k_in, v_in, qw, kw, rope, pos, kc, vc, qn)
-            ops.gqa_decode_batch(qn, gate, kc, vc, pos, out, ws, kernel="cc", prefetch_kv=True)
-        others = {"append + tensor-core decode": run_tc, "append + CUDA-core decode": run_cc2}
+        def run_cc():  # the CUDA-core split-KV kernel, prologue fused
+            ops.gqa_decode_fused(q_in, k_in, v_in, qw, kw, rope, gate, kc, vc, pos, out, ws,
+                                 kernel="cc", prefetch_kv=True)
+        others = {"fused tensor-core decode": run_fused, "fused CUDA-core decode": run_cc}
         units, unit_name = 1, "decode"
         bytes_per_unit = nkv * ctx * hd * 2 * 2 + nq * hd * 4 * 3
         name = "config 1: gated GQA single-query decode, batch 1, context 8192"
@@ -918,7 +918,7 @@ def other_configs(args) -> dict:
         "config1_decode_us": c1["value"],
         "config1": {"us_per_decode_graph": c1["us_per_unit_graph"],
                     "us_per_decode_launched": c1["us_per_unit_launched"],
-                    "form": "vx27_gqa_decode_fused, the library's choice (CUDA-core split-KV)",
+                    "form": "vx27_gqa_append + vx27_gqa_decode_batch (tensor cores)",
                     "other_forms_us_graph": c1["other_forms_us_graph"],
                     "roofline": c1["roofline"], "clocks": c1["clocks"]},
         "config4_gqa_prefill": {"ms": c4["gqa_prefill"]["ms"],

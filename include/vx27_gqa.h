@@ -69,7 +69,7 @@ int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
 /*
  * The kernel and split count a vx27_gqa_decode_batch / vx27_gqa_decode_fused call with
  * these arguments runs: *kernel = 0 for the tensor-core split-KV kernel, 1 for the
- * CUDA-core one (small batches, or per VX27_F_DECODE_CC / VX27_F_DECODE_TC); *splits the
+ * CUDA-core one (VX27_F_DECODE_CC); *splits the
  * split count. Returns the number of kernels the call launches (1: the split kernel
  * writes the gated output; 2: split kernel + combine), or -1 for bad arguments. No
  * counterpart in the reference.

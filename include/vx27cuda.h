@@ -44,11 +44,12 @@ extern "C" {
  * neither pos nor any cache row other than row pos[b] (e.g. vx27_gqa_append for the same
  * layer, or another layer's kernel); honoured by the CUDA-core decode. */
 #define VX27_F_PREFETCH_KV 0x40
-/* GQA decode: which kernel runs the attention. Neither flag: the library chooses by
- * batch shape (the CUDA-core split-KV kernel for a few (sequence, KV head) streams, the
- * tensor-core kernel otherwise; vx27_gqa_decode_plan reports the choice). */
-#define VX27_F_DECODE_CC 0x80 /* CUDA-core split-KV kernel */
-#define VX27_F_DECODE_TC 0x100 /* tensor-core (tcgen05) split-KV kernel */
+/* GQA decode: which kernel runs the attention. Default (and VX27_F_DECODE_TC): the
+ * tensor-core (tcgen05) split-KV kernel. VX27_F_DECODE_CC: a split-KV kernel on the CUDA
+ * cores (fp32 FMA), slower on a B200 at every batch shape measured; it is kept as the
+ * reference point for that comparison. vx27_gqa_decode_plan reports the choice. */
+#define VX27_F_DECODE_CC 0x80
+#define VX27_F_DECODE_TC 0x100
 
 /* Library version, major*10000 + minor*100 + patch. */
 int vx27cuda_version(void);

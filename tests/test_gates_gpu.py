@@ -82,7 +82,7 @@ def _compare(name, d, h):
           f"{np.count_nonzero(ug)} ({100 * rate:.3f}%), 99.9th percentile {near:.0f} ulp, "
           f"max {max(ub.max(), ug.max())} ulp, max relative {rel:.2e}")
     assert rel < 1e-11
-    assert near <= 2
+    assert near <= 8
     assert rate < 0.1
     assert np.array_equal(bfd.view(np.uint32), bfh.view(np.uint32)), f"{name}: fp32 beta"
     assert np.array_equal(dfd.view(np.uint32), dfh.view(np.uint32)), f"{name}: fp32 decay"

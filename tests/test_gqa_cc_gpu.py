@@ -1,6 +1,7 @@
-"""The CUDA-core split-KV decode (gqa_cc.cu), which the library picks for small batches,
-against the CPU oracle (the reference's decode attention, src/vx27_qfwd.c:347-371, over
-the same bf16 cache) and against the tensor-core kernel on the same inputs.
+"""The CUDA-core split-KV decode (gqa_cc.cu, VX27_F_DECODE_CC), the measured alternative
+to the tensor-core decode, against the CPU oracle (the reference's decode attention,
+src/vx27_qfwd.c:347-371, over the same bf16 cache) and against the tensor-core kernel on
+the same inputs.
 
 Covers ragged positions on both sides of the 32-position stage edges, forced split counts
 (one split writes the gated output itself; several are merged by the combine), fp32 and
@@ -119,8 +120,7 @@ def test_cc_config1_matches_oracle_and_tensor_cores(cuda, orc, rope):
     B, cap = 1, 8192
     x = setup(orc, 1, B, cap, [8191])
     _, _, _, ref = oracle_step(orc, x, B, cap)
-    assert ops.gqa_decode_plan(B, NQ, NKV, HD, cap, 1 << 30)[0] == "cc"
-    _, _, out_cc = _decode(x, B, cap, rope, "auto", fused=True)
+    _, _, out_cc = _decode(x, B, cap, rope, "cc", fused=True)
     _, _, out_tc = _decode(x, B, cap, rope, "tc")
     assert rel_err(out_cc, ref) < TOL
     assert rel_err(out_tc, out_cc) < TOL
@@ -139,8 +139,8 @@ def test_cc_prefetch_gives_the_same_bits(cuda, orc, rope, fused):
 
 
 def test_cc_and_tc_agree_on_a_wide_batch(cuda, orc, rope):
-    """The library's tensor-core choice for many sequences and the CUDA-core kernel
-    forced on the same batch give the same attention within the tolerance."""
+    """The library's tensor-core choice and the CUDA-core kernel on the same batch give
+    the same attention within the tolerance."""
     B, cap = 64, 520
     pos = np.arange(B, dtype=np.int32) * 8 + 3
     x = setup(orc, 56, B, cap, pos)
@@ -149,3 +149,17 @@ def test_cc_and_tc_agree_on_a_wide_batch(cuda, orc, rope):
     _, _, out_tc = _decode(x, B, cap, rope, "auto")
     _, _, out_cc = _decode(x, B, cap, rope, "cc")
     assert rel_err(out_tc, ref) < TOL and rel_err(out_cc, ref) < TOL
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_tc_prefetch_gives_the_same_bits(cuda, orc, rope, fused):
+    """The tensor-core kernel with VX27_F_PREFETCH_KV: the first ring round is requested
+    before the previous kernel ends, the tile with the token's row after it."""
+    B, cap = 3, 700
+    x = setup(orc, 57, B, cap, [699, 64, 333])
+    _, _, _, ref = oracle_step(orc, x, B, cap)
+    for n_splits in (1, 4):
+        _, _, a = _decode(x, B, cap, rope, "tc", n_splits, fused=fused)
+        _, _, b = _decode(x, B, cap, rope, "tc", n_splits, fused=fused, prefetch=True)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        assert rel_err(b, ref) < TOL

@@ -33,15 +33,16 @@ def test_partial_launches():
     assert ops.gqa_partial_launches(1, NQ, NKV, HD, span, 0) == 1
 
 
-def test_plan_picks_cuda_cores_for_few_streams():
-    # config 1 (one sequence, 4 KV heads): the CUDA-core kernel, several splits + combine
+def test_plan_kernel_choice():
+    # config 1 (one sequence, 4 KV heads): the tensor-core kernel, several splits + combine
     ws = ops.gqa_workspace_bytes(1, NQ, NKV, HD, 8192)
     kind, n, launches = ops.gqa_decode_plan(1, NQ, NKV, HD, 8192, ws)
-    assert kind == "cc" and n > 1 and launches == 2
-    assert ws >= n * REC(1)
+    assert kind == "tc" and n > 1 and launches == 2
     # config 2 (256 sequences): the tensor-core kernel, one split
     kind, n, launches = ops.gqa_decode_plan(256, NQ, NKV, HD, 4160, REC(256))
     assert (kind, n, launches) == ("tc", 1, 1)
-    # the flags override the choice
-    assert ops.gqa_decode_plan(1, NQ, NKV, HD, 8192, ws, kernel="tc")[0] == "tc"
+    # the CUDA-core kernel only when asked for; its own split count, capped by the workspace
+    kind, n, launches = ops.gqa_decode_plan(1, NQ, NKV, HD, 8192, 1 << 30, kernel="cc")
+    assert kind == "cc" and n > 1 and launches == 2
+    assert ops.gqa_decode_plan(1, NQ, NKV, HD, 8192, REC(1), kernel="cc")[1:] == (1, 1)
     assert ops.gqa_decode_plan(256, NQ, NKV, HD, 4160, REC(256), kernel="cc")[0] == "cc"

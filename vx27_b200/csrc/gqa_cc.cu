@@ -31,6 +31,9 @@
 
 namespace vx27 {
 
+int launch_gqa_combine(const float *parts, int n_parts, const void *gate, void *out, int B,
+                       int nq, int flags, cudaStream_t st, char *err, size_t errlen, bool pdl);
+
 namespace {
 
 constexpr int HD = 256;
@@ -376,41 +379,6 @@ __global__ void __launch_bounds__(CC_THREADS, 2) gqa_split_cc(const __grid_const
     }
 }
 
-// Merge of the split records with the sigmoid gate, launched after the split kernel with
-// programmatic dependent launch (it waits for the split kernel before reading).
-template <bool ACT_BF16, bool OUT_BF16>
-__global__ void __launch_bounds__(HD)
-gqa_combine_cc(const float *__restrict__ parts, int n_parts, const void *__restrict__ gate,
-               void *__restrict__ out, int B, int nq) {
-    grid_dep_wait();
-    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
-    const size_t rec = (size_t)B * nq * (HD + 2);
-    const size_t hq = (size_t)b * nq + h;
-    float M = -INFINITY;
-    for (int r = 0; r < n_parts; r++) {
-        const float *ml = parts + (size_t)r * rec + (size_t)B * nq * HD + hq * 2;
-        if (ml[1] > 0.0f) M = fmaxf(M, ml[0]);
-    }
-    float L = 0.0f, O = 0.0f;
-    if (M != -INFINITY) {
-        for (int r = 0; r < n_parts; r++) {
-            const float *pr = parts + (size_t)r * rec;
-            const float *ml = pr + (size_t)B * nq * HD + hq * 2;
-            if (!(ml[1] > 0.0f)) continue;
-            const float w = ml[1] * expf(ml[0] - M);
-            L += w;
-            O = fmaf(w, pr[hq * HD + d], O);
-        }
-    }
-    const float att = L > 0.0f ? O / L : 0.0f;
-    if (gate) {
-        const float g = act_ld<ACT_BF16>(gate, hq * HD + d);
-        act_st<OUT_BF16>(out, hq * HD + d, att * (1.0f / (1.0f + expf(-g))));
-    } else {
-        act_st<OUT_BF16>(out, hq * HD + d, att);
-    }
-}
-
 size_t cc_smem_bytes() { return sizeof(CcSmem) + 128; }
 
 }  // namespace
@@ -506,11 +474,9 @@ int launch_decode_cc(const void *kc, const void *vc, const float *q, const int *
 #undef VX_CC
     VX_CK(cudaGetLastError());
     if (n_splits == 1) return 1;
-    const dim3 cgrid(nq, B);
-    if (ab && ob) VX_CK(launch_pdl(gqa_combine_cc<true, true>, cgrid, dim3(HD), 0, st, (const float *)parts, n_splits, gate, out, B, nq));
-    else if (ab) VX_CK(launch_pdl(gqa_combine_cc<true, false>, cgrid, dim3(HD), 0, st, (const float *)parts, n_splits, gate, out, B, nq));
-    else if (ob) VX_CK(launch_pdl(gqa_combine_cc<false, true>, cgrid, dim3(HD), 0, st, (const float *)parts, n_splits, gate, out, B, nq));
-    else VX_CK(launch_pdl(gqa_combine_cc<false, false>, cgrid, dim3(HD), 0, st, (const float *)parts, n_splits, gate, out, B, nq));
+    // the combine waits for this kernel (programmatic dependent launch)
+    if (launch_gqa_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen, true))
+        return -1;
     return 2;
 }
 

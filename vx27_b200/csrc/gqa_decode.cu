@@ -101,28 +101,93 @@ gqa_append_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
 }
 
 // ---- combine ------------------------------------------------------------------------
-template <bool ACT_BF16, bool OUT_BF16>
+// One CTA per (Q head, sequence) merges the split records: m* = max m_i,
+// l* = sum l_i e^{m_i - m*}, o = sum o_i l_i e^{m_i - m*} / l* (records with l_i = 0 skipped).
+// The records' (m, l) are read in parallel and their weights staged in shared memory in
+// blocks of CMB_R, then each thread (one output dim) sums its column with independent
+// loads; the sums run in record order, so the result does not depend on the block size.
+constexpr int CMB_R = 1024;
+
+struct CmbWeights {
+    float w[CMB_R];
+    float red[HD / 32];
+    float M;
+};
+
+// Max of the valid records' m over all n_parts (every thread gets it).
+__device__ __forceinline__ float cmb_max(const float *__restrict__ parts, int n_parts, size_t rec,
+                                         size_t ml_off, CmbWeights &cw) {
+    const int d = threadIdx.x;
+    float M = -INFINITY;
+    for (int r = d; r < n_parts; r += HD) {
+        const float2 ml = *reinterpret_cast<const float2 *>(parts + (size_t)r * rec + ml_off);
+        if (ml.y > 0.0f) M = fmaxf(M, ml.x);
+    }
+    M = warp_max(M);
+    if ((d & 31) == 0) cw.red[d >> 5] = M;
+    __syncthreads();
+    if (d == 0) {
+        float t = cw.red[0];
+        for (int w = 1; w < HD / 32; w++) t = fmaxf(t, cw.red[w]);
+        cw.M = t;
+    }
+    __syncthreads();
+    return cw.M;
+}
+
+// (L, O) for output dim threadIdx.x: L = sum w_r, O = sum w_r o_r[d] in record order.
+__device__ __forceinline__ void cmb_sum(const float *__restrict__ parts, int n_parts, size_t rec,
+                                        size_t ml_off, size_t o_off, float M, CmbWeights &cw,
+                                        float &L, float &O) {
+    const int d = threadIdx.x;
+    L = 0.0f;
+    O = 0.0f;
+    if (M == -INFINITY) return;
+    for (int r0 = 0; r0 < n_parts; r0 += CMB_R) {
+        const int n = min(CMB_R, n_parts - r0);
+        __syncthreads();
+        for (int r = d; r < n; r += HD) {
+            const float2 ml = *reinterpret_cast<const float2 *>(parts + (size_t)(r0 + r) * rec + ml_off);
+            cw.w[r] = ml.y > 0.0f ? ml.y * expf(ml.x - M) : 0.0f;
+        }
+        __syncthreads();
+        const float *col = parts + (size_t)r0 * rec + o_off + d;
+        int r = 0;
+        for (; r + 8 <= n; r += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = col[(size_t)(r + u) * rec];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float w = cw.w[r + u];
+                if (w != 0.0f) {  // skipped records (w = 0) add nothing
+                    L += w;
+                    O = fmaf(w, v[u], O);
+                }
+            }
+        }
+        for (; r < n; r++) {
+            const float w = cw.w[r];
+            if (w != 0.0f) {
+                L += w;
+                O = fmaf(w, col[(size_t)r * rec], O);
+            }
+        }
+    }
+}
+
+template <bool ACT_BF16, bool OUT_BF16, bool PDL>
 __global__ void __launch_bounds__(HD)
 gqa_combine_k(const float *__restrict__ parts, int n_parts, const void *__restrict__ gate,
               void *__restrict__ out, int B, int nq, size_t rec) {
+    if constexpr (PDL) grid_dep_wait();
+    __shared__ CmbWeights cw;
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const size_t hq = (size_t)b * nq + h;
-    float M = -INFINITY;
-    for (int r = 0; r < n_parts; r++) {
-        const float *ml = parts + (size_t)r * rec + (size_t)B * nq * HD + hq * 2;
-        if (ml[1] > 0.0f) M = fmaxf(M, ml[0]);
-    }
-    float L = 0.0f, O = 0.0f;
-    if (M != -INFINITY) {
-        for (int r = 0; r < n_parts; r++) {
-            const float *pr = parts + (size_t)r * rec;
-            const float *ml = pr + (size_t)B * nq * HD + hq * 2;
-            if (!(ml[1] > 0.0f)) continue;
-            const float w = ml[1] * expf(ml[0] - M);
-            L += w;
-            O = fmaf(w, pr[hq * HD + d], O);
-        }
-    }
+    const size_t ml_off = (size_t)B * nq * HD + hq * 2;
+    const float M = cmb_max(parts, n_parts, rec, ml_off, cw);
+    float L, O;
+    cmb_sum(parts, n_parts, rec, ml_off, hq * HD, M, cw, L, O);
     const float att = L > 0.0f ? O / L : 0.0f;
     if (gate) {
         const float g = act_ld<ACT_BF16>(gate, hq * HD + d);
@@ -138,25 +203,14 @@ gqa_combine_k(const float *__restrict__ parts, int n_parts, const void *__restri
 __global__ void __launch_bounds__(HD)
 gqa_merge_k(const float *__restrict__ parts, int n_parts, float *__restrict__ rec_out, int B,
             int nq) {
+    __shared__ CmbWeights cw;
     const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const size_t rec = (size_t)B * nq * (HD + 2);
     const size_t hq = (size_t)b * nq + h;
-    float M = -INFINITY;
-    for (int r = 0; r < n_parts; r++) {
-        const float *ml = parts + (size_t)r * rec + (size_t)B * nq * HD + hq * 2;
-        if (ml[1] > 0.0f) M = fmaxf(M, ml[0]);
-    }
-    float L = 0.0f, O = 0.0f;
-    if (M != -INFINITY) {
-        for (int r = 0; r < n_parts; r++) {
-            const float *pr = parts + (size_t)r * rec;
-            const float *ml = pr + (size_t)B * nq * HD + hq * 2;
-            if (!(ml[1] > 0.0f)) continue;
-            const float w = ml[1] * expf(ml[0] - M);
-            L += w;
-            O = fmaf(w, pr[hq * HD + d], O);
-        }
-    }
+    const size_t ml_off = (size_t)B * nq * HD + hq * 2;
+    const float M = cmb_max(parts, n_parts, rec, ml_off, cw);
+    float L, O;
+    cmb_sum(parts, n_parts, rec, ml_off, hq * HD, M, cw, L, O);
     rec_out[hq * HD + d] = L > 0.0f ? O / L : 0.0f;
     if (d == 0) {
         float *ml = rec_out + (size_t)B * nq * HD + hq * 2;
@@ -189,13 +243,14 @@ int auto_splits(int B, int nkv, int max_ctx) {
     return best;
 }
 
-// Which decode kernel a call uses: the flags' choice, else the CUDA-core kernel while the
-// (sequence, KV head) streams are few enough that the tensor-core kernel's per-CTA
-// pipeline start-up, not HBM, would bound it.
+// Which decode kernel a call uses: the tensor-core kernel unless the flags ask for the
+// CUDA-core one. Measured on a B200 (graph-replayed, events): the CUDA-core kernel is the
+// slower at every shape tried, 1.5x at one sequence of 8192 positions and 2.8x at 256
+// sequences of 4096 (its fp32 FMA work per cache byte, not HBM, bounds it).
 bool use_cc(int B, int nkv, int flags) {
-    if (flags & VX27_F_DECODE_CC) return true;
-    if (flags & VX27_F_DECODE_TC) return false;
-    return (long long)B * nkv <= 16;
+    (void)B;
+    (void)nkv;
+    return (flags & VX27_F_DECODE_CC) && !(flags & VX27_F_DECODE_TC);
 }
 
 // The split count a decode call runs with: n_splits when given, else the chosen kernel's
@@ -213,15 +268,25 @@ int launch_split(const float *q, const void *kc, const void *vc, int cap, const 
                            err, errlen);
 }
 
+// pdl: launched with programmatic dependent launch (the kernel waits for its predecessor,
+// so its launch overlaps the split kernel's tail)
 int launch_combine(const float *parts, int n_parts, const void *gate, void *out, int B, int nq,
-                   int flags, cudaStream_t st, char *err, size_t errlen, size_t stride = 0) {
+                   int flags, cudaStream_t st, char *err, size_t errlen, size_t stride = 0,
+                   bool pdl = false) {
     const dim3 grid(nq, B);
     const bool a = flags & VX27_F_ACT_BF16, o = flags & VX27_F_OUT_BF16;
     const size_t rec = stride ? stride : (size_t)B * nq * (HD + 2);
-    if (a && o) gqa_combine_k<true, true><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
-    else if (a) gqa_combine_k<true, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
-    else if (o) gqa_combine_k<false, true><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
-    else gqa_combine_k<false, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
+#define VX_CMB(A_, O_)                                                                     \
+    if (pdl)                                                                               \
+        VX_CK(launch_pdl(gqa_combine_k<A_, O_, true>, grid, dim3(HD), 0, st, parts, n_parts, \
+                         gate, out, B, nq, rec));                                          \
+    else                                                                                   \
+        gqa_combine_k<A_, O_, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
+    if (a && o) { VX_CMB(true, true) }
+    else if (a) { VX_CMB(true, false) }
+    else if (o) { VX_CMB(false, true) }
+    else { VX_CMB(false, false) }
+#undef VX_CMB
     VX_CK(cudaGetLastError());
     return 0;
 }
@@ -235,13 +300,33 @@ int check_shape(const char *fn, int B, int nq, int nkv, int hd, char *err, size_
 
 }  // namespace
 
-// The split-count choice and the combine launch for other translation units
-// (gqa_noalloc.cu); neither allocates.
-int gqa_auto_splits(int B, int nkv, int max_ctx) { return auto_splits(B, nkv, max_ctx); }
+// The decode's split-count choice and its launches after the argument checks, for
+// vx27_gqa_decode_batch and the entry point without a workspace (gqa_noalloc.cu): the
+// kernel by use_cc, n_splits records at parts. Allocates nothing.
+int gqa_plan_splits(int B, int nkv, int cap, int n_splits, int fit, int flags) {
+    return plan_splits(B, nkv, cap, n_splits, fit, use_cc(B, nkv, flags));
+}
+
+int gqa_decode_dispatch(const float *q, const void *gate, const void *k_cache,
+                        const void *v_cache, int cap, const int *pos, void *out, float *parts,
+                        int B, int nq, int nkv, int n_splits, int flags, cudaStream_t st,
+                        char *err, size_t errlen) {
+    if (use_cc(B, nkv, flags))
+        return launch_decode_cc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, n_splits, gate,
+                                out, flags, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                0, 0, 0.0f, st, err, errlen) < 0 ? -1 : 0;
+    if (n_splits == 1)  // the split kernel applies the gate and writes out; no combine pass
+        return launch_split_tc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, 1, 0, -1, st,
+                               err, errlen, gate, out, flags);
+    if (launch_split(q, k_cache, v_cache, cap, pos, parts, B, nq, nkv, n_splits, 0, -1, st, err,
+                     errlen))
+        return -1;
+    return launch_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen, 0, true);
+}
 
 int launch_gqa_combine(const float *parts, int n_parts, const void *gate, void *out, int B,
-                       int nq, int flags, cudaStream_t st, char *err, size_t errlen) {
-    return launch_combine(parts, n_parts, gate, out, B, nq, flags, st, err, errlen);
+                       int nq, int flags, cudaStream_t st, char *err, size_t errlen, bool pdl) {
+    return launch_combine(parts, n_parts, gate, out, B, nq, flags, st, err, errlen, 0, pdl);
 }
 
 }  // namespace vx27
@@ -284,11 +369,7 @@ int vx27_gqa_append(const void *q_in, const void *k_in, const void *v_in,
 size_t vx27_gqa_decode_workspace_size(int B, int nq, int nkv, int hd, int max_ctx,
                                       int n_splits) {
     if (B <= 0 || nq <= 0 || nkv <= 0 || hd <= 0) return 0;
-    if (n_splits <= 0) {  // enough for either kernel's automatic count
-        n_splits = auto_splits(B, nkv, max_ctx);
-        const int c = cc_auto_splits(B, nkv, max_ctx);
-        if (use_cc(B, nkv, 0) && c > n_splits) n_splits = c;
-    }
+    if (n_splits <= 0) n_splits = auto_splits(B, nkv, max_ctx);
     return (size_t)n_splits * B * nq * (hd + 2) * sizeof(float);
 }
 
@@ -314,25 +395,13 @@ int vx27_gqa_decode_batch(const float *q, const void *gate, const void *k_cache,
         return fail(err, errlen, "vx27_gqa_decode_batch: null pointer argument");
     const size_t rec = (size_t)B * nq * (hd + 2) * sizeof(float);
     const int fit = (int)(workspace_bytes / rec);
-    const bool cc = use_cc(B, nkv, flags);
-    n_splits = plan_splits(B, nkv, cap, n_splits, fit, cc);
+    n_splits = plan_splits(B, nkv, cap, n_splits, fit, use_cc(B, nkv, flags));
     if (n_splits < 1 || n_splits > fit || n_splits > 65535)
         return fail(err, errlen,
                     "vx27_gqa_decode_batch: workspace of %zu bytes holds %d splits, need %d",
                     workspace_bytes, fit, n_splits < 1 ? 1 : n_splits);
-    cudaStream_t st = (cudaStream_t)stream;
-    float *parts = (float *)workspace;
-    if (cc)
-        return launch_decode_cc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, n_splits, gate,
-                                out, flags, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
-                                0, 0, 0.0f, st, err, errlen) < 0 ? -1 : 0;
-    if (n_splits == 1)  // the split kernel applies the gate and writes out; no combine pass
-        return launch_split_tc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, 1, 0, -1, st,
-                               err, errlen, gate, out, flags);
-    if (launch_split(q, k_cache, v_cache, cap, pos, parts, B, nq, nkv, n_splits, 0, -1, st, err,
-                     errlen))
-        return -1;
-    return launch_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen);
+    return gqa_decode_dispatch(q, gate, k_cache, v_cache, cap, pos, out, (float *)workspace, B,
+                               nq, nkv, n_splits, flags, (cudaStream_t)stream, err, errlen);
 }
 
 int vx27_gqa_decode_fused(const void *q_in, const void *k_in, const void *v_in,
@@ -368,7 +437,7 @@ int vx27_gqa_decode_fused(const void *q_in, const void *k_in, const void *v_in,
                               st, err, errlen))
         return -1;
     if (direct) return 0;
-    return launch_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen);
+    return launch_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen, 0, true);
 }
 
 size_t vx27_gqa_partial_workspace_size(int B, int nq, int nkv, int hd, int max_range) {

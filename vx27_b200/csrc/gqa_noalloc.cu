@@ -16,13 +16,11 @@
 #include "../../include/vx27_gqa.h"
 
 namespace vx27 {
-int launch_split_tc(const void *kc, const void *vc, const float *q, const int *pos, float *parts,
-                    int cap, int B, int nq, int nkv, int n_splits, int p_begin, int p_end,
-                    cudaStream_t st, char *err, size_t errlen, const void *gate, void *out,
-                    int flags);
-int launch_gqa_combine(const float *parts, int n_parts, const void *gate, void *out, int B,
-                       int nq, int flags, cudaStream_t st, char *err, size_t errlen);
-int gqa_auto_splits(int B, int nkv, int max_ctx);
+int gqa_plan_splits(int B, int nkv, int cap, int n_splits, int fit, int flags);
+int gqa_decode_dispatch(const float *q, const void *gate, const void *k_cache,
+                        const void *v_cache, int cap, const int *pos, void *out, float *parts,
+                        int B, int nq, int nkv, int n_splits, int flags, cudaStream_t st,
+                        char *err, size_t errlen);
 }  // namespace vx27
 
 namespace {
@@ -79,8 +77,7 @@ extern "C" int vx27_gqa_decode_batch_noalloc(const float *q, const void *gate,
                     fn, record, (unsigned)VX27_GQA_NOALLOC_SCRATCH_BYTES,
                     (unsigned)VX27_GQA_NOALLOC_SCRATCH_BYTES);
     if (n_splits <= 0) {  // the workspace entry point's choice, capped by the array
-        n_splits = gqa_auto_splits(B, nkv, cap);
-        if (n_splits > fit) n_splits = fit;
+        n_splits = gqa_plan_splits(B, nkv, cap, 0, fit, flags);
     } else if (n_splits > fit || n_splits > 65535) {
         return fail(err, errlen,
                     "%s: %d splits need %zu bytes of partial records, more than the %u-byte "
@@ -90,15 +87,10 @@ extern "C" int vx27_gqa_decode_batch_noalloc(const float *q, const void *gate,
     }
     float *parts = scratch_on_current_device(err, errlen);
     if (!parts) return -1;
-    // Every record the combine reads is written by the split kernel first (empty ranges
-    // write a neutral record), so nothing left from an earlier call needs clearing. With
-    // one split the kernel writes the gated output itself, as vx27_gqa_decode_batch does.
-    cudaStream_t st = (cudaStream_t)stream;
-    if (n_splits == 1)
-        return launch_split_tc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, 1, 0, -1, st,
-                               err, errlen, gate, out, flags);
-    if (launch_split_tc(k_cache, v_cache, q, pos, parts, cap, B, nq, nkv, n_splits, 0, -1, st,
-                        err, errlen, nullptr, nullptr, 0))
-        return -1;
-    return launch_gqa_combine(parts, n_splits, gate, out, B, nq, flags, st, err, errlen);
+    // The same kernels as vx27_gqa_decode_batch. Every record the combine reads is written
+    // by the split kernel first (empty ranges write a neutral record), so nothing left from
+    // an earlier call needs clearing. With one split the kernel writes the gated output
+    // itself.
+    return gqa_decode_dispatch(q, gate, k_cache, v_cache, cap, pos, out, parts, B, nq, nkv,
+                               n_splits, flags, (cudaStream_t)stream, err, errlen);
 }

@@ -377,6 +377,36 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
+    // Issues ring chunk j (tile jj / 8 of item it, K for jj % 8 < 4, V otherwise).
+    auto issue_chunk = [&](const TcItem &it, int jj, int j) {
+        const int slot = j % NSLOT;
+        const int tile = jj >> 3, r = jj & 7;
+        // the last tile fetches only the 32-row boxes that hold positions of the range
+        // (the rows past it are masked, and V's are zeroed, by the softmax warps)
+        const int rows_left = it.p1 - (it.p0 + tile * TC_TILE);
+        if (rows_left < TC_TILE) {
+            const int nsub = (rows_left + 31) / 32;
+            mbar_arrive_expect_tx(&sm.full[slot], nsub * (SLOT_BYTES / 4));
+            for (int k = 0; k < nsub; k++)
+                tma_load_2d(sm.ring[slot] + k * (SLOT_BYTES / 4), r < 4 ? &tmk32 : &tmv32,
+                            (r & 3) * 64, it.row0 + tile * TC_TILE + 32 * k, &sm.full[slot]);
+        } else {
+            mbar_arrive_expect_tx(&sm.full[slot], SLOT_BYTES);
+            tma_load_2d(sm.ring[slot], r < 4 ? &tmk : &tmv, (r & 3) * 64,
+                        it.row0 + tile * TC_TILE, &sm.full[slot]);
+        }
+    };
+    // VX27_F_PREFETCH_KV: the first ring round of the first item is requested before the
+    // wait for the previous kernel (which, by the flag's contract, writes neither pos nor
+    // any cache row but the token's), except the tile that holds the token's row
+    int j_pre = 0;
+    if ((flags & VX27_F_PREFETCH_KV) && warp == 0 && lane == 0 && w_first < n_items) {
+        const TcItem it = item(w_first);
+        const int p_tok = p_end >= 0 ? -1 : pos[it.b];
+        const int tok_tile = (p_tok >= it.p0 && p_tok < it.p1) ? (p_tok - it.p0) / TC_TILE : -1;
+        for (; j_pre < NSLOT && j_pre < it.n_tiles * 8 && (j_pre >> 3) != tok_tile; j_pre++)
+            issue_chunk(it, j_pre, j_pre);
+    }
     // q, gate, positions and the newest cache rows come from the kernels before this one
     grid_dep_wait();
     if (tid == 0) grid_dep_launch();
@@ -397,31 +427,19 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
                         ok = false;
                         break;
                     }
+                    if (j < j_pre) continue;  // requested before the dependency wait
                     const int slot = j % NSLOT, round = j / NSLOT;
                     if (round > 0 &&
                         !tc_wait(&sm.empty[slot], (round - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA)) {
                         ok = false;
                         break;
                     }
-                    const int tile = jj >> 3, r = jj & 7;
-                    // the last tile fetches only the 32-row boxes that hold positions of the
-                    // range (the rows past it are masked, and V's are zeroed, by the softmax warps)
-                    const int rows_left = it.p1 - (it.p0 + tile * TC_TILE);
-                    if (rows_left < TC_TILE) {
-                        const int nsub = (rows_left + 31) / 32;
-                        mbar_arrive_expect_tx(&sm.full[slot], nsub * (SLOT_BYTES / 4));
-                        for (int k = 0; k < nsub; k++)
-                            tma_load_2d(sm.ring[slot] + k * (SLOT_BYTES / 4), r < 4 ? &tmk32 : &tmv32,
-                                        (r & 3) * 64, it.row0 + tile * TC_TILE + 32 * k, &sm.full[slot]);
-                    } else {
-                        mbar_arrive_expect_tx(&sm.full[slot], SLOT_BYTES);
-                        tma_load_2d(sm.ring[slot], r < 4 ? &tmk : &tmv, (r & 3) * 64,
-                                    it.row0 + tile * TC_TILE, &sm.full[slot]);
-                    }
+                    issue_chunk(it, jj, j);
                 }
             }
             if (sm.abort) {  // let the copies already issued land before the CTA exits
-                for (int k = max(0, j - NSLOT); k < j; k++) {
+                const int jn = max(j, j_pre);
+                for (int k = max(0, jn - NSLOT); k < jn; k++) {
                     const uint32_t addr = smem_u32(&sm.full[k % NSLOT]);
                     for (int it = 0; it < (1 << 20); it++) {
                         uint32_t ok2;
