@@ -45,6 +45,20 @@ int vx27_gqa_append(const void *q_in, const void *k_in, const void *v_in,
                     size_t errlen);
 
 /*
+ * vx27_gqa_append for sequences in groups that have their own norm weights: sequence b
+ * uses row b / seqs_per_weight of q_norm_w and k_norm_w ([B / seqs_per_weight][hd]).
+ * With the layers of a model stacked as the batch ([layer][seq] as one index, caches and
+ * activations laid out [layer][B][...]), one call serves every layer. No counterpart in
+ * the reference (it runs the layers one at a time, src/vx27_qfwd.c:339-346).
+ */
+int vx27_gqa_append_grouped(const void *q_in, const void *k_in, const void *v_in,
+                            const float *q_norm_w, const float *k_norm_w, int seqs_per_weight,
+                            const float *rope_table, int rope_table_len, const int *pos,
+                            int slot_base, void *k_cache, void *v_cache, int cap, float *q_out,
+                            int B, int nq, int nkv, int hd, int rope_dim, float eps, int flags,
+                            void *stream, char *err, size_t errlen);
+
+/*
  * Decode attention of q (from vx27_gqa_append) over slots [0, pos[b]] of the caches,
  * softmax(q k^T / sqrt(hd)) v per Q head (Q head h reads KV head h*nkv/nq), then
  * out = att * sigmoid(gate) (src/vx27_qfwd.c:347-371). Split-KV flash decoding: each

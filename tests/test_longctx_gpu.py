@@ -40,3 +40,26 @@ def test_long_range_partial_split_and_merged(cuda):
     one.combine(one.parts.reshape(1, -1))
     torch.cuda.synchronize()
     assert rel_err(host(one.out.float()).reshape(-1), host(whole.out.float()).reshape(-1)) < 1e-2
+
+
+def test_stacked_layers_equal_per_layer_calls(cuda):
+    """One step with the layers stacked as the batch (grouped norm weights, one append and
+    one decode for all layers) against each layer run on its own: the K/V rows it appends
+    are the same bits, the outputs agree within the decode's tolerance (the split counts
+    differ)."""
+    from vx27_b200 import ops
+    from vx27_b200.longctx import HD, NKV, NQ
+    P, layers = 3000, 3
+    a = LongContextGQA(2, ctx=P, layers=layers, seed=9)
+    b = LongContextGQA(2, ctx=P, layers=layers, seed=9)
+    a.step()
+    for l in range(layers):
+        ops.gqa_append(b.q_in[l], b.k_in[l], b.v_in[l], b.q_norm_w[l], b.k_norm_w[l], b.rope,
+                       b.pos, b.kc[l], b.vc[l], b.qn[l])
+        ops.gqa_decode_batch(b.qn[l], b.gate[l], b.kc[l], b.vc[l], b.pos, b.out[l], b.ws)
+    torch.cuda.synchronize()
+    assert torch.equal(a.kc[:, :, :, P - 1], b.kc[:, :, :, P - 1])
+    assert torch.equal(a.vc[:, :, :, P - 1], b.vc[:, :, :, P - 1])
+    assert torch.equal(a.qn, b.qn)
+    assert rel_err(host(a.out.float()).reshape(-1), host(b.out.float()).reshape(-1)) < 1e-2
+    assert ops.device_status() == 0

@@ -60,6 +60,8 @@ PROTOTYPES: dict[str, tuple] = {
     "vx27_attn_1q": (None, [_p, _p, _p, _i, _p]),
     "vx27_gqa_append": (_i, [_p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _p, _i, _p, _i, _i, _i, _i,
                              _i, _f, _i, _p, _cp, _sz]),
+    "vx27_gqa_append_grouped": (_i, [_p, _p, _p, _p, _p, _i, _p, _i, _p, _i, _p, _p, _i, _p, _i,
+                                     _i, _i, _i, _i, _f, _i, _p, _cp, _sz]),
     "vx27_gqa_decode_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),
     "vx27_gqa_decode_batch": (_i, [_p, _p, _p, _p, _i, _p, _p, _p, _sz, _i, _i, _i, _i, _i, _i,
                                    _p, _cp, _sz]),

@@ -48,7 +48,7 @@ gqa_append_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
              const float *__restrict__ kw, const float *__restrict__ rope, int rope_len,
              const int *__restrict__ pos, int slot_base, uint16_t *__restrict__ kc,
              uint16_t *__restrict__ vc, int cap, float *__restrict__ q_out, int nq, int nkv,
-             int rope_dim, float eps, uint32_t *status) {
+             int rope_dim, float eps, int w_group, uint32_t *status) {
     grid_dep_wait();  // inputs and positions come from the kernels before this one
     if (threadIdx.x == 0) grid_dep_launch();
     const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
@@ -68,7 +68,8 @@ gqa_append_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
         r_s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(t / HD), eps)));
     }
     __syncthreads();
-    float w = is_q ? qw[d] : kw[d];
+    const size_t wrow = (size_t)(b / w_group) * HD;  // norm weights of this sequence's group
+    float w = is_q ? qw[wrow + d] : kw[wrow + d];
     if (ONE_P) w = __fadd_rn(w, 1.0f);
     const float y = __fmul_rn(__fmul_rn(x, r_s), w);
     y_s[d] = y;
@@ -341,7 +342,21 @@ int vx27_gqa_append(const void *q_in, const void *k_in, const void *v_in,
                     void *v_cache, int cap, float *q_out, int B, int nq, int nkv, int hd,
                     int rope_dim, float eps, int flags, void *stream, char *err,
                     size_t errlen) {
+    return vx27_gqa_append_grouped(q_in, k_in, v_in, q_norm_w, k_norm_w, B, rope_table,
+                                   rope_table_len, pos, slot_base, k_cache, v_cache, cap, q_out,
+                                   B, nq, nkv, hd, rope_dim, eps, flags, stream, err, errlen);
+}
+
+int vx27_gqa_append_grouped(const void *q_in, const void *k_in, const void *v_in,
+                            const float *q_norm_w, const float *k_norm_w, int seqs_per_weight,
+                            const float *rope_table, int rope_table_len, const int *pos,
+                            int slot_base, void *k_cache, void *v_cache, int cap, float *q_out,
+                            int B, int nq, int nkv, int hd, int rope_dim, float eps, int flags,
+                            void *stream, char *err, size_t errlen) {
     if (check_shape("vx27_gqa_append", B, nq, nkv, hd, err, errlen)) return -1;
+    if (seqs_per_weight <= 0 || B % seqs_per_weight)
+        return fail(err, errlen, "vx27_gqa_append: %d sequences per weight row does not divide B=%d",
+                    seqs_per_weight, B);
     if (rope_dim < 0 || rope_dim > hd || (rope_dim & 1))
         return fail(err, errlen, "vx27_gqa_append: rope_dim=%d", rope_dim);
     if (!q_in || !k_in || !v_in || !q_norm_w || !k_norm_w || !pos || !q_out ||
@@ -356,7 +371,7 @@ int vx27_gqa_append(const void *q_in, const void *k_in, const void *v_in,
     VX_CK(launch_pdl(gqa_append_k<A_, O_>, grid, dim3(HD), 0, st, q_in, k_in, v_in, q_norm_w, \
                      k_norm_w, rope_table, rope_table_len, pos, slot_base,                 \
                      (uint16_t *)k_cache, (uint16_t *)v_cache, cap, q_out, nq, nkv, rope_dim, \
-                     eps, dev_status()))
+                     eps, seqs_per_weight, dev_status()))
     if (a && one) VX_A(true, true);
     else if (a) VX_A(true, false);
     else if (one) VX_A(false, true);

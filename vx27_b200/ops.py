@@ -306,6 +306,10 @@ def rope_table(n_pos: int, rope_dim: int = 64, theta: float = 1e7, yarn: float =
 def gqa_append(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, pos, k_cache, v_cache, q_out,
                eps: float = 1e-6, slot_base: int = 0, norm_one_plus: bool = False,
                stream=None) -> None:
+    """QK norm + RoPE + K/V store of one token per sequence (vx27_gqa_append). The norm
+    weights are [hd], or [G, hd] for G groups of B / G consecutive sequences each with
+    their own weights (vx27_gqa_append_grouped: the layers of a model stacked as the
+    batch)."""
     B, nq, hd = q_in.shape
     nkv = k_in.shape[1]
     cap = k_cache.shape[2] if k_cache is not None else 0
@@ -313,8 +317,11 @@ def gqa_append(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, pos, k_cache, v_cache
     _need(q_in, "q_in", B * nq * hd, (f32, bf16))
     _need(k_in, "k_in", B * nkv * hd, (q_in.dtype,))
     _need(v_in, "v_in", B * nkv * hd, (q_in.dtype,))
-    _need(q_norm_w, "q_norm_w", hd, (f32,))
-    _need(k_norm_w, "k_norm_w", hd, (f32,))
+    groups = q_norm_w.numel() // hd if q_norm_w.numel() % hd == 0 else 0
+    if groups < 1 or B % groups:
+        raise Vx27Error(f"q_norm_w: {q_norm_w.numel()} values is not [G][{hd}] with G dividing {B}")
+    _need(q_norm_w, "q_norm_w", groups * hd, (f32,))
+    _need(k_norm_w, "k_norm_w", groups * hd, (f32,))
     _need(rope, "rope", 1, (f32,))
     _need(pos, "pos", B, (i32,))
     _need(k_cache, "k_cache", B * nkv * cap * hd, (bf16,), optional=True)
@@ -322,10 +329,11 @@ def gqa_append(q_in, k_in, v_in, q_norm_w, k_norm_w, rope, pos, k_cache, v_cache
     _need(q_out, "q_out", B * nq * hd, (f32,))
     flags = (F_ACT_BF16 if _is_bf16(q_in) else 0) | (F_NORM_1P if norm_one_plus else 0)
     e = errbuf()
-    rc = load().vx27_gqa_append(_t(q_in), _t(k_in), _t(v_in), _t(q_norm_w), _t(k_norm_w),
-                                _t(rope), rope.shape[0], _t(pos), slot_base, _t(k_cache),
-                                _t(v_cache), cap, _t(q_out), B, nq, nkv, hd, rope.shape[1], eps,
-                                flags, _stream(stream), e, 512)
+    rc = load().vx27_gqa_append_grouped(_t(q_in), _t(k_in), _t(v_in), _t(q_norm_w),
+                                        _t(k_norm_w), B // groups, _t(rope), rope.shape[0],
+                                        _t(pos), slot_base, _t(k_cache), _t(v_cache), cap,
+                                        _t(q_out), B, nq, nkv, hd, rope.shape[1], eps, flags,
+                                        _stream(stream), e, 512)
     check(rc, e)
 
 
