@@ -385,9 +385,7 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             float mloc = -INFINITY;
             if (ok) {
                 tc_fence_after();
-#pragma unroll
-                for (int i = 0; i < HK / 16; i++)
-                    tmem_ld16(tS + lane_off + hf * HK + 16 * i, s + 16 * i);
+                tmem_ld64(tS + lane_off + hf * HK, s);  // four loads in flight, one wait
                 tc_fence_before();
                 mbar_arrive(&sm.s_empty);
                 const int kbase = j * KT + hf * HK;

@@ -44,6 +44,26 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// 64 consecutive fp32 columns of this thread's TMEM lane as four 16-column loads in flight
+// together, one wait for all of them (same lane rule as tmem_ld16).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float *v) {
+    uint32_t r[64];
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+            "%13,%14,%15}, [%16];"
+            : "=r"(r[16 * q]), "=r"(r[16 * q + 1]), "=r"(r[16 * q + 2]), "=r"(r[16 * q + 3]),
+              "=r"(r[16 * q + 4]), "=r"(r[16 * q + 5]), "=r"(r[16 * q + 6]), "=r"(r[16 * q + 7]),
+              "=r"(r[16 * q + 8]), "=r"(r[16 * q + 9]), "=r"(r[16 * q + 10]),
+              "=r"(r[16 * q + 11]), "=r"(r[16 * q + 12]), "=r"(r[16 * q + 13]),
+              "=r"(r[16 * q + 14]), "=r"(r[16 * q + 15])
+            : "r"(taddr + 16 * q));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
+}
+
 // 4 consecutive fp32 columns (same lane rule as tmem_ld16).
 __device__ __forceinline__ void tmem_ld4(uint32_t taddr, float *v) {
     uint32_t r[4];
