@@ -552,6 +552,11 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
         fence_proxy_async();
     };
     write_sb();
+    // operand descriptors of stage 0, the state operand and U' (stepped per MMA)
+    const uint64_t d_stage0 = sdesc_sw128(smem_u32(stg), 16, 1024);
+    const uint64_t d_kt0 = sdesc_sw128(smem_u32(stg) + Lay::ST_KT, 8192, 1024);
+    const uint64_t d_sb = sdesc_sw128(smem_u32(SB), 16, 1024);
+    const uint64_t d_ub2 = sdesc_sw128(smem_u32(UB2), 16, 1024);
 
     for (int c = 0; c < n_chunks; c++) {
         const int st = c & 1;
@@ -564,14 +569,11 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
             if (!*abort_) {
                 tc_fence_after();
                 const uint32_t id = idesc_bf16(128, NB, false, false);
+                const uint64_t da = sdesc_add(d_stage0, st * Lay::STAGE);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; kk++)
-                    mma_bf16(tbase,
-                             sdesc_sw128(smem_u32(stage) + (kk >> 2) * 16384 + (kk & 3) * 32,
-                                         16, 1024),
-                             sdesc_sw128(smem_u32(SB) + (kk >> 2) * (NB * 128) + (kk & 3) * 32,
-                                         16, 1024),
-                             id, kk > 0);
+                    mma_bf16(tbase, sdesc_add(da, (kk >> 2) * 16384 + (kk & 3) * 32),
+                             sdesc_add(d_sb, (kk >> 2) * (NB * 128) + (kk & 3) * 32), id, kk > 0);
                 mma_commit(&bars[2]);
             }
         }
@@ -633,11 +635,11 @@ dn_scan_tc(Wsp ws, float *__restrict__ S, int n_chunks, uint32_t *status) {
         if (tid == 0 && !*abort_) {
             tc_fence_after();
             const uint32_t id = idesc_bf16(128, NB, true, false);
+            const uint64_t dk = sdesc_add(d_kt0, st * Lay::STAGE);
 #pragma unroll
             for (int kk = 0; kk < CK / 16; kk++)
-                mma_bf16(tbase + NB,
-                         sdesc_sw128(smem_u32(stage) + Lay::ST_KT + kk * 2048, 8192, 1024),
-                         sdesc_sw128(smem_u32(UB2) + kk * 32, 16, 1024), id, kk > 0);
+                mma_bf16(tbase + NB, sdesc_add(dk, kk * 2048), sdesc_add(d_ub2, kk * 32), id,
+                         kk > 0);
             mma_commit(&bars[3]);
         }
         if (!*abort_ && !mbar_wait(&bars[3], c & 1, status, VX_DEV_TIMEOUT_MMA)) *abort_ = 1;

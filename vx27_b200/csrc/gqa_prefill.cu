@@ -313,6 +313,8 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     } else if (warp == 1) {
         if (lane == 0) {  // ---- MMA issuer, S stream: S = Q K(m)^T once the softmax has read S(m-1)
             const uint32_t id1 = idesc_bf16(128, KT, false, false);
+            const uint64_t dq0 = sdesc_sw128(smem_u32(sm.q[0]), 16, 1024);
+            const uint64_t dr0 = sdesc_sw128(smem_u32(sm.ring[0]), 16, 1024);
             bool ok = pf_wait(&sm.qfull, 0, sm, status, VX_DEV_TIMEOUT_TMA);
             for (int m = 0; m < n_kt && ok; m++) {
                 if (m >= 1) ok = pf_wait(&sm.s_empty, (m - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
@@ -321,11 +323,12 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     ok = pf_wait(&sm.full[s2], (i / NKS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t qb = smem_u32(sm.q[c]), kb = smem_u32(sm.ring[s2]);
+                    const uint64_t dq = sdesc_add(dq0, c * (QT * 128));
+                    const uint64_t dk = sdesc_add(dr0, s2 * 16384);
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++)
-                        mma_bf16(tS, sdesc_sw128(qb + kk * 32, 16, 1024),
-                                 sdesc_sw128(kb + kk * 32, 16, 1024), id1, (c | kk) != 0);
+                        mma_bf16(tS, sdesc_add(dq, kk * 32), sdesc_add(dk, kk * 32), id1,
+                                 (c | kk) != 0);
                     mma_commit(&sm.empty[s2]);
                 }
                 if (!ok) break;
@@ -337,6 +340,8 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     } else if (warp == PF_THREADS / 32 - 1) {
         if (lane == 0) {  // ---- MMA issuer, O stream: O += P(t) V(t) once P(t) is written
             const uint32_t id2 = idesc_bf16(128, HDP, false, true);
+            const uint64_t dp0 = sdesc_sw128(smem_u32(sm.p[0][0]), 16, 1024);
+            const uint64_t dv0 = sdesc_sw128(smem_u32(sm.ring[0]), 32 * 128, 1024);
             bool ok = true;
             for (int t = 0; t < n_kt && ok; t++) {
                 const int pb = t & 1;
@@ -346,14 +351,14 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     ok = pf_wait(&sm.full[s2], (i / NVS) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t vb = smem_u32(sm.ring[s2]);
+                    const uint64_t dv = sdesc_add(dv0, s2 * 16384);
 #pragma unroll
                     for (int k2 = 0; k2 < 2; k2++) {
                         const int kk = 2 * c + k2;  // 16-key step of the 128-key tile
                         mma_bf16(tO,
-                                 sdesc_sw128(smem_u32(sm.p[pb][kk >> 2]) + (kk & 3) * 32, 16, 1024),
-                                 sdesc_sw128(vb + k2 * 2048, 32 * 128, 1024), id2,
-                                 (t > 0 || kk > 0) ? 1u : 0u);
+                                 sdesc_add(dp0, (uint32_t)(pb * 2 + (kk >> 2)) * (QT * 128) +
+                                                    (kk & 3) * 32),
+                                 sdesc_add(dv, k2 * 2048), id2, (t > 0 || kk > 0) ? 1u : 0u);
                     }
                     mma_commit(&sm.empty[s2]);
                 }

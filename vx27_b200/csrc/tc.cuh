@@ -134,6 +134,13 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
          | (1ull << 46)                               // descriptor version (sm100)
          | (2ull << 61);                              // SWIZZLE_128B
 }
+// The descriptor of the same operand layout byte_off bytes further on: the start address
+// field holds address >> 4 in 14 bits, and shared-memory addresses stay below 2^18, so the
+// addition never carries into the next field. Issue loops build one descriptor per buffer
+// and step it, instead of rebuilding every field per MMA.
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t desc, uint32_t byte_off) {
+    return desc + (uint64_t)(byte_off >> 4);
+}
 // D(tmem) (+)= A(smem) x B(smem); issued by one thread.
 __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
