@@ -351,6 +351,9 @@ dn_decode_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             if (tid == 0) mbar_arrive(&sm.pempty[pslot]);
         }
     }
+    // lanes that skipped a lane-0 role wait for it here, so whole warps reach the CTA
+    // barrier together (it requires converged warps)
+    __syncwarp();
     __syncthreads();
 }
 

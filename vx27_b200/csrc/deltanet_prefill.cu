@@ -429,6 +429,9 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     }
     if (tid == 0) bulk_wait0();
     tc_fence_before();
+    // lanes that skipped a lane-0 role wait for it here, so whole warps reach the CTA
+    // barrier together (it requires converged warps)
+    __syncwarp();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tbase, 256);
 }
@@ -736,6 +739,9 @@ dn_out_tc(Wsp ws, void *__restrict__ o, int T, int nv, int n_chunks, uint32_t *s
         }
         *okf = ok ? 1 : 0;
     }
+    // lanes that skipped a lane-0 role wait for it here, so whole warps reach the CTA
+    // barrier together (it requires converged warps)
+    __syncwarp();
     __syncthreads();
     bool ok = *okf != 0;
     if (ok) ok = mbar_wait(bar_mma, 1, status, VX_DEV_TIMEOUT_MMA);

@@ -118,6 +118,7 @@ __device__ __forceinline__ bool cc_wait_all(uint64_t *bar, uint32_t parity, CcSm
         if (!ok) dev_flag(status, VX_DEV_TIMEOUT_TMA);
         sm.flag = ok;
     }
+    __syncwarp();  // converged warps at the CTA barrier
     __syncthreads();
     return sm.flag != 0;
 }
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(CC_THREADS, 2) gqa_split_cc(const __grid_const
         for (; issued < n_sub && issued < NST; issued++) issue(issued);
         grid_dep_launch();  // the combine may be scheduled once every CTA is past here
     }
+    __syncwarp();
 
     // ---- q of the group (and, fused, the new K/V row) ------------------------------
     const size_t qrow = ((size_t)b * a.nq + kvh * G) * HD;
@@ -328,6 +330,7 @@ __global__ void __launch_bounds__(CC_THREADS, 2) gqa_split_cc(const __grid_const
         }
         __syncthreads();  // stage, scores and probabilities free again
         if (tid == 0 && i + NST < n_sub) issue(issued++);
+        __syncwarp();
     }
     if (!ok) {
         // let every issued copy land before the CTA exits (bounded)

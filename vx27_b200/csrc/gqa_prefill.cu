@@ -506,6 +506,9 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             *(volatile int *)&sm.abort = 1;
         }
     }
+    // lanes that skipped a lane-0 role wait for it here, so whole warps reach the CTA
+    // barrier together (it requires converged warps)
+    __syncwarp();
     __syncthreads();
     if (!*(volatile int *)&sm.abort) {
         // gated output rows with coalesced 16-byte loads of the gate and stores of the output

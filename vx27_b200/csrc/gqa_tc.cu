@@ -745,6 +745,9 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
             kq++;
         }
     }
+    // lanes that skipped a lane-0 role wait for it here, so whole warps reach the CTA
+    // barrier together (it requires converged warps)
+    __syncwarp();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
