@@ -79,6 +79,16 @@ __device__ __forceinline__ bool tc_wait(uint64_t *bar, uint32_t parity, TcSmem &
     }
 }
 
+// Non-blocking test: has the phase with this parity completed?
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; "
+        "selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
 // Byte offset of element (row, col) of a K-major operand stored as 128-byte swizzled
 // rows: col in [0, 64) within one chunk.
 __device__ __forceinline__ uint32_t sw128(int row, int col) {
@@ -456,62 +466,96 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
             const uint32_t id1 = idesc_bf16(128, 16, false, false);
             const uint32_t id2 = idesc_bf16(128, 16, true, false);
             const uint32_t ring0 = smem_u32(sm.ring[0]);
-            bool ok = true, prev = false;
-            int w = w_first, n_t = w < n_items ? item(w).n_tiles : 0, i = 0, kq = 0;
-            for (int g = 0; ok && (w < n_items || prev); g++) {
-                const bool cur = w < n_items;
-                if (cur) {
-                    const int bb = g & 1;
-                    if (i == 0)  // this item's q staged
-                        ok = tc_wait(&sm.q_full[kq & 1], (kq >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                    if (ok && g >= 2)
-                        ok = tc_wait(&sm.s_empty[bb], ((g >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                    const uint32_t q0 = smem_u32(sm.q[kq & 1][0]);
-                    for (int c = 0; c < 4 && ok; c++) {
-                        const int j = 8 * g + c, slot = j % NSLOT;
-                        ok = tc_wait(&sm.full[slot], (j / NSLOT) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                        if (!ok) break;
-                        tc_fence_after();
+            // Non-blocking schedule of the two MMA streams: S(gs) chunk by chunk as its K
+            // chunks land, O(go) half by half as P(go) and its V chunks are ready, each
+            // issued as soon as its inputs are there. (Waiting for S(g+1)'s K chunks before
+            // issuing O(g) held V(g)'s ring slots for most of a tile and gated the
+            // producer.) S runs at most one tile ahead of O: S(gs)'s K chunks reuse the
+            // slots of O(gs-2)'s V chunks and O(go)'s V chunks those of S(go-1)'s K
+            // chunks, so every slot's phases are awaited in order.
+            bool ok = true;
+            int ws = w_first, n_ts = ws < n_items ? item(ws).n_tiles : 0, is = 0, kqs = 0;
+            int gs = 0, cs = 0, go = 0, ho = 0;
+            bool s_started = false, o_started = false;
+            uint32_t spins = 0;
+            uint64_t t_idle = 0;
+            while (ok && (ws < n_items || go < gs)) {
+                bool progressed = false;
+                if (go < gs) {  // ---- O(go) = V(go)^T P(go)^T, two halves of 4 V chunks
+                    const int bb = go & 1;
+                    if (!o_started &&
+                        mbar_test(&sm.p_full[bb], (go >> 1) & 1) &&
+                        (go < 2 || mbar_test(&sm.o_empty[bb], ((go >> 1) - 1) & 1)))
+                        o_started = true;
+                    if (o_started) {
+                        const int j0 = 8 * go + 4 + 2 * ho, s0 = j0 % NSLOT, s1 = (j0 + 1) % NSLOT;
+                        if (mbar_test(&sm.full[s0], (j0 / NSLOT) & 1) &&
+                            mbar_test(&sm.full[s1], ((j0 + 1) / NSLOT) & 1)) {
+                            tc_fence_after();
+                            const uint32_t pb = smem_u32(sm.p[bb][0]);
 #pragma unroll
-                        for (int kk = 0; kk < 4; kk++)
-                            mma_bf16(tmem + bb * 16,
-                                     sdesc_sw128(ring0 + slot * SLOT_BYTES + kk * 32, 16, 1024),
-                                     sdesc_sw128(q0 + c * 2048 + kk * 32, 16, 1024), id1,
-                                     (c | kk) != 0);
-                        mma_commit(&sm.empty[slot]);
+                            for (int kk = 0; kk < 8; kk++)
+                                mma_bf16(tmem + 32 + bb * 32 + ho * 16,
+                                         sdesc_sw128(ring0 + s0 * SLOT_BYTES + kk * 2048, SLOT_BYTES, 1024),
+                                         sdesc_sw128(pb + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024),
+                                         id2, kk != 0);
+                            mma_commit(&sm.empty[s0]);
+                            mma_commit(&sm.empty[s1]);
+                            progressed = true;
+                            if (++ho == 2) {
+                                mma_commit(&sm.o_full[bb]);
+                                ho = 0;
+                                o_started = false;
+                                go++;
+                            }
+                        }
                     }
-                    if (ok) mma_commit(&sm.s_full[bb]);
                 }
-                if (prev && ok) {
-                    const int t = g - 1, bb = t & 1;
-                    ok = tc_wait(&sm.p_full[bb], (t >> 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                    if (ok && t >= 2)
-                        ok = tc_wait(&sm.o_empty[bb], ((t >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                    const uint32_t pb = smem_u32(sm.p[bb][0]);
-                    for (int half = 0; half < 2 && ok; half++) {
-                        const int j0 = 8 * t + 4 + 2 * half, s0 = j0 % NSLOT, s1 = (j0 + 1) % NSLOT;
-                        ok = tc_wait(&sm.full[s0], (j0 / NSLOT) & 1, sm, status, VX_DEV_TIMEOUT_MMA) &&
-                             tc_wait(&sm.full[s1], ((j0 + 1) / NSLOT) & 1, sm, status, VX_DEV_TIMEOUT_MMA);
-                        if (!ok) break;
-                        tc_fence_after();
+                if (ws < n_items && gs - go <= 1) {  // ---- S(gs) = K(gs) Q^T, 4 K chunks
+                    const int bb = gs & 1;
+                    if (!s_started && (is > 0 || mbar_test(&sm.q_full[kqs & 1], (kqs >> 1) & 1)) &&
+                        (gs < 2 || mbar_test(&sm.s_empty[bb], ((gs >> 1) - 1) & 1)))
+                        s_started = true;
+                    if (s_started) {
+                        const int j = 8 * gs + cs, slot = j % NSLOT;
+                        if (mbar_test(&sm.full[slot], (j / NSLOT) & 1)) {
+                            tc_fence_after();
+                            const uint32_t q0 = smem_u32(sm.q[kqs & 1][0]);
 #pragma unroll
-                        for (int kk = 0; kk < 8; kk++)
-                            mma_bf16(tmem + 32 + bb * 32 + half * 16,
-                                     sdesc_sw128(ring0 + s0 * SLOT_BYTES + kk * 2048, SLOT_BYTES, 1024),
-                                     sdesc_sw128(pb + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024),
-                                     id2, kk != 0);
-                        mma_commit(&sm.empty[s0]);
-                        mma_commit(&sm.empty[s1]);
+                            for (int kk = 0; kk < 4; kk++)
+                                mma_bf16(tmem + bb * 16,
+                                         sdesc_sw128(ring0 + slot * SLOT_BYTES + kk * 32, 16, 1024),
+                                         sdesc_sw128(q0 + cs * 2048 + kk * 32, 16, 1024), id1,
+                                         (cs | kk) != 0);
+                            mma_commit(&sm.empty[slot]);
+                            progressed = true;
+                            if (++cs == 4) {
+                                mma_commit(&sm.s_full[bb]);
+                                cs = 0;
+                                s_started = false;
+                                gs++;
+                                if (++is == n_ts) {  // the item's S MMAs are all issued
+                                    mma_commit(&sm.q_empty[kqs & 1]);
+                                    is = 0;
+                                    kqs++;
+                                    ws = next_work(ws + stride);
+                                    n_ts = ws < n_items ? item(ws).n_tiles : 0;
+                                }
+                            }
+                        }
                     }
-                    if (ok) mma_commit(&sm.o_full[bb]);
                 }
-                prev = cur;
-                if (cur && ++i == n_t) {  // next item with work
-                    if (ok) mma_commit(&sm.q_empty[kq & 1]);  // its S MMAs are all issued
-                    i = 0;
-                    kq++;
-                    w = next_work(w + stride);
-                    n_t = w < n_items ? item(w).n_tiles : 0;
+                if (progressed) {
+                    spins = 0;
+                } else if ((++spins & 255) == 0) {  // bounded like every wait (~2 s idle)
+                    if (*(volatile int *)&sm.abort) ok = false;
+                    const uint64_t now = globaltimer();
+                    if (spins == 256) t_idle = now;
+                    else if (now - t_idle > 2000000000ull) {
+                        *(volatile int *)&sm.abort = 1;
+                        dev_flag(status, VX_DEV_TIMEOUT_MMA);
+                        ok = false;
+                    }
                 }
             }
             mma_commit(&sm.mma_done);
