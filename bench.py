@@ -32,11 +32,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "DeltaNet+GQA decode tokens/s at 1/2/4/8 B200; % of HBM roofline"
-# DRAM bytes (read + write) per algorithmic byte of the split-KV GQA decode kernel, from an
-# ncu capture of the same kernel at 32 sequences (the full 256-sequence workload holds
-# 83 GB, too much to profile): each K/V byte is read once; the last tile of every
-# (sequence, KV head) fetches only the 32-row boxes it needs.
-GQA_SPLIT_DRAM_PER_ALGO_BYTE = 1.011
+# DRAM bytes (read + write) per algorithmic byte of the split-KV GQA decode kernel, from
+# ncu captures of the same kernel for one layer at 64 sequences (the full 256-sequence
+# workload holds 83 GB, too much to profile): each K/V byte is read once; the last tile of
+# every (sequence, KV head) fetches only the 32-row boxes it needs; the fused variant also
+# writes the new K/V rows.
+GQA_SPLIT_DRAM_PER_ALGO_BYTE = {True: 1.016, False: 1.010}  # keyed by the fused prologue
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -281,11 +282,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                        "combine pass)"),
             "achieved": round(gqa_gbs, 1), "peak": peak, "unit": "GB/s",
             "frac": round(gqa_gbs / peak, 4),
-            "traffic": int(GQA_SPLIT_DRAM_PER_ALGO_BYTE * gqa_bytes),
+            "traffic": int(GQA_SPLIT_DRAM_PER_ALGO_BYTE[args.fused_gqa] * gqa_bytes),
             "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of gqa_split_tc "
                                "for one layer at B = 64 (same kernel and per-sequence context; "
-                               f"{GQA_SPLIT_DRAM_PER_ALGO_BYTE} x its algorithmic bytes), "
-                               "scaled by the sequences of this launch"),
+                               f"{GQA_SPLIT_DRAM_PER_ALGO_BYTE[args.fused_gqa]} x its algorithmic "
+                               "bytes), scaled by the sequences of this launch"),
             "peak_source": peak_src,
             "algorithmic_bytes_per_launch": int(gqa_bytes), "avg_launch_ms": round(gqa_ms, 4),
         },
@@ -347,9 +348,24 @@ def run_layer(args) -> dict:
             ops.fill_normal(t, 3, n)
         ws = torch.empty(ops.gqa_workspace_bytes(B, nq, nkv, hd, cap) // 4 + 1, device="cuda")
         pos = torch.full((B,), args.ctx, dtype=torch.int32, device="cuda")
-        run = lambda: ops.gqa_decode_batch(q, gate, kc, vc, pos, out, ws)
-        nbytes = B * nkv * cap * hd * 2 * 2 + B * nq * hd * (4 + 2 + 2)
-        name = "gqa_split_tc (split-KV decode; one split writes the gated output), one layer"
+        if args.fused_gqa:  # the fused kernel, as the config 2 step runs it
+            q_in = torch.empty(B, nq, hd, dtype=bf, device="cuda")
+            k_in = torch.empty(B, nkv, hd, dtype=bf, device="cuda")
+            v_in = torch.empty_like(k_in)
+            for n, t in enumerate((q_in, k_in, v_in)):
+                ops.fill_normal(t, 3, 10 + n)
+            qw = torch.ones(hd, device="cuda")
+            kw = torch.ones(hd, device="cuda")
+            rope = ops.rope_table(cap)
+            run = lambda: ops.gqa_decode_fused(q_in, k_in, v_in, qw, kw, rope, gate, kc, vc, pos,
+                                               out, ws)
+            nbytes = B * nkv * cap * hd * 2 * 2 + B * (nq * hd * 2 * 3 + 2 * nkv * hd * 2 * 2)
+            name = ("gqa_split_tc with the QK norm, RoPE and K/V append fused in (one split "
+                    "writes the gated output), one layer")
+        else:
+            run = lambda: ops.gqa_decode_batch(q, gate, kc, vc, pos, out, ws)
+            nbytes = B * nkv * cap * hd * 2 * 2 + B * nq * hd * (4 + 2 + 2)
+            name = "gqa_split_tc (split-KV decode; one split writes the gated output), one layer"
     for _ in range(args.warmup):
         run()
     torch.cuda.synchronize()
@@ -1051,9 +1067,9 @@ def main() -> None:
     ap.add_argument("--no-other-configs", action="store_true",
                     help="config 2 at N = 1: skip the config 1 and config 4 figures added "
                          "after its timed region")
-    ap.add_argument("--fused-gqa", action="store_true",
-                    help="config 2: GQA layers as one fused kernel (vx27_gqa_decode_fused) "
-                         "instead of append + split-KV decode")
+    ap.add_argument("--two-kernel-gqa", dest="fused_gqa", action="store_false",
+                    help="config 2: GQA layers as append + split-KV decode instead of one "
+                         "fused kernel (vx27_gqa_decode_fused, the default)")
     ap.add_argument("--workload", choices=["config2", "config0", "config1", "config3a",
                                            "config3b", "config4", "dn_layer", "gqa_layer", "pmat"],
                     default="config2",
