@@ -483,21 +483,69 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
         named_bar_sync(1, 256);
         tc_fence_after();
         const float l_row = l_run + tmem_ld1(tX + lane_off + 4 + (hf ^ 1));
+        // bf16 gate: this thread's half row of the gate (128 values, 256 contiguous bytes) is
+        // requested before O is final, and the gated row goes from registers straight to the
+        // output; there is no staging pass through shared memory (that pass, one CTA-wide
+        // loop over the tile after a barrier, took ~10 us per CTA)
+        const int t_row = t0 + r;
+        uint4 graw[HDP / 16];
+        if constexpr (ACT_BF16) {
+            if (t_row < T) {
+                const uint4 *gp = reinterpret_cast<const uint4 *>(
+                    static_cast<const uint16_t *>(gate) + ((size_t)t_row * nq + h) * HDP +
+                    hf * (HDP / 2));
+#pragma unroll
+                for (int k = 0; k < HDP / 16; k++) graw[k] = gp[k];
+            }
+        }
         if (ok) ok = pf_wait(&sm.o_final, 0, sm, status, VX_DEV_TIMEOUT_MMA);
         ok = __all_sync(0xffffffffu, ok);
-        if (ok) {
-            // O / l into a row-major fp32 staging tile over the (now idle) slot ring, 16-byte
-            // chunks of a row XOR-swizzled by the row so a warp's stores spread over banks
+        if (ok && ACT_BF16) {
+            tc_fence_after();
+            const float inv = l_row > 0.0f ? 1.0f / l_row : 0.0f;
+            const size_t obase = ((size_t)t_row * nq + h) * HDP + hf * (HDP / 2);
+#pragma unroll 1
+            for (int i = 0; i < HDP / 128; i++) {  // 64 columns per load round
+                float o[64];
+                tmem_ld64(tO + lane_off + hf * (HDP / 2) + 64 * i, o);
+                if (t_row >= T) continue;
+#pragma unroll
+                for (int k = 0; k < 8; k++) {  // 8 columns per 16-byte gate word group
+                    const uint4 gv = graw[8 * i + k];
+                    const uint32_t gw4[4] = {gv.x, gv.y, gv.z, gv.w};
+                    float a[8];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float g0 = bf16_to_f32(gw4[e] & 0xffffu), g1 = bf16_to_f32(gw4[e] >> 16);
+                        a[2 * e] = o[8 * k + 2 * e] * inv * __frcp_rn(1.0f + __expf(-g0));
+                        a[2 * e + 1] = o[8 * k + 2 * e + 1] * inv * __frcp_rn(1.0f + __expf(-g1));
+                    }
+                    const size_t oi = obase + 64 * i + 8 * k;
+                    if constexpr (OUT_BF16) {
+                        *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out) + oi) =
+                            make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]),
+                                       pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+                    } else {
+                        float4 *op = reinterpret_cast<float4 *>(static_cast<float *>(out) + oi);
+                        op[0] = make_float4(a[0], a[1], a[2], a[3]);
+                        op[1] = make_float4(a[4], a[5], a[6], a[7]);
+                    }
+                }
+            }
+        } else if (ok) {
+            // fp32 gate: O / l into a row-major fp32 staging tile over the (now idle) slot
+            // ring, 16-byte chunks of a row XOR-swizzled by the row so a warp's stores spread
+            // over banks; the gated output follows after the CTA barrier
             tc_fence_after();
             const float inv = l_row > 0.0f ? 1.0f / l_row : 0.0f;
             float4 *row = reinterpret_cast<float4 *>(sm.ring[0]) + r * (HDP / 4);
 #pragma unroll 1
-            for (int i = 0; i < HDP / 32; i++) {
-                float o[16];
-                tmem_ld16(tO + lane_off + hf * (HDP / 2) + 16 * i, o);
+            for (int i = 0; i < HDP / 128; i++) {  // 64 columns per load round
+                float o[64];
+                tmem_ld64(tO + lane_off + hf * (HDP / 2) + 64 * i, o);
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const int ch = (hf * (HDP / 2) + 16 * i) / 4 + k;
+                for (int k = 0; k < 16; k++) {
+                    const int ch = (hf * (HDP / 2) + 64 * i) / 4 + k;
                     row[ch ^ (r & 7)] = make_float4(o[4 * k] * inv, o[4 * k + 1] * inv,
                                                     o[4 * k + 2] * inv, o[4 * k + 3] * inv);
                 }
@@ -510,57 +558,75 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     // barrier together (it requires converged warps)
     __syncwarp();
     __syncthreads();
-    if (!*(volatile int *)&sm.abort) {
-        // gated output rows with coalesced 16-byte loads of the gate and stores of the output
+    if (!ACT_BF16 && !*(volatile int *)&sm.abort) {
+        // gated output rows with coalesced 16-byte loads of the gate and stores of the
+        // output; the gate loads of GB iterations are issued together before any is used,
+        // so a thread waits for one round trip per GB iterations instead of one each (the
+        // one-at-a-time form took ~14 us per CTA)
         constexpr int VEC = OUT_BF16 ? 8 : 4;
         constexpr int PER_ROW = HDP / VEC;
+        constexpr int N_IT = QT * PER_ROW;
+        constexpr int GB = 6;
+        constexpr int GW = ACT_BF16 ? VEC / 2 : VEC;  // 32-bit gate words per iteration
         const float4 *stage = reinterpret_cast<const float4 *>(sm.ring[0]);
-        for (int it = tid; it < QT * PER_ROW; it += PF_THREADS) {
-            const int rr = it / PER_ROW, c0 = (it % PER_ROW) * VEC;
-            const int t = t0 + rr;
-            if (t >= T) continue;
-            float o[VEC], g[VEC];
+        for (int it0 = tid; it0 < N_IT; it0 += GB * PF_THREADS) {
+            uint32_t gw[GB][GW];
 #pragma unroll
-            for (int k = 0; k < VEC / 4; k++) {
-                const float4 f = stage[rr * (HDP / 4) + ((c0 / 4 + k) ^ (rr & 7))];
-                o[4 * k] = f.x; o[4 * k + 1] = f.y; o[4 * k + 2] = f.z; o[4 * k + 3] = f.w;
-            }
-            const size_t base = ((size_t)t * nq + h) * HDP + c0;
-            if constexpr (ACT_BF16) {
-                const uint16_t *gp = static_cast<const uint16_t *>(gate) + base;
-                uint32_t w[VEC / 2];
-                if constexpr (VEC == 8) {
-                    const uint4 v4 = *reinterpret_cast<const uint4 *>(gp);
-                    w[0] = v4.x; w[1] = v4.y; w[2] = v4.z; w[3] = v4.w;
+            for (int u = 0; u < GB; u++) {
+                const int it = it0 + u * PF_THREADS;
+                const int rr = it / PER_ROW, c0 = (it % PER_ROW) * VEC;
+                if (it >= N_IT || t0 + rr >= T) continue;
+                const size_t base = ((size_t)(t0 + rr) * nq + h) * HDP + c0;
+                if constexpr (ACT_BF16 && VEC == 8) {
+                    const uint4 v4 = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(gate) + base);
+                    gw[u][0] = v4.x; gw[u][1] = v4.y; gw[u][2] = v4.z; gw[u][3] = v4.w;
+                } else if constexpr (ACT_BF16) {
+                    const uint2 v2 = *reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(gate) + base);
+                    gw[u][0] = v2.x; gw[u][1] = v2.y;
                 } else {
-                    const uint2 v2 = *reinterpret_cast<const uint2 *>(gp);
-                    w[0] = v2.x; w[1] = v2.y;
-                }
+                    const uint4 *gp = reinterpret_cast<const uint4 *>(static_cast<const float *>(gate) + base);
 #pragma unroll
-                for (int k = 0; k < VEC / 2; k++) {
-                    g[2 * k] = bf16_to_f32(w[k] & 0xffffu);
-                    g[2 * k + 1] = bf16_to_f32(w[k] >> 16);
+                    for (int k = 0; k < VEC / 4; k++) {
+                        const uint4 f = gp[k];
+                        gw[u][4 * k] = f.x; gw[u][4 * k + 1] = f.y; gw[u][4 * k + 2] = f.z; gw[u][4 * k + 3] = f.w;
+                    }
                 }
-            } else {
-                const float4 *gp = reinterpret_cast<const float4 *>(static_cast<const float *>(gate) + base);
+            }
+#pragma unroll
+            for (int u = 0; u < GB; u++) {
+                const int it = it0 + u * PF_THREADS;
+                const int rr = it / PER_ROW, c0 = (it % PER_ROW) * VEC;
+                if (it >= N_IT || t0 + rr >= T) continue;
+                const size_t base = ((size_t)(t0 + rr) * nq + h) * HDP + c0;
+                float o[VEC], g[VEC];
 #pragma unroll
                 for (int k = 0; k < VEC / 4; k++) {
-                    const float4 f = gp[k];
-                    g[4 * k] = f.x; g[4 * k + 1] = f.y; g[4 * k + 2] = f.z; g[4 * k + 3] = f.w;
+                    const float4 f = stage[rr * (HDP / 4) + ((c0 / 4 + k) ^ (rr & 7))];
+                    o[4 * k] = f.x; o[4 * k + 1] = f.y; o[4 * k + 2] = f.z; o[4 * k + 3] = f.w;
                 }
-            }
+                if constexpr (ACT_BF16) {
 #pragma unroll
-            for (int e = 0; e < VEC; e++) o[e] = o[e] * (1.0f / (1.0f + expf(-g[e])));
-            if constexpr (OUT_BF16) {
-                uint32_t w[4];
+                    for (int k = 0; k < VEC / 2; k++) {
+                        g[2 * k] = bf16_to_f32(gw[u][k] & 0xffffu);
+                        g[2 * k + 1] = bf16_to_f32(gw[u][k] >> 16);
+                    }
+                } else {
 #pragma unroll
-                for (int k = 0; k < 4; k++)
-                    w[k] = (uint32_t)f32_to_bf16(o[2 * k]) | ((uint32_t)f32_to_bf16(o[2 * k + 1]) << 16);
-                *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out) + base) =
-                    make_uint4(w[0], w[1], w[2], w[3]);
-            } else {
-                *reinterpret_cast<float4 *>(static_cast<float *>(out) + base) =
-                    make_float4(o[0], o[1], o[2], o[3]);
+                    for (int e = 0; e < VEC; e++) g[e] = __uint_as_float(gw[u][e]);
+                }
+#pragma unroll
+                for (int e = 0; e < VEC; e++) o[e] = o[e] * (1.0f / (1.0f + expf(-g[e])));
+                if constexpr (OUT_BF16) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+                        w[k] = (uint32_t)f32_to_bf16(o[2 * k]) | ((uint32_t)f32_to_bf16(o[2 * k + 1]) << 16);
+                    *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out) + base) =
+                        make_uint4(w[0], w[1], w[2], w[3]);
+                } else {
+                    *reinterpret_cast<float4 *>(static_cast<float *>(out) + base) =
+                        make_float4(o[0], o[1], o[2], o[3]);
+                }
             }
         }
     }
