@@ -50,6 +50,10 @@ extern "C" {
  * reference point for that comparison. vx27_gqa_decode_plan reports the choice. */
 #define VX27_F_DECODE_CC 0x80
 #define VX27_F_DECODE_TC 0x100
+/* GQA prefill: one CTA per (query tile, query head) on one SM. By default, when the query
+ * heads per KV head are even, two neighbouring heads run as a 2-CTA cluster whose
+ * tcgen05 MMAs span both SMs, each SM loading half of every K/V tile. */
+#define VX27_F_PREFILL_CTA1 0x200
 
 /* Library version, major*10000 + minor*100 + patch. */
 int vx27cuda_version(void);

@@ -14,36 +14,39 @@ NQ, NKV, HD = 24, 4, 256
 REL_TOL = 2e-2
 
 
-def make(orc, seed, T):
-    g = lambda n, s, m=0.0, sd=1.0, b=True: orc.normal(n, seed, s, m, sd, bf16=b)
-    return dict(q=g(T * NQ * HD, 1), k=g(T * NKV * HD, 2), v=g(T * NKV * HD, 3),
-                gate=g(T * NQ * HD, 4), qw=g(HD, 5, 1.0, 0.02, False),
-                kw=g(HD, 6, 1.0, 0.02, False))
+def make(orc, seed, T, nq=NQ, nkv=NKV, bf16=True):
+    g = lambda n, s, m=0.0, sd=1.0, b=bf16: orc.normal(n, seed, s, m, sd, bf16=b)
+    return dict(q=g(T * nq * HD, 1), k=g(T * nkv * HD, 2), v=g(T * nkv * HD, 3),
+                gate=g(T * nq * HD, 4), qw=g(HD, 5, 1.0, 0.02, False),
+                kw=g(HD, 6, 1.0, 0.02, False), nq=nq, nkv=nkv, bf16=bf16)
 
 
 def oracle_rows(orc, x, T, rows):
+    nq, nkv = x["nq"], x["nkv"]
     rows = np.asarray(rows, np.int32)
-    out = np.zeros(len(rows) * NQ * HD, np.float32)
+    out = np.zeros(len(rows) * nq * HD, np.float32)
     orc.lib().orc_gqa_prefill_rows(orc.P(x["q"]), orc.P(x["k"]), orc.P(x["v"]), orc.P(x["gate"]),
-                                   orc.P(x["qw"]), orc.P(x["kw"]), T, NQ, NKV, HD, 64, 1e7, 1e-6,
-                                   orc.P(rows), len(rows), orc.P(out), orc.F_ACT_BF16)
-    return out.reshape(len(rows), NQ, HD)
+                                   orc.P(x["qw"]), orc.P(x["kw"]), T, nq, nkv, HD, 64, 1e7, 1e-6,
+                                   orc.P(rows), len(rows), orc.P(out),
+                                   orc.F_ACT_BF16 if x["bf16"] else 0)
+    return out.reshape(len(rows), nq, HD)
 
 
-def gpu_prefill(x, T, cap, rope, chunks=None, out_bf16=False):
+def gpu_prefill(x, T, cap, rope, chunks=None, out_bf16=False, cta_pairs=True):
     """Prefill in one call, or in consecutive chunks (p0 > 0 continues the cache)."""
-    q = dev(x["q"], True).view(T, NQ, HD)
-    k = dev(x["k"], True).view(T, NKV, HD)
-    v = dev(x["v"], True).view(T, NKV, HD)
-    gate = dev(x["gate"], True).view(T, NQ, HD)
-    kc = torch.full((NKV, cap, HD), float("nan"), dtype=torch.bfloat16, device="cuda")
-    vc = torch.full((NKV, cap, HD), float("nan"), dtype=torch.bfloat16, device="cuda")
-    out = torch.empty(T, NQ, HD, dtype=torch.bfloat16 if out_bf16 else torch.float32,
+    nq, nkv, b16 = x["nq"], x["nkv"], x["bf16"]
+    q = dev(x["q"], b16).view(T, nq, HD)
+    k = dev(x["k"], b16).view(T, nkv, HD)
+    v = dev(x["v"], b16).view(T, nkv, HD)
+    gate = dev(x["gate"], b16).view(T, nq, HD)
+    kc = torch.full((nkv, cap, HD), float("nan"), dtype=torch.bfloat16, device="cuda")
+    vc = torch.full((nkv, cap, HD), float("nan"), dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(T, nq, HD, dtype=torch.bfloat16 if out_bf16 else torch.float32,
                       device="cuda")
     bounds = chunks or [0, T]
     for a, b in zip(bounds, bounds[1:]):
         ops.gqa_prefill(q[a:b], k[a:b], v[a:b], gate[a:b], dev(x["qw"]), dev(x["kw"]), rope,
-                        kc, vc, out[a:b], p0=a)
+                        kc, vc, out[a:b], p0=a, cta_pairs=cta_pairs)
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     return out.float().cpu().numpy(), kc, vc
@@ -54,19 +57,21 @@ def rope(cuda):
     return ops.rope_table(40000)
 
 
+@pytest.mark.parametrize("cta_pairs", [True, False])
 @pytest.mark.parametrize("T", [1, 64, 200, 300])
-def test_small_prompts_all_rows(cuda, orc, rope, T):
+def test_small_prompts_all_rows(cuda, orc, rope, T, cta_pairs):
     x = make(orc, 10 + T, T)
-    out, _, _ = gpu_prefill(x, T, T + 64, rope)
+    out, _, _ = gpu_prefill(x, T, T + 64, rope, cta_pairs=cta_pairs)
     ref = oracle_rows(orc, x, T, range(T))
     assert rel_err(out.reshape(-1), ref.reshape(-1)) < REL_TOL
 
 
-def test_chunked_continuation_equals_oracle(cuda, orc, rope):
+@pytest.mark.parametrize("cta_pairs", [True, False])
+def test_chunked_continuation_equals_oracle(cuda, orc, rope, cta_pairs):
     """Prefill in three calls at p0 = 0, 130, 257 (cache carried between calls) == one pass."""
     T = 400
     x = make(orc, 99, T)
-    out, kc, vc = gpu_prefill(x, T, 512, rope, chunks=[0, 130, 257, 400])
+    out, kc, vc = gpu_prefill(x, T, 512, rope, chunks=[0, 130, 257, 400], cta_pairs=cta_pairs)
     ref = oracle_rows(orc, x, T, range(T))
     assert rel_err(out.reshape(-1), ref.reshape(-1)) < REL_TOL
     # the cache holds finite values past the prompt up to the next multiple of 64
@@ -83,3 +88,42 @@ def test_config4_gqa_sampled_rows(cuda, orc, rope):
     err = rel_err(out[rows].reshape(-1), ref.reshape(-1))
     print(f"config4 GQA sampled rows rel err {err:.3e}")
     assert err < REL_TOL
+
+
+@pytest.mark.parametrize("out_bf16", [False, True])
+def test_fp32_activations_both_kernels(cuda, orc, rope, out_bf16):
+    """fp32 q/k/v/gate (the staged fp32-gate epilogue), both attention kernels, all rows."""
+    T = 333
+    x = make(orc, 21, T, bf16=False)
+    ref = oracle_rows(orc, x, T, range(T))
+    outs = []
+    for pairs in (True, False):
+        out, _, _ = gpu_prefill(x, T, T + 64, rope, out_bf16=out_bf16, cta_pairs=pairs)
+        assert rel_err(out.reshape(-1), ref.reshape(-1)) < REL_TOL
+        outs.append(out)
+    assert rel_err(outs[0].reshape(-1), outs[1].reshape(-1)) < 1e-2
+
+
+@pytest.mark.parametrize("nq,nkv", [(12, 4), (8, 8), (16, 2)])
+def test_group_sizes(cuda, orc, rope, nq, nkv):
+    """Odd group sizes (3, 1) run one CTA per head; an even one (8) runs in pairs."""
+    T = 260
+    x = make(orc, 22, T, nq=nq, nkv=nkv)
+    out, _, _ = gpu_prefill(x, T, T + 64, rope)
+    ref = oracle_rows(orc, x, T, range(T))
+    assert rel_err(out.reshape(-1), ref.reshape(-1)) < REL_TOL
+
+
+def test_pairs_equal_single_sm_kernel(cuda, orc, rope):
+    """The pair kernel's M = 256 MMAs compute the same products as the single-SM kernel's
+    M = 128 ones over the same bf16 operands; over 2000 positions the two outputs agree
+    to fp32 rounding of the accumulation order (reported), well inside the tolerance."""
+    T = 2000
+    x = make(orc, 23, T)
+    a, _, _ = gpu_prefill(x, T, T, rope, cta_pairs=True)
+    b, _, _ = gpu_prefill(x, T, T, rope, cta_pairs=False)
+    err = rel_err(a.reshape(-1), b.reshape(-1))
+    print(f"pair vs single-SM rel diff {err:.3e}, identical: {np.array_equal(a, b)}")
+    assert err < 1e-4
+    rows = [0, 127, 128, 1000, 1999]
+    assert rel_err(a[rows].reshape(-1), oracle_rows(orc, x, T, rows).reshape(-1)) < REL_TOL

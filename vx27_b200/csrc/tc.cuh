@@ -171,6 +171,83 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// ---- CTA pairs (cta_group::2) ---------------------------------------------------------
+// One MMA spans the two SMs of a 2-CTA cluster: A is split by its M rows (each CTA holds
+// its 128 rows at the same shared-memory offset), B by its N rows (each CTA holds half of
+// N at the same offset), and each CTA's TMEM receives its 128 rows of D over all N. The
+// even CTA (rank 0) issues; copies and commits name mbarriers by shared::cluster address.
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of this CTA's shared variable `p` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// All threads of both CTAs; release/acquire orders shared-memory writes across the pair.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+                 ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(slot)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t base, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols)
+                 : "memory");
+}
+// D (+)= A x B over the pair (M = 256: 128 rows per CTA); issued by one thread of rank 0.
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p; }"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// One arrival on the mbarrier at shared::cluster address `bar` (either CTA of the pair)
+// once all pair MMAs this thread issued before are done.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(bar) : "memory");
+}
+// The same, one arrival on the mbarrier at this offset in EACH CTA of the pair (CTA mask
+// 0b11): one commit instead of two (a commit costs the issuing thread ~60 cycles).
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;"
+        ::"r"(smem_u32(bar)), "h"((uint16_t)3) : "memory");
+}
+// TMA 2-D load into this CTA's shared memory, its bytes counted on the mbarrier at
+// shared::cluster address `bar` (the pair's rank 0, which waits for both halves).
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const CUtensorMap *map, int x,
+                                                 int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(smem_dst)), "l"((uint64_t)map), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(void *smem_dst, const CUtensorMap *map, int x,
+                                                 int y, int z, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_u32(smem_dst)), "l"((uint64_t)map), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+// Arrive on the mbarrier at shared::cluster address `bar` (this CTA's or the peer's).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar)
+                 : "memory");
+}
+
 // Host: 2-D bf16 tensor map over rows x cols (cols contiguous, row pitch in bytes), box
 // {box_cols, box_rows}, 128-byte swizzle, zero fill out of bounds.
 int make_tmap_bf16_2d(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,

@@ -28,6 +28,7 @@ F_PREFETCH_KV = 0x40
 F_DECODE_CC = 0x80
 F_DECODE_TC = 0x100
 _KERNEL_FLAGS = {"auto": 0, "cc": F_DECODE_CC, "tc": F_DECODE_TC}
+F_PREFILL_CTA1 = 0x200
 
 
 def _np(a: np.ndarray, dtype=np.float32) -> C.c_void_p:
@@ -528,8 +529,11 @@ def pmat_multi(Ws, dtype: int, xb, ys, rows, cols: int, stream=None) -> None:
 
 def gqa_prefill(q_in, k_in, v_in, gate, q_norm_w, k_norm_w, rope, k_cache, v_cache, out,
                 workspace=None, p0: int = 0, eps: float = 1e-6, norm_one_plus: bool = False,
-                stream=None):
-    """Causal gated GQA prefill of T tokens (vx27_gqa_prefill); k_cache/v_cache [nkv][cap][hd]."""
+                stream=None, cta_pairs: bool = True):
+    """Causal gated GQA prefill of T tokens (vx27_gqa_prefill); k_cache/v_cache [nkv][cap][hd].
+    cta_pairs=False runs the attention one CTA per (query tile, head) on one SM
+    (VX27_F_PREFILL_CTA1) instead of 2-CTA pairs over two SMs (used with an even number of
+    query heads per KV head)."""
     import torch
     T, nq, hd = q_in.shape
     nkv = k_in.shape[1]
@@ -549,7 +553,7 @@ def gqa_prefill(q_in, k_in, v_in, gate, q_norm_w, k_norm_w, rope, k_cache, v_cac
     if workspace is None:
         workspace = torch.empty(need // 2 + 1, dtype=torch.int16, device=q_in.device)
     flags = (F_ACT_BF16 if _is_bf16(q_in) else 0) | (F_OUT_BF16 if _is_bf16(out) else 0) | \
-        (F_NORM_1P if norm_one_plus else 0)
+        (F_NORM_1P if norm_one_plus else 0) | (0 if cta_pairs else F_PREFILL_CTA1)
     e = errbuf()
     rc = load().vx27_gqa_prefill(_t(q_in), _t(k_in), _t(v_in), _t(gate), _t(q_norm_w),
                                  _t(k_norm_w), _t(rope), rope.shape[0], p0, _t(k_cache),
