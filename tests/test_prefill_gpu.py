@@ -127,3 +127,34 @@ def test_pairs_equal_single_sm_kernel(cuda, orc, rope):
     assert err < 1e-4
     rows = [0, 127, 128, 1000, 1999]
     assert rel_err(a[rows].reshape(-1), oracle_rows(orc, x, T, rows).reshape(-1)) < REL_TOL
+
+
+@pytest.mark.parametrize("p0", [0, 70])
+def test_prefill_cache_rows_equal_append(cuda, orc, rope, p0):
+    """The K/V rows the prefill writes (QK RMSNorm + RoPE at p0 + t, bf16) equal, bit for
+    bit, the rows the oracle's per-token append writes (src/vx27_qfwd.c:339-346)."""
+    T, cap = 150, 256
+    x = make(orc, 24, T)
+    q = dev(x["q"], True).view(T, NQ, HD)
+    k = dev(x["k"], True).view(T, NKV, HD)
+    v = dev(x["v"], True).view(T, NKV, HD)
+    gate = dev(x["gate"], True).view(T, NQ, HD)
+    kc = torch.zeros((NKV, cap, HD), dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    out = torch.empty(T, NQ, HD, device="cuda")
+    ops.gqa_prefill(q, k, v, gate, dev(x["qw"]), dev(x["kw"]), rope, kc, vc, out, p0=p0)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    L, P = orc.lib(), orc.P
+    kr = np.zeros(NKV * cap * HD, np.uint16)
+    vr = np.zeros_like(kr)
+    qo = np.zeros(NQ * HD, np.float32)
+    for t in range(T):
+        pos = np.array([p0 + t], np.int32)
+        L.orc_gqa_append(P(x["q"][t * NQ * HD:]), P(x["k"][t * NKV * HD:]),
+                         P(x["v"][t * NKV * HD:]), P(x["qw"]), P(x["kw"]), P(pos), P(kr), P(vr),
+                         cap, P(qo), 1, NQ, NKV, HD, 64, 1e7, 1e-6, orc.F_ACT_BF16)
+    kg = kc.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)
+    vg = vc.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)
+    rows = lambda a: a.reshape(NKV, cap, HD)[:, p0:p0 + T]
+    assert np.array_equal(rows(kg), rows(kr)) and np.array_equal(rows(vg), rows(vr))

@@ -65,7 +65,11 @@ static_assert(sizeof(PfSmem) + 1024 <= 232448 && sizeof(PairSmem) + 1024 <= 2324
 // with NKS2/NVS2 in the pair kernel.
 
 // ---- prep ----------------------------------------------------------------------------
-// One warp per (token, head) row, 8 consecutive dims per lane (16-byte bf16 accesses).
+// One warp per (token, head) row, 8 consecutive dims per lane (16-byte bf16 accesses), with
+// every load of the row issued before any is used (the row, the RoPE cos/sin at its
+// position, the V row of a KV head), one memory round trip per row instead of three:
+// 0.42 ms at config 4 against 0.47 (ncu); two or four rows per warp and round, with more
+// bytes in flight, measured slower (0.53 / 0.56 ms).
 // RMSNorm with a double sum of squares, NeoX RoPE on dims [0, rope_dim) (the partner of
 // dim d < rope_dim/2 is d + rope_dim/2, held rope_dim/16 lanes away), bf16 stores.
 template <bool ACT_BF16>
@@ -94,7 +98,7 @@ __device__ __forceinline__ void store8_bf16(uint16_t *p, const float *x) {
 }
 
 template <bool ACT_BF16, bool ONE_P>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 5)
 prefill_prep_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
                const void *__restrict__ v_in, const float *__restrict__ qw,
                const float *__restrict__ kw, const float *__restrict__ rope, int rope_len,
@@ -106,59 +110,67 @@ prefill_prep_k(const void *__restrict__ q_in, const void *__restrict__ k_in,
     const size_t n_rows = (size_t)T * nh;
     const int half = rope_dim / 2, hl = half / 8;  // partner lane distance
     const int d0 = lane * 8;
+    const bool rot = d0 < rope_dim;
+    const bool lo = d0 < half;
+    const int src = lo ? lane + hl : lane - hl;
+    const int i0 = lo ? d0 : d0 - half;  // this lane's cos/sin columns (when rot)
     for (size_t item = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; item < n_rows;
          item += ((size_t)gridDim.x * blockDim.x) >> 5) {
         const int t = (int)(item / nh), head = (int)(item % nh);
         const bool is_q = head < nq;
         const int h = is_q ? head : head - nq;
+        const int p = p0 + t;
         const size_t row = is_q ? ((size_t)t * nq + h) * HDP : ((size_t)t * nkv + h) * HDP;
-        float x[8];
+        // every load of the row first: the row, the RoPE cos/sin at its position, and for a
+        // KV head the V row, which goes straight to the cache
+        float x[8], cs[8], sn[8];
         load8<ACT_BF16>(is_q ? q_in : k_in, row + d0, x);
+        const bool prot = rot && p >= 0 && p < rope_len;
+        if (prot) {
+            const float4 *rr = reinterpret_cast<const float4 *>(rope + (size_t)p * rope_dim);
+            const float4 c0 = rr[i0 / 4], c1 = rr[i0 / 4 + 1];
+            const float4 s0 = rr[(half + i0) / 4], s1 = rr[(half + i0) / 4 + 1];
+            cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
+            cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+            sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
+            sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+        }
+        if (!is_q && p < cap) {
+            float v[8];
+            load8<ACT_BF16>(v_in, row + d0, v);
+            store8_bf16(vc + ((size_t)h * cap + p) * HDP + d0, v);
+        }
         double ss = 0.0;
 #pragma unroll
         for (int e = 0; e < 8; e++) ss += (double)x[e] * (double)x[e];
         ss = warp_sum_d(ss);
         const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(ss / HDP), eps)));
-        const float *wp = (is_q ? qw : kw) + d0;
+        const float *wp = (is_q ? qw : kw) + d0;  // L1-resident: every row reads them
         float y[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            float w = wp[e];
+            float w = __ldg(wp + e);
             if (ONE_P) w = __fadd_rn(w, 1.0f);
             y[e] = __fmul_rn(__fmul_rn(x[e], r), w);
         }
-        const int p = p0 + t;
         // partner values for the rotation (all lanes take part in the shuffles)
-        const bool rot = d0 < rope_dim;
-        const bool lo = d0 < half;
-        const int src = lo ? lane + hl : lane - hl;
         float yp[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) yp[e] = __shfl_sync(0xffffffffu, y[e], (src & 31));
         if (rot) {
-            if (p < 0 || p >= rope_len) {
+            if (!prot) {
                 dev_flag(status, VX_DEV_BAD_ARG);
             } else {
-                const float *rr = rope + (size_t)p * rope_dim;
-                const int i0 = lo ? d0 : d0 - half;
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
-                    const float c = rr[i0 + e], sn = rr[half + i0 + e];
                     const float x0 = lo ? y[e] : yp[e], x1 = lo ? yp[e] : y[e];
-                    y[e] = lo ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn))
-                              : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+                    y[e] = lo ? __fsub_rn(__fmul_rn(x0, cs[e]), __fmul_rn(x1, sn[e]))
+                              : __fadd_rn(__fmul_rn(x0, sn[e]), __fmul_rn(x1, cs[e]));
                 }
             }
         }
-        if (is_q) {
-            store8_bf16(qn + ((size_t)h * T + t) * HDP + d0, y);
-        } else if (p < cap) {
-            const size_t o = ((size_t)h * cap + p) * HDP + d0;
-            store8_bf16(kc + o, y);
-            float v[8];
-            load8<ACT_BF16>(v_in, row + d0, v);
-            store8_bf16(vc + o, v);
-        }
+        if (is_q) store8_bf16(qn + ((size_t)h * T + t) * HDP + d0, y);
+        else if (p < cap) store8_bf16(kc + ((size_t)h * cap + p) * HDP + d0, y);
     }
 }
 
@@ -958,7 +970,8 @@ extern "C" int vx27_gqa_prefill(const void *q_in, const void *k_in, const void *
     uint16_t *qn = (uint16_t *)workspace;
     const bool a = flags & VX27_F_ACT_BF16, one = flags & VX27_F_NORM_1P;
     const size_t prep_rows = (size_t)T * (nq + nkv);
-    const int pg = (int)std::min<size_t>((prep_rows + 7) / 8, (size_t)num_sms() * 16);
+    // one resident wave (five 8-warp blocks per SM at the kernel's 48 registers)
+    const int pg = (int)std::min<size_t>((prep_rows + 7) / 8, (size_t)num_sms() * 5);
 #define VX_P(A_, O_)                                                                         \
     prefill_prep_k<A_, O_><<<pg, 256, 0, st>>>(q_in, k_in, v_in, q_norm_w, k_norm_w,          \
                                                rope_table, rope_table_len, p0, qn,            \
