@@ -91,12 +91,22 @@ constexpr size_t SZ_U = 16384;    // U^T hi or lo: rows v, K-major over t (out M
 constexpr size_t SZ_WV = 32768;   // Wv fp32 in 8-column groups: [d/8][t][8]
 constexpr size_t SZ_SCAL = 1024;  // [0] = e^{G_C}; [64 + t] = e^{G_C - G_t} rk_t;
                                   // [128 + t] = e^{G_t} rq_t / sqrt(128)
+// The chunk's gates and decays, from dn_chunk_gates_k: beta_t, G_t = sum_{s<=t} g_s (the
+// log-decay within the chunk, double), e^{G_t}, e^{G_C - G_t} and e^{G_C}.
+struct GateRec {
+    float beta[CK], gam[CK], ec[CK];
+    float egc, pad[3];
+    double G[CK];
+};
+constexpr size_t SZ_GATE = 2048;
+static_assert(sizeof(GateRec) <= SZ_GATE, "gate record");
 constexpr size_t BLK_BYTES =
-    SZ_WKA + SZ_KT + SZ_QB + SZ_PM + 2 * SZ_SC + 2 * SZ_U + SZ_WV + SZ_SCAL;
+    SZ_WKA + SZ_KT + SZ_QB + SZ_PM + 2 * SZ_SC + 2 * SZ_U + SZ_WV + SZ_SCAL + SZ_GATE;
 
 struct Wsp {
     uint8_t *WkA, *KtA, *QB, *PmB, *ScH, *ScL, *UH, *UL;
     float *Wv, *scal;
+    GateRec *gates;
 };
 inline Wsp wsp_views(uint8_t *p, size_t nblk) {
     Wsp w;
@@ -109,7 +119,8 @@ inline Wsp wsp_views(uint8_t *p, size_t nblk) {
     w.UH = p; p += nblk * SZ_U;
     w.UL = p; p += nblk * SZ_U;
     w.Wv = reinterpret_cast<float *>(p); p += nblk * SZ_WV;
-    w.scal = reinterpret_cast<float *>(p);
+    w.scal = reinterpret_cast<float *>(p); p += nblk * SZ_SCAL;
+    w.gates = reinterpret_cast<GateRec *>(p);
     return w;
 }
 
@@ -129,12 +140,63 @@ constexpr uint32_t PREP_SMEM = P_BAR + 16 + 1024;
 
 constexpr int PREP_THREADS = 256;
 
+// Phase 0: one warp per (chunk, V head), two tokens per lane: the gates (double, from a/b
+// through dn_gates_device, or given as double with VX27_F_GATES_F64), their running sum
+// G_t within the chunk (pairs per lane, then a warp scan of the pair sums) and its
+// exponentials, into the block's gate record. Tokens past T are identity steps (beta = 0,
+// g = 0). A kernel of its own, so that the prep's CTAs start on their matrices at once
+// instead of on ~5K cycles of double-precision exponentials.
 template <bool GATES_F64>
+__global__ void __launch_bounds__(256)
+dn_chunk_gates_k(const void *__restrict__ ga, const void *__restrict__ gb,
+                 const float *__restrict__ A_log, const float *__restrict__ dt_bias, Wsp ws,
+                 int T, int nv, int n_chunks) {
+    const int lane = threadIdx.x & 31;
+    const size_t blk = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (blk >= (size_t)n_chunks * nv) return;  // warp-uniform
+    const int vh = (int)(blk / n_chunks), c = (int)(blk % n_chunks);  // blk = vh*n_chunks + c
+    GateRec &gr = ws.gates[blk];
+    double bt[2], gl[2];
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const int tt = c * CK + 2 * lane + e;
+        bt[e] = 0.0;
+        gl[e] = 0.0;
+        if (tt < T) {
+            const size_t gi = (size_t)tt * nv + vh;
+            if constexpr (GATES_F64) {
+                bt[e] = static_cast<const double *>(ga)[gi];
+                gl[e] = static_cast<const double *>(gb)[gi];
+            } else {
+                dn_gates_device((double)act_ld<true>(ga, gi), (double)A_log[vh],
+                                (double)act_ld<true>(gb, gi), (double)dt_bias[vh], &bt[e],
+                                &gl[e]);
+            }
+        }
+    }
+    double incl = gl[0] + gl[1];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const double excl = incl - (gl[0] + gl[1]);
+    const double Gt[2] = {excl + gl[0], incl};
+    const double GC = __shfl_sync(0xffffffffu, incl, 31);
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const int t = 2 * lane + e;
+        gr.beta[t] = (float)bt[e];
+        gr.G[t] = Gt[e];
+        gr.gam[t] = (float)exp(Gt[e]);
+        gr.ec[t] = (float)exp(GC - Gt[e]);
+    }
+    if (lane == 0) gr.egc = (float)exp(GC);
+}
+
 __global__ void __launch_bounds__(PREP_THREADS, 2)
 dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-           const __grid_constant__ CUtensorMap tv, const void *__restrict__ ga,
-           const void *__restrict__ gb, const float *__restrict__ A_log,
-           const float *__restrict__ dt_bias, Wsp ws, int T, int nqk, int nv, int n_chunks,
+           const __grid_constant__ CUtensorMap tv, Wsp ws, int T, int nqk, int nv, int n_chunks,
            uint32_t *status) {
     extern __shared__ uint8_t smraw[];
     uint8_t *sm = align1024(smraw);
@@ -167,71 +229,22 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         tmem_alloc(tslot, 256);
         tmem_relinquish();
     }
-    // 2. gates (tokens past T are identity steps: beta = 0, g = 0)
+    // 2. the chunk's gates and decays (dn_chunk_gates_k)
+    const GateRec &gr = ws.gates[blk];
+    float gam_t = 0.f, ec_t = 0.f;
     if (tid < CK) {
-        const int tt = t0 + tid;
-        double bt = 0.0, gl = 0.0;
-        if (tt < T) {
-            const size_t gi = (size_t)tt * nv + vh;
-            if constexpr (GATES_F64) {
-                bt = static_cast<const double *>(ga)[gi];
-                gl = static_cast<const double *>(gb)[gi];
-            } else {
-                dn_gates_device((double)act_ld<true>(ga, gi), (double)A_log[vh],
-                          (double)act_ld<true>(gb, gi), (double)dt_bias[vh], &bt, &gl);
-            }
-        }
-        beta[tid] = (float)bt;
-        G[tid] = gl;
+        beta[tid] = gr.beta[tid];
+        G[tid] = gr.G[tid];
+        gam_t = gr.gam[tid];
+        ec_t = gr.ec[tid];
     }
-    __syncthreads();  // barrier initialised, gates written
+    __syncthreads();  // barrier initialised, gates in shared memory
     bool ok = mbar_wait(bar, 0, status, VX_DEV_TIMEOUT_TMA);
-    // l2 norms from double sums of squares (src/vx27_deltanet.c:51-56), one row per thread:
-    // rows 0..63 of AKQ are k, rows 64..127 are q
-    if (tid < 2 * CK) {
-        double ss = 0.0;
-#pragma unroll
-        for (int b = 0; b < 2; b++)
-#pragma unroll
-            for (int pc = 0; pc < 8; pc++) {
-                const uint4 w4 = *reinterpret_cast<const uint4 *>(AKQ + b * 16384 + tid * 128 + pc * 16);
-                const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const double x0 = bf16_to_f32(w[e] & 0xffffu), x1 = bf16_to_f32(w[e] >> 16);
-                    ss += x0 * x0;
-                    ss += x1 * x1;
-                }
-            }
-        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, 1e-6f)));
-        if (tid < CK) rk[tid] = r;
-        else rq[tid - CK] = r;
-    }
-    if (warp == 0) {  // G_t = sum_{s<=t} g_s: pairs per lane, then a warp scan of pair sums
-        const double g0 = G[2 * lane], g1 = G[2 * lane + 1];
-        double incl = g0 + g1;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const double y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-        }
-        const double excl = incl - (g0 + g1);
-        G[2 * lane] = excl + g0;
-        G[2 * lane + 1] = incl;
-    }
     ok = __syncthreads_and(ok);
     tc_fence_after();
     const uint32_t tbase = *tslot;
     const float qscale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));
-    if (tid < CK) {
-        const float gam = (float)exp(G[tid]);
-        xs[tid] = gam * rk[tid];
-        er[tid] = (float)exp(G[CK - 1] - G[tid]) * rk[tid];
-        ws.scal[blk * 256 + 128 + tid] = gam * __fmul_rn(rq[tid], qscale);
-        ws.scal[blk * 256 + 64 + tid] = er[tid];
-    }
     if (tid == 0 && ok) {
-        ws.scal[blk * 256] = (float)exp(G[CK - 1]);
         // raw Q (rows 64..127 of each column block) -> the out kernel's B operand image, raw
         // K (rows 0..63) -> the scan's K^T operand image (MN-major: rows t, columns d)
         bulk_s2g(ws.QB + blk * SZ_QB, AKQ + 8192, 8192);
@@ -239,8 +252,9 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         bulk_s2g(ws.KtA + blk * SZ_KT, AKQ, 8192);
         bulk_s2g(ws.KtA + blk * SZ_KT + 8192, AKQ + 16384, 8192);
         bulk_commit();
-        // Gram: D[0:128, 0:64] = [K;Q] K^T
-        const uint32_t id = idesc_bf16(128, CK, false, false);
+        // Gram: D[0:128, 0:128] = [K;Q] [K;Q]^T; columns 0..63 hold [K;Q] K^T, and row r's
+        // own column r its squared norm
+        const uint32_t id = idesc_bf16(128, 2 * CK, false, false);
         const uint32_t a0 = smem_u32(AKQ);
 #pragma unroll
         for (int kk = 0; kk < D / 16; kk++) {
@@ -252,6 +266,34 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
     if (ok) ok = mbar_wait(bar, 1, status, VX_DEV_TIMEOUT_MMA);
     ok = __syncthreads_and(ok);
     tc_fence_after();
+    // 3. l2 norms (src/vx27_deltanet.c:51-56) from the Gram diagonal: the squares of bf16
+    //    values are exact in fp32 and the tensor core sums them in fp32 (the reference sums
+    //    in double; the relative difference is ~1e-7, far inside the prefill's tolerance,
+    //    and a per-row double sum took ~3.7K cycles of the CTA's float-to-double
+    //    conversions). Warps 0-3, one row per thread (rows 0..63 k, 64..127 q).
+    if (ok && warp < 4) {
+        float dg[32];
+        const uint32_t ta = tbase + ((uint32_t)(warp * 32) << 16) + warp * 32;
+        tmem_ld16(ta, dg);
+        tmem_ld16(ta + 16, dg + 16);
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; j++) ss = (j == lane) ? dg[j] : ss;
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
+        const int row = warp * 32 + lane;
+        if (row < CK) rk[row] = r;
+        else rq[row - CK] = r;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid < CK) {
+        xs[tid] = gam_t * rk[tid];
+        er[tid] = ec_t * rk[tid];
+        ws.scal[blk * 256 + 128 + tid] = gam_t * __fmul_rn(rq[tid], qscale);
+        ws.scal[blk * 256 + 64 + tid] = er[tid];
+    }
+    if (tid == 0 && ok) ws.scal[blk * 256] = gr.egc;
     if (ok) {
         // 4. Gram epilogue: rows 0..63 -> L (fp32, shared), rows 64..127 -> Pm (hi/lo image);
         //    warps w and w + 4 share a TMEM lane quarter and take one half of the columns each
@@ -271,7 +313,9 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
             for (int j = 0; j < 16; j++) {
                 const int s = c16 + j;
                 const bool keep = low ? s < t : s <= t;
-                val[j] = keep ? sc_t * rk[s] * expf((float)(Gt - G[s])) * dv[j] : 0.f;
+                // e^{G_t - G_s} by the SFU's 2^x (a few ulp; L and Pm enter the MMAs as
+                // bf16 hi + lo pairs of ~16 bits)
+                val[j] = keep ? sc_t * rk[s] * __expf((float)(Gt - G[s])) * dv[j] : 0.f;
             }
             if (low) {
 #pragma unroll
@@ -301,16 +345,26 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
         tc_fence_before();
         __syncthreads();
         // 5. Li = (I + L)^-1 by 16x16 blocks: the diagonal blocks by forward substitution
-        //    (warp w, one column per lane), then the off-diagonal blocks one block diagonal
-        //    at a time, Li_ij = -Li_ii sum_{k=j}^{i-1} L_ik Li_kj
+        //    (warp w, one column per lane; each row of L read as four 16-byte loads ahead of
+        //    its FMA chain), then the off-diagonal blocks one block diagonal at a time,
+        //    Li_ij = -Li_ii sum_{k=j}^{i-1} L_ik Li_kj, a thread per 1x4 strip of a block
+        //    (four independent chains, 16-byte operand loads). Every element's FMAs run in
+        //    the order of the element-per-thread form, whose results these equal bit for bit
+        //    in ~4x fewer cycles.
         if (warp < 4 && lane < 16) {
             const int o = warp * 16;
             float x[16];
 #pragma unroll
             for (int t2 = 0; t2 < 16; t2++) {
+                float lr[16];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const float4 v = *reinterpret_cast<const float4 *>(Lf + fsw(o + t2, o + 4 * q));
+                    lr[4 * q] = v.x; lr[4 * q + 1] = v.y; lr[4 * q + 2] = v.z; lr[4 * q + 3] = v.w;
+                }
                 float acc = (t2 == lane) ? 1.f : 0.f;
 #pragma unroll
-                for (int s2 = 0; s2 < t2; s2++) acc = fmaf(-Lf[fsw(o + t2, o + s2)], x[s2], acc);
+                for (int s2 = 0; s2 < t2; s2++) acc = fmaf(-lr[s2], x[s2], acc);
                 x[t2] = acc;
                 Li[fsw(o + t2, o + lane)] = acc;
             }
@@ -319,24 +373,39 @@ dn_prep_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUten
 #pragma unroll 1
         for (int dg = 1; dg < 4; dg++) {
             const int nb = 4 - dg;
-            for (int e = tid; e < nb * 256; e += PREP_THREADS) {
-                const int j = e >> 8, i = j + dg, r = (e >> 4) & 15, cc = e & 15;
-                float acc = 0.f;
+            // strip e: block j = e >> 6 (rows of block i = j + dg), row r, columns c0..c0+3
+            const int e = tid, j = e >> 6, i = j + dg, r = (e >> 2) & 15, c0 = (e & 3) * 4;
+            if (e < nb * 64) {
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
                 for (int kb = j; kb < i; kb++)
 #pragma unroll
-                    for (int kk = 0; kk < 16; kk++)
-                        acc = fmaf(Lf[fsw(16 * i + r, 16 * kb + kk)],
-                                   Li[fsw(16 * kb + kk, 16 * j + cc)], acc);
-                Ms[e] = acc;
+                    for (int kk = 0; kk < 16; kk++) {
+                        const float lv = Lf[fsw(16 * i + r, 16 * kb + kk)];
+                        const float4 m = *reinterpret_cast<const float4 *>(
+                            Li + fsw(16 * kb + kk, 16 * j + c0));
+                        acc[0] = fmaf(lv, m.x, acc[0]);
+                        acc[1] = fmaf(lv, m.y, acc[1]);
+                        acc[2] = fmaf(lv, m.z, acc[2]);
+                        acc[3] = fmaf(lv, m.w, acc[3]);
+                    }
+                *reinterpret_cast<float4 *>(Ms + (j << 8) + r * 16 + c0) =
+                    make_float4(acc[0], acc[1], acc[2], acc[3]);
             }
             __syncthreads();
-            for (int e = tid; e < nb * 256; e += PREP_THREADS) {
-                const int j = e >> 8, i = j + dg, r = (e >> 4) & 15, cc = e & 15;
-                float acc = 0.f;
+            if (e < nb * 64) {
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int kk = 0; kk < 16; kk++)
-                    acc = fmaf(Li[fsw(16 * i + r, 16 * i + kk)], Ms[(j << 8) + kk * 16 + cc], acc);
-                Li[fsw(16 * i + r, 16 * j + cc)] = -acc;
+                for (int kk = 0; kk < 16; kk++) {
+                    const float lv = Li[fsw(16 * i + r, 16 * i + kk)];
+                    const float4 m = *reinterpret_cast<const float4 *>(Ms + (j << 8) + kk * 16 + c0);
+                    acc[0] = fmaf(lv, m.x, acc[0]);
+                    acc[1] = fmaf(lv, m.y, acc[1]);
+                    acc[2] = fmaf(lv, m.z, acc[2]);
+                    acc[3] = fmaf(lv, m.w, acc[3]);
+                }
+                *reinterpret_cast<float4 *>(Li + fsw(16 * i + r, 16 * j + c0)) =
+                    make_float4(-acc[0], -acc[1], -acc[2], -acc[3]);
             }
             __syncthreads();
         }
@@ -824,15 +893,15 @@ extern "C" int vx27_deltanet_prefill_chunked(const void *q, const void *k, const
                           errlen))
         return -1;
 
-    if (g64) {
-        if (set_smem(dn_prep_tc<true>, PREP_SMEM, err, errlen)) return -1;
-        dn_prep_tc<true><<<dim3(n_chunks, nv), PREP_THREADS, PREP_SMEM, st>>>(
-            tq, tk, tv, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
-    } else {
-        if (set_smem(dn_prep_tc<false>, PREP_SMEM, err, errlen)) return -1;
-        dn_prep_tc<false><<<dim3(n_chunks, nv), PREP_THREADS, PREP_SMEM, st>>>(
-            tq, tk, tv, a, b, A_log, dt_bias, ws, T, nqk, nv, n_chunks, status);
-    }
+    const int gblocks = (int)(((size_t)n_chunks * nv * 32 + 255) / 256);
+    if (g64)
+        dn_chunk_gates_k<true><<<gblocks, 256, 0, st>>>(a, b, A_log, dt_bias, ws, T, nv, n_chunks);
+    else
+        dn_chunk_gates_k<false><<<gblocks, 256, 0, st>>>(a, b, A_log, dt_bias, ws, T, nv, n_chunks);
+    VX_CK(cudaGetLastError());
+    if (set_smem(dn_prep_tc, PREP_SMEM, err, errlen)) return -1;
+    dn_prep_tc<<<dim3(n_chunks, nv), PREP_THREADS, PREP_SMEM, st>>>(tq, tk, tv, ws, T, nqk, nv,
+                                                                   n_chunks, status);
     VX_CK(cudaGetLastError());
     // scan: the narrowest column blocks whose grid still fits the GPU (2 CTAs per SM for 8
     // columns, 1 for 16), else 32
