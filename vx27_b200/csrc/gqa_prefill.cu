@@ -32,22 +32,27 @@ namespace {
 constexpr int HDP = 256;
 constexpr int QT = 128;          // queries per CTA
 constexpr int KT = 128;          // keys per tile
-constexpr int NKS = 3;           // single-SM kernel: K ring slots of 16 KB
-constexpr int NVS = 3;           // V ring slots of 16 KB
+constexpr int NKS = 5;           // single-SM kernel: K ring slots of 16 KB
+constexpr int NVS = 4;           // V ring slots of 16 KB
 constexpr int NS = NKS + NVS;    // slots 0..NKS-1 hold K chunks, NKS.. V chunks
-constexpr int NKS2 = 6;          // CTA pair: K ring slots of 8 KB (this SM's half of a chunk)
-constexpr int NVS2 = 6;          // V ring slots of 8 KB
+constexpr int NKS2 = 10;         // CTA pair: K ring slots of 8 KB (this SM's half of a chunk)
+constexpr int NVS2 = 9;          // V ring slots of 8 KB
 constexpr int NS2 = NKS2 + NVS2;
 constexpr int SLOT2 = 8192;
 constexpr int PF_THREADS = 352;  // TMA warp, S-MMA warp, 8 softmax warps, O-MMA warp
 constexpr float RESCALE_LOG2 = 8.0f;
 
+// Tensor memory (512 columns): S at [0, 128) (fp32), O at [128, 384), and P(j) as bf16
+// pairs in buffer j & 1 at [384 + 64 b, 448 + 64 b), the O MMA's A operand from there (so
+// P needs no shared memory). S(j + 1) is issued as soon as the softmax has read S(j).
+constexpr uint32_t TM_O = 128, TM_P = 384;
+
 template <int NSLOT, int SLOT>
 struct AttnSmem {
     uint8_t q[4][QT * 128];      // Q tile, 4 chunks of [128 rows x 64 dims], 128B swizzle
     uint8_t ring[NSLOT][SLOT];   // K chunk [keys x 64 dims] or V chunk [32 keys x dims]
-    uint8_t p[2][2][QT * 128];   // P [128 rows x 128 keys] bf16 as two 64-key column blocks,
-                                 // two buffers (tile parity)
+    float xmax[2][2][QT];        // row maxima of the two key halves, by tile parity
+    float xsum[2][QT];           // row sums of the two halves
     uint64_t qfull, full[NSLOT], empty[NSLOT], s_full, s_empty, p_full[2], pv_done[2],
         o_final, mma_done, qk_done;
     uint32_t tmem_base;
@@ -55,9 +60,9 @@ struct AttnSmem {
 };
 using PfSmem = AttnSmem<NS, 16384>;   // K chunk [128 keys x 64 dims], V [32 keys x 256 dims]
 using PairSmem = AttnSmem<NS2, SLOT2>;  // K chunk [64 keys x 64 dims], V [32 keys x 128 dims]
-// the fp32-gate epilogue stages O / l (128 rows x 256 fp32) over the ring and P buffers
-static_assert(sizeof(PfSmem::ring) + sizeof(PfSmem::p) >= QT * HDP * 4, "staging");
-static_assert(sizeof(PairSmem::ring) + sizeof(PairSmem::p) >= QT * HDP * 4, "staging");
+// the fp32-gate epilogue stages O / l (128 rows x 256 fp32) over the ring
+static_assert(sizeof(PfSmem::ring) >= QT * HDP * 4, "staging");
+static_assert(sizeof(PairSmem::ring) >= QT * HDP * 4, "staging");
 static_assert(sizeof(PfSmem) + 1024 <= 232448 && sizeof(PairSmem) + 1024 <= 232448, "smem");
 
 // Chunk c of K(m) is the (4m + c)-th load of the K ring, chunk c of V(t) the (4t + c)-th
@@ -231,8 +236,8 @@ struct SyncOne {
         dev_flag(status, code);
     }
     __device__ bool aborted() const { return *(volatile int *)abort != 0; }
-    // every softmax thread arrives once it has read S (count 256) / written its P row
-    // (count 256)
+    // every softmax thread arrives once it has read S (count 256) / written its half row of
+    // P (count 256)
     __device__ void s_read(uint64_t *bar) const { mbar_arrive(bar); }
     __device__ void p_written(uint64_t *bar) const { mbar_arrive(bar); }
 };
@@ -247,7 +252,8 @@ struct SyncPair {
     }
     __device__ bool aborted() const { return *(volatile int *)abort != 0; }
     // one arrival per softmax warp of either CTA on rank 0's barrier (count 16): the lanes'
-    // TMEM reads / P stores (each lane fenced them) are ordered before lane 0's arrival
+    // TMEM reads of S / stores of P (each lane fenced them) are ordered before lane 0's
+    // arrival
     __device__ void s_read(uint64_t *bar) const {
         __syncwarp();
         if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(mapa_shared(bar, 0));
@@ -280,7 +286,7 @@ __device__ __forceinline__ void softmax_role(Smem &sm, const Sync &sy, uint32_t 
                                              int lane, int h, int t0, int p0, int T, int nq,
                                              int n_kt, const void *__restrict__ gate,
                                              void *__restrict__ out) {
-    const uint32_t tS = tmem, tO = tmem + 128, tX = tmem + 384;
+    const uint32_t tO = tmem + TM_O;
     const int q4 = warp & 3;
     const int hf = (warp - 2) >> 2;
     const int r = q4 * 32 + lane;
@@ -292,6 +298,7 @@ __device__ __forceinline__ void softmax_role(Smem &sm, const Sync &sy, uint32_t 
     // every softmax warp runs all n_kt iterations and the named barrier of each, also
     // after a failed wait (then skipping the tensor-memory work), so none is left waiting
     for (int j = 0; j < n_kt; j++) {
+        const int b = j & 1;
         if (ok) ok = pf_wait(sy, &sm.s_full, j & 1, VX_DEV_TIMEOUT_MMA);
         ok = __all_sync(0xffffffffu, ok);  // warp-uniform: tcgen05.ld/st are warp-wide
         constexpr int HK = KT / 2;
@@ -299,7 +306,7 @@ __device__ __forceinline__ void softmax_role(Smem &sm, const Sync &sy, uint32_t 
         float mloc = -INFINITY;
         if (ok) {
             tc_fence_after();
-            tmem_ld64(tS + lane_off + hf * HK, s);  // four loads in flight, one wait
+            tmem_ld64(tmem + lane_off + hf * HK, s);  // four loads in flight, one wait
             tc_fence_before();
             sy.s_read(&sm.s_empty);
             const int kbase = j * KT + hf * HK;
@@ -320,14 +327,10 @@ __device__ __forceinline__ void softmax_role(Smem &sm, const Sync &sy, uint32_t 
                 for (int i = 0; i < w; i++) mx[i] = fmaxf(mx[i], mx[i + w]);
             mloc = mx[0];
         }
-        // ... and over both halves: the two threads of a row share its TMEM lane, so the
-        // halves meet in spare columns (tile parity, half) past S and O
-        tmem_st1(tX + lane_off + 2 * (j & 1) + hf, mloc);
-        tmem_st_wait();
-        tc_fence_before();
+        // ... and over both halves (the two threads of a row), through shared memory
+        sm.xmax[b][hf][r] = mloc;
         named_bar_sync(1, 256);
-        tc_fence_after();
-        const float mpart = tmem_ld1(tX + lane_off + 2 * (j & 1) + (hf ^ 1));
+        const float mpart = sm.xmax[b][hf ^ 1][r];
         if (!ok) continue;
         const float mt = fmaxf(mloc, mpart) * sc2;
         float alpha = 1.0f;
@@ -339,7 +342,6 @@ __device__ __forceinline__ void softmax_role(Smem &sm, const Sync &sy, uint32_t 
         // rescale this warp's half of its O rows when one of its rows raised its max (not
         // on the first tile of a row, where O holds nothing yet), once O += P(j-1) V(j-1)
         // is done
-        const int pb = j & 1;
         const bool need = grow && alpha > 0.0f;
         if (__any_sync(0xffffffffu, need)) {
             ok = pf_wait(sy, &sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, VX_DEV_TIMEOUT_MMA);
@@ -355,42 +357,38 @@ __device__ __forceinline__ void softmax_role(Smem &sm, const Sync &sy, uint32_t 
                 for (int e = 0; e < 16; e++) o[e] *= alpha;
                 tmem_st16(ta, o);
             }
-            tmem_st_wait();
-            tc_fence_before();
         }
-        // P buffer pb is free once O += P(j-2) V(j-2) is done
+        // P buffer b is free once O += P(j-2) V(j-2) is done
         if (j >= 2) {
-            ok = pf_wait(sy, &sm.pv_done[pb], ((j >> 1) - 1) & 1, VX_DEV_TIMEOUT_MMA);
+            ok = pf_wait(sy, &sm.pv_done[b], ((j >> 1) - 1) & 1, VX_DEV_TIMEOUT_MMA);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) continue;
+            tc_fence_after();
         }
+        // P(j): this half's 64 keys as 32 columns of bf16 pairs
         float ls[4] = {0.f, 0.f, 0.f, 0.f};
-        uint8_t *prow = sm.p[pb][hf] + r * 128;
         const float nm = -m_run;
+        uint32_t pw[32];
 #pragma unroll
         for (int u = 0; u < 8; u++) {
-            uint32_t w4[4];
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const float pa = ex2_approx(fmaf(s[u * 8 + 2 * e], sc2, nm));
                 const float pb = ex2_approx(fmaf(s[u * 8 + 2 * e + 1], sc2, nm));
                 ls[e] += pa + pb;
-                w4[e] = pack_bf16x2(pa, pb);
+                pw[4 * u + e] = pack_bf16x2(pa, pb);
             }
-            *reinterpret_cast<uint4 *>(prow + (((u ^ (r & 7)) & 7) << 4)) =
-                make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
+        tmem_st32(tmem + TM_P + 64u * b + lane_off + 32 * hf, pw);
+        tmem_st_wait();
+        tc_fence_before();
         l_run = fmaf(l_run, alpha, (ls[0] + ls[1]) + (ls[2] + ls[3]));
-        fence_proxy_async();
-        sy.p_written(&sm.p_full[pb]);
+        sy.p_written(&sm.p_full[b]);
     }
     // the row sum is the sum of both halves' partial sums (same maxima, same rescales)
-    tmem_st1(tX + lane_off + 4 + hf, l_run);
-    tmem_st_wait();
-    tc_fence_before();
+    sm.xsum[hf][r] = l_run;
     named_bar_sync(1, 256);
-    tc_fence_after();
-    const float l_row = l_run + tmem_ld1(tX + lane_off + 4 + (hf ^ 1));
+    const float l_row = l_run + sm.xsum[hf ^ 1][r];
     // bf16 gate: this thread's half row of the gate (128 values, 256 contiguous bytes) is
     // requested before O is final, and the gated row goes from registers straight to the
     // output, with no staging pass through shared memory. The sigmoid uses the SFU's 2^x
@@ -568,7 +566,7 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
-    const uint32_t tS = tmem, tO = tmem + 128;
+    const uint32_t tO = tmem + TM_O;
     const SyncOne sy{&sm.abort, status};
 
     if (warp == 0) {
@@ -637,7 +635,7 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     const uint64_t dk = sdesc_add(dr0, s2 * 16384);
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++)
-                        mma_bf16(tS, sdesc_add(dq, kk * 32), sdesc_add(dk, kk * 32), id1,
+                        mma_bf16(tmem, sdesc_add(dq, kk * 32), sdesc_add(dk, kk * 32), id1,
                                  (c | kk) != 0);
                     mma_commit(&sm.empty[s2]);
                 }
@@ -648,9 +646,9 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
             pf_drain(&sm.qk_done, 0);
         }
     } else if (warp == PF_THREADS / 32 - 1) {
-        if (lane == 0) {  // ---- MMA issuer, O stream: O += P(t) V(t) once P(t) is written
+        if (lane == 0) {  // ---- MMA issuer, O stream: O += P(t) V(t) once P(t) is written,
+                          // P from tensor memory (buffer t & 1)
             const uint32_t id2 = idesc_bf16(128, HDP, false, true);
-            const uint64_t dp0 = sdesc_sw128(smem_u32(sm.p[0][0]), 16, 1024);
             const uint64_t dv0 = sdesc_sw128(smem_u32(sm.ring[0]), 32 * 128, 1024);
             bool ok = true;
             for (int t = 0; t < n_kt && ok; t++) {
@@ -664,11 +662,9 @@ prefill_attn_tc(const __grid_constant__ CUtensorMap tmq, const __grid_constant__
                     const uint64_t dv = sdesc_add(dv0, s2 * 16384);
 #pragma unroll
                     for (int k2 = 0; k2 < 2; k2++) {
-                        const int kk = 2 * c + k2;  // 16-key step of the 128-key tile
-                        mma_bf16(tO,
-                                 sdesc_add(dp0, (uint32_t)(pb * 2 + (kk >> 2)) * (QT * 128) +
-                                                    (kk & 3) * 32),
-                                 sdesc_add(dv, k2 * 2048), id2, (t > 0 || kk > 0) ? 1u : 0u);
+                        const int kk = 2 * c + k2;  // 16-key step: 8 columns of bf16 pairs
+                        mma_bf16_ts(tO, tmem + TM_P + 64u * pb + 8u * kk, sdesc_add(dv, k2 * 2048), id2,
+                                    (t > 0 || kk > 0) ? 1u : 0u);
                     }
                     mma_commit(&sm.empty[s2]);
                 }
@@ -753,7 +749,7 @@ prefill_attn_pair(const __grid_constant__ CUtensorMap tmq, const __grid_constant
     cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
-    const uint32_t tS = tmem, tO = tmem + 128;
+    const uint32_t tO = tmem + TM_O;
     const SyncPair sy{&sm.abort, status, mapa_shared(&sm.abort, rank ^ 1u)};
     // MMA completion: one arrival on the barrier of each CTA
     auto commit_both = [](uint64_t *bar) { mma_commit_pair_both(bar); };
@@ -835,7 +831,7 @@ prefill_attn_pair(const __grid_constant__ CUtensorMap tmq, const __grid_constant
                     const uint64_t dk = sdesc_add(dr0, s2 * SLOT2);
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++)
-                        mma_bf16_pair(tS, sdesc_add(dq, kk * 32), sdesc_add(dk, kk * 32), id1,
+                        mma_bf16_pair(tmem, sdesc_add(dq, kk * 32), sdesc_add(dk, kk * 32), id1,
                                       (c | kk) != 0);
                     commit_both(&sm.empty[s2]);
                 }
@@ -848,7 +844,6 @@ prefill_attn_pair(const __grid_constant__ CUtensorMap tmq, const __grid_constant
     } else if (warp == PF_THREADS / 32 - 1) {
         if (lane == 0 && rank == 0) {  // ---- MMA issuer, O stream (rank 0)
             const uint32_t id2 = idesc_bf16(256, HDP, false, true);
-            const uint64_t dp0 = sdesc_sw128(smem_u32(sm.p[0][0]), 16, 1024);
             const uint64_t dv0 = sdesc_sw128(smem_u32(sm.ring[0]), 32 * 128, 1024);
             bool ok = true;
             for (int t = 0; t < n_kt && ok; t++) {
@@ -863,10 +858,8 @@ prefill_attn_pair(const __grid_constant__ CUtensorMap tmq, const __grid_constant
 #pragma unroll
                     for (int k2 = 0; k2 < 2; k2++) {
                         const int kk = 2 * c + k2;
-                        mma_bf16_pair(tO,
-                                      sdesc_add(dp0, (uint32_t)(pb * 2 + (kk >> 2)) * (QT * 128) +
-                                                         (kk & 3) * 32),
-                                      sdesc_add(dv, k2 * 2048), id2, (t > 0 || kk > 0) ? 1u : 0u);
+                        mma_bf16_pair_ts(tO, tmem + TM_P + 64u * pb + 8u * kk, sdesc_add(dv, k2 * 2048),
+                                         id2, (t > 0 || kk > 0) ? 1u : 0u);
                     }
                     commit_both(&sm.empty[s2]);
                 }

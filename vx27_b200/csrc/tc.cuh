@@ -100,6 +100,19 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float *v) {
           "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
         : "memory");
 }
+// Store 32 consecutive 32-bit columns of this thread's TMEM lane (e.g. 64 bf16 values packed
+// two per column, the lower-indexed in the low half); completes before tcgen05.wait::st.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+        "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]),
+          "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]),
+          "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]),
+          "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]),
+          "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
 // One fp32 column of this thread's TMEM lane (load waits; store completes at tmem_st_wait).
 __device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
     uint32_t r;
@@ -148,6 +161,15 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64
         "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }"
         ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// D(tmem) (+)= A(tmem) x B(smem): A's rows are TMEM lanes, its K values packed two bf16 per
+// 32-bit column from column a_tmem on (K-major); issued by one thread.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
 // The mbarrier receives one arrival when all previously issued MMAs of this thread are done.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -210,6 +232,14 @@ __device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, u
         "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
         "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p; }"
         ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// The same with A in TMEM (each CTA's lanes hold its 128 rows of A).
+__device__ __forceinline__ void mma_bf16_pair_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p; }"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
 // One arrival on the mbarrier at shared::cluster address `bar` (either CTA of the pair)
 // once all pair MMAs this thread issued before are done.
