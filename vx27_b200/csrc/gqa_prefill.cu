@@ -3,21 +3,26 @@
 //   prep kernel   per token and head: QK RMSNorm, partial RoPE at position p0 + t (host
 //                 table), q -> bf16 Qn[nq][T][256], k/v -> the bf16 KV cache slots p0 + t
 //                 (the cache the decode continues from); src/vx27_qfwd.c:339-346 per token
-//   main kernel   one CTA per (128-query tile, query head), flash-attention forward:
+//   attention     flash-attention forward. By default a 2-CTA cluster per (128-query tile,
+//                 two query heads of one KV head) whose M = 256 tcgen05 MMAs span both SMs,
+//                 each SM holding half of every K/V chunk (prefill_attn_pair); else one CTA
+//                 per (tile, head) (prefill_attn_tc). Warp roles of a CTA:
 //     warp 0      TMA: the Q tile (128 x 256, resident); 128-key K tiles as four 64-dim
-//                 chunks and V tiles as four 32-key chunks through two rings of 16 KB
-//                 slots, one for K (read by the S-MMA warp) and one for V (the O-MMA
-//                 warp), each refilled as soon as a slot frees. A slot has one consumer,
-//                 which waits for every phase of its barriers in order; with a shared ring
-//                 a consumer that ran ahead of a slot's previous load (the other warp's)
-//                 could take that load's pending phase for its own
-//     warp 1      tcgen05.mma: S = Q K^T (128 x 128 in TMEM) and O += P V (128 x 256 in
-//                 TMEM, V read as an MN-major operand), issued as S(j+1) then O += P(j) V(j)
+//                 chunks and V tiles as four 32-key chunks through two rings, one for K
+//                 (read by the S-MMA warp) and one for V (the O-MMA warp), each refilled
+//                 as soon as a slot frees. A slot has one consumer, which waits for every
+//                 phase of its barriers in order; with a shared ring a consumer that ran
+//                 ahead of a slot's previous load (the other warp's) could take that load's
+//                 pending phase for its own
+//     warp 1      tcgen05.mma: S = Q K^T (128 x 128 fp32 in TMEM), issued as soon as the
+//                 softmax has read the previous S
+//     warp 10     tcgen05.mma: O += P V (128 x 256 fp32 in TMEM), P read from TMEM as the A
+//                 operand, V as an MN-major operand from shared memory
 //     warps 2-9   two threads per query row (its TMEM lane), one per half of the keys and of
 //                 the output columns: causal mask, running max in log2 units (the halves
-//                 meet in spare TMEM columns), p = 2^(x - m) as bf16 rows of P in shared
-//                 memory; O is rescaled in TMEM only when a row's max grows by more than
-//                 2^8 (lazy rescale); epilogue O / l * sigmoid(gate).
+//                 meet through shared memory), p = 2^(x - m) written to TMEM as bf16 pairs
+//                 (two P buffers); O is rescaled in TMEM only when a row's max grows by
+//                 more than 2^8 (lazy rescale); epilogue O / l * sigmoid(gate).
 // Query tiles are issued longest first; the six query heads of a KV head run on
 // neighbouring CTAs so their K/V tiles are served from L2.
 #include <math.h>
