@@ -577,10 +577,12 @@ def run_batch1(args, cpu: bool = True) -> dict:
             for t in range(n_tok):
                 ops.deltanet_decode_batch(S, ring, qkv[t:t + 1], a[t:t + 1], b[t:t + 1], A, dt,
                                           w, pos[t:t + 1], o[t:t + 1], nqk, nv)
+        def run_tokens():  # all 2000 tokens in one call, the state resident in the kernel
+            ops.deltanet_decode_tokens(S[0], ring[0], qkv, a, b, A, dt, w, pos, o, nqk, nv)
         units, unit_name = n_tok, "token"
         bytes_per_unit = 2 * nv * 128 * 128 * 4 + 4 * C * 4 + C * 4 + nv * 128 * 4
         name = "config 0: DeltaNet decode, batch 1, 16 heads, 2000 sequential tokens"
-        others = {}
+        others = {"vx27_deltanet_decode_tokens, one call for the 2000 tokens": run_tokens}
     else:
         ctx, nq, nkv, hd = 8192, 24, 4, 256
         cap = ctx
@@ -917,12 +919,16 @@ def run_longctx(args, rank: int, world: int, local: int) -> dict | None:
 
 # ------------------------------------------------- the other configs, briefly
 def other_configs(args) -> dict:
-    """Configs 1 and 4 on the same GPU after the config 2 timed region (its buffers freed):
-    the batch-1 GQA decode at context 8192 (replayed from a CUDA graph) and the 32768-token
-    prefill of one layer of each kind, each with its own clock samples."""
+    """Configs 0, 1 and 4 on the same GPU after the config 2 timed region (its buffers
+    freed): the batch-1 DeltaNet decode of 2000 tokens and the batch-1 GQA decode at context
+    8192 (both replayed from a CUDA graph), and the 32768-token prefill of one layer of each
+    kind, each with its own clock samples."""
     import copy
     import torch
     torch.cuda.empty_cache()
+    a0 = copy.copy(args)
+    a0.workload, a0.steps, a0.warmup = "config0", 3, 1
+    c0 = run_batch1(a0, cpu=False)
     a1 = copy.copy(args)
     a1.workload, a1.steps, a1.warmup = "config1", 200, 10
     c1 = run_batch1(a1, cpu=False)
@@ -931,6 +937,12 @@ def other_configs(args) -> dict:
     c4 = run_prefill(a4)
     torch.cuda.empty_cache()
     return {
+        "config0_token_us": c0["value"],
+        "config0": {"us_per_token_graph": c0["us_per_unit_graph"],
+                    "us_per_token_launched": c0["us_per_unit_launched"],
+                    "form": "vx27_deltanet_decode_batch, one call per token",
+                    "other_forms_us_graph": c0["other_forms_us_graph"],
+                    "roofline": c0["roofline"], "clocks": c0["clocks"]},
         "config1_decode_us": c1["value"],
         "config1": {"us_per_decode_graph": c1["us_per_unit_graph"],
                     "us_per_decode_launched": c1["us_per_unit_launched"],

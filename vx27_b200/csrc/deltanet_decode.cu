@@ -391,6 +391,286 @@ __global__ void gate_params_k(const void *__restrict__ a, const void *__restrict
     }
 }
 
+// ---- T tokens of one sequence with the state resident (vx27_deltanet_decode_tokens) -----
+// CTA (cs, vh) keeps columns [16 cs, 16 cs + 16) of V head vh's 128 x 128 state in
+// registers for all T tokens (the delta rule's columns are independent): warps 0-7 hold it,
+// one 8-row block of one column per thread, and run each token's decay, S^T k, delta,
+// update and S^T q with two column reductions. Warps 8-15 prepare the tokens ahead into a
+// ring of parameter slots: the width-4 conv + SiLU of the head's q and k channels (one per
+// thread, computed by each of the head's 8 CTAs) and of this CTA's 16 v channels from a
+// private copy of their conv history (read from the ring at the start, so any position
+// sequence reproduces T single-token calls), the l2 norms with the per-token kernel's double
+// sums, and the gates. Nothing crosses CTAs: the state goes back to global memory at the
+// end, and the ring is left untouched here (the CTAs of a QK head may run in different
+// waves, so each must find the initial history there) and brought up to date by
+// dn_tokens_ring_k afterwards. Per token this replaces one launch and a 1 MB state round
+// trip.
+constexpr int TK_SPLIT = 8;
+constexpr int TK_COLS = HD / TK_SPLIT;
+constexpr int TK_NPARAM = 4;
+constexpr int TK_NCH = 2 * HD + TK_COLS;  // q, k and this CTA's v channels
+
+struct TkParams {
+    float qn[HD], kn[HD], v[TK_COLS];
+    float beta, decay;
+};
+struct TkSmem {
+    TkParams prm[TK_NPARAM];
+    float gbeta[2][32], gdecay[2][32];  // gates of 32-token batches (gate warp -> prep)
+    float hist[TK_NCH][4];       // conv history by position & 3
+    float y[2][HD];              // conv outputs of q and k, for the norms
+    float rn[2];                 // their inverse norms
+    float red[2][8][TK_COLS];    // per-warp column partial sums (S^T k, S^T q)
+    uint64_t pfull[TK_NPARAM], pempty[TK_NPARAM], gfull[2], gempty[2];
+    int abort;
+};
+
+__device__ bool tk_wait(uint64_t *bar, uint32_t parity, TkSmem &sm, uint32_t *status,
+                        uint32_t code) {
+    const uint32_t addr = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
+            "selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+        if (ok) return true;
+        if ((it & 255) == 0) {
+            if (*(volatile int *)&sm.abort) return false;
+            const uint64_t now = gtimer();
+            if (it == 0) t0 = now;
+            else if (now - t0 > 2000000000ull) {
+                *(volatile int *)&sm.abort = 1;
+                dev_flag(status, code);
+                return false;
+            }
+        }
+    }
+}
+
+// The ring after the tokens: slot sl holds the input of the last token whose position is
+// sl mod 4 (as T single-token calls leave it), or what it held before when no token wrote
+// it.
+__global__ void dn_tokens_ring_k(float *__restrict__ ring, const void *__restrict__ qkv,
+                                 const int *__restrict__ pos, int T, int C, int act_bf16) {
+    __shared__ int last[4];
+    if (threadIdx.x < 4) last[threadIdx.x] = -1;
+    __syncthreads();
+    for (int t = threadIdx.x; t < T; t += blockDim.x) atomicMax(&last[pos[t] & 3], t);
+    __syncthreads();
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < C; c += gridDim.x * blockDim.x)
+#pragma unroll
+        for (int sl = 0; sl < 4; sl++) {
+            const int t = last[sl];
+            if (t >= 0)
+                ring[(size_t)sl * C + c] = act_bf16 ? act_ld<true>(qkv, (size_t)t * C + c)
+                                                    : act_ld<false>(qkv, (size_t)t * C + c);
+        }
+}
+
+// bar.sync over a named barrier that also ANDs a predicate over the participating threads
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, %2, %3, p; "
+        "selp.u32 %0, 1, 0, q; }"
+        : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(nthreads) : "memory");
+    return r != 0;
+}
+
+template <bool ACT_BF16, bool OUT_BF16, bool GATES_F64>
+__global__ void __launch_bounds__(544, 1)
+dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restrict__ qkv,
+            const void *__restrict__ ga, const void *__restrict__ gb,
+            const float *__restrict__ A_log, const float *__restrict__ dt_bias,
+            const float *__restrict__ conv_w, const int *__restrict__ pos, void *__restrict__ o,
+            float *__restrict__ S_ckpt, float *__restrict__ conv_ckpt, int T, int nqk, int nv,
+            uint32_t *status) {
+    __shared__ __align__(16) TkSmem sm;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int cs = blockIdx.x, vh = blockIdx.y;
+    const int col0 = cs * TK_COLS;
+    const int qk = vh * nqk / nv;
+    const int C = (2 * nqk + nv) * HD;
+    // the q/k channels' ring entries and snapshots are written by one CTA per QK head
+    const bool qk_owner = cs == 0 && ((vh == 0) || ((vh - 1) * nqk / nv != qk));
+    auto chan = [&](int ch) {
+        return ch < HD ? qk * HD + ch
+                       : ch < 2 * HD ? (nqk + qk) * HD + ch - HD : 2 * nqk * HD + vh * HD + col0 + ch - 2 * HD;
+    };
+    if (tid == 0) {
+        for (int i = 0; i < TK_NPARAM; i++) {
+            mbar_init(&sm.pfull[i], 8);  // one arrival per prep warp
+            mbar_init(&sm.pempty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&sm.gfull[i], 1);
+            mbar_init(&sm.gempty[i], 1);
+        }
+        sm.abort = 0;
+        fence_barrier_init();
+    }
+    for (int ch = tid; ch < TK_NCH; ch += blockDim.x)
+#pragma unroll
+        for (int sl = 0; sl < 4; sl++) sm.hist[ch][sl] = ring[(size_t)sl * C + chan(ch)];
+    __syncthreads();
+
+    if (warp == 16) {
+        // ---- gates: 32 tokens at a time, one per lane (double precision, as the per-token
+        // kernel forms them), into a two-batch ring
+        for (int k = 0; k * 32 < T; k++) {
+            const int gb_ = k & 1;
+            if (k >= 2 && !tk_wait(&sm.gempty[gb_], ((k >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
+                break;
+            const int t = k * 32 + lane;
+            if (t < T) {
+                const size_t gi = (size_t)t * nv + vh;
+                double beta, g;
+                if constexpr (GATES_F64) {
+                    beta = ((const double *)ga)[gi];
+                    g = ((const double *)gb)[gi];
+                } else {
+                    dn_gates_device((double)act_ld<ACT_BF16>(ga, gi), (double)A_log[vh],
+                                    (double)act_ld<ACT_BF16>(gb, gi), (double)dt_bias[vh], &beta, &g);
+                }
+                sm.gbeta[gb_][lane] = (float)beta;
+                sm.gdecay[gb_][lane] = (float)exp(g);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.gfull[gb_]);
+        }
+    } else if (warp >= 8) {
+        // ---- prep: thread j owns q channel j (j < 128) or k channel j - 128, and threads
+        // j < 16 also v channel col0 + j
+        const int j = tid - 256;
+        const int c = chan(j), cv = chan(2 * HD + (j & (TK_COLS - 1)));
+        const bool has_v = j < TK_COLS;
+        const float4 w = *reinterpret_cast<const float4 *>(conv_w + (size_t)c * 4);
+        const float4 wv = *reinterpret_cast<const float4 *>(conv_w + (size_t)cv * 4);
+        const float qs = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+        const bool own = qk_owner;  // q and k channels alike
+        auto conv = [&](float *h, float4 wt, float x, int p) {
+            float acc = __fmul_rn(wt.x, h[(p - 3) & 3]);
+            acc = __fadd_rn(acc, __fmul_rn(wt.y, h[(p - 2) & 3]));
+            acc = __fadd_rn(acc, __fmul_rn(wt.z, h[(p - 1) & 3]));
+            acc = __fadd_rn(acc, __fmul_rn(wt.w, x));
+            h[p & 3] = x;
+            return __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
+        };
+        for (int t = 0; t < T; t++) {
+            const int slot = t % TK_NPARAM;
+            const int p = pos[t];
+            const size_t xb = (size_t)t * C;
+            const float x = act_ld<ACT_BF16>(qkv, xb + c);
+            const float xv = has_v ? act_ld<ACT_BF16>(qkv, xb + cv) : 0.f;
+            if (j == 0 && (t & 31) == 0 &&
+                !tk_wait(&sm.gfull[(t >> 5) & 1], (t >> 6) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
+                *(volatile int *)&sm.abort = 1;
+            if (t >= TK_NPARAM &&
+                !tk_wait(&sm.pempty[slot], ((t / TK_NPARAM) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
+                *(volatile int *)&sm.abort = 1;
+            const bool ok = !*(volatile int *)&sm.abort;
+            const float y = conv(sm.hist[j], w, x, p);
+            const float yv = has_v ? conv(sm.hist[2 * HD + j], wv, xv, p) : 0.f;
+            if (conv_ckpt) {  // the history after token t, oldest first
+                if (own) {
+#pragma unroll
+                    for (int k2 = 0; k2 < 3; k2++)
+                        conv_ckpt[((size_t)t * C + c) * 3 + k2] = sm.hist[j][(p - 2 + k2) & 3];
+                }
+                if (has_v) {
+#pragma unroll
+                    for (int k2 = 0; k2 < 3; k2++)
+                        conv_ckpt[((size_t)t * C + cv) * 3 + k2] = sm.hist[2 * HD + j][(p - 2 + k2) & 3];
+                }
+            }
+            sm.y[j >> 7][j & (HD - 1)] = y;
+            named_bar_sync(2, 256);
+            if (warp == 8 || warp == 12) {  // the norms as the per-token kernel sums them
+                const int part = warp == 12;
+                double ss = 0.0;
+#pragma unroll
+                for (int k2 = 0; k2 < 4; k2++) {
+                    const double v = (double)sm.y[part][lane + 32 * k2];
+                    ss += v * v;
+                }
+                ss = warp_sum_d(ss);
+                if (lane == 0) sm.rn[part] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, 1e-6f)));
+            }
+            named_bar_sync(2, 256);
+            if (ok) {
+                TkParams &P = sm.prm[slot];
+                if (j < HD) P.qn[j] = __fmul_rn(__fmul_rn(y, sm.rn[0]), qs);
+                else P.kn[j - HD] = __fmul_rn(y, sm.rn[1]);
+                if (has_v) P.v[j] = yv;
+                if (j == 0) {
+                    P.beta = sm.gbeta[(t >> 5) & 1][t & 31];
+                    P.decay = sm.gdecay[(t >> 5) & 1][t & 31];
+                    // the batch's last token: its gate slots may be refilled
+                    if ((t & 31) == 31 || t == T - 1) mbar_arrive(&sm.gempty[(t >> 5) & 1]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.pfull[slot]);
+        }
+    } else {
+        // ---- state: thread (row block rb, column col) holds rows 8 rb .. 8 rb + 7
+        const int rb = tid >> 4, col = tid & (TK_COLS - 1);
+        float *Sh = S + (size_t)vh * HD * HD;
+        float s[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) s[i] = Sh[(size_t)(8 * rb + i) * HD + col0 + col];
+        bool ok = true;
+        for (int t = 0; t < T && ok; t++) {
+            const int slot = t % TK_NPARAM;
+            ok = tk_wait(&sm.pfull[slot], (t / TK_NPARAM) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
+            ok = named_bar_and(1, 256, ok);  // one outcome for all state threads
+            if (!ok) break;
+            const TkParams &P = sm.prm[slot];
+            const float decay = P.decay;
+            float kv = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                s[i] = __fmul_rn(s[i], decay);
+                kv = fmaf(s[i], P.kn[8 * rb + i], kv);
+            }
+            kv += __shfl_xor_sync(0xffffffffu, kv, 16);
+            if (lane < TK_COLS) sm.red[0][warp][col] = kv;
+            named_bar_sync(1, 256);
+            float kvt = 0.f;
+#pragma unroll
+            for (int w2 = 0; w2 < 8; w2++) kvt += sm.red[0][w2][col];
+            const float delta = (P.v[col] - kvt) * P.beta;
+            float op = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                s[i] = fmaf(P.kn[8 * rb + i], delta, s[i]);
+                op = fmaf(s[i], P.qn[8 * rb + i], op);
+            }
+            op += __shfl_xor_sync(0xffffffffu, op, 16);
+            if (lane < TK_COLS) sm.red[1][warp][col] = op;
+            if (S_ckpt) {
+                float *Sc = S_ckpt + ((size_t)t * nv + vh) * HD * HD;
+#pragma unroll
+                for (int i = 0; i < 8; i++) Sc[(size_t)(8 * rb + i) * HD + col0 + col] = s[i];
+            }
+            named_bar_sync(1, 256);
+            if (tid < TK_COLS) {
+                float ot = 0.f;
+#pragma unroll
+                for (int w2 = 0; w2 < 8; w2++) ot += sm.red[1][w2][tid];
+                act_st<OUT_BF16>(o, ((size_t)t * nv + vh) * HD + col0 + tid, ot);
+            }
+            if (tid == 0) mbar_arrive(&sm.pempty[slot]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) Sh[(size_t)(8 * rb + i) * HD + col0 + col] = s[i];
+    }
+    __syncwarp();
+    __syncthreads();
+}
+
 }  // namespace
 }  // namespace vx27
 
@@ -502,23 +782,6 @@ extern "C" int vx27_deltanet_decode_batch_gated(float *S, float *conv_ring, cons
                              stream, err, errlen);
 }
 
-namespace vx27 {
-namespace {
-// Conv history after the token at device position *pos, in the reference layout
-// state[C][3] (oldest first): the inputs of tokens p-2, p-1, p.
-__global__ void conv_ckpt_k(const float *__restrict__ ring, float *__restrict__ state,
-                            const int *__restrict__ pos, int C) {
-    const int p = *pos;
-    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < C; c += gridDim.x * blockDim.x) {
-        float *s = state + (size_t)c * 3;
-        s[0] = ring[(size_t)((p - 2) & 3) * C + c];
-        s[1] = ring[(size_t)((p - 1) & 3) * C + c];
-        s[2] = ring[(size_t)(p & 3) * C + c];
-    }
-}
-}  // namespace
-}  // namespace vx27
-
 extern "C" int vx27_deltanet_decode_tokens(float *S, float *conv_ring, const void *qkv,
                                            const void *a, const void *b, const float *A_log,
                                            const float *dt_bias, const float *conv_w,
@@ -531,27 +794,41 @@ extern "C" int vx27_deltanet_decode_tokens(float *S, float *conv_ring, const voi
     if (hd != HD) return fail(err, errlen, "%s: hd=%d unsupported (128 only)", fn, hd);
     if (nqk <= 0 || nv < nqk) return fail(err, errlen, "%s: bad shape nqk=%d nv=%d", fn, nqk, nv);
     if (!qkv || !a || !b || !pos || !o) return fail(err, errlen, "%s: null pointer argument", fn);
-    const size_t C = (size_t)(2 * nqk + nv) * HD;
-    const size_t ea = (flags & VX27_F_ACT_BF16) ? 2 : 4, eo = (flags & VX27_F_OUT_BF16) ? 2 : 4;
+    if (!S || !conv_ring || !conv_w) return fail(err, errlen, "%s: null pointer argument", fn);
+    const bool g64 = flags & VX27_F_GATES_F64;
+    if (!g64 && (!A_log || !dt_bias)) return fail(err, errlen, "%s: A_log/dt_bias required", fn);
+    if (((uintptr_t)S & 15) || ((uintptr_t)conv_w & 15))
+        return fail(err, errlen, "%s: S and conv_w must be 16-byte aligned", fn);
+    if (flags & VX27_F_QK_PRENORM)
+        return fail(err, errlen, "%s: VX27_F_QK_PRENORM needs the gated entry point (norm_w)", fn);
+    if (nv > 65535) return fail(err, errlen, "%s: nv=%d", fn, nv);
     cudaStream_t st = (cudaStream_t)stream;
-    for (int t = 0; t < T; t++) {
-        const int rc = decode_batch_impl(
-            fn, S, conv_ring, (const uint8_t *)qkv + t * C * ea, (const uint8_t *)a + t * nv * ea,
-            (const uint8_t *)b + t * nv * ea, A_log, dt_bias, conv_w, pos + t, nullptr, nullptr,
-            (uint8_t *)o + (size_t)t * nv * HD * eo, 1, nqk, nv, hd,
-            flags & ~VX27_F_PREFETCH_STATE,  // token t reads the state token t-1 wrote
-            stream, err, errlen);
-        if (rc) return rc;
-        if (S_ckpt)
-            VX_CK(cudaMemcpyAsync(S_ckpt + (size_t)t * nv * HD * HD, S,
-                                  (size_t)nv * HD * HD * sizeof(float), cudaMemcpyDeviceToDevice,
-                                  st));
-        if (conv_ckpt) {
-            conv_ckpt_k<<<(unsigned)((C + 255) / 256), 256, 0, st>>>(conv_ring,
-                                                                    conv_ckpt + (size_t)t * C * 3,
-                                                                    pos + t, (int)C);
-            VX_CK(cudaGetLastError());
-        }
+    uint32_t *status = dev_status();
+    const dim3 grid(TK_SPLIT, nv);
+    constexpr int TK_THREADS = 544;  // 8 state warps, 8 prep warps, the gate warp
+    const int key = (flags & VX27_F_ACT_BF16 ? 1 : 0) | (flags & VX27_F_OUT_BF16 ? 2 : 0) |
+                    (g64 ? 4 : 0);
+#define VX_T(K, A_, O_, G_)                                                                    \
+    case K:                                                                                    \
+        dn_tokens_k<A_, O_, G_><<<grid, TK_THREADS, 0, st>>>(S, conv_ring, qkv, a, b, A_log, dt_bias, \
+                                                      conv_w, pos, o, S_ckpt, conv_ckpt, T,    \
+                                                      nqk, nv, status);                        \
+        break;
+    switch (key) {
+        VX_T(0, false, false, false)
+        VX_T(1, true, false, false)
+        VX_T(2, false, true, false)
+        VX_T(3, true, true, false)
+        VX_T(4, false, false, true)
+        VX_T(5, true, false, true)
+        VX_T(6, false, true, true)
+        VX_T(7, true, true, true)
     }
+#undef VX_T
+    VX_CK(cudaGetLastError());
+    const int C = (2 * nqk + nv) * HD;
+    dn_tokens_ring_k<<<(C + 255) / 256, 256, 0, st>>>(conv_ring, qkv, pos, T, C,
+                                                      (flags & VX27_F_ACT_BF16) ? 1 : 0);
+    VX_CK(cudaGetLastError());
     return 0;
 }

@@ -221,17 +221,20 @@ def deltanet_decode_batch(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, 
 
 
 def deltanet_decode_tokens(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, nqk: int,
-                           nv: int, S_ckpt=None, conv_ckpt=None, stream=None) -> None:
-    """T tokens of one sequence (vx27_deltanet_decode_tokens); S [nv][128][128],
-    conv_ring [4][C], qkv [T][C], a, b [T][nv], pos [T], o [T][nv][128]; optional
+                           nv: int, S_ckpt=None, conv_ckpt=None, stream=None,
+                           gates_f64: bool = False) -> None:
+    """T tokens of one sequence (vx27_deltanet_decode_tokens, one kernel with the state
+    resident across the tokens); S [nv][128][128], conv_ring [4][C], qkv [T][C],
+    a, b [T][nv] (double beta / g_log with gates_f64), pos [T], o [T][nv][128]; optional
     S_ckpt [T][nv][128][128] and conv_ckpt [T][C][3] snapshots."""
     T = qkv.shape[0]
     _check_deltanet(S, conv_ring, qkv, a, b, A_log, dt_bias, conv_w, pos, o, 1, nqk, nv, 128,
-                    False, T=T)
+                    gates_f64, T=T)
     f32 = _dt()[0]
     _need(S_ckpt, "S_ckpt", T * nv * 128 * 128, (f32,), optional=True)
     _need(conv_ckpt, "conv_ckpt", T * (2 * nqk + nv) * 128 * 3, (f32,), optional=True)
-    flags = (F_ACT_BF16 if _is_bf16(qkv) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0)
+    flags = (F_ACT_BF16 if _is_bf16(qkv) else 0) | (F_OUT_BF16 if _is_bf16(o) else 0) | \
+        (F_GATES_F64 if gates_f64 else 0)
     e = errbuf()
     rc = load().vx27_deltanet_decode_tokens(_t(S), _t(conv_ring), _t(qkv), _t(a), _t(b),
                                             _t(A_log), _t(dt_bias), _t(conv_w), _t(pos), _t(o),
