@@ -417,9 +417,9 @@ struct TkParams {
 struct TkSmem {
     TkParams prm[TK_NPARAM];
     float gbeta[2][32], gdecay[2][32];  // gates of 32-token batches (gate warp -> prep)
+    float gv[2][32][TK_COLS];           // and the conv outputs of this CTA's v channels
     float hist[TK_NCH][4];       // conv history by position & 3
-    float y[2][HD];              // conv outputs of q and k, for the norms
-    float rn[2];                 // their inverse norms
+    double nps[2][8];            // per-prep-warp sums of squares (q: 0-3, k: 4-7), by parity
     float red[2][8][TK_COLS];    // per-warp column partial sums (S^T k, S^T q)
     uint64_t pfull[TK_NPARAM], pempty[TK_NPARAM], gfull[2], gempty[2];
     int abort;
@@ -517,13 +517,19 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
     __syncthreads();
 
     if (warp == 16) {
-        // ---- gates: 32 tokens at a time, one per lane (double precision, as the per-token
-        // kernel forms them), into a two-batch ring
+        // ---- gates and v channels, 32 tokens at a time into a two-batch ring: lane l
+        // forms token 32k + l's gates (double precision, as the per-token kernel forms
+        // them), then lanes 0-15 run their v channel's conv over the batch's tokens in order
+        const int jv = lane & (TK_COLS - 1);
+        const int cv = chan(2 * HD + jv);
+        const float4 wv = *reinterpret_cast<const float4 *>(conv_w + (size_t)cv * 4);
         for (int k = 0; k * 32 < T; k++) {
             const int gb_ = k & 1;
             if (k >= 2 && !tk_wait(&sm.gempty[gb_], ((k >> 1) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
                 break;
             const int t = k * 32 + lane;
+            const int nt = min(32, T - k * 32);
+            int pl = 0;
             if (t < T) {
                 const size_t gi = (size_t)t * nv + vh;
                 double beta, g;
@@ -536,18 +542,40 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
                 }
                 sm.gbeta[gb_][lane] = (float)beta;
                 sm.gdecay[gb_][lane] = (float)exp(g);
+                pl = pos[t];
+            }
+            // the batch's v inputs, all requested before the first is used
+            float xv[32];
+#pragma unroll
+            for (int tt = 0; tt < 32; tt++)
+                xv[tt] = (lane < TK_COLS && tt < nt)
+                             ? act_ld<ACT_BF16>(qkv, (size_t)(k * 32 + tt) * C + cv) : 0.f;
+#pragma unroll
+            for (int tt = 0; tt < 32; tt++) {
+                const int p = __shfl_sync(0xffffffffu, pl, tt);
+                if (lane < TK_COLS && tt < nt) {
+                    float *h = sm.hist[2 * HD + jv];
+                    float acc = __fmul_rn(wv.x, h[(p - 3) & 3]);
+                    acc = __fadd_rn(acc, __fmul_rn(wv.y, h[(p - 2) & 3]));
+                    acc = __fadd_rn(acc, __fmul_rn(wv.z, h[(p - 1) & 3]));
+                    acc = __fadd_rn(acc, __fmul_rn(wv.w, xv[tt]));
+                    h[p & 3] = xv[tt];
+                    sm.gv[gb_][tt][jv] = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
+                    if (conv_ckpt) {  // the history after the token, oldest first
+#pragma unroll
+                        for (int k2 = 0; k2 < 3; k2++)
+                            conv_ckpt[((size_t)(k * 32 + tt) * C + cv) * 3 + k2] = h[(p - 2 + k2) & 3];
+                    }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sm.gfull[gb_]);
         }
     } else if (warp >= 8) {
-        // ---- prep: thread j owns q channel j (j < 128) or k channel j - 128, and threads
-        // j < 16 also v channel col0 + j
+        // ---- prep: thread j owns q channel j (j < 128) or k channel j - 128
         const int j = tid - 256;
-        const int c = chan(j), cv = chan(2 * HD + (j & (TK_COLS - 1)));
-        const bool has_v = j < TK_COLS;
+        const int c = chan(j);
         const float4 w = *reinterpret_cast<const float4 *>(conv_w + (size_t)c * 4);
-        const float4 wv = *reinterpret_cast<const float4 *>(conv_w + (size_t)cv * 4);
         const float qs = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
         const bool own = qk_owner;  // q and k channels alike
         auto conv = [&](float *h, float4 wt, float x, int p) {
@@ -558,12 +586,27 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             h[p & 3] = x;
             return __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
         };
+        // token t + 2's input is requested while token t is prepared (registers rotate)
+        float x1 = 0.f, x2 = 0.f;
+        int p1 = 0, p2 = 0;
+        if (T > 0) {
+            x1 = act_ld<ACT_BF16>(qkv, c);
+            p1 = pos[0];
+        }
+        if (T > 1) {
+            x2 = act_ld<ACT_BF16>(qkv, (size_t)C + c);
+            p2 = pos[1];
+        }
         for (int t = 0; t < T; t++) {
             const int slot = t % TK_NPARAM;
-            const int p = pos[t];
-            const size_t xb = (size_t)t * C;
-            const float x = act_ld<ACT_BF16>(qkv, xb + c);
-            const float xv = has_v ? act_ld<ACT_BF16>(qkv, xb + cv) : 0.f;
+            const float x = x1;
+            const int p = p1;
+            x1 = x2;
+            p1 = p2;
+            if (t + 2 < T) {
+                x2 = act_ld<ACT_BF16>(qkv, (size_t)(t + 2) * C + c);
+                p2 = pos[t + 2];
+            }
             if (j == 0 && (t & 31) == 0 &&
                 !tk_wait(&sm.gfull[(t >> 5) & 1], (t >> 6) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
                 *(volatile int *)&sm.abort = 1;
@@ -572,38 +615,24 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
                 *(volatile int *)&sm.abort = 1;
             const bool ok = !*(volatile int *)&sm.abort;
             const float y = conv(sm.hist[j], w, x, p);
-            const float yv = has_v ? conv(sm.hist[2 * HD + j], wv, xv, p) : 0.f;
-            if (conv_ckpt) {  // the history after token t, oldest first
-                if (own) {
+            if (conv_ckpt && own) {  // the history after token t, oldest first
 #pragma unroll
-                    for (int k2 = 0; k2 < 3; k2++)
-                        conv_ckpt[((size_t)t * C + c) * 3 + k2] = sm.hist[j][(p - 2 + k2) & 3];
-                }
-                if (has_v) {
-#pragma unroll
-                    for (int k2 = 0; k2 < 3; k2++)
-                        conv_ckpt[((size_t)t * C + cv) * 3 + k2] = sm.hist[2 * HD + j][(p - 2 + k2) & 3];
-                }
+                for (int k2 = 0; k2 < 3; k2++)
+                    conv_ckpt[((size_t)t * C + c) * 3 + k2] = sm.hist[j][(p - 2 + k2) & 3];
             }
-            sm.y[j >> 7][j & (HD - 1)] = y;
+            // l2 norms from double sums of squares: a warp sum per prep warp, then every
+            // thread adds its part's four (one barrier per token)
+            const double sw = warp_sum_d((double)y * (double)y);
+            if (lane == 0) sm.nps[t & 1][warp - 8] = sw;
             named_bar_sync(2, 256);
-            if (warp == 8 || warp == 12) {  // the norms as the per-token kernel sums them
-                const int part = warp == 12;
-                double ss = 0.0;
-#pragma unroll
-                for (int k2 = 0; k2 < 4; k2++) {
-                    const double v = (double)sm.y[part][lane + 32 * k2];
-                    ss += v * v;
-                }
-                ss = warp_sum_d(ss);
-                if (lane == 0) sm.rn[part] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, 1e-6f)));
-            }
-            named_bar_sync(2, 256);
+            const double *np_ = sm.nps[t & 1] + (j < HD ? 0 : 4);
+            const double ss = (np_[0] + np_[1]) + (np_[2] + np_[3]);
+            const float rn = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, 1e-6f)));
             if (ok) {
                 TkParams &P = sm.prm[slot];
-                if (j < HD) P.qn[j] = __fmul_rn(__fmul_rn(y, sm.rn[0]), qs);
-                else P.kn[j - HD] = __fmul_rn(y, sm.rn[1]);
-                if (has_v) P.v[j] = yv;
+                if (j < HD) P.qn[j] = __fmul_rn(__fmul_rn(y, rn), qs);
+                else P.kn[j - HD] = __fmul_rn(y, rn);
+                if (j < TK_COLS) P.v[j] = sm.gv[(t >> 5) & 1][t & 31][j];
                 if (j == 0) {
                     P.beta = sm.gbeta[(t >> 5) & 1][t & 31];
                     P.decay = sm.gdecay[(t >> 5) & 1][t & 31];
@@ -625,9 +654,7 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
         for (int t = 0; t < T && ok; t++) {
             const int slot = t % TK_NPARAM;
             ok = tk_wait(&sm.pfull[slot], (t / TK_NPARAM) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
-            ok = named_bar_and(1, 256, ok);  // one outcome for all state threads
-            if (!ok) break;
-            const TkParams &P = sm.prm[slot];
+            const TkParams &P = sm.prm[slot];  // (after a failed wait: read, then discarded)
             const float decay = P.decay;
             float kv = 0.f;
 #pragma unroll
@@ -637,7 +664,8 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             }
             kv += __shfl_xor_sync(0xffffffffu, kv, 16);
             if (lane < TK_COLS) sm.red[0][warp][col] = kv;
-            named_bar_sync(1, 256);
+            ok = named_bar_and(1, 256, ok);  // the partials, and one outcome for all threads
+            if (!ok) break;
             float kvt = 0.f;
 #pragma unroll
             for (int w2 = 0; w2 < 8; w2++) kvt += sm.red[0][w2][col];
