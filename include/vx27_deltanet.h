@@ -118,7 +118,10 @@ int vx27_deltanet_gate_params_dev(const void *a, const void *b, const float *A_l
  *   S_ckpt    [T][nv][hd][hd] fp32 or NULL: the state after token t
  *   conv_ckpt [T][C][3] fp32 or NULL: the conv history after token t in the reference
  *             layout (oldest first; vx27_deltanet_conv_import restores it)
- * Flags as vx27_deltanet_decode_batch. Runs on `stream` without synchronising.
+ * Flags as vx27_deltanet_decode_batch (VX27_F_QK_PRENORM excluded). One kernel runs all T
+ * tokens with the state held on chip (8 CTAs per head, 16 state columns each), then a
+ * small kernel brings the conv ring up to date; each position sequence gives the result
+ * of T single-token calls. Runs on `stream` without synchronising.
  */
 int vx27_deltanet_decode_tokens(float *S, float *conv_ring, const void *qkv, const void *a,
                                 const void *b, const float *A_log, const float *dt_bias,
