@@ -233,10 +233,13 @@ def test_decode_tokens_with_checkpoints(cuda, orc):
     assert np.abs(host(S2).reshape(-1) - S_ref[k]).max() < TOL
 
 
-def _tokens_vs_oracle(orc, seed, nqk, nv, T, p0, bf16, s_std=0.0, gates_f64=False):
+def _tokens_vs_oracle(orc, seed, nqk, nv, T, p0, bf16, s_std=0.0, gates_f64=False,
+                     positions=None, ckpt=False):
     """One vx27_deltanet_decode_tokens call over T tokens (state resident in the kernel)
-    against the oracle stepping token by token."""
+    against the oracle stepping token by token (positions p0 + t, or the given ones); with
+    ckpt, the per-token state and conv snapshots are compared too."""
     hd = 128
+    positions = (np.arange(p0, p0 + T) if positions is None else np.asarray(positions)).astype(np.int32)
     lay = make_layer(orc, seed, 1, nqk, nv, s_std=s_std)
     Cch = lay["C"]
     lay["ring"] = orc.normal(4 * Cch, seed, 9)  # some conv history at position p0
@@ -246,15 +249,20 @@ def _tokens_vs_oracle(orc, seed, nqk, nv, T, p0, bf16, s_std=0.0, gates_f64=Fals
     S, ring = lay["S"].copy(), lay["ring"].copy()
     L = orc.lib()
     o_ref = np.zeros((T, nv * hd), np.float32)
+    S_ref, c_ref = [], []
     for t in range(T):
         o = np.zeros(nv * hd, np.float32)
         L.orc_deltanet_decode_batch_mt(orc.P(S), orc.P(ring), orc.P(np.ascontiguousarray(qkv[t])),
                                        orc.P(np.ascontiguousarray(a[t])),
                                        orc.P(np.ascontiguousarray(b[t])), orc.P(lay["A_log"]),
                                        orc.P(lay["dt_bias"]), orc.P(lay["conv_w"]),
-                                       orc.P(np.array([p0 + t], np.int32)), orc.P(o), 1, nqk, nv,
+                                       orc.P(positions[t:t + 1].copy()), orc.P(o), 1, nqk, nv,
                                        hd, orc.F_ACT_BF16 if bf16 else 0, 8)
         o_ref[t] = o
+        if ckpt:
+            S_ref.append(S.copy())
+            r4, pp = ring.reshape(4, Cch), int(positions[t])
+            c_ref.append(np.stack([r4[(pp - 2) & 3], r4[(pp - 1) & 3], r4[pp & 3]], axis=1))
     dS = dev(lay["S"]).view(nv, hd, hd)
     dring = dev(lay["ring"]).view(4, Cch)
     if gates_f64:
@@ -271,12 +279,18 @@ def _tokens_vs_oracle(orc, seed, nqk, nv, T, p0, bf16, s_std=0.0, gates_f64=Fals
     else:
         da, db = dev(a, bf16), dev(b, bf16)
     o = torch.empty(T, nv, hd, device="cuda")
-    pos = torch.arange(p0, p0 + T, dtype=torch.int32, device="cuda")
+    pos = dev(positions)
+    S_ck = torch.empty(T, nv, hd, hd, device="cuda") if ckpt else None
+    c_ck = torch.empty(T, Cch, 3, device="cuda") if ckpt else None
     ops.deltanet_decode_tokens(dS, dring, dev(qkv, bf16), da, db, dev(lay["A_log"]),
                                dev(lay["dt_bias"]), dev(lay["conv_w"]).view(Cch, 4), pos, o, nqk,
-                               nv, gates_f64=gates_f64)
+                               nv, gates_f64=gates_f64, S_ckpt=S_ck, conv_ckpt=c_ck)
     torch.cuda.synchronize()
     assert ops.device_status() == 0
+    if ckpt:
+        for t in range(T):
+            assert np.abs(host(S_ck[t]).reshape(-1) - S_ref[t]).max() < TOL
+            assert np.array_equal(host(c_ck[t]), c_ref[t])
     return (np.abs(host(o).reshape(T, -1) - o_ref).max(), np.abs(host(dS).reshape(-1) - S).max(),
             np.array_equal(host(dring).reshape(-1), ring))
 
@@ -296,4 +310,21 @@ def test_tokens_grouped_heads_bf16(cuda, orc, gates_f64):
     position (the conv history crosses the ring's wrap)."""
     err_o, err_s, ring_eq = _tokens_vs_oracle(orc, 7, 16, 48, 37, 1029, bf16=True, s_std=0.05,
                                               gates_f64=gates_f64)
+    assert err_o < TOL and err_s < TOL and ring_eq
+
+
+def test_tokens_any_positions(cuda, orc):
+    """Positions that jump and repeat (the conv history follows the ring by position, as
+    T single-token calls would) and a run long enough to cross the kernel's 32-token gate
+    batches."""
+    positions = [7, 8, 9, 13, 2, 3, 3, 40] + list(range(100, 130))
+    err_o, err_s, ring_eq = _tokens_vs_oracle(orc, 8, 2, 6, len(positions), 0, bf16=True,
+                                              s_std=0.05, positions=positions)
+    assert err_o < TOL and err_s < TOL and ring_eq
+
+
+def test_tokens_checkpoints_across_gate_batches(cuda, orc):
+    """State and conv snapshots after each of 70 tokens (three 32-token gate batches)."""
+    err_o, err_s, ring_eq = _tokens_vs_oracle(orc, 9, 2, 6, 70, 31, bf16=True, s_std=0.05,
+                                              ckpt=True)
     assert err_o < TOL and err_s < TOL and ring_eq
