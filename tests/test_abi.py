@@ -109,6 +109,28 @@ def test_batched_entry_points_reject_bad_shapes_without_gpu(vxlib):
     rc = vxlib.vx27_gqa_decode_fused(16, 16, 16, 16, 16, 16, 64, None, 16, 16, 64, 16, 16, 16, rec,
                                      1, 24, 4, 256, 21, 1e-6, 1, 0x80, None, err, 256)
     assert rc == -1 and b"rope_dim=21" in err.value
+    # the multi-token DeltaNet decode: the pre-normalisation needs the gated entry point
+    rc = vxlib.vx27_deltanet_decode_tokens(16, 16, 16, 16, 16, 16, 16, 16, 16, 16, None, None,
+                                           4, 16, 16, 128, 0x20, None, err, 256)
+    assert rc == -1 and b"VX27_F_QK_PRENORM" in err.value
+    rc = vxlib.vx27_deltanet_decode_tokens(None, 16, 16, 16, 16, 16, 16, 16, 16, 16, None, None,
+                                           4, 16, 16, 128, 0, None, err, 256)
+    assert rc == -1 and b"null pointer" in err.value
+
+
+def test_flag_values_match_the_header():
+    """The Python wrappers' flag constants are the values include/vx27cuda.h defines."""
+    import os
+    import re
+    from vx27_b200 import ops
+    hdr = open(os.path.join(os.path.dirname(__file__), "..", "include", "vx27cuda.h")).read()
+    defs = {m.group(1): int(m.group(2), 16)
+            for m in re.finditer(r"#define VX27_(F_\w+)\s+(0x[0-9a-fA-F]+)", hdr)}
+    assert {"F_ACT_BF16", "F_OUT_BF16", "F_PREFETCH_KV", "F_DECODE_CC", "F_DECODE_TC",
+            "F_PREFILL_CTA1"} <= defs.keys()
+    for name, value in defs.items():
+        if hasattr(ops, name):
+            assert getattr(ops, name) == value, name
 
 
 def test_ddmath_host_matches_c_library_nearly_always():
