@@ -395,16 +395,16 @@ __global__ void gate_params_k(const void *__restrict__ a, const void *__restrict
 // CTA (cs, vh) keeps columns [16 cs, 16 cs + 16) of V head vh's 128 x 128 state in
 // registers for all T tokens (the delta rule's columns are independent): warps 0-7 hold it,
 // one 8-row block of one column per thread, and run each token's decay, S^T k, delta,
-// update and S^T q with two column reductions. Warps 8-15 prepare the tokens ahead into a
-// ring of parameter slots: the width-4 conv + SiLU of the head's q and k channels (one per
-// thread, computed by each of the head's 8 CTAs) and of this CTA's 16 v channels from a
-// private copy of their conv history (read from the ring at the start, so any position
-// sequence reproduces T single-token calls), the l2 norms with the per-token kernel's double
-// sums, and the gates. Nothing crosses CTAs: the state goes back to global memory at the
-// end, and the ring is left untouched here (the CTAs of a QK head may run in different
-// waves, so each must find the initial history there) and brought up to date by
-// dn_tokens_ring_k afterwards. Per token this replaces one launch and a 1 MB state round
-// trip.
+// update and S^T q with two column reductions. Warps 8-15 prepare the tokens up to four
+// ahead into a ring of parameter slots: the width-4 conv + SiLU of the head's q and k
+// channels (one per thread, computed by each of the head's 8 CTAs) from a private copy of
+// their conv history (read from the ring at the start, so any position sequence reproduces
+// T single-token calls), then the l2 norms from double sums of squares. Warp 16 forms the
+// gates (double precision) and the conv of this CTA's 16 v channels 32 tokens at a time.
+// Nothing crosses CTAs: the state goes back to global memory at the end, and the ring is
+// left untouched here (the CTAs of a QK head may run in different waves, so each must find
+// the initial history there) and brought up to date by dn_tokens_ring_k afterwards. Per
+// token this replaces one launch and a 1 MB state round trip.
 constexpr int TK_SPLIT = 8;
 constexpr int TK_COLS = HD / TK_SPLIT;
 constexpr int TK_NPARAM = 4;
@@ -577,7 +577,7 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
         const int c = chan(j);
         const float4 w = *reinterpret_cast<const float4 *>(conv_w + (size_t)c * 4);
         const float qs = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-        const bool own = qk_owner;  // q and k channels alike
+        const bool own = qk_owner;  // this CTA writes the q/k channels' snapshots
         auto conv = [&](float *h, float4 wt, float x, int p) {
             float acc = __fmul_rn(wt.x, h[(p - 3) & 3]);
             acc = __fadd_rn(acc, __fmul_rn(wt.y, h[(p - 2) & 3]));
