@@ -418,8 +418,9 @@ struct TkSmem {
     TkParams prm[TK_NPARAM];
     float gbeta[2][32], gdecay[2][32];  // gates of 32-token batches (gate warp -> prep)
     float gv[2][32][TK_COLS];           // and the conv outputs of this CTA's v channels
-    float hist[TK_NCH][4];       // conv history by position & 3
-    double nps[2][8];            // per-prep-warp sums of squares (q: 0-3, k: 4-7), by parity
+    float hist[TK_NCH][4];       // conv history by position & 3 (prep group 0, v channels)
+    float hist1[2 * HD][4];      // the q/k channels' history of prep group 1
+    double nps[2][2][4][2];      // [group][token parity][warp][q, k] sums of squares
     float red[2][8][TK_COLS];    // per-warp column partial sums (S^T k, S^T q)
     uint64_t pfull[TK_NPARAM], pempty[TK_NPARAM], gfull[2], gempty[2];
     int abort;
@@ -501,19 +502,23 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
     };
     if (tid == 0) {
         for (int i = 0; i < TK_NPARAM; i++) {
-            mbar_init(&sm.pfull[i], 8);  // one arrival per prep warp
+            mbar_init(&sm.pfull[i], 4);  // one arrival per warp of the token's prep group
             mbar_init(&sm.pempty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&sm.gfull[i], 1);
-            mbar_init(&sm.gempty[i], 1);
+            mbar_init(&sm.gempty[i], 2);  // both prep groups have read the batch
         }
         sm.abort = 0;
         fence_barrier_init();
     }
     for (int ch = tid; ch < TK_NCH; ch += blockDim.x)
 #pragma unroll
-        for (int sl = 0; sl < 4; sl++) sm.hist[ch][sl] = ring[(size_t)sl * C + chan(ch)];
+        for (int sl = 0; sl < 4; sl++) {
+            const float v = ring[(size_t)sl * C + chan(ch)];
+            sm.hist[ch][sl] = v;
+            if (ch < 2 * HD) sm.hist1[ch][sl] = v;
+        }
     __syncthreads();
 
     if (warp == 16) {
@@ -572,10 +577,17 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             if (lane == 0) mbar_arrive(&sm.gfull[gb_]);
         }
     } else if (warp >= 8) {
-        // ---- prep: thread j owns q channel j (j < 128) or k channel j - 128
-        const int j = tid - 256;
-        const int c = chan(j);
-        const float4 w = *reinterpret_cast<const float4 *>(conv_w + (size_t)c * 4);
+        // ---- prep: two groups of four warps take the even and the odd tokens, so two
+        // tokens are prepared at once. Thread jj of group g owns q channel jj and k channel
+        // jj, with the group's own copy of their conv history, into which it also writes
+        // the other group's tokens' inputs in token order (the ring's semantics).
+        const int g = (warp - 8) >> 2, wg = (warp - 8) & 3;
+        const int jj = tid - 256 - 128 * g;
+        const int cq = chan(jj), ck = chan(HD + jj);
+        float *hq = g ? sm.hist1[jj] : sm.hist[jj];
+        float *hk = g ? sm.hist1[HD + jj] : sm.hist[HD + jj];
+        const float4 wq = *reinterpret_cast<const float4 *>(conv_w + (size_t)cq * 4);
+        const float4 wk = *reinterpret_cast<const float4 *>(conv_w + (size_t)ck * 4);
         const float qs = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
         const bool own = qk_owner;  // this CTA writes the q/k channels' snapshots
         auto conv = [&](float *h, float4 wt, float x, int p) {
@@ -586,58 +598,70 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             h[p & 3] = x;
             return __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
         };
-        // token t + 2's input is requested while token t is prepared (registers rotate)
-        float x1 = 0.f, x2 = 0.f;
-        int p1 = 0, p2 = 0;
-        if (T > 0) {
-            x1 = act_ld<ACT_BF16>(qkv, c);
-            p1 = pos[0];
-        }
-        if (T > 1) {
-            x2 = act_ld<ACT_BF16>(qkv, (size_t)C + c);
-            p2 = pos[1];
-        }
-        for (int t = 0; t < T; t++) {
-            const int slot = t % TK_NPARAM;
-            const float x = x1;
-            const int p = p1;
-            x1 = x2;
-            p1 = p2;
-            if (t + 2 < T) {
-                x2 = act_ld<ACT_BF16>(qkv, (size_t)(t + 2) * C + c);
-                p2 = pos[t + 2];
+        // inputs of tokens t - 1 (the other group's) and t, the next pair requested while
+        // this one is prepared
+        auto ld = [&](int t, float &xq, float &xk, int &p) {
+            if (t >= 0 && t < T) {
+                xq = act_ld<ACT_BF16>(qkv, (size_t)t * C + cq);
+                xk = act_ld<ACT_BF16>(qkv, (size_t)t * C + ck);
+                p = pos[t];
             }
-            if (j == 0 && (t & 31) == 0 &&
+        };
+        float aq = 0.f, ak = 0.f, bq = 0.f, bk = 0.f;  // tokens t - 1 and t
+        int ap = 0, bp = 0;
+        ld(g - 1, aq, ak, ap);
+        ld(g, bq, bk, bp);
+        for (int t = g; t < T; t += 2) {
+            const int slot = t % TK_NPARAM, par = (t >> 1) & 1;
+            const float pxq = aq, pxk = ak, xq = bq, xk = bk;
+            const int pp = ap, p = bp;
+            ld(t + 1, aq, ak, ap);
+            ld(t + 2, bq, bk, bp);
+            if (jj == 0 && (t & 31) == g &&
                 !tk_wait(&sm.gfull[(t >> 5) & 1], (t >> 6) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
                 *(volatile int *)&sm.abort = 1;
             if (t >= TK_NPARAM &&
                 !tk_wait(&sm.pempty[slot], ((t / TK_NPARAM) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
                 *(volatile int *)&sm.abort = 1;
             const bool ok = !*(volatile int *)&sm.abort;
-            const float y = conv(sm.hist[j], w, x, p);
+            if (t >= 1) {  // the other group's token t - 1 enters this group's history first
+                hq[pp & 3] = pxq;
+                hk[pp & 3] = pxk;
+            }
+            const float yq = conv(hq, wq, xq, p);
+            const float yk = conv(hk, wk, xk, p);
             if (conv_ckpt && own) {  // the history after token t, oldest first
 #pragma unroll
-                for (int k2 = 0; k2 < 3; k2++)
-                    conv_ckpt[((size_t)t * C + c) * 3 + k2] = sm.hist[j][(p - 2 + k2) & 3];
+                for (int k2 = 0; k2 < 3; k2++) {
+                    conv_ckpt[((size_t)t * C + cq) * 3 + k2] = hq[(p - 2 + k2) & 3];
+                    conv_ckpt[((size_t)t * C + ck) * 3 + k2] = hk[(p - 2 + k2) & 3];
+                }
             }
-            // l2 norms from double sums of squares: a warp sum per prep warp, then every
-            // thread adds its part's four (one barrier per token)
-            const double sw = warp_sum_d((double)y * (double)y);
-            if (lane == 0) sm.nps[t & 1][warp - 8] = sw;
-            named_bar_sync(2, 256);
-            const double *np_ = sm.nps[t & 1] + (j < HD ? 0 : 4);
-            const double ss = (np_[0] + np_[1]) + (np_[2] + np_[3]);
-            const float rn = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, 1e-6f)));
+            // l2 norms from double sums of squares: warp sums, then every thread adds the
+            // group's four (one barrier per token)
+            const double sq = warp_sum_d((double)yq * (double)yq);
+            const double sk = warp_sum_d((double)yk * (double)yk);
+            if (lane == 0) {
+                sm.nps[g][par][wg][0] = sq;
+                sm.nps[g][par][wg][1] = sk;
+            }
+            named_bar_sync(2 + g, 128);
+            const double(*np_)[2] = sm.nps[g][par];
+            const double ssq = (np_[0][0] + np_[1][0]) + (np_[2][0] + np_[3][0]);
+            const double ssk = (np_[0][1] + np_[1][1]) + (np_[2][1] + np_[3][1]);
+            const float rq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ssq, 1e-6f)));
+            const float rk = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ssk, 1e-6f)));
             if (ok) {
                 TkParams &P = sm.prm[slot];
-                if (j < HD) P.qn[j] = __fmul_rn(__fmul_rn(y, rn), qs);
-                else P.kn[j - HD] = __fmul_rn(y, rn);
-                if (j < TK_COLS) P.v[j] = sm.gv[(t >> 5) & 1][t & 31][j];
-                if (j == 0) {
+                P.qn[jj] = __fmul_rn(__fmul_rn(yq, rq), qs);
+                P.kn[jj] = __fmul_rn(yk, rk);
+                if (jj < TK_COLS) P.v[jj] = sm.gv[(t >> 5) & 1][t & 31][jj];
+                if (jj == 0) {
                     P.beta = sm.gbeta[(t >> 5) & 1][t & 31];
                     P.decay = sm.gdecay[(t >> 5) & 1][t & 31];
-                    // the batch's last token: its gate slots may be refilled
-                    if ((t & 31) == 31 || t == T - 1) mbar_arrive(&sm.gempty[(t >> 5) & 1]);
+                    // this group's last token of a full batch: one of the batch's two
+                    // releases (a partial batch is the last one and is not refilled)
+                    if ((t & 31) == 30 + g) mbar_arrive(&sm.gempty[(t >> 5) & 1]);
                 }
             }
             __syncwarp();
