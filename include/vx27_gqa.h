@@ -170,9 +170,9 @@ int vx27_gqa_prefill(const void *q_in, const void *k_in, const void *v_in, const
  * l = sum exp(s - m), o = sum exp(s - m) v / l. Record layout (fp32):
  *   o [B][nq][hd] followed by ml [B][nq][2]; record size B*nq*(hd+2) floats.
  * An empty range yields m = -inf, l = 0, o = 0. vx27_gqa_combine merges n_parts records
- * placed part_stride floats apart (0: back to back) -- m* = max m_i, l* = sum l_i
- * e^{m_i-m*}, o = sum o_i l_i e^{m_i-m*} / l* -- and applies the sigmoid gate (none when
- * gate is NULL).
+ * placed part_stride floats apart (0: back to back; else even, with parts 8-byte
+ * aligned) -- m* = max m_i, l* = sum l_i e^{m_i-m*}, o = sum o_i l_i e^{m_i-m*} / l* --
+ * and applies the sigmoid gate (none when gate is NULL).
  * A long range is split across CTAs and merged into the one record; the sub-records need
  * vx27_gqa_partial_workspace_size(B, nq, nkv, hd, p_end - p_begin) bytes of workspace (a
  * smaller or NULL workspace lowers the split count, down to one CTA per KV head).

@@ -116,6 +116,15 @@ def test_batched_entry_points_reject_bad_shapes_without_gpu(vxlib):
     rc = vxlib.vx27_deltanet_decode_tokens(None, 16, 16, 16, 16, 16, 16, 16, 16, 16, None, None,
                                            4, 16, 16, 128, 0, None, err, 256)
     assert rc == -1 and b"null pointer" in err.value
+    # the combine reads each record's (m, l) as 8-byte pairs: an odd record stride or an
+    # unaligned parts pointer is refused before any launch
+    P = C.c_void_p
+    rc = vxlib.vx27_gqa_combine(P(16), 2, C.c_size_t(rec // 4 + 1), None, P(16), 1, 24, 256, 0,
+                                None, err, 256)
+    assert rc == -1 and b"part_stride even" in err.value
+    rc = vxlib.vx27_gqa_combine(P(20), 2, C.c_size_t(0), None, P(16), 1, 24, 256, 0, None, err,
+                                256)
+    assert rc == -1 and b"8-byte aligned" in err.value
 
 
 def test_flag_values_match_the_header():

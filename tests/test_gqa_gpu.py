@@ -182,6 +182,48 @@ def test_partial_combine_context_parallel(cuda, orc, rope):
         assert rel_err(host(out).reshape(-1), full) < 1e-5
 
 
+@pytest.mark.parametrize("gated,out_bf16", [(True, False), (False, False), (True, True)])
+def test_combine_short_and_long_forms_agree(cuda, gated, out_bf16):
+    """vx27_gqa_combine merges up to 32 records in one pass (one L2 round trip) and more in
+    blocks; both forms sum in record order. 40 records whose last 8 are empty (l = 0, which
+    the merge skips) go through the long form and must give the short form's bits for the
+    first 32; both match the merge formula in fp64. Record 5 is empty too, and one sequence
+    has no valid record at all (its output is 0)."""
+    B, n, n_long = 2, 32, 40
+    rec = B * NQ * (HD + 2)
+    g = torch.Generator().manual_seed(17)
+    o = torch.randn(n_long, B * NQ * HD, generator=g)
+    m = torch.randn(n_long, B * NQ, generator=g) * 4.0
+    l = torch.rand(n_long, B * NQ, generator=g) * 50.0 + 0.5
+    l[5] = 0.0
+    m[5] = -float("inf")
+    l[n:] = 0.0
+    m[n:] = -float("inf")
+    l[:, NQ:] = 0.0  # sequence 1: every record empty
+    m[:, NQ:] = -float("inf")
+    parts = torch.cat([o, torch.stack([m, l], -1).reshape(n_long, -1)], 1).reshape(-1).cuda()
+    gate = torch.randn(B, NQ, HD, generator=g) if gated else None
+    odt = torch.bfloat16 if out_bf16 else torch.float32
+    outs = []
+    for k in (n, n_long):
+        out = torch.empty(B, NQ, HD, device="cuda", dtype=odt)
+        ops.gqa_combine(parts[:k * rec], k, None if gate is None else gate.cuda(), out)
+        outs.append(out.float().cpu())
+    assert torch.equal(outs[0], outs[1])
+    # fp64 restatement of the merge
+    md, ld, od = m[:n].double(), l[:n].double(), o[:n].double().view(n, B * NQ, HD)
+    M = torch.where(ld > 0, md, torch.full_like(md, -float("inf"))).amax(0)
+    w = torch.where(ld > 0, ld * torch.exp(md - M), torch.zeros_like(ld))
+    L = w.sum(0)
+    att = torch.where(L[:, None] > 0, (w[:, :, None] * od).sum(0) / L[:, None].clamp_min(1e-300),
+                      torch.zeros(B * NQ, HD, dtype=torch.float64)).view(B, NQ, HD)
+    if gate is not None:
+        att = att * torch.sigmoid(gate.double())
+    assert torch.all(outs[0][1] == 0)
+    tol = 1e-2 if out_bf16 else 1e-5
+    assert rel_err(outs[0].reshape(-1).numpy(), att.reshape(-1).numpy()) < tol
+
+
 def test_append_q_only_and_foreign_slot(cuda, orc, rope):
     """k_cache=NULL computes q only; a slot outside the shard leaves the cache untouched."""
     B, cap = 1, 64

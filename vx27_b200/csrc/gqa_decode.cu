@@ -198,6 +198,47 @@ gqa_combine_k(const float *__restrict__ parts, int n_parts, const void *__restri
     }
 }
 
+// The combine for at most CMB_FAST records, with one round trip to L2: each thread
+// requests its column of every record, and each warp the records' (m, l) (lane r: record
+// r) and the gate, all at once. Each warp then forms the max and the weights itself, so
+// no shared memory or CTA barrier is on the path. Same arithmetic and record order as
+// gqa_combine_k, hence the same bits.
+constexpr int CMB_FAST = 32;
+
+template <bool ACT_BF16, bool OUT_BF16, bool PDL>
+__global__ void __launch_bounds__(HD)
+gqa_combine32_k(const float *__restrict__ parts, int n_parts, const void *__restrict__ gate,
+                void *__restrict__ out, int B, int nq, size_t rec) {
+    if constexpr (PDL) grid_dep_wait();
+    const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x, lane = d & 31;
+    const size_t hq = (size_t)b * nq + h;
+    const float *col = parts + hq * HD + d;
+    const float *mlp = parts + (size_t)B * nq * HD + hq * 2;
+    float v[CMB_FAST];
+#pragma unroll
+    for (int r = 0; r < CMB_FAST; r++) v[r] = r < n_parts ? __ldcg(col + (size_t)r * rec) : 0.0f;
+    const float2 ml = lane < n_parts
+                          ? __ldcg(reinterpret_cast<const float2 *>(mlp + (size_t)lane * rec))
+                          : make_float2(-INFINITY, 0.0f);
+    const float g = gate ? act_ld<ACT_BF16>(gate, hq * HD + d) : 0.0f;
+    const float M = warp_max(ml.y > 0.0f ? ml.x : -INFINITY);
+    const float w = ml.y > 0.0f ? ml.y * expf(ml.x - M) : 0.0f;
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int r = 0; r < CMB_FAST; r++) {
+        const float wr = __shfl_sync(0xffffffffu, w, r);
+        if (wr != 0.0f) {  // skipped records (w = 0) add nothing
+            L += wr;
+            O = fmaf(wr, v[r], O);
+        }
+    }
+    const float att = L > 0.0f ? O / L : 0.0f;
+    if (gate)
+        act_st<OUT_BF16>(out, hq * HD + d, att * (1.0f / (1.0f + expf(-g))));
+    else
+        act_st<OUT_BF16>(out, hq * HD + d, att);
+}
+
 // Merges n_parts partial records into one partial record (same layout), for a range
 // that was split across CTAs: m = max m_i, l = sum l_i e^{m_i - m}, o = sum o_i l_i
 // e^{m_i - m} / l.
@@ -277,17 +318,21 @@ int launch_combine(const float *parts, int n_parts, const void *gate, void *out,
     const dim3 grid(nq, B);
     const bool a = flags & VX27_F_ACT_BF16, o = flags & VX27_F_OUT_BF16;
     const size_t rec = stride ? stride : (size_t)B * nq * (HD + 2);
-#define VX_CMB(A_, O_)                                                                     \
+#define VX_CMB1(K_, A_, O_)                                                                \
     if (pdl)                                                                               \
-        VX_CK(launch_pdl(gqa_combine_k<A_, O_, true>, grid, dim3(HD), 0, st, parts, n_parts, \
-                         gate, out, B, nq, rec));                                          \
+        VX_CK(launch_pdl(K_<A_, O_, true>, grid, dim3(HD), 0, st, parts, n_parts, gate, out, \
+                         B, nq, rec));                                                     \
     else                                                                                   \
-        gqa_combine_k<A_, O_, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
+        K_<A_, O_, false><<<grid, HD, 0, st>>>(parts, n_parts, gate, out, B, nq, rec);
+#define VX_CMB(A_, O_)                                                                     \
+    if (n_parts <= CMB_FAST) { VX_CMB1(gqa_combine32_k, A_, O_) }                          \
+    else { VX_CMB1(gqa_combine_k, A_, O_) }
     if (a && o) { VX_CMB(true, true) }
     else if (a) { VX_CMB(true, false) }
     else if (o) { VX_CMB(false, true) }
     else { VX_CMB(false, false) }
 #undef VX_CMB
+#undef VX_CMB1
     VX_CK(cudaGetLastError());
     return 0;
 }
@@ -498,6 +543,10 @@ int vx27_gqa_combine(const float *parts, int n_parts, size_t part_stride, const 
     if (part_stride && part_stride < rec)
         return fail(err, errlen, "vx27_gqa_combine: part_stride %zu < record size %zu",
                     part_stride, rec);
+    // each record's (m, l) pairs are read as 8-byte vectors
+    if (((uintptr_t)parts & 7) || (part_stride & 1))
+        return fail(err, errlen,
+                    "vx27_gqa_combine: parts must be 8-byte aligned and part_stride even");
     return launch_combine(parts, n_parts, gate, out, B, nq, flags, (cudaStream_t)stream, err,
                           errlen, part_stride);
 }
