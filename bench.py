@@ -633,41 +633,38 @@ def run_batch1(args, cpu: bool = True) -> dict:
         e1.record()
         torch.cuda.synchronize()
         us_launch = e0.elapsed_time(e1) * 1e3 / (reps * units)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            run()
-        graph.replay()
-        torch.cuda.synchronize()
-        e0.record()
-        for _ in range(reps):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        us_graph = e0.elapsed_time(e1) * 1e3 / (reps * units)
-        del graph
+        # graph replays: 10 warm, then enough timed replays (>= 200 for one decode, one
+        # for the 2000 tokens) that the per-replay launch jitter averages out
+        g_reps = max(reps, 200 // units, 1)
+
+        def graph_us(fn) -> float:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            for _ in range(10 if units == 1 else 1):
+                g.replay()
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(g_reps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            del g
+            return e0.elapsed_time(e1) * 1e3 / (g_reps * units)
+        us_graph = graph_us(run)
         other_us = {}
         for label, fn in others.items():
             for _ in range(args.warmup):
                 fn()
-            g2 = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g2):
-                fn()
-            g2.replay()
-            torch.cuda.synchronize()
-            e0.record()
-            for _ in range(reps):
-                g2.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            other_us[label] = round(e0.elapsed_time(e1) * 1e3 / (reps * units), 3)
-            del g2
+            other_us[label] = round(graph_us(fn), 3)
     if ops.device_status() != 0:
         raise RuntimeError("device status flag set during the batch-1 run")
     gbs = bytes_per_unit / (us_graph * 1e-6) / 1e9
     line = {
         "metric": f"microseconds per {unit_name} ({args.workload}, batch 1)",
         "value": round(us_graph, 3), "unit": f"us/{unit_name}", "n_gpus": 1,
-        "steps": reps, "warmup": args.warmup, "higher_is_better": False, "dtype": "f32",
+        "steps": reps, "graph_replays": g_reps, "warmup": args.warmup,
+        "higher_is_better": False, "dtype": "f32",
         "data": "synthetic (seeded, BASELINE.json distributions)",
         "config": {"workload": name},
         "us_per_unit_launched": round(us_launch, 3), "us_per_unit_graph": round(us_graph, 3),
