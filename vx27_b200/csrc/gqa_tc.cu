@@ -135,15 +135,41 @@ __device__ __forceinline__ uint4 pack8_bf16(const float (&x)[8]) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// A lane's 8 norm weights (dims 8*lane ..), with the zero-centred form's 1 + w applied.
+__device__ __forceinline__ void tc_norm_w8(float (&wv)[8], const float *w, const TcAppend &ap,
+                                           int lane) {
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const float v = w[8 * lane + e];
+        wv[e] = ap.one_p ? __fadd_rn(v, 1.0f) : v;
+    }
+}
+// A lane's cos / sin entries of the position's rope row rr (NULL: none), for the dims it
+// rotates (zero for dims past rope_dim).
+__device__ __forceinline__ void tc_rope8(float (&c)[8], float (&sn)[8], const float *rr,
+                                         const TcAppend &ap, int lane) {
+    const int d0 = 8 * lane, half = ap.rope_dim / 2;
+    const int i0 = d0 < half ? d0 : d0 - half;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const bool on = rr && d0 < ap.rope_dim;
+        c[e] = on ? rr[i0 + e] : 0.f;
+        sn[e] = on ? rr[half + i0 + e] : 0.f;
+    }
+}
+
 // One 256-dim row held 8 dims per lane (dims 8*lane ..): RMSNorm then the rotation, as
-// gqa_append_k rounds them; rr = the position's rope row, NULL for none (bad position).
-// Inlined into a row loop that is not unrolled: one copy of the code serves all rows, so
-// the staging warp's code does not crowd the instruction cache the other roles' loops
-// share (inlined and unrolled eight times it slowed a config 2 layer by 1.5%), and no call
-// saves and restores registers (as a called function it took ~14 us per item).
+// gqa_append_k rounds them; wv = the lane's norm weights (tc_norm_w8), c / sn = its rope
+// entries (tc_rope8), rot = whether the position's rope row exists (false for a bad
+// position). The per-row inputs are loaded once per item, so a row costs no memory round
+// trip. Inlined into a row loop that is not unrolled: one copy of the code serves all
+// rows, so the staging warp's code does not crowd the instruction cache the other roles'
+// loops share (inlined and unrolled eight times it slowed a config 2 layer by 1.5%), and no
+// call saves and restores registers (as a called function it took ~14 us per item).
 __device__ __forceinline__ void tc_norm_rope(float (&y)[8], const float (&x)[8],
-                                             const float *w, const TcAppend &ap,
-                                             const float *rr, int lane) {
+                                             const float (&wv)[8], const float (&c)[8],
+                                             const float (&sn)[8], bool rot,
+                                             const TcAppend &ap, int lane) {
     double ss = 0.0;
 #pragma unroll
     for (int e = 0; e < 8; e++) ss += (double)x[e] * (double)x[e];
@@ -151,11 +177,7 @@ __device__ __forceinline__ void tc_norm_rope(float (&y)[8], const float (&x)[8],
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(ss / HDIM), ap.eps)));
     const int d0 = 8 * lane;
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
-        float wv = w[d0 + e];
-        if (ap.one_p) wv = __fadd_rn(wv, 1.0f);
-        y[e] = __fmul_rn(__fmul_rn(x[e], r), wv);
-    }
+    for (int e = 0; e < 8; e++) y[e] = __fmul_rn(__fmul_rn(x[e], r), wv[e]);
     // the partner of dim d < half is d + half, held half / 8 lanes away
     const int half = ap.rope_dim / 2, hl = half / 8;
     const bool lo = d0 < half;
@@ -163,14 +185,12 @@ __device__ __forceinline__ void tc_norm_rope(float (&y)[8], const float (&x)[8],
 #pragma unroll
     for (int e = 0; e < 8; e++)
         yp[e] = __shfl_sync(0xffffffffu, y[e], (lo ? lane + hl : lane - hl) & 31);
-    if (rr && d0 < ap.rope_dim) {
-        const int i0 = lo ? d0 : d0 - half;
+    if (rot && d0 < ap.rope_dim) {
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            const float c = rr[i0 + e], s = rr[half + i0 + e];
             const float x0 = lo ? y[e] : yp[e], x1 = lo ? yp[e] : y[e];
-            y[e] = lo ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s))
-                      : __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+            y[e] = lo ? __fsub_rn(__fmul_rn(x0, c[e]), __fmul_rn(x1, sn[e]))
+                      : __fadd_rn(__fmul_rn(x0, sn[e]), __fmul_rn(x1, c[e]));
         }
     }
 }
@@ -307,10 +327,15 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
                 x[h][4] = raw[h][1].x; x[h][5] = raw[h][1].y; x[h][6] = raw[h][1].z; x[h][7] = raw[h][1].w;
             }
         }
+        // the item's norm weights and rope entries, once for all its rows
+        float wq[8], wk[8], rc[8], rs[8];
+        tc_norm_w8(wq, ap.qw, ap, lane);
+        if (app) tc_norm_w8(wk, ap.kw, ap, lane);
+        tc_rope8(rc, rs, rr, ap, lane);
 #pragma unroll 1
         for (int h = 0; h < G; h++) {
             float y[8], lo8[8];
-            tc_norm_rope(y, x[h], ap.qw, ap, rr, lane);
+            tc_norm_rope(y, x[h], wq, rc, rs, rr != nullptr, ap, lane);
 #pragma unroll
             for (int e = 0; e < 8; e++) lo8[e] = y[e] - bf16_to_f32(f32_to_bf16(y[e]));
             *reinterpret_cast<uint4 *>(&sm.q[qb][c][sw128(h, col)]) = pack8_bf16(y);
@@ -322,7 +347,7 @@ gqa_split_tc(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CU
             // the rows go out as bulk copies (async proxy, like the TMA loads that read them
             // back), staged in shared memory
             float y[8];
-            tc_norm_rope(y, x[G], ap.kw, ap, rr, lane);
+            tc_norm_rope(y, x[G], wk, rc, rs, rr != nullptr, ap, lane);
             *reinterpret_cast<uint4 *>(&sm.kvrow[0][16 * lane]) = pack8_bf16(y);
             *reinterpret_cast<uint4 *>(&sm.kvrow[1][16 * lane]) = pack8_bf16(x[G + 1]);
             fence_proxy_async();
