@@ -395,11 +395,12 @@ __global__ void gate_params_k(const void *__restrict__ a, const void *__restrict
 // CTA (cs, vh) keeps columns [16 cs, 16 cs + 16) of V head vh's 128 x 128 state in
 // registers for all T tokens (the delta rule's columns are independent): warps 0-7 hold it,
 // one 8-row block of one column per thread, and run each token's decay, S^T k, delta,
-// update and S^T q with two column reductions. Warps 8-15 prepare the tokens up to four
-// ahead into a ring of parameter slots: the width-4 conv + SiLU of the head's q and k
-// channels (one per thread, computed by each of the head's 8 CTAs) from a private copy of
-// their conv history (read from the ring at the start, so any position sequence reproduces
-// T single-token calls), then the l2 norms from double sums of squares. Warp 16 forms the
+// update and S^T q with two column reductions. Warps 8-15 prepare the tokens ahead into a
+// ring of parameter slots, four groups of two warps taking every fourth token: the width-4
+// conv + SiLU of the head's q and k channels (two of each per thread, computed by each of
+// the head's 8 CTAs) from the group's copy of their conv history (read from the ring at the
+// start, so any position sequence reproduces T single-token calls), then the l2 norms from
+// double sums of squares. Warp 16 forms the
 // gates (double precision) and the conv of this CTA's 16 v channels 32 tokens at a time.
 // Nothing crosses CTAs: the state goes back to global memory at the end, and the ring is
 // left untouched here (the CTAs of a QK head may run in different waves, so each must find
@@ -407,7 +408,9 @@ __global__ void gate_params_k(const void *__restrict__ a, const void *__restrict
 // token this replaces one launch and a 1 MB state round trip.
 constexpr int TK_SPLIT = 8;
 constexpr int TK_COLS = HD / TK_SPLIT;
-constexpr int TK_NPARAM = 4;
+constexpr int TK_NPARAM = 8;
+constexpr int TK_NG = 4;   // prep groups (token t goes to group t % TK_NG)
+constexpr int TK_GW = 2;   // warps per prep group; a thread owns 2 q and 2 k channels
 constexpr int TK_NCH = 2 * HD + TK_COLS;  // q, k and this CTA's v channels
 
 struct TkParams {
@@ -418,9 +421,10 @@ struct TkSmem {
     TkParams prm[TK_NPARAM];
     float gbeta[2][32], gdecay[2][32];  // gates of 32-token batches (gate warp -> prep)
     float gv[2][32][TK_COLS];           // and the conv outputs of this CTA's v channels
-    float hist[TK_NCH][4];       // conv history by position & 3 (prep group 0, v channels)
-    float hist1[2 * HD][4];      // the q/k channels' history of prep group 1
-    double nps[2][2][4][2];      // [group][token parity][warp][q, k] sums of squares
+    float hq[TK_NG][2 * HD][4];  // conv history of the q/k channels by position & 3, a copy
+                                 // per prep group
+    float hv[TK_COLS][4];        // and of this CTA's v channels (the gate warp's)
+    double nps[TK_NG][2][TK_GW][2];  // [group][token parity][warp][q, k] sums of squares
     float red[2][8][TK_COLS];    // per-warp column partial sums (S^T k, S^T q)
     uint64_t pfull[TK_NPARAM], pempty[TK_NPARAM], gfull[2], gempty[2];
     int abort;
@@ -502,12 +506,12 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
     };
     if (tid == 0) {
         for (int i = 0; i < TK_NPARAM; i++) {
-            mbar_init(&sm.pfull[i], 4);  // one arrival per warp of the token's prep group
+            mbar_init(&sm.pfull[i], TK_GW);  // one arrival per warp of the token's prep group
             mbar_init(&sm.pempty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&sm.gfull[i], 1);
-            mbar_init(&sm.gempty[i], 2);  // both prep groups have read the batch
+            mbar_init(&sm.gempty[i], TK_NG);  // every prep group has read the batch
         }
         sm.abort = 0;
         fence_barrier_init();
@@ -516,8 +520,12 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
 #pragma unroll
         for (int sl = 0; sl < 4; sl++) {
             const float v = ring[(size_t)sl * C + chan(ch)];
-            sm.hist[ch][sl] = v;
-            if (ch < 2 * HD) sm.hist1[ch][sl] = v;
+            if (ch < 2 * HD) {
+#pragma unroll
+                for (int g = 0; g < TK_NG; g++) sm.hq[g][ch][sl] = v;
+            } else {
+                sm.hv[ch - 2 * HD][sl] = v;
+            }
         }
     __syncthreads();
 
@@ -559,7 +567,7 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             for (int tt = 0; tt < 32; tt++) {
                 const int p = __shfl_sync(0xffffffffu, pl, tt);
                 if (lane < TK_COLS && tt < nt) {
-                    float *h = sm.hist[2 * HD + jv];
+                    float *h = sm.hv[jv];
                     float acc = __fmul_rn(wv.x, h[(p - 3) & 3]);
                     acc = __fadd_rn(acc, __fmul_rn(wv.y, h[(p - 2) & 3]));
                     acc = __fadd_rn(acc, __fmul_rn(wv.z, h[(p - 1) & 3]));
@@ -577,17 +585,24 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             if (lane == 0) mbar_arrive(&sm.gfull[gb_]);
         }
     } else if (warp >= 8) {
-        // ---- prep: two groups of four warps take the even and the odd tokens, so two
-        // tokens are prepared at once. Thread jj of group g owns q channel jj and k channel
-        // jj, with the group's own copy of their conv history, into which it also writes
-        // the other group's tokens' inputs in token order (the ring's semantics).
-        const int g = (warp - 8) >> 2, wg = (warp - 8) & 3;
-        const int jj = tid - 256 - 128 * g;
-        const int cq = chan(jj), ck = chan(HD + jj);
-        float *hq = g ? sm.hist1[jj] : sm.hist[jj];
-        float *hk = g ? sm.hist1[HD + jj] : sm.hist[HD + jj];
-        const float4 wq = *reinterpret_cast<const float4 *>(conv_w + (size_t)cq * 4);
-        const float4 wk = *reinterpret_cast<const float4 *>(conv_w + (size_t)ck * 4);
+        // ---- prep: TK_NG groups of TK_GW warps; group g takes the tokens t = g mod TK_NG,
+        // so TK_NG tokens are prepared at once. Thread jj of a group owns q channels jj and
+        // jj + 64 and the same k channels, with the group's own copy of their conv history,
+        // into which it first writes the other groups' tokens' inputs in token order (the
+        // ring's semantics), all read from global memory a token window ahead.
+        constexpr int NJ = 2, TW = TK_NG;  // channels of q (and of k) per thread; window
+        const int g = (warp - 8) / TK_GW, wg = (warp - 8) % TK_GW;
+        const int jj = tid - 256 - 32 * TK_GW * g;
+        float(*hh)[4] = sm.hq[g];
+        int cq[NJ], ck[NJ];
+        float4 wq[NJ], wk[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            cq[j] = chan(jj + 64 * j);
+            ck[j] = chan(HD + jj + 64 * j);
+            wq[j] = *reinterpret_cast<const float4 *>(conv_w + (size_t)cq[j] * 4);
+            wk[j] = *reinterpret_cast<const float4 *>(conv_w + (size_t)ck[j] * 4);
+        }
         const float qs = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
         const bool own = qk_owner;  // this CTA writes the q/k channels' snapshots
         auto conv = [&](float *h, float4 wt, float x, int p) {
@@ -598,25 +613,38 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             h[p & 3] = x;
             return __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
         };
-        // inputs of tokens t - 1 (the other group's) and t, the next pair requested while
-        // this one is prepared
-        auto ld = [&](int t, float &xq, float &xk, int &p) {
+        // the inputs of tokens t - TW + 1 .. t (the other groups' and this one's)
+        float xq[TW][NJ], xk[TW][NJ], nq[TW][NJ], nk[TW][NJ];
+        int xp[TW], np[TW];
+        auto ld = [&](int t, float(&q)[NJ], float(&k)[NJ], int &p) {
             if (t >= 0 && t < T) {
-                xq = act_ld<ACT_BF16>(qkv, (size_t)t * C + cq);
-                xk = act_ld<ACT_BF16>(qkv, (size_t)t * C + ck);
+#pragma unroll
+                for (int j = 0; j < NJ; j++) {
+                    q[j] = act_ld<ACT_BF16>(qkv, (size_t)t * C + cq[j]);
+                    k[j] = act_ld<ACT_BF16>(qkv, (size_t)t * C + ck[j]);
+                }
                 p = pos[t];
+            } else {
+#pragma unroll
+                for (int j = 0; j < NJ; j++) q[j] = k[j] = 0.f;
+                p = 0;
             }
         };
-        float aq = 0.f, ak = 0.f, bq = 0.f, bk = 0.f;  // tokens t - 1 and t
-        int ap = 0, bp = 0;
-        ld(g - 1, aq, ak, ap);
-        ld(g, bq, bk, bp);
-        for (int t = g; t < T; t += 2) {
-            const int slot = t % TK_NPARAM, par = (t >> 1) & 1;
-            const float pxq = aq, pxk = ak, xq = bq, xk = bk;
-            const int pp = ap, p = bp;
-            ld(t + 1, aq, ak, ap);
-            ld(t + 2, bq, bk, bp);
+#pragma unroll
+        for (int i = 0; i < TW; i++) ld(g - TW + 1 + i, nq[i], nk[i], np[i]);
+        for (int t = g; t < T; t += TK_NG) {
+            const int slot = t % TK_NPARAM, par = (t / TK_NG) & 1;
+#pragma unroll
+            for (int i = 0; i < TW; i++) {
+                xp[i] = np[i];
+#pragma unroll
+                for (int j = 0; j < NJ; j++) {
+                    xq[i][j] = nq[i][j];
+                    xk[i][j] = nk[i][j];
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < TW; i++) ld(t + 1 + i, nq[i], nk[i], np[i]);  // next window
             if (jj == 0 && (t & 31) == g &&
                 !tk_wait(&sm.gfull[(t >> 5) & 1], (t >> 6) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
                 *(volatile int *)&sm.abort = 1;
@@ -624,44 +652,67 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
                 !tk_wait(&sm.pempty[slot], ((t / TK_NPARAM) - 1) & 1, sm, status, VX_DEV_TIMEOUT_TMA))
                 *(volatile int *)&sm.abort = 1;
             const bool ok = !*(volatile int *)&sm.abort;
-            if (t >= 1) {  // the other group's token t - 1 enters this group's history first
-                hq[pp & 3] = pxq;
-                hk[pp & 3] = pxk;
-            }
-            const float yq = conv(hq, wq, xq, p);
-            const float yk = conv(hk, wk, xk, p);
-            if (conv_ckpt && own) {  // the history after token t, oldest first
+            // the other groups' tokens t - TW + 1 .. t - 1 enter this group's history first
 #pragma unroll
-                for (int k2 = 0; k2 < 3; k2++) {
-                    conv_ckpt[((size_t)t * C + cq) * 3 + k2] = hq[(p - 2 + k2) & 3];
-                    conv_ckpt[((size_t)t * C + ck) * 3 + k2] = hk[(p - 2 + k2) & 3];
+            for (int i = 0; i < TW - 1; i++) {
+                if (t - TW + 1 + i >= 0) {
+#pragma unroll
+                    for (int j = 0; j < NJ; j++) {
+                        hh[jj + 64 * j][xp[i] & 3] = xq[i][j];
+                        hh[HD + jj + 64 * j][xp[i] & 3] = xk[i][j];
+                    }
                 }
             }
+            const int p = xp[TW - 1];
+            float yq[NJ], yk[NJ];
+            double sq = 0.0, sk = 0.0;
+#pragma unroll
+            for (int j = 0; j < NJ; j++) {
+                yq[j] = conv(hh[jj + 64 * j], wq[j], xq[TW - 1][j], p);
+                yk[j] = conv(hh[HD + jj + 64 * j], wk[j], xk[TW - 1][j], p);
+                sq += (double)yq[j] * (double)yq[j];
+                sk += (double)yk[j] * (double)yk[j];
+            }
+            if (conv_ckpt && own) {  // the history after token t, oldest first
+#pragma unroll
+                for (int j = 0; j < NJ; j++)
+#pragma unroll
+                    for (int k2 = 0; k2 < 3; k2++) {
+                        conv_ckpt[((size_t)t * C + cq[j]) * 3 + k2] = hh[jj + 64 * j][(p - 2 + k2) & 3];
+                        conv_ckpt[((size_t)t * C + ck[j]) * 3 + k2] = hh[HD + jj + 64 * j][(p - 2 + k2) & 3];
+                    }
+            }
             // l2 norms from double sums of squares: warp sums, then every thread adds the
-            // group's four (one barrier per token)
-            const double sq = warp_sum_d((double)yq * (double)yq);
-            const double sk = warp_sum_d((double)yk * (double)yk);
+            // group's warps' (one barrier per token)
+            sq = warp_sum_d(sq);
+            sk = warp_sum_d(sk);
             if (lane == 0) {
                 sm.nps[g][par][wg][0] = sq;
                 sm.nps[g][par][wg][1] = sk;
             }
-            named_bar_sync(2 + g, 128);
-            const double(*np_)[2] = sm.nps[g][par];
-            const double ssq = (np_[0][0] + np_[1][0]) + (np_[2][0] + np_[3][0]);
-            const double ssk = (np_[0][1] + np_[1][1]) + (np_[2][1] + np_[3][1]);
+            named_bar_sync(2 + g, 32 * TK_GW);
+            double ssq = 0.0, ssk = 0.0;
+#pragma unroll
+            for (int w2 = 0; w2 < TK_GW; w2++) {
+                ssq += sm.nps[g][par][w2][0];
+                ssk += sm.nps[g][par][w2][1];
+            }
             const float rq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ssq, 1e-6f)));
             const float rk = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ssk, 1e-6f)));
             if (ok) {
                 TkParams &P = sm.prm[slot];
-                P.qn[jj] = __fmul_rn(__fmul_rn(yq, rq), qs);
-                P.kn[jj] = __fmul_rn(yk, rk);
+#pragma unroll
+                for (int j = 0; j < NJ; j++) {
+                    P.qn[jj + 64 * j] = __fmul_rn(__fmul_rn(yq[j], rq), qs);
+                    P.kn[jj + 64 * j] = __fmul_rn(yk[j], rk);
+                }
                 if (jj < TK_COLS) P.v[jj] = sm.gv[(t >> 5) & 1][t & 31][jj];
                 if (jj == 0) {
                     P.beta = sm.gbeta[(t >> 5) & 1][t & 31];
                     P.decay = sm.gdecay[(t >> 5) & 1][t & 31];
-                    // this group's last token of a full batch: one of the batch's two
+                    // this group's last token of a full batch: one of the batch's TK_NG
                     // releases (a partial batch is the last one and is not refilled)
-                    if ((t & 31) == 30 + g) mbar_arrive(&sm.gempty[(t >> 5) & 1]);
+                    if ((t & 31) == 32 - TK_NG + g) mbar_arrive(&sm.gempty[(t >> 5) & 1]);
                 }
             }
             __syncwarp();
