@@ -395,7 +395,7 @@ __global__ void gate_params_k(const void *__restrict__ a, const void *__restrict
 // CTA (cs, vh) keeps columns [16 cs, 16 cs + 16) of V head vh's 128 x 128 state in
 // registers for all T tokens (the delta rule's columns are independent): warps 0-7 hold it,
 // one 8-row block of one column per thread, and run each token's decay, S^T k, delta,
-// update and S^T q with two column reductions. Warps 8-15 prepare the tokens ahead into a
+// update and S^T q with two column reductions and one barrier. Warps 8-15 prepare the tokens ahead into a
 // ring of parameter slots, four groups of two warps taking every fourth token: the width-4
 // conv + SiLU of the head's q and k channels (two of each per thread, computed by each of
 // the head's 8 CTAs) from the group's copy of their conv history (read from the ring at the
@@ -415,8 +415,9 @@ constexpr int TK_NCH = 2 * HD + TK_COLS;  // q, k and this CTA's v channels
 
 struct TkParams {
     float qn[HD], kn[HD], v[TK_COLS];
-    float beta, decay;
+    float beta, decay, pad[2];  // a multiple of 16 bytes: rows are read as float4
 };
+static_assert(sizeof(TkParams) % 16 == 0, "parameter slots stay 16-byte aligned");
 struct TkSmem {
     TkParams prm[TK_NPARAM];
     float gbeta[2][32], gdecay[2][32];  // gates of 32-token batches (gate warp -> prep)
@@ -425,7 +426,7 @@ struct TkSmem {
                                  // per prep group
     float hv[TK_COLS][4];        // and of this CTA's v channels (the gate warp's)
     double nps[TK_NG][2][TK_GW][2];  // [group][token parity][warp][q, k] sums of squares
-    float red[2][8][TK_COLS];    // per-warp column partial sums (S^T k, S^T q)
+    float red[2][2][8][TK_COLS];  // [S^T k, S^T q][token parity][warp] column partial sums
     uint64_t pfull[TK_NPARAM], pempty[TK_NPARAM], gfull[2], gempty[2];
     int abort;
 };
@@ -719,54 +720,72 @@ dn_tokens_k(float *__restrict__ S, float *__restrict__ ring, const void *__restr
             if (lane == 0) mbar_arrive(&sm.pfull[slot]);
         }
     } else {
-        // ---- state: thread (row block rb, column col) holds rows 8 rb .. 8 rb + 7
+        // ---- state: thread (row block rb, column col) holds rows 8 rb .. 8 rb + 7 of
+        // column col. One CTA barrier per token: the partial sums of both reductions are
+        // kept by token parity, and token t's output (and its parameter slot's release)
+        // waits for token t + 1's barrier.
         const int rb = tid >> 4, col = tid & (TK_COLS - 1);
         float *Sh = S + (size_t)vh * HD * HD;
         float s[8];
 #pragma unroll
         for (int i = 0; i < 8; i++) s[i] = Sh[(size_t)(8 * rb + i) * HD + col0 + col];
+        auto rows8 = [&](const float *v, float (&r)[8]) {
+            const float4 a = reinterpret_cast<const float4 *>(v + 8 * rb)[0];
+            const float4 b = reinterpret_cast<const float4 *>(v + 8 * rb)[1];
+            r[0] = a.x; r[1] = a.y; r[2] = a.z; r[3] = a.w;
+            r[4] = b.x; r[5] = b.y; r[6] = b.z; r[7] = b.w;
+        };
+        // token tt's output from the per-warp partials (all threads are past writing them)
+        auto out_of = [&](int tt) {
+            if (tid < TK_COLS) {
+                float ot = 0.f;
+#pragma unroll
+                for (int w2 = 0; w2 < 8; w2++) ot += sm.red[1][tt & 1][w2][tid];
+                act_st<OUT_BF16>(o, ((size_t)tt * nv + vh) * HD + col0 + tid, ot);
+            }
+            if (tid == 0) mbar_arrive(&sm.pempty[tt % TK_NPARAM]);
+        };
         bool ok = true;
         for (int t = 0; t < T && ok; t++) {
-            const int slot = t % TK_NPARAM;
+            const int slot = t % TK_NPARAM, par = t & 1;
             ok = tk_wait(&sm.pfull[slot], (t / TK_NPARAM) & 1, sm, status, VX_DEV_TIMEOUT_TMA);
             const TkParams &P = sm.prm[slot];  // (after a failed wait: read, then discarded)
             const float decay = P.decay;
+            float kr[8];
+            rows8(P.kn, kr);
             float kv = 0.f;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 s[i] = __fmul_rn(s[i], decay);
-                kv = fmaf(s[i], P.kn[8 * rb + i], kv);
+                kv = fmaf(s[i], kr[i], kv);
             }
             kv += __shfl_xor_sync(0xffffffffu, kv, 16);
-            if (lane < TK_COLS) sm.red[0][warp][col] = kv;
+            if (lane < TK_COLS) sm.red[0][par][warp][col] = kv;
             ok = named_bar_and(1, 256, ok);  // the partials, and one outcome for all threads
             if (!ok) break;
+            if (t >= 1) out_of(t - 1);
             float kvt = 0.f;
 #pragma unroll
-            for (int w2 = 0; w2 < 8; w2++) kvt += sm.red[0][w2][col];
+            for (int w2 = 0; w2 < 8; w2++) kvt += sm.red[0][par][w2][col];
             const float delta = (P.v[col] - kvt) * P.beta;
+            float qr[8];
+            rows8(P.qn, qr);
             float op = 0.f;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-                s[i] = fmaf(P.kn[8 * rb + i], delta, s[i]);
-                op = fmaf(s[i], P.qn[8 * rb + i], op);
+                s[i] = fmaf(kr[i], delta, s[i]);
+                op = fmaf(s[i], qr[i], op);
             }
             op += __shfl_xor_sync(0xffffffffu, op, 16);
-            if (lane < TK_COLS) sm.red[1][warp][col] = op;
+            if (lane < TK_COLS) sm.red[1][par][warp][col] = op;
             if (S_ckpt) {
                 float *Sc = S_ckpt + ((size_t)t * nv + vh) * HD * HD;
 #pragma unroll
                 for (int i = 0; i < 8; i++) Sc[(size_t)(8 * rb + i) * HD + col0 + col] = s[i];
             }
-            named_bar_sync(1, 256);
-            if (tid < TK_COLS) {
-                float ot = 0.f;
-#pragma unroll
-                for (int w2 = 0; w2 < 8; w2++) ot += sm.red[1][w2][tid];
-                act_st<OUT_BF16>(o, ((size_t)t * nv + vh) * HD + col0 + tid, ot);
-            }
-            if (tid == 0) mbar_arrive(&sm.pempty[slot]);
         }
+        named_bar_sync(1, 256);  // the last token's partials (every thread leaves alike)
+        if (ok) out_of(T - 1);
 #pragma unroll
         for (int i = 0; i < 8; i++) Sh[(size_t)(8 * rb + i) * HD + col0 + col] = s[i];
     }
