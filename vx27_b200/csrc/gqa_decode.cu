@@ -4,8 +4,10 @@
 //   split kernel   tensor-core split-KV flash decoding (gqa_tc.cu), one CTA per
 //                  (sequence, KV head, split) serving the nq/nkv Q heads of the group;
 //                  writes one partial record (m, l, o) per split
-//   gqa_combine_k  log-sum-exp merge of the partial records + sigmoid output gate
-//                  (src/vx27_qfwd.c:347-371)
+//   gqa_combine32_k / gqa_combine_k
+//                  log-sum-exp merge of the partial records + sigmoid output gate
+//                  (src/vx27_qfwd.c:347-371): up to 32 records in one round trip to L2,
+//                  more in blocks, the same bits either way
 #include <math.h>
 #include "common.cuh"
 #include "../../include/vx27_gqa.h"
